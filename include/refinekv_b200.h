@@ -1,0 +1,184 @@
+/*
+ * refinekv_b200.h -- C ABI of the RefineKV decode hot path on B200 (sm_100a).
+ *
+ * The reference (Kevin-lkw/RefineKV-release v0.1.2) is a Python package whose
+ * GPU backend is a set of Triton kernels behind two launcher functions,
+ * src/refinekv/kernels/runtime.py:93 (select_blocks_triton) and :123
+ * (sparse_attention_triton), plus the torch-only summarizer
+ * src/refinekv/summary.py:46 (build_summary).  This library replaces exactly
+ * that seam.  Every entry point takes plain device pointers, element
+ * strides, sizes, scalars and a cudaStream_t passed as void*, returns an
+ * rkv_status, never allocates device memory, and only enqueues work on the
+ * given stream (no host synchronisation), so every call can be captured in a
+ * CUDA graph.
+ *
+ * Data types: K/V caches, pages and summaries are bf16; queries are bf16 or
+ * fp32 (rounded to bf16 before use, as the reference does); outputs are in
+ * the query dtype.  Head dimensions 64, 128, 192 and 256; block sizes 16,
+ * 32 and 64; GQA groups of 1..16 query rows per KV head.
+ *
+ * Caller-owned scratch: rkv_select and rkv_decode take a workspace whose
+ * size comes from the matching *_workspace_size function (same arguments,
+ * same current device).  It must be zero-filled once when it is allocated;
+ * the kernels leave it reusable.  Word 0 of the workspace (int32) is a
+ * sticky device status: nonzero bits mean a bounded device wait expired
+ * (RKV_DEVICE_TIMEOUT) or a device-side input was out of range
+ * (RKV_DEVICE_BAD_INPUT).  Calls that share a workspace must be ordered on
+ * one stream.
+ */
+#ifndef REFINEKV_B200_H_
+#define REFINEKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RKV_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define RKV_API __attribute__((visibility("default")))
+#else
+#define RKV_API
+#endif
+
+typedef enum rkv_status {
+  RKV_OK = 0,
+  RKV_ERR_INVALID_ARGUMENT = 1, /* shapes, sizes, null pointers, eps, reduction */
+  RKV_ERR_UNSUPPORTED = 2,      /* head_dim / block_size / group outside the kernel set */
+  RKV_ERR_ALIGNMENT = 3,        /* a pointer or stride is not 16-byte aligned */
+  RKV_ERR_WORKSPACE = 4,        /* workspace missing, too small or misaligned */
+  RKV_ERR_CUDA = 5              /* a CUDA runtime call failed; see rkv_last_error() */
+} rkv_status;
+
+/* Bits of the device status word (int32 at workspace offset 0). */
+#define RKV_DEVICE_TIMEOUT 1
+#define RKV_DEVICE_BAD_INPUT 2
+
+/* GQA reductions, RefineKVConfig.gqa_reduction (reference config.py:18). */
+#define RKV_GQA_MEAN 0
+#define RKV_GQA_MAX 1
+#define RKV_GQA_ANY 2
+
+/* Query / output dtypes. */
+#define RKV_DTYPE_BF16 0
+#define RKV_DTYPE_F32 1
+
+/* Phases of rkv_decode (bit mask; RKV_PHASE_ALL for a normal call). */
+#define RKV_PHASE_STATS 1  /* selector phase A: scores, deltas, LSE partials */
+#define RKV_PHASE_FINAL 2  /* selector phase B: mask, compaction, representatives */
+#define RKV_PHASE_ATTEND 4 /* pages + suffix attention and the combine */
+#define RKV_PHASE_ALL 7
+
+/*
+ * Device view of a BlockSummary (reference summary.py:10-32).
+ *   key_pages / value_pages: (heads, blocks, block_size, head_dim) bf16 with
+ *     contiguous pages (page stride block_size*head_dim, row stride
+ *     head_dim) and a free head stride (they may alias the KV cache).
+ *   counts: (blocks,) int64 tokens per block (block_size, tail for the last).
+ *   key_mean / value_mean / ellipsoid: (heads, blocks, head_dim) bf16, contiguous.
+ *   value_norm: (heads, blocks) fp32; max_value_norm: (heads,) fp32.
+ */
+typedef struct rkv_summary {
+  const void* key_pages;
+  const void* value_pages;
+  int64_t key_page_head_stride;   /* elements */
+  int64_t value_page_head_stride; /* elements */
+  const int64_t* counts;
+  const void* key_mean;
+  const void* value_mean;
+  const void* ellipsoid;
+  const float* value_norm;
+  const float* max_value_norm;
+  int64_t heads;
+  int64_t blocks;
+  int64_t block_size;
+  int64_t head_dim;
+  int64_t prompt_length;
+} rkv_summary;
+
+/*
+ * Block summaries of one prompt (replaces reference summary.py:46-113,
+ * build_summary; the page view of summary.py:35-43 is the optional copy).
+ *   keys / values: (heads, tokens, head_dim) bf16, element strides given,
+ *     innermost stride 1, 16-byte aligned rows.
+ *   key_pages_out / value_pages_out: optional (heads, blocks, block_size,
+ *     head_dim) contiguous destinations; when non-null the kernel also
+ *     writes the zero-padded page copy (needed when tokens % block_size != 0
+ *     or the cache rows are not page-contiguous).  Pass null for both or
+ *     neither.
+ *   Outputs as in rkv_summary; max_value_norm is zeroed by this call.
+ */
+RKV_API int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                  int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                  int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                  void* key_pages_out, void* value_pages_out, void* key_mean, void* value_mean,
+                  void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
+                  void* stream);
+
+/*
+ * Workspace bytes for rkv_select with `queries` query instances.
+ */
+RKV_API size_t rkv_select_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,
+                                 int64_t queries);
+
+/*
+ * Block selection for one or more queries (replaces reference
+ * kernels/runtime.py:93 select_blocks_triton; math of reference.py:10-47).
+ *   queries: (queries, heads, group, head_dim) contiguous, dtype query_dtype.
+ *   mask: (heads, blocks) uint8 (0/1, usable as a bool tensor).  With
+ *     accumulate == 0 and queries == 1 the mask is overwritten; otherwise
+ *     (accumulate != 0, or several queries) the union of the selections is
+ *     ORed into it -- several queries with accumulate == 0 first clear it.
+ *     Several queries give the prompt-anchor union of reference
+ *     integrations/transformers.py:543-552 in one pair of launches.
+ */
+RKV_API int rkv_select(const rkv_summary* summary, const void* queries, int query_dtype, int64_t queries_n,
+               int64_t group, float eps, int reduction, uint8_t* mask, int accumulate,
+               void* workspace, size_t workspace_size, void* stream);
+
+/*
+ * Workspace bytes for rkv_decode.
+ */
+RKV_API size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,
+                                 int64_t block_size);
+
+/*
+ * One decode step of one layer: selection, representatives, refined pages,
+ * suffix and combine (replaces reference kernels/runtime.py:123
+ * sparse_attention_triton; math of reference.py:50-73).
+ *   query: (heads, group, head_dim) contiguous, dtype query_dtype.
+ *   key_suffix / value_suffix: (heads, suffix_capacity, head_dim) bf16 with
+ *     element strides; may be null when suffix_capacity == 0.
+ *   suffix_length: device int32 scalar with the visible suffix length (CUDA
+ *     graph replay), or null to use suffix_length_host.
+ *   anchor_mask: (heads, blocks) uint8 or null; ORed into the selection.
+ *   output: (heads, group, head_dim) in query_dtype.
+ *   selected: (heads, blocks) uint8 mask written by the call.
+ *   phases: RKV_PHASE_ALL, or a subset for timing individual kernels (the
+ *     phases must still run in order on the stream).
+ */
+RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+               const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+               int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+               int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+               const int32_t* suffix_length, int64_t suffix_length_host,
+               const uint8_t* anchor_mask, float eps, int reduction, void* output,
+               uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
+               void* stream);
+
+/* Kernel launches one rkv_decode call makes for the given phases. */
+RKV_API int rkv_decode_launch_count(unsigned phases);
+
+/* Message of the last failing call on this host thread ("" if none). */
+RKV_API const char* rkv_last_error(void);
+RKV_API const char* rkv_status_string(int status);
+RKV_API int rkv_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REFINEKV_B200_H_ */

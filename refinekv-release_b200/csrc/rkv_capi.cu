@@ -1,0 +1,605 @@
+// extern "C" entry points of librefinekv_b200.so (declared in
+// include/refinekv_b200.h): argument checks, the launch plan shared by the
+// workspace-size functions and the launches, TMA descriptor encoding, and the
+// kernel launches.  No device memory is allocated here.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "refinekv_b200.h"
+#include "rkv_kernels.h"
+
+namespace rkv {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(RKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+bool supported_dim(int64_t d) { return d == 64 || d == 128 || d == 192 || d == 256; }
+bool supported_block(int64_t b) { return b == 16 || b == 32 || b == 64; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct DeviceInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+
+int device_info(DeviceInfo* info) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return fail(RKV_ERR_CUDA, "device index out of range");
+  if (cache[dev].sms == 0) {
+    int sms = 0, optin = 0;
+    err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(SM count)");
+    err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(shared memory)");
+    cache[dev].sms = sms;
+    cache[dev].smem_optin = optin;
+  }
+  *info = cache[dev];
+  return RKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launch plan: grid splits, pipeline depths, shared memory, workspace layout.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int tiles = 0;
+  int warps_a = 4, parts_a = 1, tpc_a = 1, stages_a = 1;
+  size_t smem_a = 0;
+  int warps_b = 4, parts_b = 1, tpc_b = 1, stages_b = 2, seg_cap = 0;
+  size_t smem_b = 0;
+  int warps_c = 4, stages_c = 2, ctas = 1;
+  size_t smem_c = 0;
+  // workspace offsets (bytes)
+  size_t status = 0, done = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
+  size_t rep_m = 0, rep_l = 0, rep_o = 0, att_m = 0, att_l = 0, att_o = 0, bytes = 0;
+};
+
+void split(int tiles, int target_parts, int* parts, int* per) {
+  int p = std::max(1, std::min(tiles, target_parts));
+  *per = static_cast<int>(cdiv(tiles, p));
+  *parts = static_cast<int>(cdiv(tiles, *per));
+}
+
+// `decode` plans rkv_decode (one query instance); otherwise rkv_select.
+int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t dim,
+              int64_t block_size, int64_t instances, bool decode) {
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc != RKV_OK) return rc;
+  pl->tiles = static_cast<int>(cdiv(blocks, kSelectTile));
+  const int64_t rows = heads * instances;
+  // Phase A: about two CTAs per SM in total.
+  split(pl->tiles, static_cast<int>(cdiv(2LL * dev.sms, rows)), &pl->parts_a, &pl->tpc_a);
+  pl->stages_a = static_cast<int>(std::min<int64_t>(2, cdiv(pl->tpc_a, pl->warps_a)));
+  pl->smem_a = stats_smem_bytes(static_cast<int>(dim), pl->warps_a, pl->stages_a,
+                                static_cast<int>(group));
+  // Phase B: about one CTA per SM; segment capacity = blocks per CTA.
+  split(pl->tiles, static_cast<int>(cdiv(dev.sms, rows)), &pl->parts_b, &pl->tpc_b);
+  pl->seg_cap = pl->tpc_b * kSelectTile;
+  pl->stages_b = decode ? 2 : 0;  // select mode stages no value tiles
+  pl->smem_b = final_smem_bytes(static_cast<int>(dim), pl->warps_b, pl->stages_b,
+                                static_cast<int>(group), pl->tpc_b);
+  if (pl->smem_a > static_cast<size_t>(dev.smem_optin) ||
+      pl->smem_b > static_cast<size_t>(dev.smem_optin)) {
+    return fail(RKV_ERR_UNSUPPORTED, "selector tiles do not fit in shared memory");
+  }
+  if (decode) {
+    // Attention: deepest ring that fits one CTA per SM, 4 warps if a stage is
+    // at most 16 KB, otherwise fewer warps with at least two stages each.
+    const int64_t stage = 2 * block_size * dim * 2;
+    const int budget = dev.smem_optin;
+    pl->warps_c = stage <= 16384 ? 4 : (stage <= 32768 ? 3 : 2);
+    for (;;) {
+      const size_t fixed = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
+                                             pl->warps_c, 0, static_cast<int>(group),
+                                             static_cast<int>(heads), pl->parts_b);
+      const int64_t per = static_cast<int64_t>(pl->warps_c) * (stage + 8 + 16);
+      const int64_t fit = (budget - static_cast<int64_t>(fixed) - 16) / per;
+      if (fit >= 2 || pl->warps_c == 1) {
+        pl->stages_c = static_cast<int>(std::min<int64_t>(8, fit));
+        break;
+      }
+      --pl->warps_c;
+    }
+    if (pl->stages_c < 2) return fail(RKV_ERR_UNSUPPORTED, "attention stages do not fit");
+    pl->smem_c = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
+                                   pl->warps_c, pl->stages_c, static_cast<int>(group),
+                                   static_cast<int>(heads), pl->parts_b);
+    pl->ctas = dev.sms;
+  }
+  // Workspace layout.
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = up256(off + bytes);
+    return at;
+  };
+  const size_t rowsg = static_cast<size_t>(rows) * group;
+  pl->status = take(256);
+  pl->done = take(static_cast<size_t>(heads) * 4);
+  pl->lse = take(rowsg * pl->parts_a * 4 * 4);
+  pl->z = take(rowsg * blocks * 4);
+  pl->delta = take(rowsg * blocks * 4);
+  if (decode) {
+    const size_t slots_b = static_cast<size_t>(heads) * pl->parts_b;
+    const size_t slots_c = static_cast<size_t>(heads) * pl->ctas;
+    pl->seg_count = take(slots_b * 4);
+    pl->sel_ids = take(slots_b * pl->seg_cap * 4);
+    pl->rep_m = take(slots_b * group * 4);
+    pl->rep_l = take(slots_b * group * 4);
+    pl->rep_o = take(slots_b * group * dim * 4);
+    pl->att_m = take(slots_c * group * 4);
+    pl->att_l = take(slots_c * group * 4);
+    pl->att_o = take(slots_c * group * dim * 4);
+  }
+  pl->bytes = off;
+  return RKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors
+// ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &found) ==
+            cudaSuccess &&
+        found == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 3-D bf16 map (dim, rows, heads) read in [box_rows x 64] boxes, 128B swizzle.
+int rows_map(CUtensorMap* map, const void* base, int64_t dim, int64_t rows, int64_t heads,
+             int64_t row_stride, int64_t head_stride, int box_rows, const char* what) {
+  EncodeTiled encode = encoder();
+  if (encode == nullptr) return fail(RKV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (!aligned16(base) || (row_stride * 2) % 16 != 0 ||
+      (heads > 1 && (head_stride * 2) % 16 != 0)) {
+    return fail(RKV_ERR_ALIGNMENT, std::string(what) + ": base and strides must be 16-byte aligned");
+  }
+  if (heads > 1 && head_stride <= 0) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, std::string(what) + ": head stride must be positive");
+  }
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(heads)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(row_stride * 2),
+                           static_cast<cuuint64_t>(heads > 1 ? head_stride * 2
+                                                             : rows * row_stride * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim,
+                            gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(RKV_ERR_INVALID_ARGUMENT,
+                std::string(what) + ": cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  }
+  return RKV_OK;
+}
+
+int check_summary(const rkv_summary* s) {
+  if (s == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
+  if (s->heads <= 0 || s->blocks <= 0 || s->prompt_length <= 0) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "summary sizes must be positive");
+  }
+  if (!supported_block(s->block_size)) {
+    return fail(RKV_ERR_UNSUPPORTED, "block_size must be 16, 32 or 64");
+  }
+  if (!supported_dim(s->head_dim)) {
+    return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+  }
+  if (cdiv(s->prompt_length, s->block_size) != s->blocks) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "blocks must equal ceil(prompt_length / block_size)");
+  }
+  if (!s->key_pages || !s->value_pages || !s->counts || !s->key_mean || !s->value_mean ||
+      !s->ellipsoid || !s->value_norm || !s->max_value_norm) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "summary has a null pointer");
+  }
+  if (s->heads > (1 << 16) || s->blocks > (1LL << 26)) {
+    return fail(RKV_ERR_UNSUPPORTED, "summary is larger than the kernels index");
+  }
+  return RKV_OK;
+}
+
+int check_selection_args(const rkv_summary* s, const void* q, int qdtype, int64_t group,
+                         float eps, int reduction) {
+  int rc = check_summary(s);
+  if (rc != RKV_OK) return rc;
+  if (q == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "query is null");
+  if (qdtype != RKV_DTYPE_BF16 && qdtype != RKV_DTYPE_F32) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "query dtype must be bf16 or fp32");
+  }
+  if (group < 1 || group > kMaxGroup) return fail(RKV_ERR_UNSUPPORTED, "group must be 1..16");
+  if (!std::isfinite(eps) || eps < 0.f) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "eps must be finite and nonnegative");
+  }
+  if (reduction != RKV_GQA_MEAN && reduction != RKV_GQA_MAX && reduction != RKV_GQA_ANY) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "reduction must be mean, max or any");
+  }
+  return RKV_OK;
+}
+
+int summary_maps(const rkv_summary* s, CUtensorMap* key_mean, CUtensorMap* ellipsoid,
+                 CUtensorMap* value_mean) {
+  const int64_t H = s->heads, nb = s->blocks, D = s->head_dim;
+  int rc = RKV_OK;
+  if (key_mean && (rc = rows_map(key_mean, s->key_mean, D, nb, H, D, nb * D, kSelectTile,
+                                 "key_mean")) != RKV_OK)
+    return rc;
+  if (ellipsoid && (rc = rows_map(ellipsoid, s->ellipsoid, D, nb, H, D, nb * D, kSelectTile,
+                                  "ellipsoid")) != RKV_OK)
+    return rc;
+  if (value_mean && (rc = rows_map(value_mean, s->value_mean, D, nb, H, D, nb * D, kSelectTile,
+                                   "value_mean")) != RKV_OK)
+    return rc;
+  return RKV_OK;
+}
+
+int check_workspace(const Plan& pl, void* ws, size_t size) {
+  if (ws == nullptr || size < pl.bytes) {
+    return fail(RKV_ERR_WORKSPACE, "workspace is missing or smaller than the required size " +
+                                       std::to_string(pl.bytes));
+  }
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
+    return fail(RKV_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  return RKV_OK;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+// Phases A and B shared by rkv_select and rkv_decode.
+int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype, int64_t inst,
+                 int64_t group, float eps, int reduction, const uint8_t* anchor, uint8_t* mask,
+                 int accumulate, void* ws, bool decode, unsigned phases, cudaStream_t stream) {
+  const int D = static_cast<int>(s->head_dim);
+  if (phases & RKV_PHASE_STATS) {
+    StatsMaps maps;
+    int rc = summary_maps(s, &maps.key_mean, &maps.ellipsoid, nullptr);
+    if (rc != RKV_OK) return rc;
+    StatsParams p = {};
+    p.query = q;
+    p.query_f32 = qdtype == RKV_DTYPE_F32;
+    p.counts = s->counts;
+    p.heads = static_cast<int>(s->heads);
+    p.group = static_cast<int>(group);
+    p.blocks = static_cast<int>(s->blocks);
+    p.instances = static_cast<int>(inst);
+    p.tiles = pl.tiles;
+    p.tiles_per_cta = pl.tpc_a;
+    p.parts = pl.parts_a;
+    p.stages = pl.stages_a;
+    p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
+    p.z = at<float>(ws, pl.z);
+    p.delta = at<float>(ws, pl.delta);
+    p.lse = at<float>(ws, pl.lse);
+    p.status = at<int>(ws, pl.status);
+    cudaError_t err = launch_stats(maps, p, D, pl.warps_a, pl.smem_a, stream, true);
+    if (err != cudaSuccess) return cuda_fail(err, "selector stats launch");
+  }
+  if (phases & RKV_PHASE_FINAL) {
+    FinalMaps maps;
+    int rc = summary_maps(s, nullptr, nullptr, &maps.value_mean);
+    if (rc != RKV_OK) return rc;
+    FinalParams p = {};
+    p.heads = static_cast<int>(s->heads);
+    p.group = static_cast<int>(group);
+    p.blocks = static_cast<int>(s->blocks);
+    p.instances = static_cast<int>(inst);
+    p.tiles = pl.tiles;
+    p.tiles_per_cta = pl.tpc_b;
+    p.parts_a = pl.parts_a;
+    p.parts = pl.parts_b;
+    p.stages = pl.stages_b;
+    p.eps = eps;
+    p.reduction = reduction;
+    p.z = at<float>(ws, pl.z);
+    p.delta = at<float>(ws, pl.delta);
+    p.lse = at<float>(ws, pl.lse);
+    p.value_norm = s->value_norm;
+    p.max_value_norm = s->max_value_norm;
+    p.anchor = anchor;
+    p.mask = mask;
+    p.accumulate = accumulate;
+    p.decode = decode ? 1 : 0;
+    p.split_probs = qdtype == RKV_DTYPE_F32;
+    if (decode) {
+      p.seg_count = at<int>(ws, pl.seg_count);
+      p.sel_ids = at<int>(ws, pl.sel_ids);
+      p.seg_cap = pl.seg_cap;
+      p.rep_m = at<float>(ws, pl.rep_m);
+      p.rep_l = at<float>(ws, pl.rep_l);
+      p.rep_o = at<float>(ws, pl.rep_o);
+    }
+    p.status = at<int>(ws, pl.status);
+    cudaError_t err = launch_final(maps, p, D, pl.warps_b, pl.smem_b, stream, true);
+    if (err != cudaSuccess) return cuda_fail(err, "selector final launch");
+  }
+  return RKV_OK;
+}
+
+}  // namespace
+
+cudaError_t ensure_smem_limit(const void* func, size_t bytes) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  struct Entry {
+    const void* func;
+    int dev;
+    size_t bytes;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : done) {
+    if (e.func == func && e.dev == dev && e.bytes >= bytes) return cudaSuccess;
+  }
+  err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bytes));
+  if (err != cudaSuccess) return err;
+  for (Entry& e : done) {
+    if (e.func == func && e.dev == dev) {
+      e.bytes = bytes;
+      return cudaSuccess;
+    }
+  }
+  done.push_back({func, dev, bytes});
+  return cudaSuccess;
+}
+
+}  // namespace rkv
+
+using namespace rkv;
+
+extern "C" {
+
+int rkv_abi_version(void) { return RKV_ABI_VERSION; }
+
+const char* rkv_last_error(void) { return g_last_error.c_str(); }
+
+const char* rkv_status_string(int status) {
+  switch (status) {
+    case RKV_OK: return "ok";
+    case RKV_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RKV_ERR_UNSUPPORTED: return "unsupported shape";
+    case RKV_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case RKV_ERR_WORKSPACE: return "bad workspace";
+    case RKV_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                  int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                  int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                  void* key_pages_out, void* value_pages_out, void* key_mean, void* value_mean,
+                  void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
+                  void* stream) {
+  g_last_error.clear();
+  if (heads <= 0 || tokens <= 0) return fail(RKV_ERR_INVALID_ARGUMENT, "empty keys/values");
+  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+  if (!supported_block(block_size)) return fail(RKV_ERR_UNSUPPORTED, "block_size must be 16, 32 or 64");
+  if (!keys || !values || !key_mean || !value_mean || !ellipsoid || !value_norm ||
+      !max_value_norm || !counts) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "null pointer");
+  }
+  if ((key_pages_out == nullptr) != (value_pages_out == nullptr)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "pass both page copies or neither");
+  }
+  if (!aligned16(keys) || !aligned16(values) || (key_token_stride * 2) % 16 ||
+      (value_token_stride * 2) % 16 || (key_head_stride * 2) % 16 ||
+      (value_head_stride * 2) % 16) {
+    return fail(RKV_ERR_ALIGNMENT, "keys/values rows must be 16-byte aligned");
+  }
+  if ((key_pages_out && !aligned16(key_pages_out)) || (value_pages_out && !aligned16(value_pages_out)) ||
+      !aligned16(key_mean) || !aligned16(value_mean) || !aligned16(ellipsoid)) {
+    return fail(RKV_ERR_ALIGNMENT, "outputs must be 16-byte aligned");
+  }
+  if (tokens > (1LL << 31) - 1 || heads > (1 << 16)) {
+    return fail(RKV_ERR_UNSUPPORTED, "prompt is larger than the kernels index");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t err = cudaMemsetAsync(max_value_norm, 0, static_cast<size_t>(heads) * 4, st);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+  SummarizeParams p = {};
+  p.keys = keys;
+  p.values = values;
+  p.key_head_stride = key_head_stride;
+  p.key_token_stride = key_token_stride;
+  p.value_head_stride = value_head_stride;
+  p.value_token_stride = value_token_stride;
+  p.heads = static_cast<int>(heads);
+  p.tokens = static_cast<int>(tokens);
+  p.block_size = static_cast<int>(block_size);
+  p.blocks = static_cast<int>(cdiv(tokens, block_size));
+  p.key_pages = key_pages_out;
+  p.value_pages = value_pages_out;
+  p.key_mean = key_mean;
+  p.value_mean = value_mean;
+  p.ellipsoid = ellipsoid;
+  p.value_norm = value_norm;
+  p.max_value_norm = max_value_norm;
+  p.counts = counts;
+  err = launch_summarize(p, static_cast<int>(head_dim), st);
+  if (err != cudaSuccess) return cuda_fail(err, "summarize launch");
+  return RKV_OK;
+}
+
+size_t rkv_select_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,
+                                 int64_t queries) {
+  if (heads <= 0 || group <= 0 || blocks <= 0 || queries <= 0 || !supported_dim(head_dim)) return 0;
+  Plan pl;
+  if (make_plan(&pl, heads, group, blocks, head_dim, 32, queries, false) != RKV_OK) return 0;
+  return pl.bytes;
+}
+
+int rkv_select(const rkv_summary* summary, const void* queries, int query_dtype, int64_t queries_n,
+               int64_t group, float eps, int reduction, uint8_t* mask, int accumulate,
+               void* workspace, size_t workspace_size, void* stream) {
+  g_last_error.clear();
+  int rc = check_selection_args(summary, queries, query_dtype, group, eps, reduction);
+  if (rc != RKV_OK) return rc;
+  if (queries_n < 1 || queries_n * summary->heads > 65535) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "queries must be 1..65535/heads");
+  }
+  if (mask == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "mask is null");
+  Plan pl;
+  rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
+                 summary->block_size, queries_n, false);
+  if (rc != RKV_OK) return rc;
+  if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int or_mode = accumulate;
+  if (!accumulate && queries_n > 1) {
+    cudaError_t err =
+        cudaMemsetAsync(mask, 0, static_cast<size_t>(summary->heads) * summary->blocks, st);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+    or_mode = 1;
+  }
+  return run_selector(pl, summary, queries, query_dtype, queries_n, group, eps, reduction, nullptr,
+                      mask, or_mode, workspace, false, RKV_PHASE_STATS | RKV_PHASE_FINAL, st);
+}
+
+size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,
+                                 int64_t block_size) {
+  if (heads <= 0 || group <= 0 || group > kMaxGroup || blocks <= 0 || !supported_dim(head_dim) ||
+      !supported_block(block_size))
+    return 0;
+  Plan pl;
+  if (make_plan(&pl, heads, group, blocks, head_dim, block_size, 1, true) != RKV_OK) return 0;
+  return pl.bytes;
+}
+
+int rkv_decode_launch_count(unsigned phases) {
+  return ((phases & RKV_PHASE_STATS) ? 1 : 0) + ((phases & RKV_PHASE_FINAL) ? 1 : 0) +
+         ((phases & RKV_PHASE_ATTEND) ? 1 : 0);
+}
+
+int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+               const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+               int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+               int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+               const int32_t* suffix_length, int64_t suffix_length_host,
+               const uint8_t* anchor_mask, float eps, int reduction, void* output,
+               uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
+               void* stream) {
+  g_last_error.clear();
+  int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
+  if (rc != RKV_OK) return rc;
+  if (output == nullptr || selected == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "output and selected must be non-null");
+  }
+  if (suffix_capacity < 0 || suffix_capacity > (1LL << 30)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_capacity out of range");
+  }
+  if (suffix_capacity > 0 && (key_suffix == nullptr || value_suffix == nullptr)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix K/V are null");
+  }
+  if (suffix_length == nullptr && (suffix_length_host < 0 || suffix_length_host > suffix_capacity)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_length_host must be in [0, suffix_capacity]");
+  }
+  if (phases == 0 || phases > RKV_PHASE_ALL) return fail(RKV_ERR_INVALID_ARGUMENT, "bad phases");
+  Plan pl;
+  rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
+                 summary->block_size, 1, true);
+  if (rc != RKV_OK) return rc;
+  if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
+                    selected, 0, workspace, true, phases, st);
+  if (rc != RKV_OK) return rc;
+  if (!(phases & RKV_PHASE_ATTEND)) return RKV_OK;
+
+  const int64_t H = summary->heads, D = summary->head_dim, B = summary->block_size;
+  AttendMaps maps;
+  rc = rows_map(&maps.key_pages, summary->key_pages, D, summary->blocks * B, H, D,
+                summary->key_page_head_stride, static_cast<int>(B), "key_pages");
+  if (rc != RKV_OK) return rc;
+  rc = rows_map(&maps.value_pages, summary->value_pages, D, summary->blocks * B, H, D,
+                summary->value_page_head_stride, static_cast<int>(B), "value_pages");
+  if (rc != RKV_OK) return rc;
+  if (suffix_capacity > 0) {
+    rc = rows_map(&maps.key_suffix, key_suffix, D, suffix_capacity, H, key_suffix_token_stride,
+                  key_suffix_head_stride, static_cast<int>(B), "key_suffix");
+    if (rc != RKV_OK) return rc;
+    rc = rows_map(&maps.value_suffix, value_suffix, D, suffix_capacity, H,
+                  value_suffix_token_stride, value_suffix_head_stride, static_cast<int>(B),
+                  "value_suffix");
+    if (rc != RKV_OK) return rc;
+  } else {
+    maps.key_suffix = maps.key_pages;
+    maps.value_suffix = maps.value_pages;
+  }
+  AttendParams p = {};
+  p.query = query;
+  p.query_f32 = query_dtype == RKV_DTYPE_F32;
+  p.out = output;
+  p.counts = summary->counts;
+  p.heads = static_cast<int>(H);
+  p.group = static_cast<int>(group);
+  p.blocks = static_cast<int>(summary->blocks);
+  p.page = static_cast<int>(B);
+  p.has_suffix = suffix_capacity > 0;
+  p.suffix_capacity = static_cast<int>(suffix_capacity);
+  p.suffix_len_ptr = suffix_length;
+  p.suffix_len_host = static_cast<int>(suffix_length_host);
+  p.seg_count = at<int>(workspace, pl.seg_count);
+  p.sel_ids = at<int>(workspace, pl.sel_ids);
+  p.parts_b = pl.parts_b;
+  p.seg_cap = pl.seg_cap;
+  p.rep_m = at<float>(workspace, pl.rep_m);
+  p.rep_l = at<float>(workspace, pl.rep_l);
+  p.rep_o = at<float>(workspace, pl.rep_o);
+  p.att_m = at<float>(workspace, pl.att_m);
+  p.att_l = at<float>(workspace, pl.att_l);
+  p.att_o = at<float>(workspace, pl.att_o);
+  p.ctas = pl.ctas;
+  p.stages = pl.stages_c;
+  p.done = at<int>(workspace, pl.done);
+  p.status = at<int>(workspace, pl.status);
+  p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
+  cudaError_t err = launch_attend(maps, p, static_cast<int>(D), pl.warps_c, pl.smem_c, st, true);
+  if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+  return RKV_OK;
+}
+
+}  // extern "C"

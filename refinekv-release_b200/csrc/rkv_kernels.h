@@ -1,0 +1,133 @@
+// Launch parameters shared by the host entry points (rkv_capi.cu) and the
+// kernels.  Plain structs: pointers, sizes, scalars.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rkv {
+
+constexpr int kSelectTile = 32;  // summary blocks per selector tile
+constexpr int kMaxGroup = 16;    // GQA rows per KV head (two n8 tiles)
+
+enum Reduction { kMean = 0, kMax = 1, kAny = 2 };
+
+struct SummarizeParams {
+  const void* keys;
+  const void* values;
+  int64_t key_head_stride, key_token_stride;      // elements
+  int64_t value_head_stride, value_token_stride;  // elements
+  int heads, tokens, blocks, block_size;
+  void* key_pages;    // optional (heads, blocks, block, dim) copy, zero padded
+  void* value_pages;  // optional
+  void* key_mean;     // bf16 (heads, blocks, dim)
+  void* value_mean;
+  void* ellipsoid;
+  float* value_norm;      // (heads, blocks)
+  float* max_value_norm;  // (heads,), zero on entry
+  int64_t* counts;        // (blocks,)
+};
+
+struct StatsMaps {
+  CUtensorMap key_mean;
+  CUtensorMap ellipsoid;
+};
+
+struct StatsParams {
+  const void* query;  // (instances, heads, group, dim)
+  int query_f32;
+  const int64_t* counts;
+  int heads, group, blocks, instances;
+  int tiles, tiles_per_cta, parts;
+  int stages;
+  float scale;
+  float* z;      // (instances*heads*group, blocks)
+  float* delta;  // (instances*heads*group, blocks)
+  float* lse;    // (instances*heads*group, parts, 4): z max, z sum, c max, c sum
+  int* status;
+};
+
+struct FinalMaps {
+  CUtensorMap value_mean;
+};
+
+struct FinalParams {
+  int heads, group, blocks, instances;
+  int tiles, tiles_per_cta, parts_a, parts;
+  int stages;
+  float eps;
+  int reduction;
+  const float* z;
+  const float* delta;
+  const float* lse;
+  const float* value_norm;
+  const float* max_value_norm;
+  const uint8_t* anchor;  // (heads, blocks) or null
+  uint8_t* mask;          // (heads, blocks)
+  int accumulate;         // OR into mask instead of overwriting it
+  int decode;             // also compact ids and accumulate representatives
+  int split_probs;        // FP32-query mode: hi/lo bf16 split of the probabilities
+  int* seg_count;         // (heads, parts)
+  int* sel_ids;           // (heads, parts, seg_cap)
+  int seg_cap;
+  float* rep_m;  // (heads, parts, group)
+  float* rep_l;
+  float* rep_o;  // (heads, parts, group, dim)
+  int* status;
+};
+
+struct AttendMaps {
+  CUtensorMap key_pages;
+  CUtensorMap value_pages;
+  CUtensorMap key_suffix;
+  CUtensorMap value_suffix;
+};
+
+struct AttendParams {
+  const void* query;  // (heads, group, dim)
+  int query_f32;
+  void* out;  // (heads, group, dim) in the query dtype
+  const int64_t* counts;
+  int heads, group, blocks, page;
+  int has_suffix;
+  int suffix_capacity;
+  const int* suffix_len_ptr;  // device scalar or null
+  int suffix_len_host;
+  const int* seg_count;
+  const int* sel_ids;
+  int parts_b, seg_cap;
+  const float* rep_m;
+  const float* rep_l;
+  const float* rep_o;
+  float* att_m;  // (heads, ctas, group)
+  float* att_l;
+  float* att_o;  // (heads, ctas, group, dim)
+  int ctas;
+  int stages;
+  int* done;  // (heads,), zero between launches
+  int* status;
+  float scale;
+};
+
+// Host launchers (defined in the .cu files); return a cudaError_t.
+cudaError_t launch_summarize(const SummarizeParams& p, int dim, cudaStream_t stream);
+cudaError_t launch_stats(const StatsMaps& maps, const StatsParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl);
+cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl);
+cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim, int warps,
+                          size_t smem, cudaStream_t stream, bool pdl);
+
+// Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
+// current device.  Done once per (kernel, device): later calls, including
+// those made while a CUDA graph is being captured, only read a cache.
+cudaError_t ensure_smem_limit(const void* func, size_t bytes);
+
+// Shared-memory footprint of each kernel for a given stage count.
+size_t stats_smem_bytes(int dim, int warps, int stages, int group);
+size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta);
+size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
+                         int parts_b);
+
+}  // namespace rkv

@@ -1,0 +1,505 @@
+// Per-step block selector (reference: src/refinekv/reference.py:10-47; the
+// reference's GPU form is kernels/selection.py:47-223 and
+// kernels/attention.py:13-137).
+//
+// Phase A (stats): per (query instance, KV head) and per tile of 32 blocks,
+// TMA stages the key-mean and ellipsoid tiles (bf16, swizzled) and computes
+//   s = (q . kbar) * D^-1/2,  delta = sqrt(max(q^2 . W2, 0)) * D^-1/2 * (1+2^-8)
+// with mma.sync (blocks on M, group rows on N).  It stores z = s + log(count)
+// and delta for phase B and keeps running (max, sum) pairs for
+// LSE_b(z) and LSE_b(z + log cosh delta), one pair per CTA and row.
+//
+// Phase B (final): merges those pairs into the row-global log Z / log C,
+// evaluates the risk of every (row, block), reduces over the group
+// (mean / max / any), forces blocks with non-finite statistics, ORs the
+// anchors, and writes the byte mask.  In decode mode it also writes the
+// selected block ids compacted in block order (one segment per CTA, so the
+// order is deterministic) and runs the representative softmax over the
+// unselected blocks of its range (logit z, value = value_mean, staged by TMA),
+// leaving one (m, l, o) partial per CTA for the combine.
+#include "rkv_device.cuh"
+#include "rkv_kernels.h"
+
+namespace rkv {
+namespace {
+
+constexpr float kInflate = 1.00390625f;  // 1 + 2^-8
+constexpr float kDeltaSplit = 10.f;
+
+// NaN-propagating clamp from above (torch.clamp(max=...)).
+__device__ __forceinline__ float clamp_hi(float x, float hi) { return x > hi ? hi : x; }
+
+// log(cosh(delta)) with the reference's two branches (reference.py:19-22).
+__device__ __forceinline__ float log_cosh(float delta) {
+  const float small = clamp_hi(delta, kDeltaSplit);
+  const float direct = logf((expf(small) + expf(-small)) * 0.5f);
+  const float large = delta + logf((1.f + expf(-2.f * delta)) * 0.5f);
+  return delta <= kDeltaSplit ? direct : large;
+}
+
+// Risk of one (row, block): distortion ("mass") + importance ("value") terms,
+// evaluated in the same operation order as reference.py:25-34.
+__device__ __forceinline__ float block_risk(float z, float delta, float log_z, float log_c,
+                                            float vnorm, float vmax) {
+  const bool near = delta <= kDeltaSplit;
+  const float small = clamp_hi(delta, kDeltaSplit);
+  const float t = expf(small);
+  const float two_vmax = 2.f * vmax;
+  const float mass_direct = (two_vmax * expf(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
+  const float e_neg = expf(-delta);
+  float one_minus = 1.f - e_neg;
+  one_minus = one_minus < 1e-30f ? 1e-30f : one_minus;
+  const float lcm1 = (delta + 2.f * logf(one_minus)) - 0.693147182464599609375f;
+  const float mass_large = two_vmax * expf((z - log_c) + lcm1);
+  const float mass = near ? mass_direct : mass_large;
+  const float tanh_half = near ? (t - 1.f) / (t + 1.f) : (1.f - e_neg) / (1.f + e_neg);
+  const float importance = ((2.f * vnorm) * expf(z - log_z)) * tanh_half;
+  return mass + importance;
+}
+
+__device__ __forceinline__ bool finite(float x) { return isfinite(x); }
+
+// Online (max, sum of exp) update with accurate exp.
+__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
+  if (x == -INFINITY) return;
+  if (x > m) {
+    s = s * expf(m - x) + 1.f;
+    m = x;
+  } else {
+    s += expf(x - m);
+  }
+}
+
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  const float top = fmaxf(m, m2);
+  const float ref = top == -INFINITY ? 0.f : top;
+  s = s * expf(m - ref) + s2 * expf(m2 - ref);
+  m = top;
+}
+
+// ------------------------------- phase A ----------------------------------
+
+template <int D, int NT>
+__global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ StatsMaps maps,
+                                                    const StatsParams p) {
+  constexpr int R = kSelectTile;
+  constexpr int kTile = R * D * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  uint8_t* tiles = smem;  // [warp][stage][key_mean | ellipsoid]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + warps * S * 2 * kTile);
+  float* red = reinterpret_cast<float*>(smem + warps * S * 2 * kTile +
+                                        round16(static_cast<size_t>(warps) * S * 8));
+
+  const int ih = blockIdx.x;  // instance * heads + head
+  const int inst = ih / p.heads, h = ih - inst * p.heads;
+  const int t0 = blockIdx.y * p.tiles_per_cta;
+  const int t1 = min(p.tiles, t0 + p.tiles_per_cta);
+  const int mine = t1 - t0 > warp ? (t1 - t0 - warp + warps - 1) / warps : 0;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&maps.key_mean);
+    tma_prefetch_desc(&maps.ellipsoid);
+  }
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[warp * S + s], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  pdl_wait();
+
+  auto issue = [&](int j) {
+    const int s = j % S;
+    uint8_t* dst = tiles + (warp * S + s) * 2 * kTile;
+    const int row = (t0 + warp + j * warps) * R;
+    mbar_expect_tx(&bars[warp * S + s], 2 * kTile);
+    tma_tile<D>(dst, &maps.key_mean, &bars[warp * S + s], row, h, R);
+    tma_tile<D>(dst + kTile, &maps.ellipsoid, &bars[warp * S + s], row, h, R);
+  };
+  if (lane == 0) {
+    for (int j = 0; j < min(S, mine); ++j) issue(j);
+  }
+
+  const void* q = static_cast<const char*>(p.query) +
+                  static_cast<size_t>(ih) * p.group * D * (p.query_f32 ? 4 : 2);
+  uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
+  load_query_frags<D, NT>(qk, q, p.query_f32, p.group, lane, false);
+  load_query_frags<D, NT>(q2, q, p.query_f32, p.group, lane, true);
+
+  float zm[NT][2], zs[NT][2], cm[NT][2], cs[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      zm[nt][j] = cm[nt][j] = -INFINITY;
+      zs[nt][j] = cs[nt][j] = 0.f;
+    }
+
+  int issued = min(S, mine);
+  for (int j = 0; j < mine; ++j) {
+    const int s = j % S;
+    if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
+      if (lane == 0) atomicOr(p.status, kStatusTimeout);
+      drain_pending(bars + warp * S, S, j, issued);
+      break;
+    }
+    const uint32_t base = smem_addr(tiles + (warp * S + s) * 2 * kTile);
+    float sk[R / 16][NT][4], sw[R / 16][NT][4];
+    score_tile<R, D, NT>(base, qk, sk, lane);
+    score_tile<R, D, NT>(base + kTile, q2, sw, lane);
+    __syncwarp();
+    if (j + S < mine) {
+      if (lane == 0) {
+        fence_proxy_async();
+        issue(j + S);
+      }
+      ++issued;
+    }
+    const int tile = t0 + warp + j * warps;
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int b = tile * R + mt * 16 + (lane >> 2) + (c >> 1) * 8;
+        const bool bok = b < p.blocks;
+        const float lc_count = bok ? logf(static_cast<float>(p.counts[b])) : 0.f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
+          if (!bok || g >= p.group) continue;
+          const float score = sk[mt][nt][c] * p.scale;
+          const float proj = sw[mt][nt][c];
+          const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
+          const float z = score + lc_count;
+          const size_t row = static_cast<size_t>(ih) * p.group + g;
+          p.z[row * p.blocks + b] = z;
+          p.delta[row * p.blocks + b] = delta;
+          lse_push(zm[nt][c & 1], zs[nt][c & 1], z);
+          lse_push(cm[nt][c & 1], cs[nt][c & 1], z + log_cosh(delta));
+        }
+      }
+    }
+  }
+
+  // Reduce the (max, sum) pairs over the 8 lanes of each column, then warps.
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, zm[nt][j], off);
+        const float os = __shfl_xor_sync(0xffffffffu, zs[nt][j], off);
+        lse_merge(zm[nt][j], zs[nt][j], om, os);
+        const float pm = __shfl_xor_sync(0xffffffffu, cm[nt][j], off);
+        const float ps = __shfl_xor_sync(0xffffffffu, cs[nt][j], off);
+        lse_merge(cm[nt][j], cs[nt][j], pm, ps);
+      }
+      if (lane < 4) {
+        float* r = red + (warp * NT * 8 + nt * 8 + 2 * lane + j) * 4;
+        r[0] = zm[nt][j];
+        r[1] = zs[nt][j];
+        r[2] = cm[nt][j];
+        r[3] = cs[nt][j];
+      }
+    }
+  __syncthreads();
+  if (threadIdx.x < p.group) {
+    const int g = threadIdx.x;
+    float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
+    for (int w = 0; w < warps; ++w) {
+      const float* r = red + (w * NT * 8 + g) * 4;
+      lse_merge(m0, s0, r[0], r[1]);
+      lse_merge(m1, s1, r[2], r[3]);
+    }
+    float* out = p.lse + ((static_cast<size_t>(ih) * p.group + g) * p.parts + blockIdx.y) * 4;
+    out[0] = m0;
+    out[1] = s0;
+    out[2] = m1;
+    out[3] = s1;
+  }
+  pdl_launch_dependents();
+}
+
+// ------------------------------- phase B ----------------------------------
+
+template <int D, int NT>
+__global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ FinalMaps maps,
+                                                    const FinalParams p) {
+  constexpr int R = kSelectTile;
+  constexpr int kTile = R * D * 2;
+  constexpr int G8 = NT * 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  const int ntiles = p.tiles_per_cta;
+  uint8_t* tiles = smem;  // [warp][stage] value_mean tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + warps * S * kTile);
+  float* log_z = reinterpret_cast<float*>(smem + warps * S * kTile +
+                                          round16(static_cast<size_t>(warps) * S * 8));
+  float* log_c = log_z + kMaxGroup;
+  uint32_t* sel_bits = reinterpret_cast<uint32_t*>(log_c + kMaxGroup);  // [ntiles]
+  uint32_t* rep_bits = sel_bits + ntiles;                               // [ntiles]
+  int* offsets = reinterpret_cast<int*>(rep_bits + ntiles);             // [ntiles + 1]
+  int* rep_list = offsets + ntiles + 1;                                 // [ntiles]
+  int* flags = rep_list + ntiles;                                       // [4]
+  float* st_m = reinterpret_cast<float*>(flags + 4);                    // [warps][G8]
+  float* st_l = st_m + warps * G8;
+  float* st_o = st_l + warps * G8;  // [warps][G8][D]
+
+  const int ih = blockIdx.x;
+  const int inst = ih / p.heads, h = ih - inst * p.heads;
+  (void)inst;
+  const int part = blockIdx.y;
+  const int t0 = part * p.tiles_per_cta;
+  const int t1 = min(p.tiles, t0 + p.tiles_per_cta);
+
+  if (p.decode && lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[warp * S + s], 1);
+    mbar_fence_init();
+  }
+  if (threadIdx.x == 0) {
+    flags[0] = 0;
+    if (p.decode) tma_prefetch_desc(&maps.value_mean);
+  }
+  __syncthreads();
+  pdl_wait();
+
+  // Row-global normalisers from the phase-A partials.
+  if (threadIdx.x < p.group) {
+    const int g = threadIdx.x;
+    const float* in = p.lse + (static_cast<size_t>(ih) * p.group + g) * p.parts_a * 4;
+    float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
+    for (int k = 0; k < p.parts_a; ++k) {
+      lse_merge(m0, s0, in[4 * k], in[4 * k + 1]);
+      lse_merge(m1, s1, in[4 * k + 2], in[4 * k + 3]);
+    }
+    const float lz = m0 + logf(s0);
+    const float lc = m1 + logf(s1);
+    log_z[g] = lz;
+    log_c[g] = lc;
+    if (!finite(lz) || !finite(lc)) atomicOr(&flags[0], 1);
+  }
+  __syncthreads();
+  const bool bad_global = flags[0] != 0;
+  const float vmax = p.max_value_norm[h];
+
+  // Pass 1: decisions, one lane per block.
+  for (int t = t0 + warp; t < t1; t += warps) {
+    const int b = t * R + lane;
+    const bool valid = b < p.blocks;
+    bool sel = false;
+    if (valid) {
+      const float vnorm = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
+      float agg = p.reduction == kMax ? -INFINITY : 0.f;
+      bool any = false, bad = false;
+      for (int g = 0; g < p.group; ++g) {
+        const size_t row = static_cast<size_t>(ih) * p.group + g;
+        const float r = block_risk(p.z[row * p.blocks + b], p.delta[row * p.blocks + b],
+                                   log_z[g], log_c[g], vnorm, vmax);
+        bad |= !finite(r);
+        if (p.reduction == kMean) {
+          agg += r;
+        } else if (p.reduction == kMax) {
+          agg = (r > agg || r != r) ? r : agg;
+        } else {
+          any |= r > p.eps;
+        }
+      }
+      bool dec;
+      if (p.reduction == kMean) {
+        dec = agg / static_cast<float>(p.group) > p.eps;
+      } else if (p.reduction == kMax) {
+        dec = agg > p.eps;
+      } else {
+        dec = any;
+      }
+      sel = dec || bad || bad_global;
+      if (p.anchor != nullptr) sel = sel || p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+      uint8_t* mk = p.mask + static_cast<size_t>(h) * p.blocks + b;
+      if (p.accumulate) {
+        if (sel) *mk = 1;
+      } else {
+        *mk = sel ? 1 : 0;
+      }
+    }
+    const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+    const uint32_t vb = __ballot_sync(0xffffffffu, valid);
+    if (lane == 0) {
+      sel_bits[t - t0] = sb;
+      rep_bits[t - t0] = vb & ~sb;
+    }
+  }
+  if (!p.decode) {
+    pdl_launch_dependents();
+    return;
+  }
+  __syncthreads();
+
+  // Deterministic compaction: tile offsets in block order, and the list of
+  // tiles holding at least one representative (rank k goes to warp k % warps).
+  if (threadIdx.x == 0) {
+    int acc = 0, reps = 0;
+    for (int k = 0; k < t1 - t0; ++k) {
+      offsets[k] = acc;
+      acc += __popc(sel_bits[k]);
+      if (rep_bits[k] != 0u) rep_list[reps++] = k;
+    }
+    offsets[t1 - t0] = acc;
+    flags[1] = reps;
+    p.seg_count[h * p.parts + part] = acc;
+  }
+  __syncthreads();
+  int* ids = p.sel_ids + (static_cast<size_t>(h) * p.parts + part) * p.seg_cap;
+  for (int t = t0 + warp; t < t1; t += warps) {
+    const uint32_t sb = sel_bits[t - t0];
+    if ((sb >> lane) & 1u) ids[offsets[t - t0] + __popc(sb & ((1u << lane) - 1u))] = t * R + lane;
+  }
+
+  const int n_reps = flags[1];
+  const int mine = n_reps > warp ? (n_reps - warp + warps - 1) / warps : 0;
+  auto issue = [&](int j) {
+    const int s = j % S;
+    mbar_expect_tx(&bars[warp * S + s], kTile);
+    tma_tile<D>(tiles + (warp * S + s) * kTile, &maps.value_mean, &bars[warp * S + s],
+                (t0 + rep_list[warp + j * warps]) * R, h, R);
+  };
+  int issued = min(S, mine);
+  if (lane == 0) {
+    for (int j = 0; j < issued; ++j) issue(j);
+  }
+  float m[NT][2], l[NT][2], o[D / 16][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = -INFINITY;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
+  }
+  for (int j = 0; j < mine; ++j) {
+    const int s = j % S;
+    if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
+      if (lane == 0) atomicOr(p.status, kStatusTimeout);
+      drain_pending(bars + warp * S, S, j, issued);
+      break;
+    }
+    const int k = rep_list[warp + j * warps];
+    const uint32_t reps = rep_bits[k];
+    const int tile = t0 + k;
+    float logit[R / 16][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+        const bool rep = (reps >> r) & 1u;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
+          logit[mt][nt][c] =
+              (rep && g < p.group)
+                  ? p.z[(static_cast<size_t>(ih) * p.group + g) * p.blocks + tile * R + r]
+                  : -INFINITY;
+        }
+      }
+    attend_tile<R, D, NT>(logit, smem_addr(tiles + (warp * S + s) * kTile), m, l, o,
+                          p.split_probs != 0, lane);
+    __syncwarp();
+    if (j + S < mine) {
+      if (lane == 0) {
+        fence_proxy_async();
+        issue(j + S);
+      }
+      ++issued;
+    }
+  }
+  reduce_l<NT>(l);
+  stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
+  __syncthreads();
+  const size_t slot = static_cast<size_t>(h) * p.parts + part;
+  merge_stashed<D>(st_m, st_l, st_o, warps, G8, p.group, p.rep_m + slot * p.group,
+                   p.rep_l + slot * p.group, p.rep_o + slot * p.group * D, threadIdx.x,
+                   blockDim.x);
+  pdl_launch_dependents();
+}
+
+template <typename Kernel, typename Maps, typename Params>
+cudaError_t launch_k(Kernel kernel, const Maps& maps, const Params& p, dim3 grid, int warps,
+                     size_t smem, cudaStream_t stream, bool pdl) {
+  cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
+  if (err != cudaSuccess) return err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, maps, p);
+}
+
+template <int D>
+cudaError_t stats_dispatch(const StatsMaps& maps, const StatsParams& p, int warps, size_t smem,
+                           cudaStream_t stream, bool pdl) {
+  const dim3 grid(p.instances * p.heads, p.parts);
+  if (p.group <= 8) return launch_k(stats_kernel<D, 1>, maps, p, grid, warps, smem, stream, pdl);
+  return launch_k(stats_kernel<D, 2>, maps, p, grid, warps, smem, stream, pdl);
+}
+
+template <int D>
+cudaError_t final_dispatch(const FinalMaps& maps, const FinalParams& p, int warps, size_t smem,
+                           cudaStream_t stream, bool pdl) {
+  const dim3 grid(p.instances * p.heads, p.parts);
+  if (p.group <= 8) return launch_k(final_kernel<D, 1>, maps, p, grid, warps, smem, stream, pdl);
+  return launch_k(final_kernel<D, 2>, maps, p, grid, warps, smem, stream, pdl);
+}
+
+}  // namespace
+
+size_t stats_smem_bytes(int dim, int warps, int stages, int group) {
+  const int g8 = group <= 8 ? 8 : 16;
+  return kSmemSlack + static_cast<size_t>(warps) * stages * 2 * kSelectTile * dim * 2 +
+         round16(static_cast<size_t>(warps) * stages * 8) + static_cast<size_t>(warps) * g8 * 4 * 4;
+}
+
+size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta) {
+  const int g8 = group <= 8 ? 8 : 16;
+  size_t bytes = kSmemSlack + static_cast<size_t>(warps) * stages * kSelectTile * dim * 2;
+  bytes += round16(static_cast<size_t>(warps) * stages * 8);
+  bytes += 2 * kMaxGroup * 4;
+  bytes += static_cast<size_t>(tiles_per_cta) * 4 * 4 + 4 + 16;
+  bytes += static_cast<size_t>(warps) * g8 * 4 * 2 + static_cast<size_t>(warps) * g8 * dim * 4;
+  return bytes;
+}
+
+cudaError_t launch_stats(const StatsMaps& maps, const StatsParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl) {
+  switch (dim) {
+    case 64: return stats_dispatch<64>(maps, p, warps, smem, stream, pdl);
+    case 128: return stats_dispatch<128>(maps, p, warps, smem, stream, pdl);
+    case 192: return stats_dispatch<192>(maps, p, warps, smem, stream, pdl);
+    case 256: return stats_dispatch<256>(maps, p, warps, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl) {
+  switch (dim) {
+    case 64: return final_dispatch<64>(maps, p, warps, smem, stream, pdl);
+    case 128: return final_dispatch<128>(maps, p, warps, smem, stream, pdl);
+    case 192: return final_dispatch<192>(maps, p, warps, smem, stream, pdl);
+    case 256: return final_dispatch<256>(maps, p, warps, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace rkv

@@ -1,0 +1,150 @@
+"""Prompt block summaries computed by the CUDA summarizer.
+
+Mirrors ``src/refinekv/summary.py`` of the reference: the same ``BlockSummary``
+fields, shapes and dtypes, and the same ``build_summary`` signature and
+validation errors.  The computation is one call of ``rkv_summarize``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _native
+from .config import RefineKVConfig
+
+SUPPORTED_HEAD_DIMS = (64, 128, 192, 256)
+
+
+@dataclass
+class BlockSummary:
+    """Per-KV-head page summaries; the original K/V stay available for refinement.
+
+    Same fields as the reference ``BlockSummary`` (``summary.py:10-32``):
+    ``keys``/``values`` are (kv_heads, pages, block_size, head_dim) page views
+    that alias the cache when the prompt is page-aligned and page-contiguous
+    (head stride free) and are a zero-padded copy otherwise; ``counts`` is
+    int64 (pages,); ``key_mean``, ``value_mean`` and ``ellipsoid`` are bf16
+    (kv_heads, pages, head_dim); ``value_norm`` is FP32 (kv_heads, pages) and
+    ``max_value_norm`` FP32 (kv_heads,).  A summary belongs to one immutable
+    prompt prefix.
+    """
+
+    keys: torch.Tensor
+    values: torch.Tensor
+    counts: torch.Tensor
+    key_mean: torch.Tensor
+    value_mean: torch.Tensor
+    ellipsoid: torch.Tensor
+    value_norm: torch.Tensor
+    max_value_norm: torch.Tensor
+    prompt_length: int
+    block_size: int
+    _abi: object = field(default=None, repr=False, compare=False)
+
+    @property
+    def num_blocks(self) -> int:
+        return self.counts.numel()
+
+    def abi(self) -> _native.Summary:
+        """The ``rkv_summary`` view handed to the C ABI (built once)."""
+        if self._abi is None:
+            self._abi = _native.Summary(
+                key_pages=self.keys.data_ptr(),
+                value_pages=self.values.data_ptr(),
+                key_page_head_stride=self.keys.stride(0),
+                value_page_head_stride=self.values.stride(0),
+                counts=self.counts.data_ptr(),
+                key_mean=self.key_mean.data_ptr(),
+                value_mean=self.value_mean.data_ptr(),
+                ellipsoid=self.ellipsoid.data_ptr(),
+                value_norm=self.value_norm.data_ptr(),
+                max_value_norm=self.max_value_norm.data_ptr(),
+                heads=self.keys.shape[0],
+                blocks=self.num_blocks,
+                block_size=self.block_size,
+                head_dim=self.keys.shape[-1],
+                prompt_length=self.prompt_length,
+            )
+        return self._abi
+
+
+def require_cuda_tensor(tensor: torch.Tensor, what: str) -> None:
+    if not tensor.is_cuda:
+        raise RuntimeError(
+            f"{what} must be a CUDA tensor: refinekv_b200 runs on B200 GPUs only "
+            "and has no CPU implementation")
+
+
+def _page_alias(tensor: torch.Tensor, block: int):
+    """(heads, tokens, dim) -> page view without copying, or None if a copy is needed."""
+    heads, tokens, dim = tensor.shape
+    if tokens % block or tensor.stride(2) != 1 or tensor.stride(1) != dim:
+        return None
+    if tensor.data_ptr() % 16 or (tensor.stride(0) * 2) % 16:
+        return None
+    return tensor.as_strided((heads, tokens // block, block, dim),
+                             (tensor.stride(0), block * dim, dim, 1))
+
+
+@torch.no_grad()
+def build_summary(keys: torch.Tensor, values: torch.Tensor,
+                  config: RefineKVConfig | None = None) -> BlockSummary:
+    """Build BF16 block summaries in one pass over the prompt K/V.
+
+    ``keys``/``values``: (kv_heads, tokens, head_dim) bf16 CUDA tensors (any
+    head/token strides, innermost stride 1).  Raises the reference's
+    ``ValueError``/``TypeError`` for bad shapes, devices and dtypes
+    (``summary.py:46-60``), ``TypeError`` for non-bf16 caches (the CUDA path
+    is bf16-only, like the reference's Triton backend), ``ValueError`` for
+    unsupported head dimensions and ``RuntimeError`` for CPU tensors.
+    """
+    config = config or RefineKVConfig()
+    if keys.ndim != 3 or keys.shape != values.shape or min(keys.shape) <= 0:
+        raise ValueError(
+            "keys and values must have the same nonempty (kv_heads, tokens, dim) shape")
+    if keys.device != values.device or keys.dtype != values.dtype:
+        raise ValueError("keys and values must have the same device and dtype")
+    if not keys.is_floating_point():
+        raise TypeError("keys and values must be floating point")
+    require_cuda_tensor(keys, "keys")
+    if keys.dtype != torch.bfloat16:
+        raise TypeError("the CUDA summarizer requires BF16 keys and values")
+    heads, tokens, dim = keys.shape
+    if dim not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim must be one of {SUPPORTED_HEAD_DIMS}")
+    keys, values = keys.detach(), values.detach()
+    if keys.stride(2) != 1 or keys.data_ptr() % 16 or (keys.stride(1) * 2) % 16 or (
+            keys.stride(0) * 2) % 16:
+        keys = keys.contiguous()
+    if values.stride(2) != 1 or values.data_ptr() % 16 or (values.stride(1) * 2) % 16 or (
+            values.stride(0) * 2) % 16:
+        values = values.contiguous()
+
+    block = config.block_size
+    blocks = -(-tokens // block)
+    dev = keys.device
+    key_pages, value_pages = _page_alias(keys, block), _page_alias(values, block)
+    copy_pages = key_pages is None or value_pages is None
+    if copy_pages:
+        key_pages = torch.empty(heads, blocks, block, dim, device=dev, dtype=keys.dtype)
+        value_pages = torch.empty_like(key_pages)
+    key_mean = torch.empty(heads, blocks, dim, device=dev, dtype=torch.bfloat16)
+    value_mean = torch.empty_like(key_mean)
+    ellipsoid = torch.empty_like(key_mean)
+    value_norm = torch.empty(heads, blocks, device=dev, dtype=torch.float32)
+    max_value_norm = torch.empty(heads, device=dev, dtype=torch.float32)
+    counts = torch.empty(blocks, device=dev, dtype=torch.int64)
+    lib = _native.load()
+    with torch.cuda.device(dev):
+        _native.check(lib.rkv_summarize(
+            keys.data_ptr(), values.data_ptr(), heads, tokens, dim,
+            keys.stride(0), keys.stride(1), values.stride(0), values.stride(1), block,
+            key_pages.data_ptr() if copy_pages else None,
+            value_pages.data_ptr() if copy_pages else None,
+            key_mean.data_ptr(), value_mean.data_ptr(), ellipsoid.data_ptr(),
+            value_norm.data_ptr(), max_value_norm.data_ptr(), counts.data_ptr(),
+            torch.cuda.current_stream(dev).cuda_stream))
+    return BlockSummary(key_pages, value_pages, counts, key_mean, value_mean, ellipsoid,
+                        value_norm, max_value_norm, tokens, block)

@@ -1,0 +1,137 @@
+"""The C-ABI library loads, exports every declared symbol and validates arguments (no GPU)."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+import torch
+
+from refinekv_b200 import RefineKVConfig, _native
+
+REPO = pathlib.Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from conftest import native_build_module
+
+    native_build_module().build()
+    return _native.load()
+
+
+def _declared_symbols():
+    names = set()
+    for header in (REPO / "include").glob("*.h"):
+        text = header.read_text()
+        names.update(re.findall(r"RKV_API\s+[\w\s\*]+?\b(rkv_\w+)\s*\(", text))
+    return names
+
+
+def test_header_declares_the_binding_surface():
+    assert _declared_symbols() == set(_native.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.rkv_abi_version() == _native.ABI_VERSION
+
+
+def test_library_exports_nothing_else(lib):
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    public = {name for name in exported if not name.startswith("_")}
+    assert public == set(_native.EXPORTS)
+
+
+def test_status_strings(lib):
+    assert lib.rkv_status_string(0) == b"ok"
+    assert lib.rkv_status_string(_native.RKV_ERR_ALIGNMENT) == b"misaligned pointer or stride"
+    assert lib.rkv_decode_launch_count(_native.PHASE_ALL) == 3
+    assert lib.rkv_decode_launch_count(_native.PHASE_ATTEND) == 1
+
+
+def test_summarize_rejects_bad_arguments_before_touching_a_device(lib):
+    args = [ctypes.c_void_p(16), ctypes.c_void_p(16), 2, 64, 96, 0, 96, 0, 96, 32,
+            None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
+            ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), None]
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # head_dim 96
+    assert b"head_dim" in lib.rkv_last_error()
+    args[4], args[9] = 128, 24
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # block 24
+    args[9] = 32
+    args[0] = ctypes.c_void_p(18)
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_ALIGNMENT
+    args[0] = None
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_INVALID_ARGUMENT
+
+
+def test_decode_rejects_bad_arguments_before_touching_a_device(lib):
+    s = _native.Summary(key_pages=16, value_pages=16, counts=16, key_mean=16, value_mean=16,
+                        ellipsoid=16, value_norm=16, max_value_norm=16, heads=2, blocks=3,
+                        block_size=32, head_dim=128, prompt_length=71)
+
+    def call(summary, group=4, eps=0.01, reduction=2):
+        return lib.rkv_decode(ctypes.byref(summary), 16, 0, group, None, None, 0, 0, 0, 0, 0,
+                              None, 0, None, eps, reduction, 16, 16, None, 0, 7, None)
+
+    assert call(s, group=17) == _native.RKV_ERR_UNSUPPORTED
+    assert call(s, eps=-1.0) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert call(s, eps=float("nan")) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert call(s, reduction=5) == _native.RKV_ERR_INVALID_ARGUMENT
+    bad = _native.Summary.from_buffer_copy(s)
+    bad.blocks = 4  # ceil(71 / 32) == 3
+    assert call(bad) == _native.RKV_ERR_INVALID_ARGUMENT
+    bad = _native.Summary.from_buffer_copy(s)
+    bad.block_size = 8
+    assert call(bad) == _native.RKV_ERR_UNSUPPORTED
+
+
+def test_workspace_size_needs_a_device(lib):
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    assert lib.rkv_decode_workspace_size(8, 4, 4096, 128, 32) == 0
+
+
+@pytest.mark.parametrize(
+    "kwargs", [{"eps": float("nan")}, {"eps": -1}, {"block_size": 10}, {"anchor_tokens": -1},
+               {"gqa_reduction": "sum"}, {"backend": "jax"}, {"summary_chunk_blocks": 0}])
+def test_invalid_config_is_rejected(kwargs):
+    with pytest.raises(ValueError):
+        RefineKVConfig(**kwargs)
+
+
+def test_config_defaults_match_reference():
+    c = RefineKVConfig()
+    assert (c.block_size, c.eps, c.gqa_reduction, c.anchor_tokens, c.full_attention_layers,
+            c.backend, c.summary_chunk_blocks, c.collect_stats) == (
+        32, 0.01, "any", 0, 0, "auto", 512, False)
+
+
+def test_cpu_tensors_fail_loudly():
+    from refinekv_b200 import build_summary, select_blocks
+
+    keys = torch.zeros(2, 64, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        build_summary(keys, keys)
+    with pytest.raises(ValueError, match="same nonempty"):
+        build_summary(keys, keys[:, :3])
+    with pytest.raises(TypeError, match="floating point"):
+        build_summary(keys.to(torch.int32), keys.to(torch.int32))
+
+    class _Summary:  # enough of a summary for argument validation
+        keys = torch.zeros(2, 2, 32, 128)
+        block_size = 32
+        num_blocks = 2
+
+    q = torch.zeros(2, 4, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        select_blocks(q, _Summary())
+    with pytest.raises(ValueError, match="torch"):
+        select_blocks(q, _Summary(), RefineKVConfig(backend="torch"))
+    with pytest.raises(ValueError, match="query must have shape"):
+        select_blocks(q[:, :, 0], _Summary())
