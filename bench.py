@@ -1,0 +1,578 @@
+#!/usr/bin/env python
+"""RefineKV decode attention phase on B200: microseconds per decode step at 128K.
+
+Workload (attention phase): Llama-3.1-8B attention
+geometry -- 32 layers, 8 KV heads, GQA group 4, head_dim 128 -- over a
+131072-token synthetic bf16 prompt per layer (seeded generator, see
+refinekv_b200/synthetic.py), block_size 32, eps 0.01, GQA "any", 32 prompt
+anchors.  Following the reference's speed protocol (128 generated tokens,
+timing the last 125), the default run decodes W=3 warm-up steps and times
+K=125 steps.  A step is one decode step of all 32 layers: for each layer the
+selector (2 kernels) and the split attention with its combine (1 kernel),
+replayed from a per-step CUDA graph with the device-side suffix length.
+
+Every layer's KV (512 MiB) is larger than L2, so no flush is needed between
+steps.  value = device time per step (CUDA events, max over ranks).  e2e =
+the same step through the public Python API (sparse_attention), eager, with
+the step's queries and new K/V tokens copied from pinned host memory and the
+outputs copied back inside the timed region.
+
+--gpus N shards the KV heads across N ranks (one process per GPU, torchrun);
+there is no per-step collective (strong scaling: fixed total work).
+
+--impl reference times the reference algorithm on the host CPU (the oracle
+restatement of the reference PyTorch backend, all host threads), one layer
+per step at the same geometry, scaled to 32 layers.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import re
+import statistics
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+for _p in (REPO, REPO / "refinekv-release_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "attention-phase µs/decode step at 128K; achieved HBM GB/s vs B200 peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=125)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--tokens", type=int, default=131072)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--group", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--block-size", type=int, default=32)
+    ap.add_argument("--eps", type=float, default=0.01)
+    ap.add_argument("--reduction", default="any")
+    ap.add_argument("--anchors", type=int, default=32)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--cpu-samples", type=int, default=12)
+    args = ap.parse_args()
+    if args.warmup < 0 or args.steps < 1:
+        ap.error("--steps must be >= 1 and --warmup >= 0")
+    return args
+
+
+def workload_config(args, world):
+    return {
+        "workload": "llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
+        else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}",
+        "layers": args.layers,
+        "prompt_tokens": args.tokens,
+        "kv_heads": args.kv_heads,
+        "group": args.group,
+        "head_dim": args.head_dim,
+        "block_size": args.block_size,
+        "eps": args.eps,
+        "gqa_reduction": args.reduction,
+        "anchor_tokens": args.anchors,
+        "decode_steps": args.warmup + args.steps,
+        "parallelism": f"kv-head shard x{world}",
+        "cache_flush": "none needed: every layer's KV (heads x tokens x 256 B x 2) exceeds L2",
+        "cuda_graph": True,
+        "seed": args.seed,
+    }
+
+
+def measured_hbm_peak():
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "of measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "of fallback (6.65 TB/s pool measurement)"
+
+
+def profiled_traffic(kernel_file: str):
+    """dram bytes per launch and the pages it covered, from a committed ncu summary."""
+    path = REPO / "profiles" / kernel_file
+    if not path.exists():
+        return None
+    text = path.read_text()
+    b = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    u = re.search(r"pages_per_launch:\s*([0-9.eE+]+)", text)
+    if not b or not u:
+        return None
+    return float(b.group(1)), float(u.group(1))
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, read-only)
+# ---------------------------------------------------------------------------
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    def __init__(self, device: torch.device, period_s: float = 0.01):
+        self.samples = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.handle = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                    uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as error:  # NVML missing: report no clocks rather than fail
+            self.error = str(error)
+
+    def _reasons(self):
+        nv = self.nvml
+        for name in ("nvmlDeviceGetCurrentClocksEventReasons",
+                     "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            fn = getattr(nv, name, None)
+            if fn is not None:
+                try:
+                    return int(fn(self.handle))
+                except Exception:
+                    continue
+        return 0
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                self.samples.append((mhz, self._reasons()))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": getattr(self, "error", "nvml unavailable")}
+        busy = [(m, r) for m, r in self.samples if not r & 0x1] or self.samples
+        reasons = 0
+        for _, r in busy:
+            reasons |= r
+        return {
+            "sm_mhz": statistics.median(m for m, _ in busy) if busy else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(name for bit, name in _REASONS.items() if reasons & bit),
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU)
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference algorithm on the host CPU
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import refinekv_oracle as ora
+    from refinekv_b200 import synthetic
+
+    cores = torch.get_num_threads()
+    torch.set_num_threads(max(cores, os.cpu_count() or cores))
+    cores = torch.get_num_threads()
+    # Same generator and device as the B200 arm, so both time the same data.
+    gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
+    data = synthetic.make_layer(args.seed, 0, args.kv_heads, args.tokens, args.head_dim,
+                                args.block_size, device=gen_dev)
+    summary = ora.build_summary(data.keys, data.values, args.block_size)
+    planted = data.planted_mean
+    anchors = synthetic.make_queries(args.seed, 0, -1, planted, args.group, args.anchors).cpu()
+    anchor = ora.anchor_union(anchors, summary, args.eps, args.reduction) if args.anchors else None
+    cap = args.warmup + args.steps
+    tokens = [synthetic.make_decode_token(args.seed, 0, s, args.kv_heads, args.head_dim,
+                                          args.tokens + s, device=gen_dev) for s in range(cap)]
+    suffix_k = torch.cat([k for k, _ in tokens], 1).cpu()
+    suffix_v = torch.cat([v for _, v in tokens], 1).cpu()
+    times = []
+    for step in range(cap):
+        q = synthetic.make_queries(args.seed, 0, step, planted, args.group)[0].cpu()
+        ks, vs = suffix_k[:, :step + 1], suffix_v[:, :step + 1]
+        t0 = time.perf_counter()
+        ora.sparse_attention(q, summary, ks, vs, args.eps, args.reduction, anchor_mask=anchor)
+        dt = time.perf_counter() - t0
+        if step >= args.warmup:
+            times.append(dt)
+    per_layer_us = statistics.median(times) * 1e6
+    value = per_layer_us * args.layers
+    sample = (f"1 layer per step ({args.kv_heads} KV heads x {args.tokens} tokens, reference "
+              f"PyTorch algorithm via the CPU oracle), median of {len(times)} steps, "
+              f"x{args.layers} layers")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "us/step",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(value / 1e3, 3),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 math on bf16 data",
+        "data": "synthetic",
+        "config": workload_config(args, 1),
+        "cpu_baseline": {"value": round(value, 1), "unit": "us/step", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+class Layer:
+    pass
+
+
+def build_layers(args, rank, world, dev):
+    from refinekv_b200 import RefineKVConfig, build_summary, synthetic
+    from refinekv_b200.attention import select_blocks_union
+
+    H = args.kv_heads
+    h0, h1 = rank * H // world, (rank + 1) * H // world
+    cfg = RefineKVConfig(block_size=args.block_size, eps=args.eps,
+                         gqa_reduction=args.reduction, anchor_tokens=args.anchors)
+    cap = args.warmup + args.steps
+    layers = []
+    summarize_ms = []
+    for li in range(args.layers):
+        data = synthetic.make_layer(args.seed, li, H, args.tokens, args.head_dim,
+                                    args.block_size, device=dev)
+        L = Layer()
+        L.keys = data.keys[h0:h1].contiguous() if world > 1 else data.keys
+        L.values = data.values[h0:h1].contiguous() if world > 1 else data.values
+        del data.keys, data.values
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        L.summary = build_summary(L.keys, L.values, cfg)
+        end.record()
+        end.synchronize()
+        summarize_ms.append(start.elapsed_time(end))
+        anchors = synthetic.make_queries(args.seed, li, -1, data.planted_mean, args.group,
+                                         args.anchors)[:, h0:h1]
+        L.anchor = select_blocks_union(anchors.contiguous(), L.summary, cfg) if args.anchors else None
+        L.q = torch.stack([synthetic.make_queries(args.seed, li, s, data.planted_mean,
+                                                  args.group)[0, h0:h1]
+                           for s in range(cap)]).contiguous()
+        ks, vs = [], []
+        for s in range(cap):
+            k, v = synthetic.make_decode_token(args.seed, li, s, H, args.head_dim,
+                                               args.tokens + s, device=dev)
+            ks.append(k[h0:h1])
+            vs.append(v[h0:h1])
+        L.suffix_k = torch.cat(ks, 1).contiguous()
+        L.suffix_v = torch.cat(vs, 1).contiguous()
+        L.workspace = {}
+        layers.append(L)
+    return layers, cfg, summarize_ms
+
+
+def run_b200(args):
+    rank, world, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if args.kv_heads % world:
+        raise SystemExit(f"--gpus {world} must divide the {args.kv_heads} KV heads "
+                         "(sequence split is not part of this bench)")
+    from refinekv_b200 import _native, sparse_attention
+
+    lib = _native.load()
+    layers, cfg, summarize_ms = build_layers(args, rank, world, dev)
+    cap = args.warmup + args.steps
+    length = torch.zeros((), device=dev, dtype=torch.int32)
+    heads_local = args.kv_heads // world
+
+    # one CUDA graph per decode step: bump the visible suffix, then all layers
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for L in layers:  # allocate every workspace before capture
+            sparse_attention(L.q[0], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                             workspace=L.workspace, suffix_length=length)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graphs = []
+    for s in range(cap):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            length.add_(1)
+            for L in layers:
+                sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg,
+                                 anchor_mask=L.anchor, workspace=L.workspace,
+                                 suffix_length=length)
+        graphs.append(g)
+
+    length.zero_()
+    barrier(world)
+    for s in range(args.warmup):
+        graphs[s].replay()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        start.record()
+        for s in range(args.warmup, cap):
+            graphs[s].replay()
+        end.record()
+        end.synchronize()
+    barrier(world)
+    local_ms = start.elapsed_time(end)
+    total_ms = max_over_ranks(local_ms, world)
+    us_per_step = total_ms * 1e3 / args.steps
+    for L in layers:
+        from refinekv_b200.attention import device_status
+
+        if device_status(L.workspace):
+            raise RuntimeError("device status word set during the timed run")
+    del graphs
+
+    # ---- per-phase timing pass (eager, same steps) for the roofline --------
+    counts_all = [L.summary.counts for L in layers]
+    sel_tokens = torch.zeros((), device=dev, dtype=torch.int64)
+    sel_pages = torch.zeros((), device=dev, dtype=torch.int64)
+    phase_events = []
+    for s in range(args.warmup, cap):
+        length.fill_(s + 1)
+        for L, counts in zip(layers, counts_all):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                             workspace=L.workspace, suffix_length=length,
+                             _phases=_native.PHASE_STATS | _native.PHASE_FINAL)
+            e1.record()
+            sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                             workspace=L.workspace, suffix_length=length,
+                             _phases=_native.PHASE_ATTEND)
+            e2.record()
+            phase_events.append((e0, e1, e2))
+            sel = L.workspace["selected"]
+            sel_pages += sel.sum()
+            sel_tokens += (sel.to(torch.int64) * counts).sum()
+    torch.cuda.synchronize(dev)
+    select_ms = [a.elapsed_time(b) for a, b, _ in phase_events]
+    attend_ms = [b.elapsed_time(c) for _, b, c in phase_events]
+    launches = len(phase_events)  # = steps x layers
+    pages = int(sel_pages.item())
+    tokens_refined = int(sel_tokens.item())
+    D, G, B = args.head_dim, args.group, args.block_size
+    nb = -(-args.tokens // B)
+    # algorithmic bytes (our formats, workspace scratch excluded)
+    suffix_total = args.layers * heads_local * sum(s + 1 for s in range(args.warmup, cap))
+    qo_bytes = 2 * heads_local * G * D * 2
+    attend_bytes = (tokens_refined + suffix_total) * D * 2 * 2 / launches + qo_bytes
+    attend_avg_ms = statistics.mean(attend_ms)
+    peak, peak_note = measured_hbm_peak()
+    attend_gbs = attend_bytes / (attend_avg_ms * 1e-3) / 1e9
+    unselected = launches * heads_local * nb - pages
+    summary_bytes = (heads_local * nb * D * 2 * 2 + nb * 8 + heads_local * nb * 4 + heads_local * 4
+                     + heads_local * nb * (2 if args.anchors else 1))
+    step_bytes = args.layers * (summary_bytes + qo_bytes) + (
+        tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
+    traffic = profiled_traffic("attend_llama8b_128k.md")
+    traffic_per_launch = None
+    if traffic is not None:
+        dram_bytes, pages_profiled = traffic
+        traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
+    step_gbs = sum_over_ranks(step_bytes, world) / (us_per_step * 1e-6) / 1e9
+
+    # ---- end to end through the public API with host buffers ---------------
+    e2e = None
+    if not args.skip_e2e:
+        pin = dict(pin_memory=True)
+        q_host = torch.stack([L.q for L in layers], 1).cpu().pin_memory()  # (cap, L, H, G, 1, D)
+        kv_host = torch.stack([torch.stack([L.suffix_k, L.suffix_v]) for L in layers]).cpu()
+        kv_host = kv_host.permute(3, 0, 1, 2, 4).contiguous().pin_memory()  # (cap, L, 2, H, D)
+        out_host = torch.empty(cap, args.layers, heads_local, G, 1, D, dtype=torch.bfloat16, **pin)
+        q_dev = [torch.empty_like(L.q[0]) for L in layers]
+        barrier(world)
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for s in range(cap):
+            if s == args.warmup:
+                barrier(world)
+                e_start.record()
+            for li, L in enumerate(layers):
+                q_dev[li].copy_(q_host[s, li], non_blocking=True)
+                L.suffix_k[:, s].copy_(kv_host[s, li, 0], non_blocking=True)
+                L.suffix_v[:, s].copy_(kv_host[s, li, 1], non_blocking=True)
+            for li, L in enumerate(layers):
+                res = sparse_attention(q_dev[li], L.summary, L.suffix_k[:, :s + 1],
+                                       L.suffix_v[:, :s + 1], cfg, anchor_mask=L.anchor,
+                                       workspace=L.workspace)
+                out_host[s, li].copy_(res.output, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()  # the host reads the step's outputs
+        e_end.record()
+        e_end.synchronize()
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+        h2d = args.layers * (q_dev[0].numel() * 2 + 2 * heads_local * D * 2)
+        d2h = args.layers * heads_local * G * D * 2
+        e2e = {"value": round(e2e_ms * 1e3 / args.steps, 1), "unit": "us/step",
+               "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
+               "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
+               "path": "refinekv_b200.sparse_attention (eager, per layer) via the C ABI"}
+
+    # ---- CPU baseline: the reference algorithm on the host (rank 0, N=1) ---
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        from oracle import refinekv_oracle as ora
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        L = layers[0]
+        s_cpu = ora.as_cpu_summary(L.summary)
+        anchor = L.anchor.cpu() if L.anchor is not None else None
+        times = []
+        for i in range(args.cpu_samples):
+            s = args.warmup + i % args.steps
+            q = L.q[s].cpu()
+            ks, vs = L.suffix_k[:, :s + 1].cpu(), L.suffix_v[:, :s + 1].cpu()
+            t0 = time.perf_counter()
+            ora.sparse_attention(q, s_cpu, ks, vs, args.eps, args.reduction, anchor_mask=anchor)
+            times.append(time.perf_counter() - t0)
+        cpu_us = statistics.median(times[1:] or times) * 1e6 * args.layers
+        cpu = {"value": round(cpu_us, 1), "unit": "us/step", "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"layer 0, {args.cpu_samples} decode steps of the same workload through "
+                         f"the CPU oracle (reference PyTorch algorithm), median x{args.layers} "
+                         "layers"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(us_per_step, 2),
+            "unit": "us/step",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(us_per_step / 1e3, 4),
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded: LogNormal-scaled RoPE keys, N(0,1) values, 6 planted "
+                    "blocks per layer; stands in for the paper's LongBench prompts)",
+            "config": workload_config(args, world),
+            "hbm": {"achieved_gbs": round(step_gbs, 1), "peak_gbs": peak,
+                    "frac": round(step_gbs / peak, 4), "bytes_per_step":
+                        int(sum_over_ranks(step_bytes, world)), "note": peak_note},
+            "roofline": {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
+                         "traffic": None if traffic_per_launch is None else int(traffic_per_launch),
+                         "kernel": f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}>",
+                         "algorithmic_bytes_per_launch": int(attend_bytes),
+                         "avg_launch_us": round(attend_avg_ms * 1e3, 2),
+                         "peak_note": peak_note},
+            "phase_us_per_layer": {"select": round(statistics.mean(select_ms) * 1e3, 2),
+                                   "attend": round(attend_avg_ms * 1e3, 2)},
+            "selected_fraction": round(pages / (launches * heads_local * nb), 5),
+            "summarize_us_per_layer": round(statistics.median(summarize_ms) * 1e3, 1),
+            "gpu_launches": args.steps * args.layers * lib.rkv_decode_launch_count(
+                _native.PHASE_ALL),
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -41,22 +41,24 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
   size_t off = 0;
   uint8_t* ring = smem;  // [warp][stage][K | V]
   off += static_cast<size_t>(warps) * S * kStage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + off);
-  off += round16(static_cast<size_t>(warps) * S * 8);
-  int4* desc = reinterpret_cast<int4*>(smem + off);  // {head, row, valid, suffix}
-  off += static_cast<size_t>(warps) * S * 16;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + off);  // [warp][stage][K, V]
+  off += round16(static_cast<size_t>(warps) * S * 16);
+  int* valid_rows = reinterpret_cast<int*>(smem + off);  // [warp][stage]
+  off += round16(static_cast<size_t>(warps) * S * 4);
   long long* hstart = reinterpret_cast<long long*>(smem + off);  // [H + 1]
   off += round16(static_cast<size_t>(H + 1) * 8);
   int* seg_pre = reinterpret_cast<int*>(smem + off);  // [H][PB + 1]
   off += round16(static_cast<size_t>(H) * (PB + 1) * 4);
   int* flags = reinterpret_cast<int*>(smem + off);  // [4]
   off += 16;
+  int* pending = reinterpret_cast<int*>(smem + off);  // [H][3] heads this CTA combines
+  off += round16(static_cast<size_t>(H) * 12);
   float* st_m = reinterpret_cast<float*>(smem + off);  // [warps][G8]
   float* st_l = st_m + warps * G8;
   float* st_o = st_l + warps * G8;  // [warps][G8][D]
 
   if (lane == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[warp * S + s], 1);
+    for (int s = 0; s < 2 * S; ++s) mbar_init(&bars[warp * 2 * S + s], 1);
     mbar_fence_init();
   }
   if (threadIdx.x == 0) {
@@ -79,13 +81,16 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
   }
   const int n_suffix = (suffix_len + R - 1) / R;
 
+  // Selected-page counts of every (head, selector segment), loaded in
+  // parallel, then prefix sums per head.
+  for (int i = threadIdx.x; i < H * PB; i += blockDim.x) {
+    seg_pre[(i / PB) * (PB + 1) + (i % PB) + 1] = __ldcg(p.seg_count + i);
+  }
+  __syncthreads();
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    int acc = 0;
-    seg_pre[h * (PB + 1)] = 0;
-    for (int k = 0; k < PB; ++k) {
-      acc += p.seg_count[h * PB + k];
-      seg_pre[h * (PB + 1) + k + 1] = acc;
-    }
+    int* pre = seg_pre + h * (PB + 1);
+    pre[0] = 0;
+    for (int k = 1; k <= PB; ++k) pre[k] += pre[k - 1];
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -111,89 +116,165 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
 
   const int count_w = hi - lo > warp ? static_cast<int>((hi - lo - warp + warps - 1) / warps) : 0;
 
-  // Lane 0 decodes and issues local item j of this warp.  Its head cursor
-  // only moves forward because the warp's items are issued in order.
-  int issue_head = 0;
-  auto issue = [&](int j) {
+  // Item descriptors {head, first row, valid rows, is_suffix} are decoded 32
+  // at a time, one per lane, one batch ahead of use, so the loads of the
+  // selected ids and counts are off the issue path.  Each lane's head
+  // cursor only moves forward because batches are decoded in order.
+  int lane_head = 0;
+  auto decode = [&](int base) {
+    const int j = base + lane;
+    int4 d = make_int4(0, 0, 0, 0);
+    if (j >= count_w) return d;
     const long long k = lo + warp + static_cast<long long>(j) * warps;
-    while (hstart[issue_head + 1] <= k) ++issue_head;
-    const int h = issue_head;
+    while (hstart[lane_head + 1] <= k) ++lane_head;
+    const int h = lane_head;
     const int pos = static_cast<int>(k - hstart[h]);
     const int* pre = seg_pre + h * (PB + 1);
-    int row, valid, is_suffix;
     if (pos < pre[PB]) {
-      int a = 0, b = PB;  // find seg with pre[seg] <= pos < pre[seg + 1]
+      int a = 0, b = PB;  // segment with pre[a] <= pos < pre[a + 1]
       while (b - a > 1) {
         const int mid = (a + b) >> 1;
         if (pre[mid] <= pos) a = mid; else b = mid;
       }
-      const int block = p.sel_ids[(static_cast<size_t>(h) * PB + a) * p.seg_cap + (pos - pre[a])];
-      row = block * R;
-      valid = static_cast<int>(p.counts[block]);
-      is_suffix = 0;
+      const int block = __ldg(p.sel_ids + (static_cast<size_t>(h) * PB + a) * p.seg_cap +
+                              (pos - pre[a]));
+      d = make_int4(h, block * R, min(R, p.prompt_length - block * R), 0);
     } else {
       const int c = pos - pre[PB];
-      row = c * R;
-      valid = min(R, suffix_len - c * R);
-      is_suffix = 1;
+      d = make_int4(h, c * R, min(R, suffix_len - c * R), 1);
     }
-    const int s = j % S;
-    desc[warp * S + s] = make_int4(h, row, valid, is_suffix);
-    uint8_t* dst = ring + (warp * S + s) * kStage;
-    mbar_expect_tx(&bars[warp * S + s], kStage);
-    tma_tile<D>(dst, is_suffix ? &maps.key_suffix : &maps.key_pages, &bars[warp * S + s], row, h,
-                R);
-    tma_tile<D>(dst + kTile, is_suffix ? &maps.value_suffix : &maps.value_pages,
-                &bars[warp * S + s], row, h, R);
+    return d;
   };
-  int issued = min(S, count_w);
-  if (lane == 0) {
-    for (int j = 0; j < issued; ++j) issue(j);
+  int batch_base = 0;
+  int4 cur = decode(0);
+  int4 nxt = decode(32);
+  auto item = [&](int j) {  // whole warp; j never skips ahead of the batch
+    if (j >= batch_base + 32) {
+      batch_base += 32;
+      cur = nxt;
+      nxt = decode(batch_base + 32);
+    }
+    const int src = j - batch_base;
+    return make_int4(__shfl_sync(0xffffffffu, cur.x, src), __shfl_sync(0xffffffffu, cur.y, src),
+                     __shfl_sync(0xffffffffu, cur.z, src), __shfl_sync(0xffffffffu, cur.w, src));
+  };
+  // K and V of a stage have their own barriers: K is refilled as soon as the
+  // scores are computed, V after the value product.
+  auto issue_k = [&](int j, const int4& d) {
+    if (lane == 0) {
+      const int s = j % S;
+      valid_rows[warp * S + s] = d.z;
+      uint64_t* bk = &bars[(warp * S + s) * 2];
+      mbar_expect_tx(bk, kTile);
+      tma_tile<D>(ring + (warp * S + s) * kStage, d.w ? &maps.key_suffix : &maps.key_pages, bk,
+                  d.y, d.x, R);
+    }
+  };
+  auto issue_v = [&](int j, const int4& d) {
+    if (lane == 0) {
+      const int s = j % S;
+      uint64_t* bv = &bars[(warp * S + s) * 2 + 1];
+      mbar_expect_tx(bv, kTile);
+      tma_tile<D>(ring + (warp * S + s) * kStage + kTile,
+                  d.w ? &maps.value_suffix : &maps.value_pages, bv, d.y, d.x, R);
+    }
+  };
+  const int first_fill = min(S, count_w);
+  for (int j = 0; j < first_fill; ++j) {
+    const int4 d = item(j);
+    issue_k(j, d);
+    issue_v(j, d);
   }
+  int issued_k = first_fill, issued_v = first_fill;
 
-  // Merge this head's partials (selector representatives + attention CTAs
-  // [first, last]) and write the output rows.
-  auto combine = [&](int h, long long first, long long last) {
+  // Merge head h's partials (selector representatives + attention CTAs
+  // [first, last]) and write its output rows.  Row maxima and denominators
+  // first (one warp per row), then one float4 of output per thread, with the
+  // partial loads issued 16 at a time so they overlap.
+  float* comb = st_m;  // reuses the stash: [2][G]
+  auto combine = [&](int h, int first, int last) {
     const int G = p.group;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-      const int g = idx / D, d = idx - g * D;
+    const int n_att = last - first + 1;
+    const int nsrc = PB + n_att;
+    auto slot_of = [&](int k) {
+      return k < PB ? static_cast<size_t>(h * PB + k) * G
+                    : static_cast<size_t>(h * p.ctas + first + k - PB) * G;
+    };
+    for (int g = warp; g < G; g += warps) {
       float top = -INFINITY;
-      for (int k = 0; k < PB; ++k) top = fmaxf(top, __ldcg(p.rep_m + (h * PB + k) * G + g));
-      for (long long c = first; c <= last; ++c)
-        top = fmaxf(top, __ldcg(p.att_m + (h * p.ctas + c) * G + g));
+      for (int k = lane; k < nsrc; k += 32) {
+        top = fmaxf(top, __ldcg((k < PB ? p.rep_m : p.att_m) + slot_of(k) + g));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
       const float ref = top == -INFINITY ? 0.f : top;
-      float acc = 0.f, den = 0.f;
-      for (int k = 0; k < PB; ++k) {
-        const size_t slot = static_cast<size_t>(h * PB + k) * G + g;
-        const float w = __expf(__ldcg(p.rep_m + slot) - ref);
-        acc += w * __ldcg(p.rep_o + slot * D + d);
-        den += w * __ldcg(p.rep_l + slot);
+      float den = 0.f;
+      for (int k = lane; k < nsrc; k += 32) {
+        const size_t slot = slot_of(k) + g;
+        den += __ldcg((k < PB ? p.rep_l : p.att_l) + slot) *
+               __expf(__ldcg((k < PB ? p.rep_m : p.att_m) + slot) - ref);
       }
-      for (long long c = first; c <= last; ++c) {
-        const size_t slot = static_cast<size_t>(h * p.ctas + c) * G + g;
-        const float w = __expf(__ldcg(p.att_m + slot) - ref);
-        acc += w * __ldcg(p.att_o + slot * D + d);
-        den += w * __ldcg(p.att_l + slot);
-      }
-      const float out = acc / fmaxf(den, 1e-30f);
-      const size_t o = (static_cast<size_t>(h) * G + g) * D + d;
-      if (p.query_f32) {
-        static_cast<float*>(p.out)[o] = out;
-      } else {
-        static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(out);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+      if (lane == 0) {
+        comb[g] = ref;
+        comb[G + g] = fmaxf(den, 1e-30f);
       }
     }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * (D / 4); idx += blockDim.x) {
+      const int g = idx / (D / 4), d4 = idx - g * (D / 4);
+      const float ref = comb[g];
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < nsrc; k0 += 16) {
+        float w[16];
+        float4 v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int k = k0 + u;
+          w[u] = -INFINITY;
+          v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (k < nsrc) {
+            const size_t slot = slot_of(k) + g;
+            w[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + slot);
+            v[u] = __ldcg(reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) +
+                                                          slot * D) + d4);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float e = __expf(w[u] - ref);
+          acc.x += e * v[u].x;
+          acc.y += e * v[u].y;
+          acc.z += e * v[u].z;
+          acc.w += e * v[u].w;
+        }
+      }
+      const float inv = 1.f / comb[G + g];
+      const size_t o = (static_cast<size_t>(h) * G + g) * D + d4 * 4;
+      if (p.query_f32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      } else {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + o;
+        *reinterpret_cast<uint2*>(out) =
+            make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
+      }
+    }
+    __syncthreads();
   };
-  // Count this CTA's contribution to head h; the last of `expected` combines.
-  auto arrive = [&](int h, int expected, long long first, long long last) {
+  // Count this CTA's contribution to head h.  The last of `expected`
+  // arrivals owns the head's combine, which runs after this CTA's own pages
+  // so that a combine never delays the streaming of other pages.
+  if (threadIdx.x == 0) flags[1] = 0;
+  auto arrive = [&](int h, int expected, int first, int last) {
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) flags[0] = atomicAdd(p.done + h, 1) == expected - 1;
-    __syncthreads();
-    if (flags[0]) {
-      __threadfence();
-      combine(h, first, last);
-      if (threadIdx.x == 0) p.done[h] = 0;
+    if (threadIdx.x == 0 && atomicAdd(p.done + h, 1) == expected - 1) {
+      int* e = pending + 3 * flags[1]++;
+      e[0] = h;
+      e[1] = first;
+      e[2] = last;
     }
     __syncthreads();
   };
@@ -226,13 +307,15 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
       for (; jj < j_end; ++jj) {
         if (aborted) continue;
         const int s = jj % S;
-        if (!warp_wait(&bars[warp * S + s], (jj / S) & 1)) {
+        const uint32_t par = (jj / S) & 1;
+        uint64_t* bk = &bars[(warp * S + s) * 2];
+        if (!warp_wait(bk, par)) {
           if (lane == 0) atomicOr(p.status, kStatusTimeout);
-          drain_pending(bars + warp * S, S, jj, issued);
+          drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
           aborted = true;
           continue;
         }
-        const int valid = desc[warp * S + s].z;
+        const int valid = valid_rows[warp * S + s];
         const uint32_t base = smem_addr(ring + (warp * S + s) * kStage);
         float logit[R / 16][NT][4];
         score_tile<R, D, NT>(base, qb, logit, lane);
@@ -245,14 +328,31 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
             for (int nt = 0; nt < NT; ++nt)
               logit[mt][nt][c] = r < valid ? logit[mt][nt][c] * p.scale : -INFINITY;
           }
-        attend_tile<R, D, NT>(logit, base + kTile, m, l, o, p.query_f32 != 0, lane);
         __syncwarp();
-        if (jj + S < count_w) {
-          if (lane == 0) {
-            fence_proxy_async();
-            issue(jj + S);
-          }
-          ++issued;
+        const bool refill = jj + S < count_w;
+        int4 next = make_int4(0, 0, 0, 0);
+        if (refill) {
+          next = item(jj + S);
+          if (lane == 0) fence_proxy_async();
+          issue_k(jj + S, next);
+          ++issued_k;
+        }
+        softmax_update<R, D, NT>(logit, m, l, o);
+        uint32_t hi_frag[R / 16][NT][2], lo_frag[R / 16][NT][2];
+        prob_frags<R, NT>(logit, hi_frag, lo_frag, p.query_f32 != 0);
+        if (!warp_wait(bk + 1, par)) {
+          if (lane == 0) atomicOr(p.status, kStatusTimeout);
+          drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
+          aborted = true;
+          continue;
+        }
+        accumulate_values<R, D, NT>(base + kTile, hi_frag, o, lane);
+        if (p.query_f32) accumulate_values<R, D, NT>(base + kTile, lo_frag, o, lane);
+        __syncwarp();
+        if (refill) {
+          if (lane == 0) fence_proxy_async();
+          issue_v(jj + S, next);
+          ++issued_v;
         }
       }
       reduce_l<NT>(l);
@@ -262,9 +362,9 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
       merge_stashed<D>(st_m, st_l, st_o, warps, G8, p.group, p.att_m + slot * p.group,
                        p.att_l + slot * p.group, p.att_o + slot * p.group * D, threadIdx.x,
                        blockDim.x);
-      const long long first = cta_of(hstart[h]);
-      const long long last = cta_of(hstart[h + 1] - 1);
-      arrive(h, static_cast<int>(last - first + 1), first, last);
+      const int first = static_cast<int>(cta_of(hstart[h]));
+      const int last = static_cast<int>(cta_of(hstart[h + 1] - 1));
+      arrive(h, last - first + 1, first, last);
     }
   }
   pdl_launch_dependents();
@@ -275,6 +375,13 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
     if (hstart[h + 1] != hstart[h]) continue;
     const long long owner = T == 0 ? h % p.ctas : cta_of(hstart[h] < T ? hstart[h] : T - 1);
     if (owner == cta) arrive(h, 1, 0, -1);
+  }
+  __threadfence();
+  __syncthreads();
+  for (int i = 0; i < flags[1]; ++i) {
+    const int* e = pending + 3 * i;
+    combine(e[0], e[1], e[2]);
+    if (threadIdx.x == 0) p.done[e[0]] = 0;
   }
 }
 
@@ -323,10 +430,11 @@ size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, in
   const int g8 = group <= 8 ? 8 : 16;
   size_t bytes = kSmemSlack;
   bytes += static_cast<size_t>(warps) * stages * 2 * page * dim * 2;  // TMA ring
-  bytes += round16(static_cast<size_t>(warps) * stages * 8);           // barriers
-  bytes += static_cast<size_t>(warps) * stages * 16;                   // item descriptors
+  bytes += round16(static_cast<size_t>(warps) * stages * 16);          // K and V barriers
+  bytes += round16(static_cast<size_t>(warps) * stages * 4);           // valid rows
   bytes += round16(static_cast<size_t>(heads + 1) * 8);
   bytes += round16(static_cast<size_t>(heads) * (parts_b + 1) * 4) + 16;
+  bytes += round16(static_cast<size_t>(heads) * 12);  // pending combines
   bytes += static_cast<size_t>(warps) * g8 * 4 * 2 + static_cast<size_t>(warps) * g8 * dim * 4;
   return bytes;
 }

@@ -116,7 +116,7 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
       const size_t fixed = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
                                              pl->warps_c, 0, static_cast<int>(group),
                                              static_cast<int>(heads), pl->parts_b);
-      const int64_t per = static_cast<int64_t>(pl->warps_c) * (stage + 8 + 16);
+      const int64_t per = static_cast<int64_t>(pl->warps_c) * (stage + 16 + 4);
       const int64_t fit = (budget - static_cast<int64_t>(fixed) - 16) / per;
       if (fit >= 2 || pl->warps_c == 1) {
         pl->stages_c = static_cast<int>(std::min<int64_t>(8, fit));
@@ -578,6 +578,7 @@ int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, i
   p.group = static_cast<int>(group);
   p.blocks = static_cast<int>(summary->blocks);
   p.page = static_cast<int>(B);
+  p.prompt_length = static_cast<int>(summary->prompt_length);
   p.has_suffix = suffix_capacity > 0;
   p.suffix_capacity = static_cast<int>(suffix_capacity);
   p.suffix_len_ptr = suffix_length;

@@ -89,6 +89,13 @@ __device__ __forceinline__ void drain_pending(uint64_t* bars, int stages, int fr
   for (int j = from; j < issued; ++j) mbar_wait(&bars[j % stages], (j / stages) & 1);
 }
 
+// Same for rings whose stages hold separate K and V barriers ([stage][2]).
+__device__ __forceinline__ void drain_pending(uint64_t* bars, int stages, int from, int issued_k,
+                                              int issued_v) {
+  for (int j = from; j < issued_k; ++j) mbar_wait(&bars[(j % stages) * 2], (j / stages) & 1);
+  for (int j = from; j < issued_v; ++j) mbar_wait(&bars[(j % stages) * 2 + 1], (j / stages) & 1);
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled, 3-D: x = channel, y = row, z = head).  No multicast anywhere.
 // ---------------------------------------------------------------------------
@@ -233,21 +240,40 @@ __device__ __forceinline__ void load_query_frags(uint32_t (&qb)[D / 16][NT][2], 
   }
 }
 
-// acc[mt][nt] = tile[mt*16 .. +16) . q^T for a swizzled [R x D] tile.
+// bf16(q^2) fragments from the bf16 q fragments (the ellipsoid term).
+template <int D, int NT>
+__device__ __forceinline__ void square_frags(const uint32_t (&qb)[D / 16][NT][2],
+                                             uint32_t (&q2)[D / 16][NT][2]) {
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&qb[ks][nt][half]);
+        const float x0 = __low2float(v), x1 = __high2float(v);
+        q2[ks][nt][half] = pack_bf16(x0 * x0, x1 * x1);
+      }
+}
+
+// acc[mt][nt] = tile[mt*16 .. +16) . q^T for a swizzled [R x D] tile.  The
+// k-steps are the outer loop so the R/16 independent accumulator chains
+// interleave.
 template <int R, int D, int NT>
 __device__ __forceinline__ void score_tile(uint32_t tile, const uint32_t (&qb)[D / 16][NT][2],
                                            float (&acc)[R / 16][NT][4], int lane) {
 #pragma unroll
-  for (int mt = 0; mt < R / 16; ++mt) {
+  for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int nt = 0; nt < NT; ++nt)
       acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
-    }
-    const int row = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
+  for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt) {
       uint32_t a[4];
-      ldsm_x4(tile + swz(row, ks * 2 + (lane >> 4), R), a);
+      ldsm_x4(tile + swz(mt * 16 + row, ks * 2 + (lane >> 4), R), a);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma_bf16(acc[mt][nt], a, qb[ks][nt][0], qb[ks][nt][1]);
     }

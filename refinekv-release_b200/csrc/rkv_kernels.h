@@ -90,6 +90,7 @@ struct AttendParams {
   void* out;  // (heads, group, dim) in the query dtype
   const int64_t* counts;
   int heads, group, blocks, page;
+  int prompt_length;  // rows of block b: min(page, prompt_length - b * page)
   int has_suffix;
   int suffix_capacity;
   const int* suffix_len_ptr;  // device scalar or null

@@ -59,17 +59,6 @@ __device__ __forceinline__ float block_risk(float z, float delta, float log_z, f
 
 __device__ __forceinline__ bool finite(float x) { return isfinite(x); }
 
-// Online (max, sum of exp) update with accurate exp.
-__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
-  if (x == -INFINITY) return;
-  if (x > m) {
-    s = s * expf(m - x) + 1.f;
-    m = x;
-  } else {
-    s += expf(x - m);
-  }
-}
-
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   const float top = fmaxf(m, m2);
   const float ref = top == -INFINITY ? 0.f : top;
@@ -127,7 +116,7 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
                   static_cast<size_t>(ih) * p.group * D * (p.query_f32 ? 4 : 2);
   uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
   load_query_frags<D, NT>(qk, q, p.query_f32, p.group, lane, false);
-  load_query_frags<D, NT>(q2, q, p.query_f32, p.group, lane, true);
+  square_frags<D, NT>(qk, q2);
 
   float zm[NT][2], zs[NT][2], cm[NT][2], cs[NT][2];
 #pragma unroll
@@ -159,29 +148,69 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
       ++issued;
     }
     const int tile = t0 + warp + j * warps;
+    // This lane's blocks are rows lane/4 and lane/4 + 8 of each m-tile.
+    float log_count[R / 16][2];
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int b = tile * R + mt * 16 + (lane >> 2) + hf * 8;
+        log_count[mt][hf] = b < p.blocks ? logf(static_cast<float>(__ldg(p.counts + b))) : 0.f;
+      }
+    // z and z + log cosh(delta) of every element first (independent), then
+    // one (max, sum) update per column: no serial exp chain.
+    float zv[R / 16][NT][4], cv[R / 16][NT][4];
 #pragma unroll
     for (int mt = 0; mt < R / 16; ++mt) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int b = tile * R + mt * 16 + (lane >> 2) + (c >> 1) * 8;
-        const bool bok = b < p.blocks;
-        const float lc_count = bok ? logf(static_cast<float>(p.counts[b])) : 0.f;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
-          if (!bok || g >= p.group) continue;
+          zv[mt][nt][c] = -INFINITY;
+          cv[mt][nt][c] = -INFINITY;
+          if (b >= p.blocks || g >= p.group) continue;
           const float score = sk[mt][nt][c] * p.scale;
           const float proj = sw[mt][nt][c];
           const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
-          const float z = score + lc_count;
+          const float z = score + log_count[mt][c >> 1];
           const size_t row = static_cast<size_t>(ih) * p.group + g;
           p.z[row * p.blocks + b] = z;
           p.delta[row * p.blocks + b] = delta;
-          lse_push(zm[nt][c & 1], zs[nt][c & 1], z);
-          lse_push(cm[nt][c & 1], cs[nt][c & 1], z + log_cosh(delta));
+          zv[mt][nt][c] = z;
+          cv[mt][nt][c] = z + log_cosh(delta);
         }
       }
     }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int jc = 0; jc < 2; ++jc) {
+        float tz = -INFINITY, tc = -INFINITY;
+        bool nan = false;
+#pragma unroll
+        for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const float a = zv[mt][nt][2 * hf + jc], b = cv[mt][nt][2 * hf + jc];
+            tz = fmaxf(tz, a);
+            tc = fmaxf(tc, b);
+            nan |= (a != a) || (b != b);
+          }
+        float sz = 0.f, sc = 0.f;
+        const float rz = tz == -INFINITY ? 0.f : tz, rc = tc == -INFINITY ? 0.f : tc;
+#pragma unroll
+        for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            sz += expf(zv[mt][nt][2 * hf + jc] - rz);
+            sc += expf(cv[mt][nt][2 * hf + jc] - rc);
+          }
+        if (nan) sz = sc = NAN;  // a NaN row statistic must stay non-finite
+        lse_merge(zm[nt][jc], zs[nt][jc], tz, sz);
+        lse_merge(cm[nt][jc], cs[nt][jc], tc, sc);
+      }
   }
 
   // Reduce the (max, sum) pairs over the 8 lanes of each column, then warps.
@@ -226,7 +255,10 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
 
 // ------------------------------- phase B ----------------------------------
 
-template <int D, int NT>
+// GM = group rows evaluated per block (the group padded to 4, 8 or 16); the
+// padding rows repeat row 0 and are masked out of the reduction, which keeps
+// the per-row risk evaluations branch-free and independent.
+template <int D, int NT, int GM>
 __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ FinalMaps maps,
                                                     const FinalParams p) {
   constexpr int R = kSelectTile;
@@ -270,38 +302,64 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   __syncthreads();
   pdl_wait();
 
-  // Row-global normalisers from the phase-A partials.
-  if (threadIdx.x < p.group) {
-    const int g = threadIdx.x;
+  // Row-global normalisers from the phase-A partials: one warp per row,
+  // lanes load partials in parallel and merge them with shuffles.
+  for (int g = warp; g < p.group; g += warps) {
     const float* in = p.lse + (static_cast<size_t>(ih) * p.group + g) * p.parts_a * 4;
     float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    for (int k = 0; k < p.parts_a; ++k) {
-      lse_merge(m0, s0, in[4 * k], in[4 * k + 1]);
-      lse_merge(m1, s1, in[4 * k + 2], in[4 * k + 3]);
+    for (int k = lane; k < p.parts_a; k += 32) {
+      const float4 v = *reinterpret_cast<const float4*>(in + 4 * k);
+      lse_merge(m0, s0, v.x, v.y);
+      lse_merge(m1, s1, v.z, v.w);
     }
-    const float lz = m0 + logf(s0);
-    const float lc = m1 + logf(s1);
-    log_z[g] = lz;
-    log_c[g] = lc;
-    if (!finite(lz) || !finite(lc)) atomicOr(&flags[0], 1);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m0, off);
+      const float os = __shfl_xor_sync(0xffffffffu, s0, off);
+      const float pm = __shfl_xor_sync(0xffffffffu, m1, off);
+      const float ps = __shfl_xor_sync(0xffffffffu, s1, off);
+      lse_merge(m0, s0, om, os);
+      lse_merge(m1, s1, pm, ps);
+    }
+    if (lane == 0) {
+      const float lz = m0 + logf(s0);
+      const float lc = m1 + logf(s1);
+      log_z[g] = lz;
+      log_c[g] = lc;
+      if (!finite(lz) || !finite(lc)) atomicOr(&flags[0], 1);
+    }
   }
   __syncthreads();
   const bool bad_global = flags[0] != 0;
   const float vmax = p.max_value_norm[h];
 
-  // Pass 1: decisions, one lane per block.
+  // Pass 1: decisions, one lane per block.  All rows' z and delta are
+  // loaded before any risk is evaluated so the loads overlap.
   for (int t = t0 + warp; t < t1; t += warps) {
     const int b = t * R + lane;
     const bool valid = b < p.blocks;
     bool sel = false;
     if (valid) {
       const float vnorm = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
+      float zr[GM], dr[GM], lz[GM], lc[GM];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        const int gg = g < p.group ? g : 0;
+        const size_t row = static_cast<size_t>(ih) * p.group + gg;
+        zr[g] = p.z[row * p.blocks + b];
+        dr[g] = p.delta[row * p.blocks + b];
+        lz[g] = log_z[gg];
+        lc[g] = log_c[gg];
+      }
+      float risk[GM];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) risk[g] = block_risk(zr[g], dr[g], lz[g], lc[g], vnorm, vmax);
       float agg = p.reduction == kMax ? -INFINITY : 0.f;
       bool any = false, bad = false;
-      for (int g = 0; g < p.group; ++g) {
-        const size_t row = static_cast<size_t>(ih) * p.group + g;
-        const float r = block_risk(p.z[row * p.blocks + b], p.delta[row * p.blocks + b],
-                                   log_z[g], log_c[g], vnorm, vmax);
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g >= p.group) continue;
+        const float r = risk[g];
         bad |= !finite(r);
         if (p.reduction == kMean) {
           agg += r;
@@ -458,8 +516,9 @@ template <int D>
 cudaError_t final_dispatch(const FinalMaps& maps, const FinalParams& p, int warps, size_t smem,
                            cudaStream_t stream, bool pdl) {
   const dim3 grid(p.instances * p.heads, p.parts);
-  if (p.group <= 8) return launch_k(final_kernel<D, 1>, maps, p, grid, warps, smem, stream, pdl);
-  return launch_k(final_kernel<D, 2>, maps, p, grid, warps, smem, stream, pdl);
+  if (p.group <= 4) return launch_k(final_kernel<D, 1, 4>, maps, p, grid, warps, smem, stream, pdl);
+  if (p.group <= 8) return launch_k(final_kernel<D, 1, 8>, maps, p, grid, warps, smem, stream, pdl);
+  return launch_k(final_kernel<D, 2, 16>, maps, p, grid, warps, smem, stream, pdl);
 }
 
 }  // namespace

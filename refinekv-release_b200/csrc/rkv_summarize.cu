@@ -36,7 +36,7 @@ __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b 
 __device__ __forceinline__ float nan_min(float a, float b) { return (b < a || b != b) ? b : a; }
 
 template <int D>
-__global__ void __launch_bounds__(256) summarize_kernel(const SummarizeParams p) {
+__global__ void __launch_bounds__(256, 2) summarize_kernel(const SummarizeParams p) {
   constexpr int kChunks = D / 8;
   constexpr int kLanes = kChunks <= 8 ? 8 : (kChunks <= 16 ? 16 : 32);
   constexpr int kPagesPerWarp = 32 / kLanes;
@@ -55,18 +55,20 @@ __global__ void __launch_bounds__(256) summarize_kernel(const SummarizeParams p)
 
   pdl_wait();
 
-  const __nv_bfloat16* kbase = static_cast<const __nv_bfloat16*>(p.keys) + h * p.key_head_stride +
-                               static_cast<long long>(b) * B * p.key_token_stride + cl * 8;
-  const __nv_bfloat16* vbase = static_cast<const __nv_bfloat16*>(p.values) +
-                               h * p.value_head_stride +
-                               static_cast<long long>(b) * B * p.value_token_stride + cl * 8;
-  uint4* kpage = p.key_pages ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
-                                                        page * B * D + cl * 8)
-                             : nullptr;
-  uint4* vpage = p.value_pages
-                     ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
-                                                page * B * D + cl * 8)
-                     : nullptr;
+  const __nv_bfloat16* __restrict__ kbase =
+      static_cast<const __nv_bfloat16*>(p.keys) + h * p.key_head_stride +
+      static_cast<long long>(b) * B * p.key_token_stride + cl * 8;
+  const __nv_bfloat16* __restrict__ vbase =
+      static_cast<const __nv_bfloat16*>(p.values) + h * p.value_head_stride +
+      static_cast<long long>(b) * B * p.value_token_stride + cl * 8;
+  uint4* __restrict__ kpage =
+      p.key_pages ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
+                                             page * B * D + cl * 8)
+                  : nullptr;
+  uint4* __restrict__ vpage =
+      p.value_pages ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
+                                               page * B * D + cl * 8)
+                    : nullptr;
 
   float ksum[8], kmax[8], kmin[8], vsum[8];
 #pragma unroll
@@ -78,35 +80,46 @@ __global__ void __launch_bounds__(256) summarize_kernel(const SummarizeParams p)
   }
   float vnorm = -INFINITY;
 
-#pragma unroll 4
-  for (int t = 0; t < B; ++t) {
-    const bool row = lane_ok && t < count;
-    uint4 ku = make_uint4(0, 0, 0, 0), vu = make_uint4(0, 0, 0, 0);
-    if (row) {
-      ku = __ldg(reinterpret_cast<const uint4*>(kbase + t * p.key_token_stride));
-      vu = __ldg(reinterpret_cast<const uint4*>(vbase + t * p.value_token_stride));
-    }
-    if (kpage != nullptr && lane_ok) {
-      kpage[t * (D / 8)] = ku;
-      vpage[t * (D / 8)] = vu;
-    }
-    float kf[8], vf[8];
-    unpack8(ku, kf);
-    unpack8(vu, vf);
-    float sq = 0.f;
+  // Rows are read kBatch at a time: every load of a batch is in flight
+  // before the first is used.
+  constexpr int kBatch = 8;
+  for (int t0 = 0; t0 < B; t0 += kBatch) {
+    uint4 kb[kBatch], vb[kBatch];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (row) {
-        ksum[i] += kf[i];
-        vsum[i] += vf[i];
-        kmax[i] = nan_max(kmax[i], kf[i]);
-        kmin[i] = nan_min(kmin[i], kf[i]);
+    for (int i = 0; i < kBatch; ++i) {
+      kb[i] = make_uint4(0, 0, 0, 0);
+      vb[i] = make_uint4(0, 0, 0, 0);
+      if (lane_ok && t0 + i < count) {
+        kb[i] = __ldg(reinterpret_cast<const uint4*>(kbase + (t0 + i) * p.key_token_stride));
+        vb[i] = __ldg(reinterpret_cast<const uint4*>(vbase + (t0 + i) * p.value_token_stride));
       }
-      sq += vf[i] * vf[i];
     }
 #pragma unroll
-    for (int off = 1; off < kLanes; off <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-    if (row) vnorm = nan_max(vnorm, sqrtf(sq));
+    for (int i = 0; i < kBatch; ++i) {
+      const int t = t0 + i;
+      const bool row = lane_ok && t < count;
+      if (kpage != nullptr && lane_ok) {
+        kpage[t * (D / 8)] = kb[i];
+        vpage[t * (D / 8)] = vb[i];
+      }
+      float kf[8], vf[8];
+      unpack8(kb[i], kf);
+      unpack8(vb[i], vf);
+      float sq = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (row) {
+          ksum[c] += kf[c];
+          vsum[c] += vf[c];
+          kmax[c] = nan_max(kmax[c], kf[c]);
+          kmin[c] = nan_min(kmin[c], kf[c]);
+        }
+        sq += vf[c] * vf[c];
+      }
+#pragma unroll
+      for (int off = 1; off < kLanes; off <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+      if (row) vnorm = nan_max(vnorm, sqrtf(sq));
+    }
   }
 
   const float cnt = static_cast<float>(count > 0 ? count : 1);
@@ -121,24 +134,35 @@ __global__ void __launch_bounds__(256) summarize_kernel(const SummarizeParams p)
     rscale[i] = __frsqrt_rn(width2[i]);
   }
 
-  // Pass 2: largest normalised centred squared distance of a real row.
+  // Pass 2: largest normalised centred squared distance of a real row
+  // (the page was just read, so these loads hit L2).
   float dmax = -INFINITY;
-#pragma unroll 4
-  for (int t = 0; t < B; ++t) {
-    const bool row = lane_ok && t < count;
-    float dsum = 0.f;
-    if (row) {
-      float kf[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(kbase + t * p.key_token_stride)), kf);
+  for (int t0 = 0; t0 < B; t0 += kBatch) {
+    uint4 kb[kBatch];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float c = (kf[i] - kmean[i]) * rscale[i];
-        dsum += c * c;
+    for (int i = 0; i < kBatch; ++i) {
+      kb[i] = make_uint4(0, 0, 0, 0);
+      if (lane_ok && t0 + i < count) {
+        kb[i] = __ldg(reinterpret_cast<const uint4*>(kbase + (t0 + i) * p.key_token_stride));
       }
     }
 #pragma unroll
-    for (int off = 1; off < kLanes; off <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
-    if (t < count) dmax = nan_max(dmax, dsum);
+    for (int i = 0; i < kBatch; ++i) {
+      const int t = t0 + i;
+      float dsum = 0.f;
+      if (lane_ok && t < count) {
+        float kf[8];
+        unpack8(kb[i], kf);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float x = (kf[c] - kmean[c]) * rscale[c];
+          dsum += x * x;
+        }
+      }
+#pragma unroll
+      for (int off = 1; off < kLanes; off <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
+      if (t < count) dmax = nan_max(dmax, dsum);
+    }
   }
   float rho2 = dmax < 0.f ? 0.f : dmax;
   rho2 = sqrtf(rho2);
