@@ -431,7 +431,7 @@ def run_b200(args):
             e1.record()
             sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
                              workspace=L.workspace, suffix_length=length,
-                             _phases=_native.PHASE_ATTEND)
+                             _phases=_native.PHASE_ATTEND | _native.PHASE_COMBINE)
             e2.record()
             phase_events.append((e0, e1, e2))
             sel = L.workspace["selected"]

@@ -69,8 +69,9 @@ typedef enum rkv_status {
 /* Phases of rkv_decode (bit mask; RKV_PHASE_ALL for a normal call). */
 #define RKV_PHASE_STATS 1  /* selector phase A: scores, deltas, LSE partials */
 #define RKV_PHASE_FINAL 2  /* selector phase B: mask, compaction, representatives */
-#define RKV_PHASE_ATTEND 4 /* pages + suffix attention and the combine */
-#define RKV_PHASE_ALL 7
+#define RKV_PHASE_ATTEND 4  /* refined pages + suffix: one partial per attention warp */
+#define RKV_PHASE_COMBINE 8 /* LSE combine of all partials into the output */
+#define RKV_PHASE_ALL 15
 
 /*
  * Device view of a BlockSummary (reference summary.py:10-32).

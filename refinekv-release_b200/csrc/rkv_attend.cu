@@ -1,5 +1,5 @@
-// Split decode attention over refined pages and the generated suffix, plus
-// the LSE combine with the representative partials (reference:
+// Split decode attention over refined pages and the generated suffix, and the
+// LSE combine with the representative partials (reference:
 // src/refinekv/reference.py:50-73; the reference's GPU form is
 // kernels/attention.py:166-329).
 //
@@ -11,23 +11,71 @@
 // the per-head selection counts are.  Everything is read from device memory
 // (selection counts, suffix length), so the launch is graph-safe.
 //
-// Per CTA: 4 warps, each streaming its own items (k = lo + warp + j*4)
-// through a private ring of TMA stages [K page | V page].  For an item the
-// warp computes S^T = K . q^T (tokens on M, group rows on N) with mma.sync,
-// masks rows past the page's token count, updates its online softmax, turns
-// the probabilities into the P^T operand with movmatrix and accumulates
-// O^T += V^T . P^T.  At each head boundary inside its range the CTA merges
-// its warps and writes one (m, l, o) partial.  The CTA that completes a head
-// last (atomic ticket) merges that head's partials with the selector's
-// representative partials and writes the output row in the query dtype.
+// attend_kernel: one CTA per SM, independent warps.  Warp w of a CTA takes
+// the CTA's items k = lo + w + j*warps and streams them through its own ring
+// of TMA stages (K page | V page, with separate barriers so K is refilled as
+// soon as the scores are done).  Per item: S^T = K . q^T (tokens on M, group
+// rows on N) with mma.sync, mask rows past the item's token count, online
+// softmax, probabilities -> P^T operand by movmatrix, O^T += V^T . P^T.  At
+// each head boundary in its range the warp writes its own (m, l, o^T)
+// partial and goes on streaming: there is no CTA barrier in the loop.
+//
+// combine_kernel: per (head, 32 channels), merges the selector's
+// representative partials with the attention warps' partials of that head
+// and writes the output rows in the query dtype.
 #include "rkv_device.cuh"
 #include "rkv_kernels.h"
 
 namespace rkv {
 namespace {
 
+// Which CTA holds global item x when T items are cut into C ranges
+// (ranges are nonempty because C <= T).
+struct WorkList {
+  long long T;
+  long long C;
+  __device__ long long cta_of(long long x) const { return ((x + 1) * C + T - 1) / T - 1; }
+};
+
+__device__ __forceinline__ int visible_suffix(int has_suffix, const int* len_ptr, int len_host,
+                                              int capacity, int* status) {
+  if (!has_suffix) return 0;
+  int len = len_ptr != nullptr ? *len_ptr : len_host;
+  if (len < 0 || len > capacity) {
+    if (threadIdx.x == 0) atomicOr(status, kStatusBadInput);
+    len = len < 0 ? 0 : capacity;
+  }
+  return len;
+}
+
+// seg_pre[h][0..PB] = prefix sums of the selected-page counts over the
+// selector segments of head h; hstart[0..H] = first global item of each
+// head.  Called by every thread of the CTA.
+__device__ __forceinline__ void build_work_list(const int* seg_count, int H, int PB, int n_suffix,
+                                                int* seg_pre, long long* hstart) {
+  for (int i = threadIdx.x; i < H * PB; i += blockDim.x) {
+    seg_pre[(i / PB) * (PB + 1) + (i % PB) + 1] = __ldcg(seg_count + i);
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    int* pre = seg_pre + h * (PB + 1);
+    pre[0] = 0;
+    for (int k = 1; k <= PB; ++k) pre[k] += pre[k - 1];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long acc = 0;
+    hstart[0] = 0;
+    for (int h = 0; h < H; ++h) {
+      acc += seg_pre[h * (PB + 1) + PB] + n_suffix;
+      hstart[h + 1] = acc;
+    }
+  }
+  __syncthreads();
+}
+
 template <int R, int D, int NT>
-__global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ AttendMaps maps,
+__global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ AttendMaps maps,
                                                         const AttendParams p) {
   constexpr int kTile = R * D * 2;
   constexpr int kStage = 2 * kTile;
@@ -48,14 +96,6 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
   long long* hstart = reinterpret_cast<long long*>(smem + off);  // [H + 1]
   off += round16(static_cast<size_t>(H + 1) * 8);
   int* seg_pre = reinterpret_cast<int*>(smem + off);  // [H][PB + 1]
-  off += round16(static_cast<size_t>(H) * (PB + 1) * 4);
-  int* flags = reinterpret_cast<int*>(smem + off);  // [4]
-  off += 16;
-  int* pending = reinterpret_cast<int*>(smem + off);  // [H][3] heads this CTA combines
-  off += round16(static_cast<size_t>(H) * 12);
-  float* st_m = reinterpret_cast<float*>(smem + off);  // [warps][G8]
-  float* st_l = st_m + warps * G8;
-  float* st_o = st_l + warps * G8;  // [warps][G8][D]
 
   if (lane == 0) {
     for (int s = 0; s < 2 * S; ++s) mbar_init(&bars[warp * 2 * S + s], 1);
@@ -70,56 +110,26 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
     }
   }
   pdl_wait();
+  pdl_launch_dependents();
+  // K/V pages are read once per step: evict them first so that the selector's
+  // outputs and the partials the combine reads stay in L2.
+  const uint64_t stream_policy = l2_evict_first_policy();
 
-  int suffix_len = 0;
-  if (p.has_suffix) {
-    suffix_len = p.suffix_len_ptr != nullptr ? *p.suffix_len_ptr : p.suffix_len_host;
-    if (suffix_len < 0 || suffix_len > p.suffix_capacity) {
-      if (threadIdx.x == 0) atomicOr(p.status, kStatusBadInput);
-      suffix_len = suffix_len < 0 ? 0 : p.suffix_capacity;
-    }
-  }
-  const int n_suffix = (suffix_len + R - 1) / R;
-
-  // Selected-page counts of every (head, selector segment), loaded in
-  // parallel, then prefix sums per head.
-  for (int i = threadIdx.x; i < H * PB; i += blockDim.x) {
-    seg_pre[(i / PB) * (PB + 1) + (i % PB) + 1] = __ldcg(p.seg_count + i);
-  }
-  __syncthreads();
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    int* pre = seg_pre + h * (PB + 1);
-    pre[0] = 0;
-    for (int k = 1; k <= PB; ++k) pre[k] += pre[k - 1];
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    long long acc = 0;
-    hstart[0] = 0;
-    for (int h = 0; h < H; ++h) {
-      acc += seg_pre[h * (PB + 1) + PB] + n_suffix;
-      hstart[h + 1] = acc;
-    }
-  }
-  __syncthreads();
-
-  const long long T = hstart[H];
-  const long long C = T < p.ctas ? T : p.ctas;  // CTAs that own a nonempty range
+  const int suffix_len = visible_suffix(p.has_suffix, p.suffix_len_ptr, p.suffix_len_host,
+                                        p.suffix_capacity, p.status);
+  build_work_list(p.seg_count, H, PB, (suffix_len + R - 1) / R, seg_pre, hstart);
+  WorkList wl;
+  wl.T = hstart[H];
+  wl.C = wl.T < p.ctas ? wl.T : p.ctas;
   const long long cta = blockIdx.x;
-  long long lo = 0, hi = 0;
-  if (cta < C) {
-    lo = T * cta / C;
-    hi = T * (cta + 1) / C;
-  }
-  // CTA whose range holds global item x (ranges are nonempty when C <= T).
-  auto cta_of = [&](long long x) { return ((x + 1) * C + T - 1) / T - 1; };
-
+  if (cta >= wl.C) return;  // no items: this CTA owns no partial
+  const long long lo = wl.T * cta / wl.C, hi = wl.T * (cta + 1) / wl.C;
   const int count_w = hi - lo > warp ? static_cast<int>((hi - lo - warp + warps - 1) / warps) : 0;
 
   // Item descriptors {head, first row, valid rows, is_suffix} are decoded 32
   // at a time, one per lane, one batch ahead of use, so the loads of the
-  // selected ids and counts are off the issue path.  Each lane's head
-  // cursor only moves forward because batches are decoded in order.
+  // selected ids are off the issue path.  Each lane's head cursor only moves
+  // forward because batches are decoded in order.
   int lane_head = 0;
   auto decode = [&](int base) {
     const int j = base + lane;
@@ -148,7 +158,7 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
   int batch_base = 0;
   int4 cur = decode(0);
   int4 nxt = decode(32);
-  auto item = [&](int j) {  // whole warp; j never skips ahead of the batch
+  auto item = [&](int j) {  // whole warp; j advances by one per call
     if (j >= batch_base + 32) {
       batch_base += 32;
       cur = nxt;
@@ -166,8 +176,8 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
       valid_rows[warp * S + s] = d.z;
       uint64_t* bk = &bars[(warp * S + s) * 2];
       mbar_expect_tx(bk, kTile);
-      tma_tile<D>(ring + (warp * S + s) * kStage, d.w ? &maps.key_suffix : &maps.key_pages, bk,
-                  d.y, d.x, R);
+      tma_tile_hint<D>(ring + (warp * S + s) * kStage, d.w ? &maps.key_suffix : &maps.key_pages,
+                       bk, d.y, d.x, R, stream_policy);
     }
   };
   auto issue_v = [&](int j, const int4& d) {
@@ -175,8 +185,9 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
       const int s = j % S;
       uint64_t* bv = &bars[(warp * S + s) * 2 + 1];
       mbar_expect_tx(bv, kTile);
-      tma_tile<D>(ring + (warp * S + s) * kStage + kTile,
-                  d.w ? &maps.value_suffix : &maps.value_pages, bv, d.y, d.x, R);
+      tma_tile_hint<D>(ring + (warp * S + s) * kStage + kTile,
+                       d.w ? &maps.value_suffix : &maps.value_pages, bv, d.y, d.x, R,
+                       stream_policy);
     }
   };
   const int first_fill = min(S, count_w);
@@ -187,213 +198,327 @@ __global__ void __launch_bounds__(128, 1) attend_kernel(const __grid_constant__ 
   }
   int issued_k = first_fill, issued_v = first_fill;
 
-  // Merge head h's partials (selector representatives + attention CTAs
-  // [first, last]) and write its output rows.  Row maxima and denominators
-  // first (one warp per row), then one float4 of output per thread, with the
-  // partial loads issued 16 at a time so they overlap.
-  float* comb = st_m;  // reuses the stash: [2][G]
-  auto combine = [&](int h, int first, int last) {
-    const int G = p.group;
-    const int n_att = last - first + 1;
-    const int nsrc = PB + n_att;
-    auto slot_of = [&](int k) {
-      return k < PB ? static_cast<size_t>(h * PB + k) * G
-                    : static_cast<size_t>(h * p.ctas + first + k - PB) * G;
-    };
-    for (int g = warp; g < G; g += warps) {
-      float top = -INFINITY;
-      for (int k = lane; k < nsrc; k += 32) {
-        top = fmaxf(top, __ldcg((k < PB ? p.rep_m : p.att_m) + slot_of(k) + g));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
-      const float ref = top == -INFINITY ? 0.f : top;
-      float den = 0.f;
-      for (int k = lane; k < nsrc; k += 32) {
-        const size_t slot = slot_of(k) + g;
-        den += __ldcg((k < PB ? p.rep_l : p.att_l) + slot) *
-               __expf(__ldcg((k < PB ? p.rep_m : p.att_m) + slot) - ref);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-      if (lane == 0) {
-        comb[g] = ref;
-        comb[G + g] = fmaxf(den, 1e-30f);
-      }
-    }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < G * (D / 4); idx += blockDim.x) {
-      const int g = idx / (D / 4), d4 = idx - g * (D / 4);
-      const float ref = comb[g];
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k0 = 0; k0 < nsrc; k0 += 16) {
-        float w[16];
-        float4 v[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const int k = k0 + u;
-          w[u] = -INFINITY;
-          v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (k < nsrc) {
-            const size_t slot = slot_of(k) + g;
-            w[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + slot);
-            v[u] = __ldcg(reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) +
-                                                          slot * D) + d4);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const float e = __expf(w[u] - ref);
-          acc.x += e * v[u].x;
-          acc.y += e * v[u].y;
-          acc.z += e * v[u].z;
-          acc.w += e * v[u].w;
-        }
-      }
-      const float inv = 1.f / comb[G + g];
-      const size_t o = (static_cast<size_t>(h) * G + g) * D + d4 * 4;
-      if (p.query_f32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-      } else {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + o;
-        *reinterpret_cast<uint2*>(out) =
-            make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
-      }
-    }
-    __syncthreads();
-  };
-  // Count this CTA's contribution to head h.  The last of `expected`
-  // arrivals owns the head's combine, which runs after this CTA's own pages
-  // so that a combine never delays the streaming of other pages.
-  if (threadIdx.x == 0) flags[1] = 0;
-  auto arrive = [&](int h, int expected, int first, int last) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(p.done + h, 1) == expected - 1) {
-      int* e = pending + 3 * flags[1]++;
-      e[0] = h;
-      e[1] = first;
-      e[2] = last;
-    }
-    __syncthreads();
-  };
-
   bool aborted = false;
   int jj = 0;  // next local item to consume
-  if (lo < hi) {
-    int h = 0;
-    while (hstart[h + 1] <= lo) ++h;
-    for (; h < H && hstart[h] < hi; ++h) {
-      if (hstart[h + 1] == hstart[h]) continue;
-      const long long seg_hi = hi < hstart[h + 1] ? hi : hstart[h + 1];
-      const int j_end =
-          seg_hi - lo > warp ? static_cast<int>((seg_hi - lo - warp + warps - 1) / warps) : 0;
-      uint32_t qb[D / 16][NT][2];
-      load_query_frags<D, NT>(
-          qb,
-          static_cast<const char*>(p.query) +
-              static_cast<size_t>(h) * p.group * D * (p.query_f32 ? 4 : 2),
-          p.query_f32, p.group, lane, false);
-      float m[NT][2], l[NT][2], o[D / 16][NT][4];
+  int last_head = -1;
+  int h = 0;
+  while (hstart[h + 1] <= lo) ++h;
+  for (; h < H && hstart[h] < hi; ++h) {
+    if (hstart[h + 1] == hstart[h]) continue;
+    const long long seg_hi = hi < hstart[h + 1] ? hi : hstart[h + 1];
+    const int j_end =
+        seg_hi - lo > warp ? static_cast<int>((seg_hi - lo - warp + warps - 1) / warps) : 0;
+    uint32_t qb[D / 16][NT][2];
+    load_query_frags<D, NT>(
+        qb,
+        static_cast<const char*>(p.query) +
+            static_cast<size_t>(h) * p.group * D * (p.query_f32 ? 4 : 2),
+        p.query_f32, p.group, lane, false);
+    float m[NT][2], l[NT][2], o[D / 16][NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        m[nt][0] = m[nt][1] = -INFINITY;
-        l[nt][0] = l[nt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) {
+      m[nt][0] = m[nt][1] = -INFINITY;
+      l[nt][0] = l[nt][1] = 0.f;
 #pragma unroll
-        for (int dt = 0; dt < D / 16; ++dt)
-          o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
+      for (int dt = 0; dt < D / 16; ++dt)
+        o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
+    }
+    for (; jj < j_end; ++jj) {
+      if (aborted) continue;
+      const int s = jj % S;
+      const uint32_t par = (jj / S) & 1;
+      uint64_t* bk = &bars[(warp * S + s) * 2];
+      if (!warp_wait(bk, par)) {
+        if (lane == 0) atomicOr(p.status, kStatusTimeout);
+        drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
+        aborted = true;
+        continue;
       }
-      for (; jj < j_end; ++jj) {
-        if (aborted) continue;
-        const int s = jj % S;
-        const uint32_t par = (jj / S) & 1;
-        uint64_t* bk = &bars[(warp * S + s) * 2];
-        if (!warp_wait(bk, par)) {
-          if (lane == 0) atomicOr(p.status, kStatusTimeout);
-          drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
-          aborted = true;
-          continue;
-        }
-        const int valid = valid_rows[warp * S + s];
-        const uint32_t base = smem_addr(ring + (warp * S + s) * kStage);
-        float logit[R / 16][NT][4];
-        score_tile<R, D, NT>(base, qb, logit, lane);
+      const int valid = valid_rows[warp * S + s];
+      const uint32_t base = smem_addr(ring + (warp * S + s) * kStage);
+      float logit[R / 16][NT][4];
+      score_tile<R, D, NT>(base, qb, logit, lane);
 #pragma unroll
-        for (int mt = 0; mt < R / 16; ++mt)
+      for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+        for (int c = 0; c < 4; ++c) {
+          const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-              logit[mt][nt][c] = r < valid ? logit[mt][nt][c] * p.scale : -INFINITY;
-          }
-        __syncwarp();
-        const bool refill = jj + S < count_w;
-        int4 next = make_int4(0, 0, 0, 0);
-        if (refill) {
-          next = item(jj + S);
-          if (lane == 0) fence_proxy_async();
-          issue_k(jj + S, next);
-          ++issued_k;
+          for (int nt = 0; nt < NT; ++nt)
+            logit[mt][nt][c] = r < valid ? logit[mt][nt][c] * p.scale : -INFINITY;
         }
-        softmax_update<R, D, NT>(logit, m, l, o);
-        uint32_t hi_frag[R / 16][NT][2], lo_frag[R / 16][NT][2];
-        prob_frags<R, NT>(logit, hi_frag, lo_frag, p.query_f32 != 0);
-        if (!warp_wait(bk + 1, par)) {
-          if (lane == 0) atomicOr(p.status, kStatusTimeout);
-          drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
-          aborted = true;
-          continue;
-        }
-        accumulate_values<R, D, NT>(base + kTile, hi_frag, o, lane);
-        if (p.query_f32) accumulate_values<R, D, NT>(base + kTile, lo_frag, o, lane);
-        __syncwarp();
-        if (refill) {
-          if (lane == 0) fence_proxy_async();
-          issue_v(jj + S, next);
-          ++issued_v;
-        }
+      __syncwarp();
+      const bool refill = jj + S < count_w;
+      int4 next = make_int4(0, 0, 0, 0);
+      if (refill) {
+        next = item(jj + S);
+        if (lane == 0) fence_proxy_async();
+        issue_k(jj + S, next);
+        ++issued_k;
       }
-      reduce_l<NT>(l);
-      stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
-      __syncthreads();
-      const size_t slot = static_cast<size_t>(h) * p.ctas + cta;
-      merge_stashed<D>(st_m, st_l, st_o, warps, G8, p.group, p.att_m + slot * p.group,
-                       p.att_l + slot * p.group, p.att_o + slot * p.group * D, threadIdx.x,
-                       blockDim.x);
-      const int first = static_cast<int>(cta_of(hstart[h]));
-      const int last = static_cast<int>(cta_of(hstart[h + 1] - 1));
-      arrive(h, last - first + 1, first, last);
+      softmax_update<R, D, NT>(logit, m, l, o);
+      uint32_t hi_frag[R / 16][NT][2], lo_frag[R / 16][NT][2];
+      prob_frags<R, NT>(logit, hi_frag, lo_frag, p.query_f32 != 0);
+      if (!warp_wait(bk + 1, par)) {
+        if (lane == 0) atomicOr(p.status, kStatusTimeout);
+        drain_pending(bars + warp * S * 2, S, jj, issued_k, issued_v);
+        aborted = true;
+        continue;
+      }
+      accumulate_values<R, D, NT>(base + kTile, hi_frag, o, lane);
+      if (p.query_f32) accumulate_values<R, D, NT>(base + kTile, lo_frag, o, lane);
+      __syncwarp();
+      if (refill) {
+        if (lane == 0) fence_proxy_async();
+        issue_v(jj + S, next);
+        ++issued_v;
+      }
+    }
+    // This warp's partial for head h (empty, m = -inf, if it had no item).
+    reduce_l<NT>(l);
+    if (hstart[h + 1] >= hi) {
+      // The CTA's last head: park the partial in this warp's own (now idle)
+      // ring stage; the warps are merged into one partial after the loop.
+      float* st = reinterpret_cast<float*>(ring + static_cast<size_t>(warp) * S * kStage);
+      stash_warp_partial<D, NT>(st, st + G8, st + 2 * G8, 0, lane, m, l, o);
+      last_head = h;
+      continue;
+    }
+    const size_t slot = (static_cast<size_t>(h) * p.ctas + cta) * warps + warp;
+    float* op = p.att_o + slot * D * G8;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int g0 = nt * 8 + 2 * (lane & 3);
+      if (lane < 4) {
+        *reinterpret_cast<float2*>(p.att_m + slot * G8 + g0) = make_float2(m[nt][0], m[nt][1]);
+        *reinterpret_cast<float2*>(p.att_l + slot * G8 + g0) = make_float2(l[nt][0], l[nt][1]);
+      }
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        const int d0 = dt * 16 + (lane >> 2);
+        *reinterpret_cast<float2*>(op + d0 * G8 + g0) = make_float2(o[dt][nt][0], o[dt][nt][1]);
+        *reinterpret_cast<float2*>(op + (d0 + 8) * G8 + g0) =
+            make_float2(o[dt][nt][2], o[dt][nt][3]);
+      }
     }
   }
-  pdl_launch_dependents();
-
-  // Heads with no item (nothing refined, empty suffix) still need their
-  // representative partials combined: one owner CTA per such head.
-  for (int h = 0; h < H; ++h) {
-    if (hstart[h + 1] != hstart[h]) continue;
-    const long long owner = T == 0 ? h % p.ctas : cta_of(hstart[h] < T ? hstart[h] : T - 1);
-    if (owner == cta) arrive(h, 1, 0, -1);
-  }
-  __threadfence();
+  // One partial for the last head of this CTA's range, slot (head, cta, 0):
+  // merge the warps' parked partials.
   __syncthreads();
-  for (int i = 0; i < flags[1]; ++i) {
-    const int* e = pending + 3 * i;
-    combine(e[0], e[1], e[2]);
-    if (threadIdx.x == 0) p.done[e[0]] = 0;
+  if (last_head >= 0) {
+    const size_t slot = (static_cast<size_t>(last_head) * p.ctas + cta) * warps;
+    auto stash = [&](int w) {
+      return reinterpret_cast<const float*>(ring + static_cast<size_t>(w) * S * kStage);
+    };
+    for (int idx = threadIdx.x; idx < G8 * D; idx += blockDim.x) {
+      const int d = idx / G8, g = idx - d * G8;
+      float top = -INFINITY;
+      for (int w = 0; w < warps; ++w) top = fmaxf(top, stash(w)[g]);
+      const float ref = top == -INFINITY ? 0.f : top;
+      float acc = 0.f, den = 0.f;
+      for (int w = 0; w < warps; ++w) {
+        const float* st = stash(w);
+        const float mw = st[g];
+        const float sc = mw == -INFINITY ? 0.f : __expf(mw - ref);
+        acc += sc * st[2 * G8 + g * D + d];
+        den += sc * st[G8 + g];
+      }
+      p.att_o[slot * D * G8 + d * G8 + g] = acc;
+      if (d == 0) {
+        p.att_m[slot * G8 + g] = top;
+        p.att_l[slot * G8 + g] = den;
+      }
+    }
   }
 }
 
-template <int R, int D, int NT>
-cudaError_t launch_attend_t(const AttendMaps& maps, const AttendParams& p, int warps, size_t smem,
-                            cudaStream_t stream, bool pdl) {
-  auto kernel = attend_kernel<R, D, NT>;
-  cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
-  if (err != cudaSuccess) return err;
+// Shared-memory layout of combine_kernel (also sized by the host).
+struct CombineLayout {
+  size_t hstart, seg_pre, stats, wgt, lsum, red, bytes;
+  __host__ __device__ CombineLayout(int H, int PB, int G8, int max_sources) {
+    size_t off = 0;
+    hstart = off;
+    off += round16(static_cast<size_t>(H + 1) * 8);
+    seg_pre = off;
+    off += round16(static_cast<size_t>(H) * (PB + 1) * 4);
+    stats = off;
+    off += round16(static_cast<size_t>(2) * G8 * 4);
+    wgt = off;
+    off += round16(static_cast<size_t>(max_sources) * G8 * 4);
+    lsum = off;
+    off += round16(static_cast<size_t>(max_sources) * G8 * 4);
+    red = off;
+    off += static_cast<size_t>(8) * 32 * G8 * 4;
+    bytes = off + kSmemSlack;
+  }
+};
+
+// grid (heads, dim / 32), 8 warps; lane = output channel.  After the work
+// list (one round of loads), every load of the combine is issued at once:
+// the m and l of every partial of the head (staged in shared memory and
+// turned into weights exp(m - M_g)) and this warp's o^T rows (every 8th
+// partial, kBatch per round, kept in registers).  The warps' sums are then
+// added in shared memory.
+template <int D, int G8>
+__global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
+  constexpr int kWarps = 8;
+  constexpr int kBatch = G8 == 8 ? 12 : 6;
+  constexpr int kStage = 4;  // m/l entries staged per thread per round
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, d = blockIdx.y * 32 + lane;
+  const int H = p.heads, PB = p.parts_b;
+  const CombineLayout lay(H, PB, G8, p.max_sources);
+  long long* hstart = reinterpret_cast<long long*>(smem + lay.hstart);
+  int* seg_pre = reinterpret_cast<int*>(smem + lay.seg_pre);
+  float* top = reinterpret_cast<float*>(smem + lay.stats);  // [G8] row maxima
+  float* den = top + G8;                                    // [G8] denominators
+  float* wgt = reinterpret_cast<float*>(smem + lay.wgt);    // [sources][G8]
+  float* lsum = reinterpret_cast<float*>(smem + lay.lsum);  // [sources][G8]
+  float* red = reinterpret_cast<float*>(smem + lay.red);    // [warps][32][G8]
+
+  pdl_wait();
+  pdl_launch_dependents();
+  const int suffix_len = visible_suffix(p.has_suffix, p.suffix_len_ptr, p.suffix_len_host,
+                                        p.suffix_capacity, p.status);
+  build_work_list(p.seg_count, H, PB, (suffix_len + p.page - 1) / p.page, seg_pre, hstart);
+  WorkList wl;
+  wl.T = hstart[H];
+  wl.C = wl.T < p.ctas ? wl.T : p.ctas;
+  // Attention partials of head h: CTAs [first, last] of its items.  A CTA
+  // whose range ends inside head h merged its warps into slot warp 0; only
+  // the last of them can run on into the next head and then left one
+  // partial per warp.
+  int n_att = 0, n_merged = 0;
+  long long first = 0;
+  if (hstart[h + 1] > hstart[h]) {
+    first = wl.cta_of(hstart[h]);
+    const long long last = wl.cta_of(hstart[h + 1] - 1);
+    const long long last_hi = wl.T * (last + 1) / wl.C;
+    n_merged = static_cast<int>(last - first);
+    n_att = n_merged + (last_hi > hstart[h + 1] ? p.warps : 1);
+  }
+  const int nsrc = PB + n_att;
+  if (nsrc > p.max_sources) {  // cannot happen with the host's plan; never read past the table
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusBadInput);
+    return;
+  }
+  auto src_index = [&](int k) -> size_t {
+    if (k < PB) return static_cast<size_t>(h) * PB + k;
+    const int a = k - PB;  // merged CTAs first, then the last CTA's slots
+    const long long c = first + (a < n_merged ? a : n_merged);
+    const int w = a < n_merged ? 0 : a - n_merged;
+    return (static_cast<size_t>(h) * p.ctas + c) * p.warps + w;
+  };
+  auto o_row = [&](int k) {
+    return reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) + src_index(k) * D * G8 +
+                                           d * G8);
+  };
+  // This warp's first round of o rows, issued before anything else is waited on.
+  float4 v[kBatch][G8 / 4];
+  auto load_round = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int k = k0 + u * kWarps;
+#pragma unroll
+      for (int q = 0; q < G8 / 4; ++q) {
+        v[u][q] = k < nsrc ? __ldcg(o_row(k) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  load_round(warp);
+  // m and l of every source, loaded kStage at a time per thread.
+  for (int i0 = threadIdx.x; i0 < nsrc * G8; i0 += blockDim.x * kStage) {
+    float mv[kStage], lv[kStage];
+#pragma unroll
+    for (int u = 0; u < kStage; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nsrc * G8) {
+        const int k = i / G8, g = i - k * G8;
+        const size_t at = src_index(k) * G8 + g;
+        mv[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + at);
+        lv[u] = __ldcg((k < PB ? p.rep_l : p.att_l) + at);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStage; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nsrc * G8) {
+        wgt[i] = mv[u];
+        lsum[i] = lv[u];
+      }
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G8; g += kWarps) {
+    float mx = -INFINITY;
+    for (int k = lane; k < nsrc; k += 32) mx = fmaxf(mx, wgt[k * G8 + g]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) top[g] = mx == -INFINITY ? 0.f : mx;
+  }
+  __syncthreads();
+  // Weights; an empty partial (m = -inf) gets weight 0 and contributes nothing.
+  for (int i = threadIdx.x; i < nsrc * G8; i += blockDim.x) {
+    const float m = wgt[i];
+    const float w = m == -INFINITY ? 0.f : __expf(m - top[i % G8]);
+    wgt[i] = w;
+    lsum[i] = w == 0.f ? 0.f : lsum[i] * w;
+  }
+  __syncthreads();
+  for (int g = warp; g < G8; g += kWarps) {
+    float s = 0.f;
+    for (int k = lane; k < nsrc; k += 32) s += lsum[k * G8 + g];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) den[g] = fmaxf(s, 1e-30f);
+  }
+  float acc[G8];
+#pragma unroll
+  for (int g = 0; g < G8; ++g) acc[g] = 0.f;
+  for (int k0 = warp;; k0 += kBatch * kWarps) {
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int k = k0 + u * kWarps;
+      if (k >= nsrc) continue;
+#pragma unroll
+      for (int q = 0; q < G8 / 4; ++q) {
+        const float* w = wgt + k * G8 + 4 * q;
+        // An unused slot may hold a stale value: weight 0 must not multiply it.
+        if (w[0] != 0.f) acc[4 * q + 0] += w[0] * v[u][q].x;
+        if (w[1] != 0.f) acc[4 * q + 1] += w[1] * v[u][q].y;
+        if (w[2] != 0.f) acc[4 * q + 2] += w[2] * v[u][q].z;
+        if (w[3] != 0.f) acc[4 * q + 3] += w[3] * v[u][q].w;
+      }
+    }
+    if (k0 + kBatch * kWarps >= nsrc) break;
+    load_round(k0 + kBatch * kWarps);
+  }
+#pragma unroll
+  for (int g = 0; g < G8; ++g) red[(warp * 32 + lane) * G8 + g] = acc[g];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 32 * G8; i += blockDim.x) {
+    const int ln = i / G8, g = i - ln * G8;
+    if (g >= p.group) continue;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[(w * 32 + ln) * G8 + g];
+    const float out = s / den[g];
+    const size_t o = (static_cast<size_t>(h) * p.group + g) * D + blockIdx.y * 32 + ln;
+    if (p.query_f32) {
+      static_cast<float*>(p.out)[o] = out;
+    } else {
+      static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(out);
+    }
+  }
+}
+
+cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, bool pdl, void** args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.ctas);
-  cfg.blockDim = dim3(warps * 32);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -401,7 +526,17 @@ cudaError_t launch_attend_t(const AttendMaps& maps, const AttendParams& p, int w
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, maps, p);
+  return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
+template <int R, int D, int NT>
+cudaError_t launch_attend_t(const AttendMaps& maps, const AttendParams& p, int warps, size_t smem,
+                            cudaStream_t stream, bool pdl) {
+  const void* kernel = reinterpret_cast<const void*>(attend_kernel<R, D, NT>);
+  cudaError_t err = ensure_smem_limit(kernel, smem);
+  if (err != cudaSuccess) return err;
+  void* args[] = {const_cast<AttendMaps*>(&maps), const_cast<AttendParams*>(&p)};
+  return launch_pdl(kernel, dim3(p.ctas), dim3(warps * 32), smem, stream, pdl, args);
 }
 
 template <int R, int D>
@@ -423,20 +558,38 @@ cudaError_t attend_dim(const AttendMaps& maps, const AttendParams& p, int dim, i
   }
 }
 
+template <int D, int G8>
+cudaError_t launch_combine_t(const CombineParams& p, cudaStream_t stream, bool pdl) {
+  const void* kernel = reinterpret_cast<const void*>(combine_kernel<D, G8>);
+  const size_t smem = CombineLayout(p.heads, p.parts_b, G8, p.max_sources).bytes;
+  cudaError_t err = ensure_smem_limit(kernel, smem);
+  if (err != cudaSuccess) return err;
+  void* args[] = {const_cast<CombineParams*>(&p)};
+  return launch_pdl(kernel, dim3(p.heads, D / 32), dim3(256), smem, stream, pdl, args);
+}
+
+template <int D>
+cudaError_t combine_g(const CombineParams& p, cudaStream_t stream, bool pdl) {
+  if (p.group <= 8) return launch_combine_t<D, 8>(p, stream, pdl);
+  return launch_combine_t<D, 16>(p, stream, pdl);
+}
+
 }  // namespace
 
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
                          int parts_b) {
-  const int g8 = group <= 8 ? 8 : 16;
+  (void)group;
   size_t bytes = kSmemSlack;
   bytes += static_cast<size_t>(warps) * stages * 2 * page * dim * 2;  // TMA ring
   bytes += round16(static_cast<size_t>(warps) * stages * 16);          // K and V barriers
   bytes += round16(static_cast<size_t>(warps) * stages * 4);           // valid rows
   bytes += round16(static_cast<size_t>(heads + 1) * 8);
-  bytes += round16(static_cast<size_t>(heads) * (parts_b + 1) * 4) + 16;
-  bytes += round16(static_cast<size_t>(heads) * 12);  // pending combines
-  bytes += static_cast<size_t>(warps) * g8 * 4 * 2 + static_cast<size_t>(warps) * g8 * dim * 4;
+  bytes += round16(static_cast<size_t>(heads) * (parts_b + 1) * 4);
   return bytes;
+}
+
+size_t combine_smem_bytes(int heads, int parts_b, int group, int max_sources) {
+  return CombineLayout(heads, parts_b, group <= 8 ? 8 : 16, max_sources).bytes;
 }
 
 cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim, int warps,
@@ -445,6 +598,16 @@ cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim
     case 16: return attend_dim<16>(maps, p, dim, warps, smem, stream, pdl);
     case 32: return attend_dim<32>(maps, p, dim, warps, smem, stream, pdl);
     case 64: return attend_dim<64>(maps, p, dim, warps, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream, bool pdl) {
+  switch (dim) {
+    case 64: return combine_g<64>(p, stream, pdl);
+    case 128: return combine_g<128>(p, stream, pdl);
+    case 192: return combine_g<192>(p, stream, pdl);
+    case 256: return combine_g<256>(p, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

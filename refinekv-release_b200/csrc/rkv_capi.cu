@@ -72,6 +72,8 @@ struct Plan {
   size_t smem_b = 0;
   int warps_c = 4, stages_c = 2, ctas = 1;
   size_t smem_c = 0;
+  int g8 = 8, max_sources = 0;
+  size_t smem_d = 0;  // combine
   // workspace offsets (bytes)
   size_t status = 0, done = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
   size_t rep_m = 0, rep_l = 0, rep_o = 0, att_m = 0, att_l = 0, att_o = 0, bytes = 0;
@@ -107,28 +109,42 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
     return fail(RKV_ERR_UNSUPPORTED, "selector tiles do not fit in shared memory");
   }
   if (decode) {
-    // Attention: deepest ring that fits one CTA per SM, 4 warps if a stage is
-    // at most 16 KB, otherwise fewer warps with at least two stages each.
+    // Attention: one CTA per SM with about 128 KB of TMA ring, split over as
+    // many warps as possible (3..8) with one stage each (more for small
+    // stages).  Measured on B200: fewer bytes in flight per SM and more
+    // warps beat deeper per-warp rings (6-8 warps x 1 stage: ~91 us per
+    // 128K layer vs ~101 us for 4 warps x 3 stages).
     const int64_t stage = 2 * block_size * dim * 2;
-    const int budget = dev.smem_optin;
-    pl->warps_c = stage <= 16384 ? 4 : (stage <= 32768 ? 3 : 2);
-    for (;;) {
-      const size_t fixed = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
-                                             pl->warps_c, 0, static_cast<int>(group),
-                                             static_cast<int>(heads), pl->parts_b);
-      const int64_t per = static_cast<int64_t>(pl->warps_c) * (stage + 16 + 4);
-      const int64_t fit = (budget - static_cast<int64_t>(fixed) - 16) / per;
-      if (fit >= 2 || pl->warps_c == 1) {
-        pl->stages_c = static_cast<int>(std::min<int64_t>(8, fit));
-        break;
+    const int64_t ring = 128 * 1024;
+    pl->warps_c = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(8, ring / stage)));
+    pl->stages_c =
+        static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, ring / (pl->warps_c * stage))));
+    // The CTA merge parks each warp's (m, l, o^T) in that warp's ring slice.
+    const int64_t g8 = group <= 8 ? 8 : 16;
+    const int64_t stash = (2 * g8 + g8 * dim) * 4;
+    while (pl->stages_c * stage < stash) ++pl->stages_c;
+    while (attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), pl->warps_c,
+                             pl->stages_c, static_cast<int>(group), static_cast<int>(heads),
+                             pl->parts_b) > static_cast<size_t>(dev.smem_optin)) {
+      if (pl->stages_c > 1 && (pl->stages_c - 1) * stage >= stash) {
+        --pl->stages_c;
+      } else if (pl->warps_c > 1) {
+        --pl->warps_c;
+      } else {
+        return fail(RKV_ERR_UNSUPPORTED, "attention stages do not fit");
       }
-      --pl->warps_c;
     }
-    if (pl->stages_c < 2) return fail(RKV_ERR_UNSUPPORTED, "attention stages do not fit");
     pl->smem_c = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
                                    pl->warps_c, pl->stages_c, static_cast<int>(group),
                                    static_cast<int>(heads), pl->parts_b);
     pl->ctas = dev.sms;
+    pl->g8 = group <= 8 ? 8 : 16;
+    pl->max_sources = pl->parts_b + pl->ctas * pl->warps_c;
+    pl->smem_d = combine_smem_bytes(static_cast<int>(heads), pl->parts_b, static_cast<int>(group),
+                                    pl->max_sources);
+    if (pl->smem_d > static_cast<size_t>(dev.smem_optin)) {
+      return fail(RKV_ERR_UNSUPPORTED, "combine source table does not fit in shared memory");
+    }
   }
   // Workspace layout.
   size_t off = 0;
@@ -145,15 +161,15 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   pl->delta = take(rowsg * blocks * 4);
   if (decode) {
     const size_t slots_b = static_cast<size_t>(heads) * pl->parts_b;
-    const size_t slots_c = static_cast<size_t>(heads) * pl->ctas;
+    const size_t slots_c = static_cast<size_t>(heads) * pl->ctas * pl->warps_c;
     pl->seg_count = take(slots_b * 4);
     pl->sel_ids = take(slots_b * pl->seg_cap * 4);
-    pl->rep_m = take(slots_b * group * 4);
-    pl->rep_l = take(slots_b * group * 4);
-    pl->rep_o = take(slots_b * group * dim * 4);
-    pl->att_m = take(slots_c * group * 4);
-    pl->att_l = take(slots_c * group * 4);
-    pl->att_o = take(slots_c * group * dim * 4);
+    pl->rep_m = take(slots_b * pl->g8 * 4);
+    pl->rep_l = take(slots_b * pl->g8 * 4);
+    pl->rep_o = take(slots_b * pl->g8 * dim * 4);
+    pl->att_m = take(slots_c * pl->g8 * 4);
+    pl->att_l = take(slots_c * pl->g8 * 4);
+    pl->att_o = take(slots_c * pl->g8 * dim * 4);
   }
   pl->bytes = off;
   return RKV_OK;
@@ -511,7 +527,7 @@ size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t blocks, i
 
 int rkv_decode_launch_count(unsigned phases) {
   return ((phases & RKV_PHASE_STATS) ? 1 : 0) + ((phases & RKV_PHASE_FINAL) ? 1 : 0) +
-         ((phases & RKV_PHASE_ATTEND) ? 1 : 0);
+         ((phases & RKV_PHASE_ATTEND) ? 1 : 0) + ((phases & RKV_PHASE_COMBINE) ? 1 : 0);
 }
 
 int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
@@ -547,59 +563,81 @@ int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, i
   rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
                     selected, 0, workspace, true, phases, st);
   if (rc != RKV_OK) return rc;
-  if (!(phases & RKV_PHASE_ATTEND)) return RKV_OK;
-
   const int64_t H = summary->heads, D = summary->head_dim, B = summary->block_size;
-  AttendMaps maps;
-  rc = rows_map(&maps.key_pages, summary->key_pages, D, summary->blocks * B, H, D,
-                summary->key_page_head_stride, static_cast<int>(B), "key_pages");
-  if (rc != RKV_OK) return rc;
-  rc = rows_map(&maps.value_pages, summary->value_pages, D, summary->blocks * B, H, D,
-                summary->value_page_head_stride, static_cast<int>(B), "value_pages");
-  if (rc != RKV_OK) return rc;
-  if (suffix_capacity > 0) {
-    rc = rows_map(&maps.key_suffix, key_suffix, D, suffix_capacity, H, key_suffix_token_stride,
-                  key_suffix_head_stride, static_cast<int>(B), "key_suffix");
+  const int* suffix_ptr = suffix_length;
+  if (phases & RKV_PHASE_ATTEND) {
+    AttendMaps maps;
+    rc = rows_map(&maps.key_pages, summary->key_pages, D, summary->blocks * B, H, D,
+                  summary->key_page_head_stride, static_cast<int>(B), "key_pages");
     if (rc != RKV_OK) return rc;
-    rc = rows_map(&maps.value_suffix, value_suffix, D, suffix_capacity, H,
-                  value_suffix_token_stride, value_suffix_head_stride, static_cast<int>(B),
-                  "value_suffix");
+    rc = rows_map(&maps.value_pages, summary->value_pages, D, summary->blocks * B, H, D,
+                  summary->value_page_head_stride, static_cast<int>(B), "value_pages");
     if (rc != RKV_OK) return rc;
-  } else {
-    maps.key_suffix = maps.key_pages;
-    maps.value_suffix = maps.value_pages;
+    if (suffix_capacity > 0) {
+      rc = rows_map(&maps.key_suffix, key_suffix, D, suffix_capacity, H, key_suffix_token_stride,
+                    key_suffix_head_stride, static_cast<int>(B), "key_suffix");
+      if (rc != RKV_OK) return rc;
+      rc = rows_map(&maps.value_suffix, value_suffix, D, suffix_capacity, H,
+                    value_suffix_token_stride, value_suffix_head_stride, static_cast<int>(B),
+                    "value_suffix");
+      if (rc != RKV_OK) return rc;
+    } else {
+      maps.key_suffix = maps.key_pages;
+      maps.value_suffix = maps.value_pages;
+    }
+    AttendParams p = {};
+    p.query = query;
+    p.query_f32 = query_dtype == RKV_DTYPE_F32;
+    p.counts = summary->counts;
+    p.heads = static_cast<int>(H);
+    p.group = static_cast<int>(group);
+    p.blocks = static_cast<int>(summary->blocks);
+    p.page = static_cast<int>(B);
+    p.prompt_length = static_cast<int>(summary->prompt_length);
+    p.has_suffix = suffix_capacity > 0;
+    p.suffix_capacity = static_cast<int>(suffix_capacity);
+    p.suffix_len_ptr = suffix_ptr;
+    p.suffix_len_host = static_cast<int>(suffix_length_host);
+    p.seg_count = at<int>(workspace, pl.seg_count);
+    p.sel_ids = at<int>(workspace, pl.sel_ids);
+    p.parts_b = pl.parts_b;
+    p.seg_cap = pl.seg_cap;
+    p.att_m = at<float>(workspace, pl.att_m);
+    p.att_l = at<float>(workspace, pl.att_l);
+    p.att_o = at<float>(workspace, pl.att_o);
+    p.ctas = pl.ctas;
+    p.stages = pl.stages_c;
+    p.status = at<int>(workspace, pl.status);
+    p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
+    cudaError_t err = launch_attend(maps, p, static_cast<int>(D), pl.warps_c, pl.smem_c, st, true);
+    if (err != cudaSuccess) return cuda_fail(err, "attention launch");
   }
-  AttendParams p = {};
-  p.query = query;
-  p.query_f32 = query_dtype == RKV_DTYPE_F32;
-  p.out = output;
-  p.counts = summary->counts;
-  p.heads = static_cast<int>(H);
-  p.group = static_cast<int>(group);
-  p.blocks = static_cast<int>(summary->blocks);
-  p.page = static_cast<int>(B);
-  p.prompt_length = static_cast<int>(summary->prompt_length);
-  p.has_suffix = suffix_capacity > 0;
-  p.suffix_capacity = static_cast<int>(suffix_capacity);
-  p.suffix_len_ptr = suffix_length;
-  p.suffix_len_host = static_cast<int>(suffix_length_host);
-  p.seg_count = at<int>(workspace, pl.seg_count);
-  p.sel_ids = at<int>(workspace, pl.sel_ids);
-  p.parts_b = pl.parts_b;
-  p.seg_cap = pl.seg_cap;
-  p.rep_m = at<float>(workspace, pl.rep_m);
-  p.rep_l = at<float>(workspace, pl.rep_l);
-  p.rep_o = at<float>(workspace, pl.rep_o);
-  p.att_m = at<float>(workspace, pl.att_m);
-  p.att_l = at<float>(workspace, pl.att_l);
-  p.att_o = at<float>(workspace, pl.att_o);
-  p.ctas = pl.ctas;
-  p.stages = pl.stages_c;
-  p.done = at<int>(workspace, pl.done);
-  p.status = at<int>(workspace, pl.status);
-  p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
-  cudaError_t err = launch_attend(maps, p, static_cast<int>(D), pl.warps_c, pl.smem_c, st, true);
-  if (err != cudaSuccess) return cuda_fail(err, "attention launch");
+  if (phases & RKV_PHASE_COMBINE) {
+    CombineParams c = {};
+    c.query_f32 = query_dtype == RKV_DTYPE_F32;
+    c.out = output;
+    c.heads = static_cast<int>(H);
+    c.group = static_cast<int>(group);
+    c.page = static_cast<int>(B);
+    c.has_suffix = suffix_capacity > 0;
+    c.suffix_capacity = static_cast<int>(suffix_capacity);
+    c.suffix_len_ptr = suffix_ptr;
+    c.suffix_len_host = static_cast<int>(suffix_length_host);
+    c.seg_count = at<int>(workspace, pl.seg_count);
+    c.parts_b = pl.parts_b;
+    c.rep_m = at<float>(workspace, pl.rep_m);
+    c.rep_l = at<float>(workspace, pl.rep_l);
+    c.rep_o = at<float>(workspace, pl.rep_o);
+    c.att_m = at<float>(workspace, pl.att_m);
+    c.att_l = at<float>(workspace, pl.att_l);
+    c.att_o = at<float>(workspace, pl.att_o);
+    c.ctas = pl.ctas;
+    c.warps = pl.warps_c;
+    c.max_sources = pl.max_sources;
+    c.status = at<int>(workspace, pl.status);
+    cudaError_t err = launch_combine(c, static_cast<int>(D), st, true);
+    if (err != cudaSuccess) return cuda_fail(err, "combine launch");
+  }
   return RKV_OK;
 }
 

@@ -108,6 +108,24 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Same load with an L2 cache-policy hint (used with an evict-first policy for
+// K/V pages that are streamed once per step).
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int x, int y, int z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -126,6 +144,16 @@ __device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, uint
 #pragma unroll
   for (int i = 0; i < D / 64; ++i) {
     tma_load_3d(static_cast<char*>(dst) + i * rows * 128, map, bar, i * 64, row, head);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void tma_tile_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                              int row, int head, int rows, uint64_t policy) {
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    tma_load_3d_hint(static_cast<char*>(dst) + i * rows * 128, map, bar, i * 64, row, head,
+                     policy);
   }
 }
 
@@ -254,6 +282,45 @@ __device__ __forceinline__ void square_frags(const uint32_t (&qb)[D / 16][NT][2]
         const float x0 = __low2float(v), x1 = __high2float(v);
         q2[ks][nt][half] = pack_bf16(x0 * x0, x1 * x1);
       }
+}
+
+// Groups of at most 4 rows: one n8 tile carries [q | q^2] and the reduction
+// runs over 2*D (first the key-mean tile against q, then the ellipsoid tile
+// against q^2).  Columns 0-3 of the result are q.kbar, columns 4-7 are
+// q^2.W2, so every lane of the epilogue holds useful values.
+template <int D>
+__device__ __forceinline__ void pack4_frags(const uint32_t (&qb)[D / 16][1][2],
+                                            uint32_t (&packed)[2 * D / 16][2], int lane) {
+  const bool upper = (lane >> 2) >= 4;  // columns 4-7 hold q^2
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&qb[ks][0][half]);
+      const float x0 = __low2float(v), x1 = __high2float(v);
+      packed[ks][half] = upper ? 0u : qb[ks][0][half];
+      packed[D / 16 + ks][half] = upper ? pack_bf16(x0 * x0, x1 * x1) : 0u;
+    }
+}
+
+template <int R, int D>
+__device__ __forceinline__ void score_tile_pair(uint32_t tile_a, uint32_t tile_b,
+                                                const uint32_t (&packed)[2 * D / 16][2],
+                                                float (&acc)[R / 16][4], int lane) {
+#pragma unroll
+  for (int mt = 0; mt < R / 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+  const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int ks = 0; ks < 2 * D / 16; ++ks) {
+    const uint32_t tile = ks < D / 16 ? tile_a : tile_b;
+    const int kk = ks < D / 16 ? ks : ks - D / 16;
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt) {
+      uint32_t a[4];
+      ldsm_x4(tile + swz(mt * 16 + row, kk * 2 + (lane >> 4), R), a);
+      mma_bf16(acc[mt], a, packed[ks][0], packed[ks][1]);
+    }
+  }
 }
 
 // acc[mt][nt] = tile[mt*16 .. +16) . q^T for a swizzled [R x D] tile.  The
@@ -426,25 +493,26 @@ __device__ __forceinline__ void stash_warp_partial(float* sm_m, float* sm_l, flo
   }
 }
 
-// Merge `warps` stashed partials and write rows g < group to global
-// (m_out[g], l_out[g], o_out[g*D + d]).  Called by `threads` threads.
+// Merge `warps` stashed partials and write all g8 rows to global as one
+// partial: m_out[g], l_out[g] and o^T in o_out[d * g8 + g].  Called by
+// `threads` threads.
 template <int D>
 __device__ __forceinline__ void merge_stashed(const float* sm_m, const float* sm_l,
-                                              const float* sm_o, int warps, int g8, int group,
-                                              float* m_out, float* l_out, float* o_out, int tid,
-                                              int threads) {
-  for (int idx = tid; idx < group * D; idx += threads) {
-    const int g = idx / D, d = idx - g * D;
+                                              const float* sm_o, int warps, int g8, float* m_out,
+                                              float* l_out, float* o_out, int tid, int threads) {
+  for (int idx = tid; idx < g8 * D; idx += threads) {
+    const int d = idx / g8, g = idx - d * g8;
     float top = -INFINITY;
     for (int w = 0; w < warps; ++w) top = fmaxf(top, sm_m[w * g8 + g]);
     const float ref = top == -INFINITY ? 0.f : top;
     float acc = 0.f, den = 0.f;
     for (int w = 0; w < warps; ++w) {
-      const float s = __expf(sm_m[w * g8 + g] - ref);
+      const float m = sm_m[w * g8 + g];
+      const float s = m == -INFINITY ? 0.f : __expf(m - ref);
       acc += s * sm_o[(w * g8 + g) * D + d];
       den += s * sm_l[w * g8 + g];
     }
-    o_out[g * D + d] = acc;
+    o_out[d * g8 + g] = acc;
     if (d == 0) {
       m_out[g] = top;
       l_out[g] = den;

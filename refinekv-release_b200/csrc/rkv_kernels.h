@@ -71,9 +71,9 @@ struct FinalParams {
   int* seg_count;         // (heads, parts)
   int* sel_ids;           // (heads, parts, seg_cap)
   int seg_cap;
-  float* rep_m;  // (heads, parts, group)
+  float* rep_m;  // (heads, parts, G8)
   float* rep_l;
-  float* rep_o;  // (heads, parts, group, dim)
+  float* rep_o;  // (heads, parts, dim, G8): o^T, group rows innermost
   int* status;
 };
 
@@ -87,7 +87,6 @@ struct AttendMaps {
 struct AttendParams {
   const void* query;  // (heads, group, dim)
   int query_f32;
-  void* out;  // (heads, group, dim) in the query dtype
   const int64_t* counts;
   int heads, group, blocks, page;
   int prompt_length;  // rows of block b: min(page, prompt_length - b * page)
@@ -98,17 +97,35 @@ struct AttendParams {
   const int* seg_count;
   const int* sel_ids;
   int parts_b, seg_cap;
-  const float* rep_m;
-  const float* rep_l;
-  const float* rep_o;
-  float* att_m;  // (heads, ctas, group)
+  // One partial per (head, attention warp): m, l (heads, ctas*warps, G8) and
+  // o^T (heads, ctas*warps, dim, G8).
+  float* att_m;
   float* att_l;
-  float* att_o;  // (heads, ctas, group, dim)
+  float* att_o;
   int ctas;
   int stages;
-  int* done;  // (heads,), zero between launches
   int* status;
   float scale;
+};
+
+struct CombineParams {
+  int query_f32;
+  void* out;  // (heads, group, dim) in the query dtype
+  int heads, group, page;
+  int has_suffix, suffix_capacity;
+  const int* suffix_len_ptr;
+  int suffix_len_host;
+  const int* seg_count;
+  int parts_b;
+  const float* rep_m;  // (heads, parts_b, G8)
+  const float* rep_l;
+  const float* rep_o;  // (heads, parts_b, dim, G8)
+  const float* att_m;  // (heads, ctas*warps, G8)
+  const float* att_l;
+  const float* att_o;  // (heads, ctas*warps, dim, G8)
+  int ctas, warps;     // the attention launch's grid
+  int max_sources;     // capacity of the shared-memory source table
+  int* status;
 };
 
 // Host launchers (defined in the .cu files); return a cudaError_t.
@@ -119,6 +136,7 @@ cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, i
                          size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim, int warps,
                           size_t smem, cudaStream_t stream, bool pdl);
+cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream, bool pdl);
 
 // Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
 // current device.  Done once per (kernel, device): later calls, including
@@ -130,5 +148,6 @@ size_t stats_smem_bytes(int dim, int warps, int stages, int group);
 size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta);
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
                          int parts_b);
+size_t combine_smem_bytes(int heads, int parts_b, int group, int max_sources);
 
 }  // namespace rkv

@@ -68,7 +68,9 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
 
 // ------------------------------- phase A ----------------------------------
 
-template <int D, int NT>
+// PACK4 (groups of at most 4 rows): q and q^2 share one n8 tile, see
+// score_tile_pair; each lane then finishes 4 (block, row) elements.
+template <int D, int NT, bool PACK4>
 __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ StatsMaps maps,
                                                     const StatsParams p) {
   constexpr int R = kSelectTile;
@@ -99,6 +101,7 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
   }
   __syncwarp();
   pdl_wait();
+  pdl_launch_dependents();
 
   auto issue = [&](int j) {
     const int s = j % S;
@@ -115,8 +118,15 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
   const void* q = static_cast<const char*>(p.query) +
                   static_cast<size_t>(ih) * p.group * D * (p.query_f32 ? 4 : 2);
   uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
-  load_query_frags<D, NT>(qk, q, p.query_f32, p.group, lane, false);
-  square_frags<D, NT>(qk, q2);
+  uint32_t packed[PACK4 ? 2 * D / 16 : 1][2];
+  if constexpr (PACK4) {
+    uint32_t q1[D / 16][1][2];
+    load_query_frags<D, 1>(q1, q, p.query_f32, p.group, lane & 15, false);
+    pack4_frags<D>(q1, packed, lane);
+  } else {
+    load_query_frags<D, NT>(qk, q, p.query_f32, p.group, lane, false);
+    square_frags<D, NT>(qk, q2);
+  }
 
   float zm[NT][2], zs[NT][2], cm[NT][2], cs[NT][2];
 #pragma unroll
@@ -136,9 +146,37 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
       break;
     }
     const uint32_t base = smem_addr(tiles + (warp * S + s) * 2 * kTile);
-    float sk[R / 16][NT][4], sw[R / 16][NT][4];
-    score_tile<R, D, NT>(base, qk, sk, lane);
-    score_tile<R, D, NT>(base + kTile, q2, sw, lane);
+    // Per element: score (q.kbar) and projection (q^2.W2) of (block row, group row).
+    float sc[R / 16][NT][4], pr[R / 16][NT][4];
+    int row_of[R / 16][2];  // this lane's block rows per m-tile and half
+    int g_base;             // group row of element column j is g_base + j (PACK4)
+    if constexpr (PACK4) {
+      float acc[R / 16][4];
+      score_tile_pair<R, D>(base, base + kTile, packed, acc, lane);
+      const bool upper = (lane >> 1) & 1;  // holds q^2.W2 before the exchange
+#pragma unroll
+      for (int mt = 0; mt < R / 16; ++mt) {
+        const float send0 = upper ? acc[mt][0] : acc[mt][2];
+        const float send1 = upper ? acc[mt][1] : acc[mt][3];
+        const float recv0 = __shfl_xor_sync(0xffffffffu, send0, 2);
+        const float recv1 = __shfl_xor_sync(0xffffffffu, send1, 2);
+        sc[mt][0][0] = upper ? recv0 : acc[mt][0];
+        sc[mt][0][1] = upper ? recv1 : acc[mt][1];
+        pr[mt][0][0] = upper ? acc[mt][2] : recv0;
+        pr[mt][0][1] = upper ? acc[mt][3] : recv1;
+        row_of[mt][0] = mt * 16 + (lane >> 2) + (upper ? 8 : 0);
+      }
+      g_base = 2 * (lane & 1);
+    } else {
+      score_tile<R, D, NT>(base, qk, sc, lane);
+      score_tile<R, D, NT>(base + kTile, q2, pr, lane);
+#pragma unroll
+      for (int mt = 0; mt < R / 16; ++mt) {
+        row_of[mt][0] = mt * 16 + (lane >> 2);
+        row_of[mt][1] = row_of[mt][0] + 8;
+      }
+      g_base = 0;
+    }
     __syncwarp();
     if (j + S < mine) {
       if (lane == 0) {
@@ -148,38 +186,35 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
       ++issued;
     }
     const int tile = t0 + warp + j * warps;
-    // This lane's blocks are rows lane/4 and lane/4 + 8 of each m-tile.
-    float log_count[R / 16][2];
-#pragma unroll
-    for (int mt = 0; mt < R / 16; ++mt)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int b = tile * R + mt * 16 + (lane >> 2) + hf * 8;
-        log_count[mt][hf] = b < p.blocks ? logf(static_cast<float>(__ldg(p.counts + b))) : 0.f;
-      }
     // z and z + log cosh(delta) of every element first (independent), then
     // one (max, sum) update per column: no serial exp chain.
+    constexpr int kHalves = PACK4 ? 1 : 2;
     float zv[R / 16][NT][4], cv[R / 16][NT][4];
 #pragma unroll
     for (int mt = 0; mt < R / 16; ++mt) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int b = tile * R + mt * 16 + (lane >> 2) + (c >> 1) * 8;
+      for (int hf = 0; hf < kHalves; ++hf) {
+        const int b = tile * R + row_of[mt][hf];
+        const float log_count = b < p.blocks ? logf(static_cast<float>(__ldg(p.counts + b))) : 0.f;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
-          zv[mt][nt][c] = -INFINITY;
-          cv[mt][nt][c] = -INFINITY;
-          if (b >= p.blocks || g >= p.group) continue;
-          const float score = sk[mt][nt][c] * p.scale;
-          const float proj = sw[mt][nt][c];
-          const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
-          const float z = score + log_count[mt][c >> 1];
-          const size_t row = static_cast<size_t>(ih) * p.group + g;
-          p.z[row * p.blocks + b] = z;
-          p.delta[row * p.blocks + b] = delta;
-          zv[mt][nt][c] = z;
-          cv[mt][nt][c] = z + log_cosh(delta);
+        for (int jc = 0; jc < 2; ++jc) {
+          const int c = 2 * hf + jc;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int g = PACK4 ? g_base + jc : nt * 8 + 2 * (lane & 3) + jc;
+            zv[mt][nt][c] = -INFINITY;
+            cv[mt][nt][c] = -INFINITY;
+            if (b >= p.blocks || g >= p.group) continue;
+            const float score = sc[mt][nt][c] * p.scale;
+            const float proj = pr[mt][nt][c];
+            const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
+            const float z = score + log_count;
+            const size_t rowg = static_cast<size_t>(ih) * p.group + g;
+            p.z[rowg * p.blocks + b] = z;
+            p.delta[rowg * p.blocks + b] = delta;
+            zv[mt][nt][c] = z;
+            cv[mt][nt][c] = z + log_cosh(delta);
+          }
         }
       }
     }
@@ -192,34 +227,35 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
 #pragma unroll
         for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
+          for (int hf = 0; hf < kHalves; ++hf) {
             const float a = zv[mt][nt][2 * hf + jc], b = cv[mt][nt][2 * hf + jc];
             tz = fmaxf(tz, a);
             tc = fmaxf(tc, b);
             nan |= (a != a) || (b != b);
           }
-        float sz = 0.f, sc = 0.f;
+        float sz = 0.f, sc2 = 0.f;
         const float rz = tz == -INFINITY ? 0.f : tz, rc = tc == -INFINITY ? 0.f : tc;
 #pragma unroll
         for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
+          for (int hf = 0; hf < kHalves; ++hf) {
             sz += expf(zv[mt][nt][2 * hf + jc] - rz);
-            sc += expf(cv[mt][nt][2 * hf + jc] - rc);
+            sc2 += expf(cv[mt][nt][2 * hf + jc] - rc);
           }
-        if (nan) sz = sc = NAN;  // a NaN row statistic must stay non-finite
+        if (nan) sz = sc2 = NAN;  // a NaN row statistic must stay non-finite
         lse_merge(zm[nt][jc], zs[nt][jc], tz, sz);
-        lse_merge(cm[nt][jc], cs[nt][jc], tc, sc);
+        lse_merge(cm[nt][jc], cs[nt][jc], tc, sc2);
       }
   }
 
-  // Reduce the (max, sum) pairs over the 8 lanes of each column, then warps.
+  // Reduce the (max, sum) pairs over the lanes that share a column (8 lanes;
+  // 16 with PACK4), then across warps.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
 #pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
+      for (int off = PACK4 ? 2 : 4; off < 32; off <<= 1) {
         const float om = __shfl_xor_sync(0xffffffffu, zm[nt][j], off);
         const float os = __shfl_xor_sync(0xffffffffu, zs[nt][j], off);
         lse_merge(zm[nt][j], zs[nt][j], om, os);
@@ -227,8 +263,10 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
         const float ps = __shfl_xor_sync(0xffffffffu, cs[nt][j], off);
         lse_merge(cm[nt][j], cs[nt][j], pm, ps);
       }
-      if (lane < 4) {
-        float* r = red + (warp * NT * 8 + nt * 8 + 2 * lane + j) * 4;
+      const bool writer = PACK4 ? lane < 2 : lane < 4;
+      if (writer) {
+        const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
+        float* r = red + (warp * NT * 8 + g) * 4;
         r[0] = zm[nt][j];
         r[1] = zs[nt][j];
         r[2] = cm[nt][j];
@@ -250,7 +288,6 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
     out[2] = m1;
     out[3] = s1;
   }
-  pdl_launch_dependents();
 }
 
 // ------------------------------- phase B ----------------------------------
@@ -301,6 +338,7 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   }
   __syncthreads();
   pdl_wait();
+  pdl_launch_dependents();
 
   // Row-global normalisers from the phase-A partials: one warp per row,
   // lanes load partials in parallel and merge them with shuffles.
@@ -393,10 +431,7 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
       rep_bits[t - t0] = vb & ~sb;
     }
   }
-  if (!p.decode) {
-    pdl_launch_dependents();
-    return;
-  }
+  if (!p.decode) return;
   __syncthreads();
 
   // Deterministic compaction: tile offsets in block order, and the list of
@@ -420,6 +455,14 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   }
 
   const int n_reps = flags[1];
+  const size_t slot = static_cast<size_t>(h) * p.parts + part;
+  if (n_reps == 0) {  // nothing to represent: an empty partial (weight 0 in the combine)
+    if (threadIdx.x < G8) {
+      p.rep_m[slot * G8 + threadIdx.x] = -INFINITY;
+      p.rep_l[slot * G8 + threadIdx.x] = 0.f;
+    }
+    return;
+  }
   const int mine = n_reps > warp ? (n_reps - warp + warps - 1) / warps : 0;
   auto issue = [&](int j) {
     const int s = j % S;
@@ -479,11 +522,8 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   reduce_l<NT>(l);
   stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
   __syncthreads();
-  const size_t slot = static_cast<size_t>(h) * p.parts + part;
-  merge_stashed<D>(st_m, st_l, st_o, warps, G8, p.group, p.rep_m + slot * p.group,
-                   p.rep_l + slot * p.group, p.rep_o + slot * p.group * D, threadIdx.x,
-                   blockDim.x);
-  pdl_launch_dependents();
+  merge_stashed<D>(st_m, st_l, st_o, warps, G8, p.rep_m + slot * G8, p.rep_l + slot * G8,
+                   p.rep_o + slot * G8 * D, threadIdx.x, blockDim.x);
 }
 
 template <typename Kernel, typename Maps, typename Params>
@@ -508,8 +548,13 @@ template <int D>
 cudaError_t stats_dispatch(const StatsMaps& maps, const StatsParams& p, int warps, size_t smem,
                            cudaStream_t stream, bool pdl) {
   const dim3 grid(p.instances * p.heads, p.parts);
-  if (p.group <= 8) return launch_k(stats_kernel<D, 1>, maps, p, grid, warps, smem, stream, pdl);
-  return launch_k(stats_kernel<D, 2>, maps, p, grid, warps, smem, stream, pdl);
+  if (p.group <= 4) {
+    return launch_k(stats_kernel<D, 1, true>, maps, p, grid, warps, smem, stream, pdl);
+  }
+  if (p.group <= 8) {
+    return launch_k(stats_kernel<D, 1, false>, maps, p, grid, warps, smem, stream, pdl);
+  }
+  return launch_k(stats_kernel<D, 2, false>, maps, p, grid, warps, smem, stream, pdl);
 }
 
 template <int D>

@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(256, 2) summarize_kernel(const SummarizeParams
   const int count = page_ok ? min(B, p.tokens - b * B) : 0;
 
   pdl_wait();
+  pdl_launch_dependents();
 
   const __nv_bfloat16* __restrict__ kbase =
       static_cast<const __nv_bfloat16*>(p.keys) + h * p.key_head_stride +
@@ -183,7 +184,6 @@ __global__ void __launch_bounds__(256, 2) summarize_kernel(const SummarizeParams
       if (h == 0) p.counts[b] = count;
     }
   }
-  pdl_launch_dependents();
 }
 
 template <int D>

@@ -30,7 +30,8 @@ DTYPE_F32 = 1
 PHASE_STATS = 1
 PHASE_FINAL = 2
 PHASE_ATTEND = 4
-PHASE_ALL = 7
+PHASE_COMBINE = 8
+PHASE_ALL = 15
 
 #: Every symbol the header declares.
 EXPORTS = (

@@ -51,7 +51,7 @@ def test_library_exports_nothing_else(lib):
 def test_status_strings(lib):
     assert lib.rkv_status_string(0) == b"ok"
     assert lib.rkv_status_string(_native.RKV_ERR_ALIGNMENT) == b"misaligned pointer or stride"
-    assert lib.rkv_decode_launch_count(_native.PHASE_ALL) == 3
+    assert lib.rkv_decode_launch_count(_native.PHASE_ALL) == 4
     assert lib.rkv_decode_launch_count(_native.PHASE_ATTEND) == 1
 
 
@@ -77,7 +77,7 @@ def test_decode_rejects_bad_arguments_before_touching_a_device(lib):
 
     def call(summary, group=4, eps=0.01, reduction=2):
         return lib.rkv_decode(ctypes.byref(summary), 16, 0, group, None, None, 0, 0, 0, 0, 0,
-                              None, 0, None, eps, reduction, 16, 16, None, 0, 7, None)
+                              None, 0, None, eps, reduction, 16, 16, None, 0, 15, None)
 
     assert call(s, group=17) == _native.RKV_ERR_UNSUPPORTED
     assert call(s, eps=-1.0) == _native.RKV_ERR_INVALID_ARGUMENT
