@@ -18,7 +18,8 @@
 // rows on N) with mma.sync, mask rows past the item's token count, online
 // softmax, probabilities -> P^T operand by movmatrix, O^T += V^T . P^T.  At
 // each head boundary in its range the warp writes its own (m, l, o^T)
-// partial and goes on streaming: there is no CTA barrier in the loop.
+// partial and goes on streaming: there is no CTA barrier in the loop; the
+// warps' partials for the CTA's last head are merged into one at the end.
 //
 // combine_kernel: per (head, 32 channels), merges the selector's
 // representative partials with the attention warps' partials of that head
@@ -36,6 +37,14 @@ struct WorkList {
   long long C;
   __device__ long long cta_of(long long x) const { return ((x + 1) * C + T - 1) / T - 1; }
 };
+
+// Partial slots are indexed by (head, CTA) pairs that own items.  Along the
+// CTAs' contiguous ranges a CTA covers heads h_a..h_b and the next CTA starts
+// at head h_b or later, so head + cta strictly increases over the owned pairs:
+// it is a collision-free index below heads + ctas.
+__device__ __forceinline__ size_t pair_slot(long long head, long long cta) {
+  return static_cast<size_t>(head + cta);
+}
 
 __device__ __forceinline__ int visible_suffix(int has_suffix, const int* len_ptr, int len_host,
                                               int capacity, int* status) {
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       last_head = h;
       continue;
     }
-    const size_t slot = (static_cast<size_t>(h) * p.ctas + cta) * warps + warp;
+    const size_t slot = pair_slot(h, cta) * warps + warp;
     float* op = p.att_o + slot * D * G8;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -306,7 +315,7 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
   // merge the warps' parked partials.
   __syncthreads();
   if (last_head >= 0) {
-    const size_t slot = (static_cast<size_t>(last_head) * p.ctas + cta) * warps;
+    const size_t slot = pair_slot(last_head, cta) * warps;
     auto stash = [&](int w) {
       return reinterpret_cast<const float*>(ring + static_cast<size_t>(w) * S * kStage);
     };
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     const int a = k - PB;  // merged CTAs first, then the last CTA's slots
     const long long c = first + (a < n_merged ? a : n_merged);
     const int w = a < n_merged ? 0 : a - n_merged;
-    return (static_cast<size_t>(h) * p.ctas + c) * p.warps + w;
+    return pair_slot(h, c) * p.warps + w;
   };
   auto o_row = [&](int k) {
     return reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) + src_index(k) * D * G8 +

@@ -161,7 +161,8 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   pl->delta = take(rowsg * blocks * 4);
   if (decode) {
     const size_t slots_b = static_cast<size_t>(heads) * pl->parts_b;
-    const size_t slots_c = static_cast<size_t>(heads) * pl->ctas * pl->warps_c;
+    // (head, cta) pairs that own items are indexed by head + cta.
+    const size_t slots_c = static_cast<size_t>(heads + pl->ctas) * pl->warps_c;
     pl->seg_count = take(slots_b * 4);
     pl->sel_ids = take(slots_b * pl->seg_cap * 4);
     pl->rep_m = take(slots_b * pl->g8 * 4);

@@ -97,8 +97,9 @@ struct AttendParams {
   const int* seg_count;
   const int* sel_ids;
   int parts_b, seg_cap;
-  // One partial per (head, attention warp): m, l (heads, ctas*warps, G8) and
-  // o^T (heads, ctas*warps, dim, G8).
+  // One partial per (head, CTA, warp), (head, CTA) pairs indexed by head +
+  // cta: m, l ((heads + ctas) * warps, G8) and o^T ((heads + ctas) * warps,
+  // dim, G8).
   float* att_m;
   float* att_l;
   float* att_o;
@@ -120,9 +121,9 @@ struct CombineParams {
   const float* rep_m;  // (heads, parts_b, G8)
   const float* rep_l;
   const float* rep_o;  // (heads, parts_b, dim, G8)
-  const float* att_m;  // (heads, ctas*warps, G8)
+  const float* att_m;  // ((heads + ctas) * warps, G8)
   const float* att_l;
-  const float* att_o;  // (heads, ctas*warps, dim, G8)
+  const float* att_o;  // ((heads + ctas) * warps, dim, G8)
   int ctas, warps;     // the attention launch's grid
   int max_sources;     // capacity of the shared-memory source table
   int* status;
