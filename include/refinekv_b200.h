@@ -170,6 +170,34 @@ RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_
                uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
                void* stream);
 
+/*
+ * rkv_decode without a workspace, for callers that cannot allocate device
+ * memory on the decode path: runtimes that record the step into a CUDA graph
+ * while allocation is not allowed, hosts that reach this library only through
+ * its C ABI and have no device allocator of their own, or serving stacks whose
+ * device memory is partitioned before decoding starts.  This entry point has
+ * no counterpart in the reference.
+ *   Same arguments and results as rkv_decode with phases = RKV_PHASE_ALL,
+ *   minus the workspace.  Scratch comes from one array of
+ *   RKV_DECODE_STATIC_SCRATCH_BYTES inside the library's device image, which
+ *   every GPU that loads the library holds until the process exits;
+ *   geometries whose rkv_decode_workspace_size exceeds it are rejected with
+ *   RKV_ERR_WORKSPACE.  All calls on a device share that array and it keeps
+ *   the last call's contents (the status word is cleared at the start of each
+ *   call), so calls that can overlap on the GPU race: order them on one
+ *   stream.  The first call on each device looks up the array's address, with
+ *   that device current; make it before any stream capture.  Allocates
+ *   nothing.
+ */
+#define RKV_DECODE_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
+RKV_API int rkv_decode_static(const rkv_summary* summary, const void* query, int query_dtype,
+                              int64_t group, const void* key_suffix, const void* value_suffix,
+                              int64_t suffix_capacity, int64_t key_suffix_head_stride,
+                              int64_t key_suffix_token_stride, int64_t value_suffix_head_stride,
+                              int64_t value_suffix_token_stride, const int32_t* suffix_length,
+                              int64_t suffix_length_host, const uint8_t* anchor_mask, float eps,
+                              int reduction, void* output, uint8_t* selected, void* stream);
+
 /* Kernel launches one rkv_decode call makes for the given phases. */
 RKV_API int rkv_decode_launch_count(unsigned phases);
 

@@ -375,6 +375,8 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
 
 }  // namespace
 
+void set_last_error(const std::string& message) { g_last_error = message; }
+
 cudaError_t ensure_smem_limit(const void* func, size_t bytes) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);

@@ -40,6 +40,7 @@ EXPORTS = (
     "rkv_select",
     "rkv_decode_workspace_size",
     "rkv_decode",
+    "rkv_decode_static",
     "rkv_decode_launch_count",
     "rkv_last_error",
     "rkv_status_string",
@@ -85,6 +86,10 @@ _SIGNATURES = {
                                   c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr, c_i64, c_ptr,
                                   ctypes.c_float, ctypes.c_int, c_ptr, c_ptr, c_ptr,
                                   ctypes.c_size_t, ctypes.c_uint, c_ptr]),
+    "rkv_decode_static": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64,
+                                         c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr,
+                                         c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
+                                         c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
     "rkv_last_error": (ctypes.c_char_p, []),
     "rkv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
