@@ -201,6 +201,60 @@ RKV_API int rkv_decode_static(const rkv_summary* summary, const void* query, int
 /* Kernel launches one rkv_decode call makes for the given phases. */
 RKV_API int rkv_decode_launch_count(unsigned phases);
 
+/*
+ * Sequence split: the prompt blocks of each KV head are spread over `ranks`
+ * GPUs (contiguous block ranges; the generated-token suffix on one of them),
+ * for when GPUs outnumber KV heads.  The reference runs one GPU per sequence
+ * and has no such mode; the math is the same decode step (reference.py:50-73)
+ * with its two row-global reductions -- the selector normalisers log Z and
+ * log C (reference.py:15-17) and the softmax denominator -- merged across
+ * ranks.  A split step is three calls with two all-gathers between them,
+ * issued by the host over its own communicator (NCCL in refinekv_b200.parallel):
+ *
+ *   rkv_decode_split(..., RKV_SPLIT_STATS)   selector phase A; writes this
+ *                                            rank's stats slab
+ *   all-gather of the stats region           (ranks x stats_slab bytes, in place)
+ *   rkv_decode_split(..., RKV_SPLIT_ATTEND)  selector phase B over all ranks'
+ *                                            slabs, attention, combine into this
+ *                                            rank's output slab (m, l, o per row)
+ *   all-gather of the output region          (ranks x output_slab bytes, in place)
+ *   rkv_decode_split(..., RKV_SPLIT_MERGE)   LSE merge of the ranks' rows into
+ *                                            `output` (every rank gets it)
+ *
+ * The exchange buffer holds the stats region (ranks stats slabs) followed by
+ * the output region (ranks output slabs).  Every rank of a group must pass the
+ * same heads, group, head_dim, ranks and max_blocks (the largest block count
+ * of any rank), which fix the slab sizes.  Each rank's summary covers only its
+ * own blocks, except max_value_norm, which must hold the maximum over all
+ * ranks (one all-reduce after summarising).  The workspace is the one
+ * rkv_decode_workspace_size gives for this rank's blocks; the same workspace
+ * and exchange buffer must be passed to the three calls of a step.
+ */
+#define RKV_SPLIT_STATS 1
+#define RKV_SPLIT_ATTEND 2
+#define RKV_SPLIT_MERGE 4
+
+/* Slab sizes (bytes, multiples of 256) of one rank in the two exchange regions. */
+RKV_API int rkv_split_exchange_slabs(int64_t heads, int64_t group, int64_t max_blocks,
+                                     int64_t head_dim, size_t* stats_slab, size_t* output_slab);
+
+/*
+ * One stage of a sequence-split decode step (arguments as rkv_decode, plus
+ * the split geometry).  `selected` covers this rank's blocks; `output` is
+ * written by RKV_SPLIT_MERGE only.  `exchange` must be 256-byte aligned and
+ * hold ranks * (stats_slab + output_slab) bytes.
+ */
+RKV_API int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dtype,
+                             int64_t group, const void* key_suffix, const void* value_suffix,
+                             int64_t suffix_capacity, int64_t key_suffix_head_stride,
+                             int64_t key_suffix_token_stride, int64_t value_suffix_head_stride,
+                             int64_t value_suffix_token_stride, const int32_t* suffix_length,
+                             int64_t suffix_length_host, const uint8_t* anchor_mask, float eps,
+                             int reduction, void* output, uint8_t* selected, void* workspace,
+                             size_t workspace_size, int64_t ranks, int64_t rank,
+                             int64_t max_blocks, void* exchange, size_t exchange_size,
+                             unsigned stage, void* stream);
+
 /* Message of the last failing call on this host thread ("" if none). */
 RKV_API const char* rkv_last_error(void);
 RKV_API const char* rkv_status_string(int status);

@@ -151,13 +151,8 @@ def _log_cosh(delta: torch.Tensor) -> torch.Tensor:
     return torch.where(delta <= _DIRECT_DELTA_MAX, direct, large)
 
 
-@torch.no_grad()
-def selection_statistics(query: torch.Tensor, summary):
-    """Per (kv head, group row, block): z, risk, log_Z, log_C (``reference.py:10-34``).
-
-    ``query`` is (kv_heads, group, 1, dim) in any float dtype; it is rounded
-    to bf16 first, and so is its square (``:11-12``).
-    """
+def _scores(query: torch.Tensor, summary):
+    """z = q.kbar/sqrt(D) + log count and the inflated bound delta (``reference.py:11-16``)."""
     q = query[:, :, 0].to(torch.bfloat16).float()
     q_sq = q.square().to(torch.bfloat16).float()
     scale = q.shape[-1] ** -0.5
@@ -165,10 +160,24 @@ def selection_statistics(query: torch.Tensor, summary):
     spread = torch.einsum("hgd,hbd->hgb", q_sq, summary.ellipsoid.float())
     delta = spread.clamp_min(0).sqrt() * scale * _DELTA_INFLATION
     z = score + summary.counts.float().log().view(1, 1, -1)
+    return z, delta
 
+
+@torch.no_grad()
+def selection_statistics(query: torch.Tensor, summary):
+    """Per (kv head, group row, block): z, risk, log_Z, log_C (``reference.py:10-34``).
+
+    ``query`` is (kv_heads, group, 1, dim) in any float dtype; it is rounded
+    to bf16 first, and so is its square (``:11-12``).
+    """
+    z, delta = _scores(query, summary)
     log_z = torch.logsumexp(z, -1, keepdim=True)
     log_c = torch.logsumexp(z + _log_cosh(delta), -1, keepdim=True)
+    return z, _risk(z, delta, log_z, log_c, summary), log_z, log_c
 
+
+def _risk(z, delta, log_z, log_c, summary):
+    """Distortion + importance risk given the row normalisers (``reference.py:24-34``)."""
     small = delta.clamp(max=_DIRECT_DELTA_MAX)
     t = small.exp()
     near = delta <= _DIRECT_DELTA_MAX
@@ -182,7 +191,7 @@ def selection_statistics(query: torch.Tensor, summary):
     # importance ("value") term (reference.py:32-33)
     tanh_half = torch.where(near, (t - 1) / (t + 1), (1 - e_neg) / (1 + e_neg))
     importance = 2 * summary.value_norm.unsqueeze(1) * (z - log_z).exp() * tanh_half
-    return z, mass + importance, log_z, log_c
+    return mass + importance
 
 
 def reduce_group(risk: torch.Tensor, eps: float, reduction: str) -> torch.Tensor:
@@ -294,3 +303,76 @@ def merge_partials(m, l, o):
     w = torch.where(torch.isfinite(m), (m - top).exp(), torch.zeros_like(m))
     denom = (l * w).sum(-1, keepdim=True).clamp_min(1e-30)
     return (o * w.unsqueeze(-1)).sum(-2) / denom
+
+
+# --------------------------------------------------------------------------
+# Sequence split (prompt blocks spread over ranks)
+# --------------------------------------------------------------------------
+# The reference has no multi-GPU mode.  These functions write the decode step
+# of ``reference.py:10-73`` as per-rank pieces and merges, so that a test can
+# run them on separate (CPU, gloo) ranks and compare with the one-piece
+# functions above: log Z and log C (``reference.py:15-17``) and the softmax
+# denominator are the only sums that cross block ranges.
+
+@torch.no_grad()
+def normalizer_partials(query, summary):
+    """(heads, group, 4): max and sum of exp(. - max) for z and z + log cosh(delta) over this summary's blocks."""
+    z, delta = _scores(query, summary)
+    c = z + _log_cosh(delta)
+    mz, mc = z.amax(-1, keepdim=True), c.amax(-1, keepdim=True)
+    sz, sc = (z - mz).exp().sum(-1, keepdim=True), (c - mc).exp().sum(-1, keepdim=True)
+    return torch.cat([mz, sz, mc, sc], -1)
+
+
+def merge_normalizers(partials):
+    """(ranks, heads, group, 4) partials -> log Z, log C of shape (heads, group, 1)."""
+    def lse(m, s):
+        top = m.amax(0)
+        return top + (s * (m - top).exp()).sum(0).log()
+    return (lse(partials[..., 0], partials[..., 1]).unsqueeze(-1),
+            lse(partials[..., 2], partials[..., 3]).unsqueeze(-1))
+
+
+@torch.no_grad()
+def select_blocks_given(query, summary, log_z, log_c, eps: float, reduction: str):
+    """``select_blocks`` with row normalisers computed over the whole prompt elsewhere."""
+    z, delta = _scores(query, summary)
+    risk = _risk(z, delta, log_z, log_c, summary)
+    chosen = reduce_group(risk, eps, reduction)
+    forced_all = (~torch.isfinite(log_z) | ~torch.isfinite(log_c)).any(1)
+    forced_one = (~torch.isfinite(risk)).any(1)
+    return chosen | forced_all | forced_one, z
+
+
+@torch.no_grad()
+def mixed_attention_partial(query, summary, key_suffix, value_suffix, selected, z):
+    """This rank's share of ``mixed_attention``: per row (max, sum) and the normalised output.
+
+    Returns m, l of shape (heads, group) and o of shape (heads, group, dim).
+    """
+    q = query[:, :, 0].to(torch.bfloat16).float()
+    scale = q.shape[-1] ** -0.5
+    row_ids = torch.arange(summary.block_size)
+    ms, ls, os_ = [], [], []
+    for h in range(q.shape[0]):
+        live = selected[h, :, None] & (row_ids[None] < summary.counts[:, None])
+        k_rows = torch.cat([summary.keys[h][live].to(torch.bfloat16).float(),
+                            key_suffix[h].to(torch.bfloat16).float()])
+        v_rows = torch.cat([summary.values[h][live].to(torch.bfloat16).float(),
+                            value_suffix[h].to(torch.bfloat16).float()])
+        logits = torch.cat([z[h][:, ~selected[h]], q[h] @ k_rows.T * scale], -1)
+        vals = torch.cat([summary.value_mean[h][~selected[h]].float(), v_rows], 0)
+        m = logits.amax(-1, keepdim=True)
+        p = (logits - m).exp()
+        l = p.sum(-1, keepdim=True)
+        ms.append(m[:, 0])
+        ls.append(l[:, 0])
+        os_.append((p @ vals) / l)
+    return torch.stack(ms), torch.stack(ls), torch.stack(os_)
+
+
+def merge_rank_outputs(m, l, o):
+    """(ranks, heads, group), (ranks, heads, group), (ranks, heads, group, dim) -> (heads, group, 1, dim)."""
+    top = m.amax(0)
+    w = l * (m - top).exp()
+    return ((w.unsqueeze(-1) * o).sum(0) / w.sum(0).unsqueeze(-1)).unsqueeze(2)

@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     for (int k = lane; k < nsrc; k += 32) s += lsum[k * G8 + g];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) den[g] = fmaxf(s, 1e-30f);
+    if (lane == 0) den[g] = s;
   }
   float acc[G8];
 #pragma unroll
@@ -513,12 +513,52 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) s += red[(w * 32 + ln) * G8 + g];
-    const float out = s / den[g];
-    const size_t o = (static_cast<size_t>(h) * p.group + g) * D + blockIdx.y * 32 + ln;
-    if (p.query_f32) {
+    const float out = s / fmaxf(den[g], 1e-30f);
+    const size_t row = static_cast<size_t>(h) * p.group + g;
+    const size_t o = row * D + blockIdx.y * 32 + ln;
+    if (p.part_o != nullptr) {  // sequence split: this rank's row partial
+      p.part_o[o] = out;
+      if (blockIdx.y == 0 && ln == 0) {
+        p.part_ml[row * 2] = top[g];
+        p.part_ml[row * 2 + 1] = den[g];
+      }
+    } else if (p.query_f32) {
       static_cast<float*>(p.out)[o] = out;
     } else {
       static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(out);
+    }
+  }
+}
+
+// Sequence split: out[row, d] = sum_r w_r o_r[row, d] / sum_r w_r with
+// w_r = l_r exp(m_r - max_r m_r) over the ranks whose row is non-empty.
+// One CTA per KV head, one thread per (group row, dim) element.
+template <int D>
+__global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int h = blockIdx.x;
+  for (int i = threadIdx.x; i < p.group * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    const size_t row = static_cast<size_t>(h) * p.group + g;
+    float top = -INFINITY;
+    for (int r = 0; r < p.ranks; ++r) {
+      const float* ml = p.part_ml + r * p.slab_floats + row * 2;
+      if (ml[1] > 0.f) top = fmaxf(top, ml[0]);
+    }
+    float num = 0.f, den = 0.f;
+    for (int r = 0; r < p.ranks; ++r) {
+      const float* ml = p.part_ml + r * p.slab_floats + row * 2;
+      if (!(ml[1] > 0.f)) continue;
+      const float w = ml[1] * __expf(ml[0] - top);
+      den += w;
+      num += w * p.part_o[r * p.slab_floats + row * D + d];
+    }
+    const float out = num / fmaxf(den, 1e-30f);
+    if (p.query_f32) {
+      static_cast<float*>(p.out)[row * D + d] = out;
+    } else {
+      static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(out);
     }
   }
 }
@@ -583,6 +623,13 @@ cudaError_t combine_g(const CombineParams& p, cudaStream_t stream, bool pdl) {
   return launch_combine_t<D, 16>(p, stream, pdl);
 }
 
+template <int D>
+cudaError_t launch_merge_t(const MergeParams& p, cudaStream_t stream, bool pdl) {
+  void* args[] = {const_cast<MergeParams*>(&p)};
+  return launch_pdl(reinterpret_cast<const void*>(merge_kernel<D>), dim3(p.heads), dim3(256), 0,
+                    stream, pdl, args);
+}
+
 }  // namespace
 
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
@@ -617,6 +664,16 @@ cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream,
     case 128: return combine_g<128>(p, stream, pdl);
     case 192: return combine_g<192>(p, stream, pdl);
     case 256: return combine_g<256>(p, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, bool pdl) {
+  switch (dim) {
+    case 64: return launch_merge_t<64>(p, stream, pdl);
+    case 128: return launch_merge_t<128>(p, stream, pdl);
+    case 192: return launch_merge_t<192>(p, stream, pdl);
+    case 256: return launch_merge_t<256>(p, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

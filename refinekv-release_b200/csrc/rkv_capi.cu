@@ -86,15 +86,22 @@ void split(int tiles, int target_parts, int* parts, int* per) {
 }
 
 // `decode` plans rkv_decode (one query instance); otherwise rkv_select.
+// `fixed_parts_a` > 0 pins the phase-A grid (a sequence split needs the same
+// partial count on every rank; CTAs past the last tile write empty partials).
 int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t dim,
-              int64_t block_size, int64_t instances, bool decode) {
+              int64_t block_size, int64_t instances, bool decode, int fixed_parts_a = 0) {
   DeviceInfo dev;
   int rc = device_info(&dev);
   if (rc != RKV_OK) return rc;
   pl->tiles = static_cast<int>(cdiv(blocks, kSelectTile));
   const int64_t rows = heads * instances;
   // Phase A: about two CTAs per SM in total.
-  split(pl->tiles, static_cast<int>(cdiv(2LL * dev.sms, rows)), &pl->parts_a, &pl->tpc_a);
+  if (fixed_parts_a > 0) {
+    pl->parts_a = fixed_parts_a;
+    pl->tpc_a = static_cast<int>(cdiv(pl->tiles, fixed_parts_a));
+  } else {
+    split(pl->tiles, static_cast<int>(cdiv(2LL * dev.sms, rows)), &pl->parts_a, &pl->tpc_a);
+  }
   pl->stages_a = static_cast<int>(std::min<int64_t>(2, cdiv(pl->tpc_a, pl->warps_a)));
   pl->smem_a = stats_smem_bytes(static_cast<int>(dim), pl->warps_a, pl->stages_a,
                                 static_cast<int>(group));
@@ -175,6 +182,44 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   pl->bytes = off;
   return RKV_OK;
 }
+
+// Sequence split: phase-A partials per row on every rank (fixed by the
+// largest rank's block count, not by the device, so that all ranks agree) and
+// the slab sizes of the exchange buffer.
+constexpr int kSplitStatsCtas = 296;
+
+struct SplitGeometry {
+  int parts_a = 1;
+  size_t stats_slab = 0;   // bytes: (heads * group, parts_a, 4) fp32
+  size_t ml_bytes = 0;     // bytes of the (rows, 2) block at the start of an output slab
+  size_t output_slab = 0;  // bytes: (rows, 2) then (rows, dim) fp32
+};
+
+SplitGeometry split_geometry(int64_t heads, int64_t group, int64_t max_blocks, int64_t dim) {
+  SplitGeometry g;
+  int per = 1;
+  split(static_cast<int>(cdiv(max_blocks, kSelectTile)),
+        static_cast<int>(cdiv(kSplitStatsCtas, heads)), &g.parts_a, &per);
+  const size_t rows = static_cast<size_t>(heads) * group;
+  g.stats_slab = up256(rows * g.parts_a * 16);
+  g.ml_bytes = up256(rows * 8);
+  g.output_slab = g.ml_bytes + up256(rows * dim * 4);
+  return g;
+}
+
+// Where the kernels of one rank of a split step read and write.
+struct SplitTarget {
+  int ranks = 1, rank = 0;
+  SplitGeometry geo;
+  char* exchange = nullptr;
+  float* stats_slab(int r) const { return reinterpret_cast<float*>(exchange + r * geo.stats_slab); }
+  float* output_ml(int r) const {
+    return reinterpret_cast<float*>(exchange + ranks * geo.stats_slab + r * geo.output_slab);
+  }
+  float* output_o(int r) const {
+    return reinterpret_cast<float*>(reinterpret_cast<char*>(output_ml(r)) + geo.ml_bytes);
+  }
+};
 
 // ---------------------------------------------------------------------------
 // TMA descriptors
@@ -304,9 +349,12 @@ T* at(void* ws, size_t off) {
 }
 
 // Phases A and B shared by rkv_select and rkv_decode.
+// With `split`, phase A writes this rank's stats slab and phase B reads all
+// ranks' slabs.
 int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype, int64_t inst,
                  int64_t group, float eps, int reduction, const uint8_t* anchor, uint8_t* mask,
-                 int accumulate, void* ws, bool decode, unsigned phases, cudaStream_t stream) {
+                 int accumulate, void* ws, bool decode, unsigned phases, cudaStream_t stream,
+                 const SplitTarget* split = nullptr) {
   const int D = static_cast<int>(s->head_dim);
   if (phases & RKV_PHASE_STATS) {
     StatsMaps maps;
@@ -327,7 +375,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
     p.z = at<float>(ws, pl.z);
     p.delta = at<float>(ws, pl.delta);
-    p.lse = at<float>(ws, pl.lse);
+    p.lse = split ? split->stats_slab(split->rank) : at<float>(ws, pl.lse);
     p.status = at<int>(ws, pl.status);
     cudaError_t err = launch_stats(maps, p, D, pl.warps_a, pl.smem_a, stream, true);
     if (err != cudaSuccess) return cuda_fail(err, "selector stats launch");
@@ -350,7 +398,9 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.reduction = reduction;
     p.z = at<float>(ws, pl.z);
     p.delta = at<float>(ws, pl.delta);
-    p.lse = at<float>(ws, pl.lse);
+    p.lse = split ? split->stats_slab(0) : at<float>(ws, pl.lse);
+    p.lse_slabs = split ? split->ranks : 1;
+    p.lse_slab_floats = split ? split->geo.stats_slab / 4 : 0;
     p.value_norm = s->value_norm;
     p.max_value_norm = s->max_value_norm;
     p.anchor = anchor;
@@ -533,15 +583,21 @@ int rkv_decode_launch_count(unsigned phases) {
          ((phases & RKV_PHASE_ATTEND) ? 1 : 0) + ((phases & RKV_PHASE_COMBINE) ? 1 : 0);
 }
 
-int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
-               const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
-               int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
-               int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
-               const int32_t* suffix_length, int64_t suffix_length_host,
-               const uint8_t* anchor_mask, float eps, int reduction, void* output,
-               uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
-               void* stream) {
-  g_last_error.clear();
+}  // extern "C"
+
+namespace {
+
+// rkv_decode, and one rank's share of a sequence-split step when `split` is
+// given (phase A into the rank's stats slab, phase B over all slabs, combine
+// into the rank's output slab).
+int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+                const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+                int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+                int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+                const int32_t* suffix_length, int64_t suffix_length_host,
+                const uint8_t* anchor_mask, float eps, int reduction, void* output,
+                uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
+                void* stream, const SplitTarget* split) {
   int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
   if (rc != RKV_OK) return rc;
   if (output == nullptr || selected == nullptr) {
@@ -559,12 +615,12 @@ int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, i
   if (phases == 0 || phases > RKV_PHASE_ALL) return fail(RKV_ERR_INVALID_ARGUMENT, "bad phases");
   Plan pl;
   rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
-                 summary->block_size, 1, true);
+                 summary->block_size, 1, true, split ? split->geo.parts_a : 0);
   if (rc != RKV_OK) return rc;
   if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
-                    selected, 0, workspace, true, phases, st);
+                    selected, 0, workspace, true, phases, st, split);
   if (rc != RKV_OK) return rc;
   const int64_t H = summary->heads, D = summary->head_dim, B = summary->block_size;
   const int* suffix_ptr = suffix_length;
@@ -637,9 +693,117 @@ int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, i
     c.ctas = pl.ctas;
     c.warps = pl.warps_c;
     c.max_sources = pl.max_sources;
+    c.part_ml = split ? split->output_ml(split->rank) : nullptr;
+    c.part_o = split ? split->output_o(split->rank) : nullptr;
     c.status = at<int>(workspace, pl.status);
     cudaError_t err = launch_combine(c, static_cast<int>(D), st, true);
     if (err != cudaSuccess) return cuda_fail(err, "combine launch");
+  }
+  return RKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+               const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+               int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+               int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+               const int32_t* suffix_length, int64_t suffix_length_host,
+               const uint8_t* anchor_mask, float eps, int reduction, void* output,
+               uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
+               void* stream) {
+  g_last_error.clear();
+  return decode_impl(summary, query, query_dtype, group, key_suffix, value_suffix,
+                     suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                     value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                     suffix_length_host, anchor_mask, eps, reduction, output, selected,
+                     workspace, workspace_size, phases, stream, nullptr);
+}
+
+int rkv_split_exchange_slabs(int64_t heads, int64_t group, int64_t max_blocks, int64_t head_dim,
+                             size_t* stats_slab, size_t* output_slab) {
+  g_last_error.clear();
+  if (heads <= 0 || heads > (1 << 16) || group < 1 || group > kMaxGroup || max_blocks <= 0 ||
+      max_blocks > (1LL << 26)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "split geometry out of range");
+  }
+  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+  if (stats_slab == nullptr || output_slab == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "null output pointer");
+  }
+  const SplitGeometry geo = split_geometry(heads, group, max_blocks, head_dim);
+  *stats_slab = geo.stats_slab;
+  *output_slab = geo.output_slab;
+  return RKV_OK;
+}
+
+int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+                     const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+                     int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+                     int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+                     const int32_t* suffix_length, int64_t suffix_length_host,
+                     const uint8_t* anchor_mask, float eps, int reduction, void* output,
+                     uint8_t* selected, void* workspace, size_t workspace_size, int64_t ranks,
+                     int64_t rank, int64_t max_blocks, void* exchange, size_t exchange_size,
+                     unsigned stage, void* stream) {
+  g_last_error.clear();
+  int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
+  if (rc != RKV_OK) return rc;
+  if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");
+  }
+  if (max_blocks < summary->blocks || max_blocks > (1LL << 26)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "max_blocks must be at least this rank's block count");
+  }
+  if (stage == 0 || stage > (RKV_SPLIT_STATS | RKV_SPLIT_ATTEND | RKV_SPLIT_MERGE)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "bad split stage");
+  }
+  SplitTarget target;
+  target.ranks = static_cast<int>(ranks);
+  target.rank = static_cast<int>(rank);
+  target.geo = split_geometry(summary->heads, group, max_blocks, summary->head_dim);
+  target.exchange = static_cast<char*>(exchange);
+  const size_t need = static_cast<size_t>(ranks) * (target.geo.stats_slab + target.geo.output_slab);
+  if (exchange == nullptr || exchange_size < need) {
+    return fail(RKV_ERR_WORKSPACE, "exchange buffer is missing or smaller than the required size " +
+                                       std::to_string(need));
+  }
+  if ((reinterpret_cast<uintptr_t>(exchange) & 255u) != 0) {
+    return fail(RKV_ERR_ALIGNMENT, "exchange buffer must be 256-byte aligned");
+  }
+  if (output == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "output must be non-null");
+  if (stage & RKV_SPLIT_STATS) {
+    rc = decode_impl(summary, query, query_dtype, group, key_suffix, value_suffix,
+                     suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                     value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                     suffix_length_host, anchor_mask, eps, reduction, output, selected, workspace,
+                     workspace_size, RKV_PHASE_STATS, stream, &target);
+    if (rc != RKV_OK) return rc;
+  }
+  if (stage & RKV_SPLIT_ATTEND) {
+    rc = decode_impl(summary, query, query_dtype, group, key_suffix, value_suffix,
+                     suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                     value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                     suffix_length_host, anchor_mask, eps, reduction, output, selected, workspace,
+                     workspace_size, RKV_PHASE_FINAL | RKV_PHASE_ATTEND | RKV_PHASE_COMBINE,
+                     stream, &target);
+    if (rc != RKV_OK) return rc;
+  }
+  if (stage & RKV_SPLIT_MERGE) {
+    MergeParams m = {};
+    m.query_f32 = query_dtype == RKV_DTYPE_F32;
+    m.out = output;
+    m.heads = static_cast<int>(summary->heads);
+    m.group = static_cast<int>(group);
+    m.ranks = target.ranks;
+    m.part_ml = target.output_ml(0);
+    m.part_o = target.output_o(0);
+    m.slab_floats = target.geo.output_slab / 4;
+    const cudaError_t err = launch_merge(m, static_cast<int>(summary->head_dim),
+                                         static_cast<cudaStream_t>(stream), true);
+    if (err != cudaSuccess) return cuda_fail(err, "split merge launch");
   }
   return RKV_OK;
 }

@@ -60,7 +60,11 @@ struct FinalParams {
   int reduction;
   const float* z;
   const float* delta;
+  // Phase-A partials: lse_slabs slabs of (instances*heads*group, parts_a, 4),
+  // lse_slab_floats apart (one slab per rank of a sequence split, else one).
   const float* lse;
+  int lse_slabs;
+  size_t lse_slab_floats;
   const float* value_norm;
   const float* max_value_norm;
   const uint8_t* anchor;  // (heads, blocks) or null
@@ -126,7 +130,23 @@ struct CombineParams {
   const float* att_o;  // ((heads + ctas) * warps, dim, G8)
   int ctas, warps;     // the attention launch's grid
   int max_sources;     // capacity of the shared-memory source table
+  // Sequence split: when non-null, each row's merged (max, sum) goes to
+  // part_ml[row * 2 + {0, 1}] and its normalised output to part_o[row * dim
+  // + d] (FP32) instead of `out`.
+  float* part_ml;
+  float* part_o;
   int* status;
+};
+
+// LSE merge of the ranks' rows of a sequence split (rkv_decode_split).
+struct MergeParams {
+  int query_f32;
+  void* out;  // (heads, group, dim) in the query dtype
+  int heads, group;
+  int ranks;
+  const float* part_ml;  // slab r: part_ml + r * slab_floats, (rows, 2)
+  const float* part_o;   // slab r: part_o + r * slab_floats, (rows, dim)
+  size_t slab_floats;
 };
 
 // Host launchers (defined in the .cu files); return a cudaError_t.
@@ -138,6 +158,7 @@ cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, i
 cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim, int warps,
                           size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream, bool pdl);
+cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, bool pdl);
 
 // Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
 // current device.  Done once per (kernel, device): later calls, including

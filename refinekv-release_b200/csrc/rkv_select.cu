@@ -340,13 +340,16 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   pdl_wait();
   pdl_launch_dependents();
 
-  // Row-global normalisers from the phase-A partials: one warp per row,
-  // lanes load partials in parallel and merge them with shuffles.
+  // Row-global normalisers from the phase-A partials (of every rank's slab
+  // under a sequence split): one warp per row, lanes load partials in
+  // parallel and merge them with shuffles.
   for (int g = warp; g < p.group; g += warps) {
     const float* in = p.lse + (static_cast<size_t>(ih) * p.group + g) * p.parts_a * 4;
     float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    for (int k = lane; k < p.parts_a; k += 32) {
-      const float4 v = *reinterpret_cast<const float4*>(in + 4 * k);
+    for (int k = lane; k < p.parts_a * p.lse_slabs; k += 32) {
+      const int slab = k / p.parts_a, part_k = k - slab * p.parts_a;
+      const float4 v =
+          *reinterpret_cast<const float4*>(in + slab * p.lse_slab_floats + 4 * part_k);
       lse_merge(m0, s0, v.x, v.y);
       lse_merge(m1, s1, v.z, v.w);
     }

@@ -33,6 +33,10 @@ PHASE_ATTEND = 4
 PHASE_COMBINE = 8
 PHASE_ALL = 15
 
+SPLIT_STATS = 1
+SPLIT_ATTEND = 2
+SPLIT_MERGE = 4
+
 #: Every symbol the header declares.
 EXPORTS = (
     "rkv_summarize",
@@ -42,6 +46,8 @@ EXPORTS = (
     "rkv_decode",
     "rkv_decode_static",
     "rkv_decode_launch_count",
+    "rkv_split_exchange_slabs",
+    "rkv_decode_split",
     "rkv_last_error",
     "rkv_status_string",
     "rkv_abi_version",
@@ -91,6 +97,14 @@ _SIGNATURES = {
                                          c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
                                          c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
+    "rkv_split_exchange_slabs": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64,
+                                                ctypes.POINTER(ctypes.c_size_t),
+                                                ctypes.POINTER(ctypes.c_size_t)]),
+    "rkv_decode_split": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64,
+                                        c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr,
+                                        c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
+                                        c_ptr, ctypes.c_size_t, c_i64, c_i64, c_i64, c_ptr,
+                                        ctypes.c_size_t, ctypes.c_uint, c_ptr]),
     "rkv_last_error": (ctypes.c_char_p, []),
     "rkv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "rkv_abi_version": (ctypes.c_int, []),
