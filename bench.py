@@ -18,7 +18,11 @@ the step's queries and new K/V tokens copied from pinned host memory and the
 outputs copied back inside the timed region.
 
 --gpus N shards the KV heads across N ranks (one process per GPU, torchrun);
-there is no per-step collective (strong scaling: fixed total work).
+with N dividing the 8 KV heads there is no per-step collective (strong
+scaling: fixed total work).  When N does not divide the heads, or with
+--seq-ranks S, each head's prompt blocks are split over S ranks, which
+exchange the selector normalisers and the (max, sum, output) rows of each
+step over NCCL (refinekv_b200.parallel).
 
 --impl reference times the reference algorithm on the host CPU (the oracle
 restatement of the reference PyTorch backend, all host threads), one layer
@@ -52,6 +56,8 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--seq-ranks", type=int, default=None,
+                    help="ranks per sequence group (default: split heads first)")
     ap.add_argument("--steps", type=int, default=125)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
@@ -74,7 +80,7 @@ def parse_args():
     return args
 
 
-def workload_config(args, world):
+def workload_config(args, world, plan=None):
     return {
         "workload": "llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
         else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}",
@@ -88,7 +94,8 @@ def workload_config(args, world):
         "gqa_reduction": args.reduction,
         "anchor_tokens": args.anchors,
         "decode_steps": args.warmup + args.steps,
-        "parallelism": f"kv-head shard x{world}",
+        "parallelism": (f"kv-head shard x{plan.head_shards}, sequence split x{plan.seq_ranks}"
+                        if plan is not None else f"kv-head shard x{world}"),
         "cache_flush": "none needed: every layer's KV (heads x tokens x 256 B x 2) exceeds L2",
         "cuda_graph": True,
         "seed": args.seed,
@@ -314,12 +321,12 @@ class Layer:
     pass
 
 
-def build_layers(args, rank, world, dev):
-    from refinekv_b200 import RefineKVConfig, build_summary, synthetic
-    from refinekv_b200.attention import select_blocks_union
+def build_layers(args, plan, group, dev):
+    from refinekv_b200 import RefineKVConfig, build_summary, parallel, synthetic
 
     H = args.kv_heads
-    h0, h1 = rank * H // world, (rank + 1) * H // world
+    h0, h1 = plan.head_lo, plan.head_hi
+    world = plan.world
     cfg = RefineKVConfig(block_size=args.block_size, eps=args.eps,
                          gqa_reduction=args.reduction, anchor_tokens=args.anchors)
     cap = args.warmup + args.steps
@@ -329,29 +336,37 @@ def build_layers(args, rank, world, dev):
         data = synthetic.make_layer(args.seed, li, H, args.tokens, args.head_dim,
                                     args.block_size, device=dev)
         L = Layer()
-        L.keys = data.keys[h0:h1].contiguous() if world > 1 else data.keys
-        L.values = data.values[h0:h1].contiguous() if world > 1 else data.values
+        L.keys, L.values = parallel.shard_prompt(data.keys, data.values, plan)
+        if world > 1:  # keep only this rank's share resident
+            L.keys, L.values = L.keys.contiguous(), L.values.contiguous()
         del data.keys, data.values
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # A few ms of spin ahead of the events keep the host's launch time of
+        # the summary call out of its measured device time.
+        torch.cuda._sleep(10_000_000)
         start.record()
-        L.summary = build_summary(L.keys, L.values, cfg)
+        L.summary = build_summary(L.keys, L.values, cfg)  # the kernel alone; merged below
         end.record()
         end.synchronize()
         summarize_ms.append(start.elapsed_time(end))
+        parallel.merge_max_value_norm(L.summary.max_value_norm, group)
         anchors = synthetic.make_queries(args.seed, li, -1, data.planted_mean, args.group,
                                          args.anchors)[:, h0:h1]
-        L.anchor = select_blocks_union(anchors.contiguous(), L.summary, cfg) if args.anchors else None
+        L.anchor = (parallel.select_blocks_union_split(anchors.contiguous(), L.summary, cfg, plan,
+                                                       group) if args.anchors else None)
         L.q = torch.stack([synthetic.make_queries(args.seed, li, s, data.planted_mean,
                                                   args.group)[0, h0:h1]
                            for s in range(cap)]).contiguous()
-        ks, vs = [], []
-        for s in range(cap):
-            k, v = synthetic.make_decode_token(args.seed, li, s, H, args.head_dim,
-                                               args.tokens + s, device=dev)
-            ks.append(k[h0:h1])
-            vs.append(v[h0:h1])
-        L.suffix_k = torch.cat(ks, 1).contiguous()
-        L.suffix_v = torch.cat(vs, 1).contiguous()
+        L.suffix_k = L.suffix_v = None  # the generated tokens live on the group's last rank
+        if plan.holds_suffix:
+            ks, vs = [], []
+            for s in range(cap):
+                k, v = synthetic.make_decode_token(args.seed, li, s, H, args.head_dim,
+                                                   args.tokens + s, device=dev)
+                ks.append(k[h0:h1])
+                vs.append(v[h0:h1])
+            L.suffix_k = torch.cat(ks, 1).contiguous()
+            L.suffix_v = torch.cat(vs, 1).contiguous()
         L.workspace = {}
         layers.append(L)
     return layers, cfg, summarize_ms
@@ -361,24 +376,26 @@ def run_b200(args):
     rank, world, local = dist_setup()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if args.kv_heads % world:
-        raise SystemExit(f"--gpus {world} must divide the {args.kv_heads} KV heads "
-                         "(sequence split is not part of this bench)")
-    from refinekv_b200 import _native, sparse_attention
+    from refinekv_b200 import _native, parallel
 
+    plan = parallel.plan_shards(args.kv_heads, args.tokens, args.block_size, world, rank,
+                                args.seq_ranks)
+    group = parallel.new_seq_group(plan)
+    decode = parallel.SplitDecode(plan, group)
     lib = _native.load()
-    layers, cfg, summarize_ms = build_layers(args, rank, world, dev)
+    layers, cfg, summarize_ms = build_layers(args, plan, group, dev)
     cap = args.warmup + args.steps
     length = torch.zeros((), device=dev, dtype=torch.int32)
-    heads_local = args.kv_heads // world
+    heads_local = plan.heads
+    split = plan.seq_ranks > 1
 
     # one CUDA graph per decode step: bump the visible suffix, then all layers
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
         for L in layers:  # allocate every workspace before capture
-            sparse_attention(L.q[0], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
-                             workspace=L.workspace, suffix_length=length)
+            decode(L.q[0], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                   workspace=L.workspace, suffix_length=length)
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     graphs = []
@@ -387,9 +404,8 @@ def run_b200(args):
         with torch.cuda.graph(g):
             length.add_(1)
             for L in layers:
-                sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg,
-                                 anchor_mask=L.anchor, workspace=L.workspace,
-                                 suffix_length=length)
+                decode(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                       workspace=L.workspace, suffix_length=length)
         graphs.append(g)
 
     length.zero_()
@@ -413,40 +429,74 @@ def run_b200(args):
 
         if device_status(L.workspace):
             raise RuntimeError("device status word set during the timed run")
-    del graphs
+    del graphs, g  # graphs that hold NCCL calls must go before the process group
 
-    # ---- per-phase timing pass (eager, same steps) for the roofline --------
+    # ---- per-phase timing (CUDA graphs, same steps) for the roofline -------
+    # Without a sequence split, each timed step's selector launches (stats +
+    # final) and attention launches (attend + combine) for all layers are
+    # captured as two graphs and replayed between CUDA events, so the phase
+    # times hold no host launch gaps.  With a split, the unit is the whole
+    # split step of a layer, taken from the timed run above; one untimed
+    # eager pass then counts the selected pages.
+    from refinekv_b200 import sparse_attention
+
     counts_all = [L.summary.counts for L in layers]
     sel_tokens = torch.zeros((), device=dev, dtype=torch.int64)
     sel_pages = torch.zeros((), device=dev, dtype=torch.int64)
-    phase_events = []
-    for s in range(args.warmup, cap):
-        length.fill_(s + 1)
+
+    def count_selected():
+        nonlocal sel_pages, sel_tokens
         for L, counts in zip(layers, counts_all):
-            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            e0.record()
-            sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
-                             workspace=L.workspace, suffix_length=length,
-                             _phases=_native.PHASE_STATS | _native.PHASE_FINAL)
-            e1.record()
-            sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
-                             workspace=L.workspace, suffix_length=length,
-                             _phases=_native.PHASE_ATTEND | _native.PHASE_COMBINE)
-            e2.record()
-            phase_events.append((e0, e1, e2))
             sel = L.workspace["selected"]
             sel_pages += sel.sum()
             sel_tokens += (sel.to(torch.int64) * counts).sum()
+
+    select_ms, attend_ms = [], []
+    if split:
+        for s in range(args.warmup, cap):
+            length.fill_(s + 1)
+            for L in layers:
+                decode(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg, anchor_mask=L.anchor,
+                       workspace=L.workspace, suffix_length=length)
+            count_selected()
+        attend_ms = [us_per_step / 1e3 / args.layers]
+    else:
+        phase_graphs = []
+        for s in range(args.warmup, cap):
+            pair = (torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph())
+            for graph, phases in zip(pair, (_native.PHASE_STATS | _native.PHASE_FINAL,
+                                            _native.PHASE_ATTEND | _native.PHASE_COMBINE)):
+                with torch.cuda.graph(graph):
+                    for L in layers:
+                        sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg,
+                                         anchor_mask=L.anchor, workspace=L.workspace,
+                                         suffix_length=length, _phases=phases)
+            phase_graphs.append((s, pair))
+        del pair, graph
+        events = []
+        for s, (g_sel, g_att) in phase_graphs:
+            length.fill_(s + 1)
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record()
+            g_sel.replay()
+            e1.record()
+            g_att.replay()
+            e2.record()
+            events.append((e0, e1, e2))
+            count_selected()
+        torch.cuda.synchronize(dev)
+        select_ms = [a.elapsed_time(b) / args.layers for a, b, _ in events]
+        attend_ms = [b.elapsed_time(c) / args.layers for _, b, c in events]
+        del phase_graphs, g_sel, g_att
     torch.cuda.synchronize(dev)
-    select_ms = [a.elapsed_time(b) for a, b, _ in phase_events]
-    attend_ms = [b.elapsed_time(c) for _, b, c in phase_events]
-    launches = len(phase_events)  # = steps x layers
+    launches = args.steps * args.layers
     pages = int(sel_pages.item())
     tokens_refined = int(sel_tokens.item())
     D, G, B = args.head_dim, args.group, args.block_size
-    nb = -(-args.tokens // B)
+    nb = plan.blocks
     # algorithmic bytes (our formats, workspace scratch excluded)
-    suffix_total = args.layers * heads_local * sum(s + 1 for s in range(args.warmup, cap))
+    suffix_total = (args.layers * heads_local * sum(s + 1 for s in range(args.warmup, cap))
+                    if plan.holds_suffix else 0)
     qo_bytes = 2 * heads_local * G * D * 2
     attend_bytes = (tokens_refined + suffix_total) * D * 2 * 2 / launches + qo_bytes
     attend_avg_ms = statistics.mean(attend_ms)
@@ -459,18 +509,22 @@ def run_b200(args):
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
     traffic = profiled_traffic("attend_llama8b_128k.md")
     traffic_per_launch = None
-    if traffic is not None:
+    if traffic is not None and not split:
         dram_bytes, pages_profiled = traffic
         traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
-    step_gbs = sum_over_ranks(step_bytes, world) / (us_per_step * 1e-6) / 1e9
+    step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
+    step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9
 
     # ---- end to end through the public API with host buffers ---------------
     e2e = None
     if not args.skip_e2e:
         pin = dict(pin_memory=True)
         q_host = torch.stack([L.q for L in layers], 1).cpu().pin_memory()  # (cap, L, H, G, 1, D)
-        kv_host = torch.stack([torch.stack([L.suffix_k, L.suffix_v]) for L in layers]).cpu()
-        kv_host = kv_host.permute(3, 0, 1, 2, 4).contiguous().pin_memory()  # (cap, L, 2, H, D)
+        kv_host = None
+        if plan.holds_suffix:
+            kv_host = torch.stack([torch.stack([L.suffix_k, L.suffix_v]) for L in layers]).cpu()
+            kv_host = kv_host.permute(3, 0, 1, 2, 4).contiguous().pin_memory()  # (cap, L, 2, H, D)
+        reads_output = plan.seq_rank == 0  # every rank of a sequence group gets the output
         out_host = torch.empty(cap, args.layers, heads_local, G, 1, D, dtype=torch.bfloat16, **pin)
         q_dev = [torch.empty_like(L.q[0]) for L in layers]
         barrier(world)
@@ -481,23 +535,29 @@ def run_b200(args):
                 e_start.record()
             for li, L in enumerate(layers):
                 q_dev[li].copy_(q_host[s, li], non_blocking=True)
-                L.suffix_k[:, s].copy_(kv_host[s, li, 0], non_blocking=True)
-                L.suffix_v[:, s].copy_(kv_host[s, li, 1], non_blocking=True)
+                if kv_host is not None:
+                    L.suffix_k[:, s].copy_(kv_host[s, li, 0], non_blocking=True)
+                    L.suffix_v[:, s].copy_(kv_host[s, li, 1], non_blocking=True)
             for li, L in enumerate(layers):
-                res = sparse_attention(q_dev[li], L.summary, L.suffix_k[:, :s + 1],
-                                       L.suffix_v[:, :s + 1], cfg, anchor_mask=L.anchor,
-                                       workspace=L.workspace)
-                out_host[s, li].copy_(res.output, non_blocking=True)
+                res = decode(q_dev[li], L.summary,
+                             L.suffix_k[:, :s + 1] if plan.holds_suffix else None,
+                             L.suffix_v[:, :s + 1] if plan.holds_suffix else None, cfg,
+                             anchor_mask=L.anchor, workspace=L.workspace)
+                if reads_output:
+                    out_host[s, li].copy_(res.output, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()  # the host reads the step's outputs
         e_end.record()
         e_end.synchronize()
         e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
-        h2d = args.layers * (q_dev[0].numel() * 2 + 2 * heads_local * D * 2)
-        d2h = args.layers * heads_local * G * D * 2
+        h2d = args.layers * (q_dev[0].numel() * 2
+                             + (2 * heads_local * D * 2 if plan.holds_suffix else 0))
+        d2h = args.layers * heads_local * G * D * 2 if reads_output else 0
         e2e = {"value": round(e2e_ms * 1e3 / args.steps, 1), "unit": "us/step",
                "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
-               "path": "refinekv_b200.sparse_attention (eager, per layer) via the C ABI"}
+               "path": ("refinekv_b200.parallel.SplitDecode (eager, per layer) via the C ABI"
+                        if split else
+                        "refinekv_b200.sparse_attention (eager, per layer) via the C ABI")}
 
     # ---- CPU baseline: the reference algorithm on the host (rank 0, N=1) ---
     cpu = None
@@ -538,23 +598,29 @@ def run_b200(args):
             "dtype": "bf16",
             "data": "synthetic (seeded: LogNormal-scaled RoPE keys, N(0,1) values, 6 planted "
                     "blocks per layer; stands in for the paper's LongBench prompts)",
-            "config": workload_config(args, world),
+            "config": workload_config(args, world, plan),
             "hbm": {"achieved_gbs": round(step_gbs, 1), "peak_gbs": peak,
-                    "frac": round(step_gbs / peak, 4), "bytes_per_step":
-                        int(sum_over_ranks(step_bytes, world)), "note": peak_note},
+                    "frac": round(step_gbs / peak, 4), "bytes_per_step": int(step_bytes_all),
+                    "note": peak_note},
             "roofline": {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
                          "traffic": None if traffic_per_launch is None else int(traffic_per_launch),
-                         "kernel": f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}>",
+                         "kernel": ("rkv split decode step (selector, attention, exchanges, "
+                                    "merge)" if split else
+                                    f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}>"),
                          "algorithmic_bytes_per_launch": int(attend_bytes),
                          "avg_launch_us": round(attend_avg_ms * 1e3, 2),
                          "peak_note": peak_note},
-            "phase_us_per_layer": {"select": round(statistics.mean(select_ms) * 1e3, 2),
-                                   "attend": round(attend_avg_ms * 1e3, 2)},
+            "phase_us_per_layer": ({"split_step": round(attend_avg_ms * 1e3, 2)} if split else
+                                   {"select": round(statistics.mean(select_ms) * 1e3, 2),
+                                    "attend": round(attend_avg_ms * 1e3, 2)}),
             "selected_fraction": round(pages / (launches * heads_local * nb), 5),
+            # median over layers (layer 0 carries one-time module loading)
             "summarize_us_per_layer": round(statistics.median(summarize_ms) * 1e3, 1),
-            "gpu_launches": args.steps * args.layers * lib.rkv_decode_launch_count(
-                _native.PHASE_ALL),
+            # our kernels per layer-step: 4 (stats, final, attend, combine), or 5 under a
+            # sequence split (the same four plus the rank merge; NCCL's kernels not counted)
+            "gpu_launches": args.steps * args.layers * (
+                lib.rkv_decode_launch_count(_native.PHASE_ALL) + (1 if split else 0)),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "cpu_baseline": cpu,

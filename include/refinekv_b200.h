@@ -233,6 +233,27 @@ RKV_API int rkv_decode_launch_count(unsigned phases);
 #define RKV_SPLIT_STATS 1
 #define RKV_SPLIT_ATTEND 2
 #define RKV_SPLIT_MERGE 4
+#define RKV_SPLIT_FINAL 2 /* rkv_select_split: phase B over all ranks' slabs */
+
+/*
+ * Block selection of rkv_select under a sequence split (the prompt-anchor
+ * union at prefill): the same two-step exchange without attention.
+ *   rkv_select_split(..., RKV_SPLIT_STATS)  phase A into this rank's slab
+ *   all-gather of the exchange buffer        (ranks x slab bytes, in place)
+ *   rkv_select_split(..., RKV_SPLIT_FINAL)  phase B over all slabs; writes
+ *                                           `mask` for this rank's blocks
+ * Slab bytes come from rkv_select_split_slab (0 for an invalid geometry);
+ * queries_n and max_blocks must be equal on all ranks.  `mask`, `accumulate`
+ * and the workspace are as for rkv_select.
+ */
+RKV_API size_t rkv_select_split_slab(int64_t heads, int64_t group, int64_t max_blocks,
+                                     int64_t queries);
+RKV_API int rkv_select_split(const rkv_summary* summary, const void* queries, int query_dtype,
+                             int64_t queries_n, int64_t group, float eps, int reduction,
+                             uint8_t* mask, int accumulate, void* workspace,
+                             size_t workspace_size, int64_t ranks, int64_t rank,
+                             int64_t max_blocks, void* exchange, size_t exchange_size,
+                             unsigned stage, void* stream);
 
 /* Slab sizes (bytes, multiples of 256) of one rank in the two exchange regions. */
 RKV_API int rkv_split_exchange_slabs(int64_t heads, int64_t group, int64_t max_blocks,

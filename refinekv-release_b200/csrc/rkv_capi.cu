@@ -195,15 +195,18 @@ struct SplitGeometry {
   size_t output_slab = 0;  // bytes: (rows, 2) then (rows, dim) fp32
 };
 
-SplitGeometry split_geometry(int64_t heads, int64_t group, int64_t max_blocks, int64_t dim) {
+// `instances` query instances per rank (rkv_select_split); dim == 0 for
+// selection only (no output slab).
+SplitGeometry split_geometry(int64_t heads, int64_t group, int64_t max_blocks, int64_t dim,
+                             int64_t instances = 1) {
   SplitGeometry g;
   int per = 1;
   split(static_cast<int>(cdiv(max_blocks, kSelectTile)),
-        static_cast<int>(cdiv(kSplitStatsCtas, heads)), &g.parts_a, &per);
+        static_cast<int>(cdiv(kSplitStatsCtas, heads * instances)), &g.parts_a, &per);
   const size_t rows = static_cast<size_t>(heads) * group;
-  g.stats_slab = up256(rows * g.parts_a * 16);
-  g.ml_bytes = up256(rows * 8);
-  g.output_slab = g.ml_bytes + up256(rows * dim * 4);
+  g.stats_slab = up256(rows * instances * g.parts_a * 16);
+  g.ml_bytes = dim > 0 ? up256(rows * 8) : 0;
+  g.output_slab = dim > 0 ? g.ml_bytes + up256(rows * dim * 4) : 0;
   return g;
 }
 
@@ -541,10 +544,15 @@ size_t rkv_select_workspace_size(int64_t heads, int64_t group, int64_t blocks, i
   return pl.bytes;
 }
 
-int rkv_select(const rkv_summary* summary, const void* queries, int query_dtype, int64_t queries_n,
-               int64_t group, float eps, int reduction, uint8_t* mask, int accumulate,
-               void* workspace, size_t workspace_size, void* stream) {
-  g_last_error.clear();
+}  // extern "C"
+
+namespace {
+
+// rkv_select, or one rank's stage of rkv_select_split when `split` is given.
+int select_impl(const rkv_summary* summary, const void* queries, int query_dtype,
+                int64_t queries_n, int64_t group, float eps, int reduction, uint8_t* mask,
+                int accumulate, void* workspace, size_t workspace_size, unsigned phases,
+                void* stream, const SplitTarget* split) {
   int rc = check_selection_args(summary, queries, query_dtype, group, eps, reduction);
   if (rc != RKV_OK) return rc;
   if (queries_n < 1 || queries_n * summary->heads > 65535) {
@@ -553,19 +561,80 @@ int rkv_select(const rkv_summary* summary, const void* queries, int query_dtype,
   if (mask == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "mask is null");
   Plan pl;
   rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
-                 summary->block_size, queries_n, false);
+                 summary->block_size, queries_n, false, split ? split->geo.parts_a : 0);
   if (rc != RKV_OK) return rc;
   if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int or_mode = accumulate;
   if (!accumulate && queries_n > 1) {
-    cudaError_t err =
-        cudaMemsetAsync(mask, 0, static_cast<size_t>(summary->heads) * summary->blocks, st);
-    if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+    if (phases & RKV_PHASE_FINAL) {
+      cudaError_t err =
+          cudaMemsetAsync(mask, 0, static_cast<size_t>(summary->heads) * summary->blocks, st);
+      if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
+    }
     or_mode = 1;
   }
   return run_selector(pl, summary, queries, query_dtype, queries_n, group, eps, reduction, nullptr,
-                      mask, or_mode, workspace, false, RKV_PHASE_STATS | RKV_PHASE_FINAL, st);
+                      mask, or_mode, workspace, false, phases, st, split);
+}
+
+}  // namespace
+
+extern "C" {
+
+int rkv_select(const rkv_summary* summary, const void* queries, int query_dtype, int64_t queries_n,
+               int64_t group, float eps, int reduction, uint8_t* mask, int accumulate,
+               void* workspace, size_t workspace_size, void* stream) {
+  g_last_error.clear();
+  return select_impl(summary, queries, query_dtype, queries_n, group, eps, reduction, mask,
+                     accumulate, workspace, workspace_size, RKV_PHASE_STATS | RKV_PHASE_FINAL,
+                     stream, nullptr);
+}
+
+size_t rkv_select_split_slab(int64_t heads, int64_t group, int64_t max_blocks, int64_t queries) {
+  if (heads <= 0 || heads > (1 << 16) || group < 1 || group > kMaxGroup || max_blocks <= 0 ||
+      max_blocks > (1LL << 26) || queries < 1 || queries * heads > 65535) {
+    return 0;
+  }
+  return split_geometry(heads, group, max_blocks, 0, queries).stats_slab;
+}
+
+int rkv_select_split(const rkv_summary* summary, const void* queries, int query_dtype,
+                     int64_t queries_n, int64_t group, float eps, int reduction, uint8_t* mask,
+                     int accumulate, void* workspace, size_t workspace_size, int64_t ranks,
+                     int64_t rank, int64_t max_blocks, void* exchange, size_t exchange_size,
+                     unsigned stage, void* stream) {
+  g_last_error.clear();
+  if (summary == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
+  if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");
+  }
+  if (max_blocks < summary->blocks || max_blocks > (1LL << 26)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "max_blocks must be at least this rank's block count");
+  }
+  if (queries_n < 1 || queries_n * summary->heads > 65535) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "queries must be 1..65535/heads");
+  }
+  if (stage == 0 || stage > (RKV_SPLIT_STATS | RKV_SPLIT_FINAL)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "bad split stage");
+  }
+  SplitTarget target;
+  target.ranks = static_cast<int>(ranks);
+  target.rank = static_cast<int>(rank);
+  target.geo = split_geometry(summary->heads, group, max_blocks, 0, queries_n);
+  target.exchange = static_cast<char*>(exchange);
+  const size_t need = static_cast<size_t>(ranks) * target.geo.stats_slab;
+  if (exchange == nullptr || exchange_size < need) {
+    return fail(RKV_ERR_WORKSPACE, "exchange buffer is missing or smaller than the required size " +
+                                       std::to_string(need));
+  }
+  if ((reinterpret_cast<uintptr_t>(exchange) & 255u) != 0) {
+    return fail(RKV_ERR_ALIGNMENT, "exchange buffer must be 256-byte aligned");
+  }
+  const unsigned phases = ((stage & RKV_SPLIT_STATS) ? RKV_PHASE_STATS : 0u) |
+                          ((stage & RKV_SPLIT_FINAL) ? RKV_PHASE_FINAL : 0u);
+  return select_impl(summary, queries, query_dtype, queries_n, group, eps, reduction, mask,
+                     accumulate, workspace, workspace_size, phases, stream, &target);
 }
 
 size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,

@@ -36,6 +36,7 @@ PHASE_ALL = 15
 SPLIT_STATS = 1
 SPLIT_ATTEND = 2
 SPLIT_MERGE = 4
+SPLIT_FINAL = 2
 
 #: Every symbol the header declares.
 EXPORTS = (
@@ -46,6 +47,8 @@ EXPORTS = (
     "rkv_decode",
     "rkv_decode_static",
     "rkv_decode_launch_count",
+    "rkv_select_split_slab",
+    "rkv_select_split",
     "rkv_split_exchange_slabs",
     "rkv_decode_split",
     "rkv_last_error",
@@ -97,6 +100,11 @@ _SIGNATURES = {
                                          c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
                                          c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
+    "rkv_select_split_slab": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64]),
+    "rkv_select_split": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64, c_i64,
+                                        ctypes.c_float, ctypes.c_int, c_ptr, ctypes.c_int, c_ptr,
+                                        ctypes.c_size_t, c_i64, c_i64, c_i64, c_ptr,
+                                        ctypes.c_size_t, ctypes.c_uint, c_ptr]),
     "rkv_split_exchange_slabs": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64,
                                                 ctypes.POINTER(ctypes.c_size_t),
                                                 ctypes.POINTER(ctypes.c_size_t)]),

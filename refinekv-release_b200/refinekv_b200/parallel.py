@@ -178,6 +178,47 @@ def exchange_slabs(heads: int, group: int, max_blocks: int, head_dim: int) -> tu
     return stats.value, output.value
 
 
+@torch.no_grad()
+def select_blocks_union_split(queries, summary: BlockSummary, config: RefineKVConfig,
+                              plan: ShardPlan, group, *, workspace=None) -> torch.Tensor:
+    """``select_blocks_union`` on a rank of a sequence group: this rank's blocks of the OR mask.
+
+    ``queries`` is (anchors, kv_heads, group, 1, head_dim), the same on every
+    rank of the group; the selector normalisers are merged over the group
+    (``rkv_select_split``), so the mask equals the one-GPU mask's slice.
+    """
+    from .attention import select_blocks_union
+
+    if plan.seq_ranks == 1:
+        return select_blocks_union(queries, summary, config, workspace=workspace)
+    if queries.ndim != 5 or queries.shape[3] != 1:
+        raise ValueError("queries must have shape (anchors, kv_heads, group_size, 1, head_dim)")
+    _validate(queries[0], summary, config)
+    _check_backend(queries[0], config)
+    count, heads, group_size, _, dim = queries.shape
+    dev = queries.device
+    q = queries.reshape(count, heads, group_size, dim).contiguous()
+    mask = torch.empty(heads, summary.num_blocks, device=dev, dtype=torch.uint8)
+    lib = _native.load()
+    slab = lib.rkv_select_split_slab(heads, group_size, plan.max_blocks, count)
+    if slab == 0:
+        raise ValueError("selection geometry out of range")
+    ranks = plan.seq_ranks
+    with torch.cuda.device(dev):
+        nbytes = lib.rkv_select_workspace_size(heads, group_size, summary.num_blocks, dim, count)
+        scratch = _scratch(workspace, f"rkv_select_scratch_{count}", nbytes, dev)
+        exchange = _scratch(workspace, f"rkv_select_exchange_{count}", ranks * slab, dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        args = (summary.abi(), q.data_ptr(), _query_code(q), count, group_size, config.eps,
+                _native.GQA_CODES[config.gqa_reduction], mask.data_ptr(), 0, scratch.data_ptr(),
+                scratch.numel(), ranks, plan.seq_rank, plan.max_blocks, exchange.data_ptr(),
+                exchange.numel())
+        _native.check(lib.rkv_select_split(*args, _native.SPLIT_STATS, stream))
+        all_gather_slabs(exchange[:ranks * slab], slab, plan.seq_rank, group)
+        _native.check(lib.rkv_select_split(*args, _native.SPLIT_FINAL, stream))
+    return mask.view(torch.bool)
+
+
 class SplitDecode:
     """One layer's decode step on a rank of a sequence group.
 

@@ -26,6 +26,7 @@ import torch.distributed as dist  # noqa: E402
 
 from oracle import refinekv_oracle as ora  # noqa: E402
 from refinekv_b200 import RefineKVConfig, build_summary, parallel, sparse_attention, synthetic  # noqa: E402
+from refinekv_b200.attention import select_blocks_union  # noqa: E402
 
 
 def main() -> None:
@@ -47,6 +48,9 @@ def main() -> None:
     seq_group = parallel.new_seq_group(plan)
     k, v = parallel.shard_prompt(data.keys, data.values, plan)
     summary = parallel.build_shard_summary(k, v, cfg, plan, seq_group)
+    anchors = (synthetic.make_queries(21, 0, -1, data.planted_mean, group, 8, torch.float32)
+               * 32.0).to(torch.bfloat16)
+    anchor = parallel.select_blocks_union_split(anchors, summary, cfg, plan, seq_group)
     decode = parallel.SplitDecode(plan, seq_group)
     mine_k = ks if plan.holds_suffix else None
     mine_v = vs if plan.holds_suffix else None
@@ -55,9 +59,17 @@ def main() -> None:
     s_cpu = ora.as_cpu_summary(full)
     margin = ora.margin_blocks(q.cpu(), s_cpu, cfg.eps, cfg.gqa_reduction)
     failures = []
+    full_anchor = select_blocks_union(anchors, full, cfg)
+    anchor_margin = torch.zeros_like(margin)
+    for a in anchors.cpu():
+        anchor_margin |= ora.margin_blocks(a, s_cpu, cfg.eps, cfg.gqa_reduction)
+    lo, hi = plan.block_lo, plan.block_hi
+    if ((anchor.cpu() != full_anchor[:, lo:hi].cpu()) & ~anchor_margin[:, lo:hi]).any():
+        failures.append("anchor union differs outside the margin")
 
     def check(out, selected, n, what):
-        want = sparse_attention(q, full, ks[:, :n], vs[:, :n], cfg, return_selected=True)
+        want = sparse_attention(q, full, ks[:, :n], vs[:, :n], cfg, anchor_mask=full_anchor,
+                                return_selected=True)
         lo, hi = plan.block_lo, plan.block_hi
         bad = (selected.cpu() != want.selected[:, lo:hi].cpu()) & ~margin[:, lo:hi]
         if bad.any():
@@ -67,19 +79,21 @@ def main() -> None:
             failures.append(f"{what}: max abs error {err}")
 
     workspace = {}
-    res = decode(q, summary, mine_k, mine_v, cfg, workspace=workspace, return_selected=True)
+    res = decode(q, summary, mine_k, mine_v, cfg, anchor_mask=anchor, workspace=workspace,
+                 return_selected=True)
     check(res.output, res.selected, cap, "eager")
 
     length = torch.tensor(cap, device=dev, dtype=torch.int32)
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
-        decode(q, summary, mine_k, mine_v, cfg, workspace=workspace, suffix_length=length)
+        decode(q, summary, mine_k, mine_v, cfg, anchor_mask=anchor, workspace=workspace,
+               suffix_length=length)
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        out = decode(q, summary, mine_k, mine_v, cfg, workspace=workspace,
+        out = decode(q, summary, mine_k, mine_v, cfg, anchor_mask=anchor, workspace=workspace,
                      suffix_length=length).output
     for n in (3, 11):
         length.fill_(n)

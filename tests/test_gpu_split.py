@@ -139,6 +139,52 @@ def test_emulated_split_with_anchors_and_device_suffix_length():
     _check(outs, mask, q, data, ks[:, :11], vs[:, :11], cfg, anchor=anchor)
 
 
+@pytest.mark.parametrize("ranks", [2, 3])
+def test_emulated_anchor_union_split(ranks):
+    """rkv_select_split over several anchor queries equals the one-GPU union outside the margin."""
+    from refinekv_b200.attention import select_blocks_union
+
+    heads, group, dim, block, tokens, count = 4, 7, 128, 64, 7000, 4
+    cfg = RefineKVConfig(block_size=block, eps=3.0, gqa_reduction="max")
+    data = synthetic.make_layer(13, 0, heads, tokens, dim, block, device=DEV)
+    anchors = (synthetic.make_queries(13, 0, -1, data.planted_mean, group, count, torch.float32)
+               * 32.0).to(torch.bfloat16)
+    full = build_summary(data.keys, data.values, cfg)
+    want = select_blocks_union(anchors, full, cfg)
+    plans = [parallel.plan_shards(heads, tokens, block, ranks, r, seq_ranks=ranks)
+             for r in range(ranks)]
+    summaries = [build_summary(*parallel.shard_prompt(data.keys, data.values, p), cfg)
+                 for p in plans]
+    vmax = torch.stack([x.max_value_norm for x in summaries]).amax(0)
+    for x in summaries:
+        x.max_value_norm.copy_(vmax)
+    lib = _native.load()
+    slab = lib.rkv_select_split_slab(heads, group, plans[0].max_blocks, count)
+    exchange = torch.zeros(ranks * slab, device=DEV, dtype=torch.uint8)
+    q = anchors.reshape(count, heads, group, dim).contiguous()
+    calls, masks = [], []
+    for p, x in zip(plans, summaries):
+        ws = torch.zeros(lib.rkv_select_workspace_size(heads, group, x.num_blocks, dim, count),
+                         device=DEV, dtype=torch.uint8)
+        m = torch.full((heads, x.num_blocks), 7, device=DEV, dtype=torch.uint8)
+        calls.append((x.abi(), q.data_ptr(), 0, count, group, cfg.eps, 1, m.data_ptr(), 0,
+                      ws.data_ptr(), ws.numel(), ranks, p.seq_rank, p.max_blocks,
+                      exchange.data_ptr(), exchange.numel(), ws))
+        masks.append(m)
+    stream = torch.cuda.current_stream().cuda_stream
+    for stage in (_native.SPLIT_STATS, _native.SPLIT_FINAL):
+        for c in calls:
+            _native.check(lib.rkv_select_split(*c[:-1], stage, stream))
+    torch.cuda.synchronize()
+    got = torch.cat(masks, 1).bool().cpu()
+    s_cpu = ora.as_cpu_summary(full)
+    margin = torch.zeros_like(got)
+    for a in anchors.cpu():
+        margin |= ora.margin_blocks(a, s_cpu, cfg.eps, cfg.gqa_reduction)
+    assert 0 < int(want.sum()) < want.numel()
+    assert not ((got != want.cpu()) & ~margin).any()
+
+
 def test_split_rejects_bad_geometry():
     lib = _native.load()
     cfg = RefineKVConfig(eps=0.01)
