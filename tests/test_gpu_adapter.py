@@ -1,0 +1,146 @@
+"""Transformers adapter on the B200 kernels (the reference's CUDA adapter tests, ``test_transformers.py:144-219``).
+
+Tiny random-init Llama/Qwen2 models as in the reference, but with head_dim
+64 (hidden 256, 4 query / 2 KV heads): the CUDA kernels cover head
+dimensions 64-256.  Checks: dynamic and static caches give the same tokens;
+CUDA-graph decode gives the eager tokens (including a repetition penalty and,
+beyond the reference, dense ``full_attention_layers`` under the graph); the
+decode really runs through librefinekv_b200 (call counts and stats).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from refinekv_b200 import RefineKV, RefineKVConfig  # noqa: E402
+from refinekv_b200.integrations import transformers as adapter  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(family="llama", *, hidden=256, heads=4, kv_heads=2, layers=2, vocab=64):
+    torch.manual_seed(9)
+    config_type, model_type = (
+        (transformers.LlamaConfig, transformers.LlamaForCausalLM) if family == "llama"
+        else (transformers.Qwen2Config, transformers.Qwen2ForCausalLM))
+    config = config_type(vocab_size=vocab, hidden_size=hidden, intermediate_size=2 * hidden,
+                         num_hidden_layers=layers, num_attention_heads=heads,
+                         num_key_value_heads=kv_heads, pad_token_id=0, eos_token_id=None)
+    return model_type(config).eval().to("cuda", torch.bfloat16)
+
+
+def _options(length, new_tokens=8):
+    ids = torch.arange(length, device="cuda")[None] % 61 + 3
+    return dict(input_ids=ids, attention_mask=torch.ones_like(ids), max_new_tokens=new_tokens,
+                min_new_tokens=new_tokens, eos_token_id=None, forced_eos_token_id=None,
+                do_sample=False)
+
+
+@pytest.fixture
+def counted(monkeypatch):
+    calls = {"decode": 0, "summaries": 0}
+    real_decode, real_summary = adapter.sparse_attention, adapter.build_summary
+
+    def decode(*args, **kwargs):
+        calls["decode"] += 1
+        return real_decode(*args, **kwargs)
+
+    def summary(*args, **kwargs):
+        calls["summaries"] += 1
+        return real_summary(*args, **kwargs)
+
+    monkeypatch.setattr(adapter, "sparse_attention", decode)
+    monkeypatch.setattr(adapter, "build_summary", summary)
+    return calls
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_dynamic_and_static_caches_give_the_same_tokens(family, counted):
+    model = _model(family)
+    config = RefineKVConfig(eps=1e6, anchor_tokens=2, collect_stats=True)
+    opts = _options(39, 4)
+    with RefineKV(model, config) as session:
+        dynamic = model.generate(**opts)
+        assert session.stats["decode_attention_calls"] == 6
+        assert 0 < session.stats["equivalent_access_ratio"] <= 1
+    with RefineKV(model, config):
+        static = model.generate(**opts, cache_implementation="static")
+    assert torch.equal(dynamic, static)
+    assert counted["decode"] == 12 and counted["summaries"] == 4
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+@pytest.mark.parametrize("reduction,anchors", [("mean", 0), ("any", 2)])
+def test_cuda_graph_decode_matches_eager(family, reduction, anchors):
+    model = _model(family)
+    if family == "qwen2":
+        model.generation_config.repetition_penalty = 1.05
+    config = RefineKVConfig(eps=0.01, gqa_reduction=reduction, anchor_tokens=anchors)
+    requests = []
+    for length in (39, 17, 300):
+        opts = _options(length)
+        with RefineKV(model, config):
+            requests.append((opts, model.generate(**opts)))
+    with RefineKV(model, config, cuda_graph=True):
+        for opts, eager in requests:
+            assert torch.equal(model.generate(**opts), eager)
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_cuda_graph_with_dense_layers_matches_eager(family):
+    """full_attention_layers under CUDA graphs (the reference refuses this combination)."""
+    model = _model(family, layers=3)
+    config = RefineKVConfig(eps=0.05, anchor_tokens=2, full_attention_layers=1)
+    opts = _options(200)
+    with RefineKV(model, config):
+        eager = model.generate(**opts)
+    with RefineKV(model, config, cuda_graph=True):
+        assert torch.equal(model.generate(**opts), eager)
+
+
+def test_full_layers_match_native_generation():
+    model = _model()
+    opts = _options(39, 4)
+    with torch.inference_mode():
+        native = model.generate(**opts)
+    with RefineKV(model, RefineKVConfig(full_attention_layers=2, collect_stats=True)) as session:
+        assert torch.equal(model.generate(**opts), native)
+        assert session.stats["equivalent_access_ratio"] == 1
+
+
+def test_eps_zero_decode_logits_track_native():
+    """eps=0 expands every page: one RefineKV decode step is dense attention by another kernel."""
+    from transformers import DynamicCache
+
+    model = _model(hidden=1024, heads=8, kv_heads=2, layers=2, vocab=512)  # head_dim 128
+    ids = torch.arange(2048, device="cuda")[None] % 509 + 3
+
+    def prefill_and_step():
+        cache = DynamicCache(config=model.config)
+        first = model(input_ids=ids, past_key_values=cache, use_cache=True).logits[:, -1:]
+        token = first.argmax(-1)
+        return token, model(input_ids=token, past_key_values=cache,
+                            use_cache=True).logits[0, -1].float()
+
+    with torch.inference_mode():
+        token, native = prefill_and_step()
+    with RefineKV(model, RefineKVConfig(eps=0)) as session:
+        token2, refined = prefill_and_step()
+        assert all(state.summary is not None for state in session._layers.values())
+    assert torch.equal(token, token2)
+    scale = float(native.abs().max())
+    assert float((refined - native).abs().max()) <= 0.02 * scale
+
+
+def test_cuda_graph_rejects_stats_and_variable_output():
+    model = _model()
+    ids = torch.tensor([[3, 4, 5]], device="cuda")
+    with RefineKV(model, RefineKVConfig(collect_stats=True), cuda_graph=True):
+        with pytest.raises(ValueError, match="no stats"):
+            model.generate(input_ids=ids, max_new_tokens=4, min_new_tokens=4, eos_token_id=None)
+    with RefineKV(model, cuda_graph=True):
+        with pytest.raises(ValueError, match="fixed output"):
+            model.generate(input_ids=ids, max_new_tokens=4, eos_token_id=None)
