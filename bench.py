@@ -73,6 +73,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-dense", action="store_true")
     ap.add_argument("--cpu-samples", type=int, default=12)
     args = ap.parse_args()
     if args.warmup < 0 or args.steps < 1:
@@ -515,7 +516,52 @@ def run_b200(args):
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
     step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9
 
+    # ---- dense decode attention over the same prompt KV (reference point) --
+    # The dense alternative RefineKV competes with: one query token against
+    # every prompt K/V row of each layer, PyTorch SDPA (GQA), replayed from a
+    # CUDA graph over all layers.
+    dense = None
+    if not split and not args.skip_dense:
+        import torch.nn.functional as F
+
+        qd = [L.q[cap - 1].reshape(1, heads_local * args.group, 1, args.head_dim) for L in layers]
+        kd = [L.keys.unsqueeze(0) for L in layers]
+        vd = [L.values.unsqueeze(0) for L in layers]
+
+        def dense_step():
+            for q_, k_, v_ in zip(qd, kd, vd):
+                F.scaled_dot_product_attention(q_, k_, v_, enable_gqa=True)
+
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            dense_step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        dense_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(dense_graph):
+            dense_step()
+        for _ in range(3):
+            dense_graph.replay()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        d0.record()
+        for _ in range(reps):
+            dense_graph.replay()
+        d1.record()
+        d1.synchronize()
+        del dense_graph
+        dense_layer_us = d0.elapsed_time(d1) * 1e3 / (reps * args.layers)
+        dense = {"us_per_layer": round(dense_layer_us, 2),
+                 "us_per_step": round(dense_layer_us * args.layers, 1),
+                 "impl": "torch.nn.functional.scaled_dot_product_attention (enable_gqa), bf16, "
+                         "prompt K/V only, CUDA graph over all layers"}
+
     # ---- end to end through the public API with host buffers ---------------
+    # Each step copies its queries and new K/V token from pinned host memory,
+    # runs every layer's decode through the public call and copies the
+    # outputs back; the host waits for them before the next step.  As in the
+    # adapter's CUDA-graph decode, each step is one captured graph (copies
+    # included); the same steps issued eagerly, call by call, are reported
+    # beside it.
     e2e = None
     if not args.skip_e2e:
         pin = dict(pin_memory=True)
@@ -527,37 +573,63 @@ def run_b200(args):
         reads_output = plan.seq_rank == 0  # every rank of a sequence group gets the output
         out_host = torch.empty(cap, args.layers, heads_local, G, 1, D, dtype=torch.bfloat16, **pin)
         q_dev = [torch.empty_like(L.q[0]) for L in layers]
-        barrier(world)
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        for s in range(cap):
-            if s == args.warmup:
-                barrier(world)
-                e_start.record()
+
+        def e2e_step(s, *, graph_mode):
+            if graph_mode:
+                length.fill_(s + 1)
             for li, L in enumerate(layers):
                 q_dev[li].copy_(q_host[s, li], non_blocking=True)
                 if kv_host is not None:
                     L.suffix_k[:, s].copy_(kv_host[s, li, 0], non_blocking=True)
                     L.suffix_v[:, s].copy_(kv_host[s, li, 1], non_blocking=True)
             for li, L in enumerate(layers):
-                res = decode(q_dev[li], L.summary,
-                             L.suffix_k[:, :s + 1] if plan.holds_suffix else None,
-                             L.suffix_v[:, :s + 1] if plan.holds_suffix else None, cfg,
-                             anchor_mask=L.anchor, workspace=L.workspace)
+                if graph_mode:
+                    res = decode(q_dev[li], L.summary, L.suffix_k, L.suffix_v, cfg,
+                                 anchor_mask=L.anchor, workspace=L.workspace,
+                                 suffix_length=length)
+                else:
+                    res = decode(q_dev[li], L.summary,
+                                 L.suffix_k[:, :s + 1] if plan.holds_suffix else None,
+                                 L.suffix_v[:, :s + 1] if plan.holds_suffix else None, cfg,
+                                 anchor_mask=L.anchor, workspace=L.workspace)
                 if reads_output:
                     out_host[s, li].copy_(res.output, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()  # the host reads the step's outputs
-        e_end.record()
-        e_end.synchronize()
-        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+
+        def timed(run_step):
+            barrier(world)
+            e_start = torch.cuda.Event(enable_timing=True)
+            e_end = torch.cuda.Event(enable_timing=True)
+            for s in range(cap):
+                if s == args.warmup:
+                    barrier(world)
+                    e_start.record()
+                run_step(s)
+                torch.cuda.current_stream(dev).synchronize()  # the host reads the step's outputs
+            e_end.record()
+            e_end.synchronize()
+            return max_over_ranks(e_start.elapsed_time(e_end), world) * 1e3 / args.steps
+
+        eager_us = timed(lambda s: e2e_step(s, graph_mode=False))
+        e2e_graphs = []
+        for s in range(cap):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                e2e_step(s, graph_mode=True)
+            e2e_graphs.append(graph)
+        del graph
+        graph_us = timed(lambda s: e2e_graphs[s].replay())
+        del e2e_graphs
         h2d = args.layers * (q_dev[0].numel() * 2
                              + (2 * heads_local * D * 2 if plan.holds_suffix else 0))
         d2h = args.layers * heads_local * G * D * 2 if reads_output else 0
-        e2e = {"value": round(e2e_ms * 1e3 / args.steps, 1), "unit": "us/step",
+        api = "refinekv_b200.parallel.SplitDecode" if split else "refinekv_b200.sparse_attention"
+        e2e = {"value": round(graph_us, 1), "unit": "us/step",
                "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
-               "path": ("refinekv_b200.parallel.SplitDecode (eager, per layer) via the C ABI"
-                        if split else
-                        "refinekv_b200.sparse_attention (eager, per layer) via the C ABI")}
+               "path": f"{api} via the C ABI, one CUDA graph per step (pinned-host copies "
+                       "inside), host waits for each step's outputs",
+               "eager_value": round(eager_us, 1),
+               "eager_path": f"{api}, eager call per layer, same copies and waits"}
 
     # ---- CPU baseline: the reference algorithm on the host (rank 0, N=1) ---
     cpu = None
@@ -623,6 +695,7 @@ def run_b200(args):
                 lib.rkv_decode_launch_count(_native.PHASE_ALL) + (1 if split else 0)),
             "clocks": clocks.summary(),
             "e2e": e2e,
+            "dense_attention": dense,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
