@@ -509,20 +509,39 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   if (tokens > (1LL << 31) - 1 || heads > (1 << 16)) {
     return fail(RKV_ERR_UNSUPPORTED, "prompt is larger than the kernels index");
   }
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc != RKV_OK) return rc;
+  SummarizeMaps maps;
+  rc = rows_map(&maps.keys, keys, head_dim, tokens, heads, key_token_stride, key_head_stride,
+                static_cast<int>(block_size), "keys");
+  if (rc != RKV_OK) return rc;
+  rc = rows_map(&maps.values, values, head_dim, tokens, heads, value_token_stride,
+                value_head_stride, static_cast<int>(block_size), "values");
+  if (rc != RKV_OK) return rc;
+  // Persistent grid: one CTA per SM with about 128 KB of TMA ring per CTA,
+  // as many warps as fit (3..8) with one or more stages each.
+  const int64_t stage = 2 * block_size * head_dim * 2;
+  const int warps = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(8, 131072 / stage)));
+  const int stages =
+      static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, 131072 / (warps * stage))));
+  const size_t smem = summarize_smem_bytes(static_cast<int>(head_dim), static_cast<int>(block_size),
+                                           warps, stages);
+  if (smem > static_cast<size_t>(dev.smem_optin)) {
+    return fail(RKV_ERR_UNSUPPORTED, "summarizer stages do not fit in shared memory");
+  }
+  const int64_t blocks = cdiv(tokens, block_size);
+  const int ctas = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(dev.sms, cdiv(heads * blocks, warps))));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t err = cudaMemsetAsync(max_value_norm, 0, static_cast<size_t>(heads) * 4, st);
   if (err != cudaSuccess) return cuda_fail(err, "cudaMemsetAsync");
   SummarizeParams p = {};
-  p.keys = keys;
-  p.values = values;
-  p.key_head_stride = key_head_stride;
-  p.key_token_stride = key_token_stride;
-  p.value_head_stride = value_head_stride;
-  p.value_token_stride = value_token_stride;
   p.heads = static_cast<int>(heads);
   p.tokens = static_cast<int>(tokens);
   p.block_size = static_cast<int>(block_size);
-  p.blocks = static_cast<int>(cdiv(tokens, block_size));
+  p.blocks = static_cast<int>(blocks);
+  p.stages = stages;
   p.key_pages = key_pages_out;
   p.value_pages = value_pages_out;
   p.key_mean = key_mean;
@@ -531,7 +550,7 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   p.value_norm = value_norm;
   p.max_value_norm = max_value_norm;
   p.counts = counts;
-  err = launch_summarize(p, static_cast<int>(head_dim), st);
+  err = launch_summarize(maps, p, static_cast<int>(head_dim), ctas, warps, smem, st);
   if (err != cudaSuccess) return cuda_fail(err, "summarize launch");
   return RKV_OK;
 }

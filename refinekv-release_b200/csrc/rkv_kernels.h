@@ -13,12 +13,14 @@ constexpr int kMaxGroup = 16;    // GQA rows per KV head (two n8 tiles)
 
 enum Reduction { kMean = 0, kMax = 1, kAny = 2 };
 
+struct SummarizeMaps {
+  CUtensorMap keys;    // (dim, tokens, heads) bf16, [block_size x 64] boxes, 128B swizzle
+  CUtensorMap values;
+};
+
 struct SummarizeParams {
-  const void* keys;
-  const void* values;
-  int64_t key_head_stride, key_token_stride;      // elements
-  int64_t value_head_stride, value_token_stride;  // elements
   int heads, tokens, blocks, block_size;
+  int stages;         // TMA stages per warp
   void* key_pages;    // optional (heads, blocks, block, dim) copy, zero padded
   void* value_pages;  // optional
   void* key_mean;     // bf16 (heads, blocks, dim)
@@ -150,7 +152,8 @@ struct MergeParams {
 };
 
 // Host launchers (defined in the .cu files); return a cudaError_t.
-cudaError_t launch_summarize(const SummarizeParams& p, int dim, cudaStream_t stream);
+cudaError_t launch_summarize(const SummarizeMaps& maps, const SummarizeParams& p, int dim,
+                             int ctas, int warps, size_t smem, cudaStream_t stream);
 cudaError_t launch_stats(const StatsMaps& maps, const StatsParams& p, int dim, int warps,
                          size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, int warps,
@@ -166,6 +169,7 @@ cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, boo
 cudaError_t ensure_smem_limit(const void* func, size_t bytes);
 
 // Shared-memory footprint of each kernel for a given stage count.
+size_t summarize_smem_bytes(int dim, int block, int warps, int stages);
 size_t stats_smem_bytes(int dim, int warps, int stages, int group);
 size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta);
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,

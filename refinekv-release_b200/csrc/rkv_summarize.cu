@@ -1,12 +1,19 @@
 // Post-prefill block summarizer (reference: src/refinekv/summary.py:46-113).
 //
-// One lane group per (head, page): each lane owns 8 channels (one 16-byte
-// vector) of every row of the page.  Pass 1 streams the page once from HBM
-// and accumulates FP32 sums of K and V, the per-channel K range and the
-// largest V row norm; it also writes the zero-padded page copy when the
-// caller needs one.  Pass 2 re-reads the (now L2-resident) K rows for the
-// centred radius.  HBM traffic: K and V once, plus the optional page copy
-// and the ~5% of summaries written.
+// Persistent grid, one CTA per SM; the (head, page) list is cut into equal
+// contiguous ranges, one per CTA, and warp w of a CTA takes pages
+// lo + w + j * warps.  Each warp streams its pages through its own ring of
+// TMA stages (K page | V page, [rows x 64] boxes, 128-byte swizzle; rows past
+// the prompt read as zeros) and computes everything from shared memory, so
+// HBM sees K and V exactly once:
+//   * lane per 16-byte channel chunk: FP32 sums of K and V, per-channel K
+//     range -> bf16 means, squared half widths, 1/width;
+//   * lane per row: V row norms and the centred, width-normalised squared
+//     distance of every real K row -> the page's value norm and radius;
+//   * the bf16 ellipsoid (radius^2 * width^2 * (1 + 2^-8)), the optional
+//     zero-padded page copy, counts and the per-head maximum value norm.
+// Statistics over rows are reduced in a different order than the reference's
+// torch reductions (FP32); the bf16 outputs agree to an ulp.
 #include "rkv_device.cuh"
 #include "rkv_kernels.h"
 
@@ -35,186 +42,240 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
 __device__ __forceinline__ float nan_min(float a, float b) { return (b < a || b != b) ? b : a; }
 
-template <int D>
-__global__ void __launch_bounds__(256, 2) summarize_kernel(const SummarizeParams p) {
-  constexpr int kChunks = D / 8;
-  constexpr int kLanes = kChunks <= 8 ? 8 : (kChunks <= 16 ? 16 : 32);
-  constexpr int kPagesPerWarp = 32 / kLanes;
-  const int lane = threadIdx.x & 31;
-  const int sub = lane / kLanes, cl = lane % kLanes;
-  const long long page =
-      (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) *
-          kPagesPerWarp +
-      sub;
-  const bool page_ok = page < static_cast<long long>(p.heads) * p.blocks;
-  const bool lane_ok = page_ok && cl < kChunks;
-  const int h = page_ok ? static_cast<int>(page / p.blocks) : 0;
-  const int b = page_ok ? static_cast<int>(page % p.blocks) : 0;
-  const int B = p.block_size;
-  const int count = page_ok ? min(B, p.tokens - b * B) : 0;
+template <int D, int R>
+__global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant__ SummarizeMaps maps,
+                                                           const SummarizeParams p) {
+  constexpr int kTile = R * D * 2;
+  constexpr int kStage = 2 * kTile;
+  constexpr int kChunks = D / 8;                               // 16-byte chunks per row
+  constexpr int kLpc = 32 % kChunks == 0 ? 32 / kChunks : 1;   // lanes per chunk (row interleave)
+  constexpr int kActive = kChunks * kLpc;                      // lanes of the per-chunk pass
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const int warps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.stages;
+  uint8_t* ring = smem;  // [warp][stage][K | V]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(warps) * S * kStage);
+  float* scratch = reinterpret_cast<float*>(smem + static_cast<size_t>(warps) * S * kStage +
+                                            round16(static_cast<size_t>(warps) * S * 8));
+  float* kmean_s = scratch + warp * 2 * D;  // this warp's [D] bf16-rounded K means
+  float* rscale_s = kmean_s + D;            // and [D] reciprocal half widths
 
+  const long long pages = static_cast<long long>(p.heads) * p.blocks;
+  const long long lo = pages * blockIdx.x / gridDim.x;
+  const long long hi = pages * (blockIdx.x + 1) / gridDim.x;
+  const int mine = hi - lo > warp ? static_cast<int>((hi - lo - warp + warps - 1) / warps) : 0;
+
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[warp * S + s], 1);
+    mbar_fence_init();
+  }
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&maps.keys);
+    tma_prefetch_desc(&maps.values);
+  }
+  __syncwarp();
   pdl_wait();
   pdl_launch_dependents();
+  const uint64_t policy = l2_evict_first_policy();
 
-  const __nv_bfloat16* __restrict__ kbase =
-      static_cast<const __nv_bfloat16*>(p.keys) + h * p.key_head_stride +
-      static_cast<long long>(b) * B * p.key_token_stride + cl * 8;
-  const __nv_bfloat16* __restrict__ vbase =
-      static_cast<const __nv_bfloat16*>(p.values) + h * p.value_head_stride +
-      static_cast<long long>(b) * B * p.value_token_stride + cl * 8;
-  uint4* __restrict__ kpage =
-      p.key_pages ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
-                                             page * B * D + cl * 8)
-                  : nullptr;
-  uint4* __restrict__ vpage =
-      p.value_pages ? reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
-                                               page * B * D + cl * 8)
-                    : nullptr;
-
-  float ksum[8], kmax[8], kmin[8], vsum[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    ksum[i] = 0.f;
-    vsum[i] = 0.f;
-    kmax[i] = -INFINITY;
-    kmin[i] = INFINITY;
+  auto page_of = [&](int j) { return lo + warp + static_cast<long long>(j) * warps; };
+  auto issue = [&](int j) {  // lane 0
+    const long long pg = page_of(j);
+    const int h = static_cast<int>(pg / p.blocks), b = static_cast<int>(pg % p.blocks);
+    const int s = j % S;
+    uint8_t* dst = ring + static_cast<size_t>(warp * S + s) * kStage;
+    mbar_expect_tx(&bars[warp * S + s], kStage);
+    tma_tile_hint<D>(dst, &maps.keys, &bars[warp * S + s], b * R, h, R, policy);
+    tma_tile_hint<D>(dst + kTile, &maps.values, &bars[warp * S + s], b * R, h, R, policy);
+  };
+  const int first = min(S, mine);
+  if (lane == 0) {
+    for (int j = 0; j < first; ++j) issue(j);
   }
-  float vnorm = -INFINITY;
+  int issued = first;
 
-  // Rows are read kBatch at a time: every load of a batch is in flight
-  // before the first is used.
-  constexpr int kBatch = 8;
-  for (int t0 = 0; t0 < B; t0 += kBatch) {
-    uint4 kb[kBatch], vb[kBatch];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      kb[i] = make_uint4(0, 0, 0, 0);
-      vb[i] = make_uint4(0, 0, 0, 0);
-      if (lane_ok && t0 + i < count) {
-        kb[i] = __ldg(reinterpret_cast<const uint4*>(kbase + (t0 + i) * p.key_token_stride));
-        vb[i] = __ldg(reinterpret_cast<const uint4*>(vbase + (t0 + i) * p.value_token_stride));
-      }
+  for (int j = 0; j < mine; ++j) {
+    const int s = j % S;
+    const long long pg = page_of(j);
+    const int h = static_cast<int>(pg / p.blocks), b = static_cast<int>(pg % p.blocks);
+    const int count = min(R, p.tokens - b * R);
+    if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
+      // A wait that ran out: mark the head's value-norm bound NaN (the
+      // selector then expands every page of it) and stop this warp.
+      if (lane == 0) atomicMax(reinterpret_cast<int*>(p.max_value_norm + h), 0x7fffffff);
+      drain_pending(bars + warp * S, S, j, issued);
+      break;
     }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int t = t0 + i;
-      const bool row = lane_ok && t < count;
-      if (kpage != nullptr && lane_ok) {
-        kpage[t * (D / 8)] = kb[i];
-        vpage[t * (D / 8)] = vb[i];
-      }
-      float kf[8], vf[8];
-      unpack8(kb[i], kf);
-      unpack8(vb[i], vf);
-      float sq = 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        if (row) {
-          ksum[c] += kf[c];
-          vsum[c] += vf[c];
-          kmax[c] = nan_max(kmax[c], kf[c]);
-          kmin[c] = nan_min(kmin[c], kf[c]);
-        }
-        sq += vf[c] * vf[c];
-      }
-#pragma unroll
-      for (int off = 1; off < kLanes; off <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-      if (row) vnorm = nan_max(vnorm, sqrtf(sq));
-    }
-  }
+    const uint8_t* kt = ring + static_cast<size_t>(warp * S + s) * kStage;
+    const uint8_t* vt = kt + kTile;
 
-  const float cnt = static_cast<float>(count > 0 ? count : 1);
-  float kmean[8], vmean[8], width2[8], rscale[8];
+    // Lane per channel chunk: sums and K range over the real rows.
+    float ksum[8], vsum[8], kmax[8], kmin[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    kmean[i] = bf16_round(ksum[i] / cnt);
-    vmean[i] = bf16_round(vsum[i] / cnt);
-    float w = nan_max(kmax[i] - kmean[i], kmean[i] - kmin[i]);
-    w = w < 1e-6f ? 1e-6f : w;
-    width2[i] = bf16_round(w * w);
-    rscale[i] = __frsqrt_rn(width2[i]);
-  }
-
-  // Pass 2: largest normalised centred squared distance of a real row
-  // (the page was just read, so these loads hit L2).
-  float dmax = -INFINITY;
-  for (int t0 = 0; t0 < B; t0 += kBatch) {
-    uint4 kb[kBatch];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      kb[i] = make_uint4(0, 0, 0, 0);
-      if (lane_ok && t0 + i < count) {
-        kb[i] = __ldg(reinterpret_cast<const uint4*>(kbase + (t0 + i) * p.key_token_stride));
-      }
+    for (int i = 0; i < 8; ++i) {
+      ksum[i] = vsum[i] = 0.f;
+      kmax[i] = -INFINITY;
+      kmin[i] = INFINITY;
     }
+    const int c16 = lane % kChunks;
+    if (lane < kActive) {
+      for (int r = lane / kChunks; r < count; r += kLpc) {
+        float kf[8], vf[8];
+        unpack8(*reinterpret_cast<const uint4*>(kt + swz(r, c16, R)), kf);
+        unpack8(*reinterpret_cast<const uint4*>(vt + swz(r, c16, R)), vf);
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int t = t0 + i;
-      float dsum = 0.f;
-      if (lane_ok && t < count) {
-        float kf[8];
-        unpack8(kb[i], kf);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float x = (kf[c] - kmean[c]) * rscale[c];
-          dsum += x * x;
+        for (int i = 0; i < 8; ++i) {
+          ksum[i] += kf[i];
+          vsum[i] += vf[i];
+          kmax[i] = nan_max(kmax[i], kf[i]);
+          kmin[i] = nan_min(kmin[i], kf[i]);
         }
       }
-#pragma unroll
-      for (int off = 1; off < kLanes; off <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, off);
-      if (t < count) dmax = nan_max(dmax, dsum);
     }
-  }
-  float rho2 = dmax < 0.f ? 0.f : dmax;
-  rho2 = sqrtf(rho2);
-  rho2 = rho2 * rho2;
-
-  if (lane_ok) {
-    float ell[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ell[i] = (rho2 * width2[i]) * 1.00390625f;
-    const long long off = page * D + cl * 8;
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_mean) + off) = pack8(kmean);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_mean) + off) = pack8(vmean);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.ellipsoid) + off) = pack8(ell);
-    if (cl == 0) {
-      p.value_norm[page] = vnorm;
+    for (int off = kChunks; off < kActive; off <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ksum[i] += __shfl_xor_sync(0xffffffffu, ksum[i], off);
+        vsum[i] += __shfl_xor_sync(0xffffffffu, vsum[i], off);
+        kmax[i] = nan_max(kmax[i], __shfl_xor_sync(0xffffffffu, kmax[i], off));
+        kmin[i] = nan_min(kmin[i], __shfl_xor_sync(0xffffffffu, kmin[i], off));
+      }
+    }
+    const float cnt = static_cast<float>(count);
+    float width2[8];
+    if (lane < kChunks) {
+      float kmean[8], vmean[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        kmean[i] = bf16_round(ksum[i] / cnt);
+        vmean[i] = bf16_round(vsum[i] / cnt);
+        float w = nan_max(kmax[i] - kmean[i], kmean[i] - kmin[i]);
+        w = w < 1e-6f ? 1e-6f : w;
+        width2[i] = bf16_round(w * w);
+        kmean_s[c16 * 8 + i] = kmean[i];
+        rscale_s[c16 * 8 + i] = __frsqrt_rn(width2[i]);
+      }
+      const size_t off = static_cast<size_t>(pg) * D + c16 * 8;
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_mean) + off) = pack8(kmean);
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_mean) + off) = pack8(vmean);
+    }
+    __syncwarp();
+
+    // Lane per row: V row norm and the centred, normalised K distance.
+    float vnorm = -INFINITY, dmax = -INFINITY;
+    for (int r = lane; r < count; r += 32) {
+      float sq = 0.f, dist = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < kChunks; ++c) {
+        float kf[8], vf[8];
+        unpack8(*reinterpret_cast<const uint4*>(kt + swz(r, c, R)), kf);
+        unpack8(*reinterpret_cast<const uint4*>(vt + swz(r, c, R)), vf);
+        const float4 m0 = *reinterpret_cast<const float4*>(kmean_s + c * 8);
+        const float4 m1 = *reinterpret_cast<const float4*>(kmean_s + c * 8 + 4);
+        const float4 s0 = *reinterpret_cast<const float4*>(rscale_s + c * 8);
+        const float4 s1 = *reinterpret_cast<const float4*>(rscale_s + c * 8 + 4);
+        const float mean[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        const float scale[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          sq += vf[i] * vf[i];
+          const float x = (kf[i] - mean[i]) * scale[i];
+          dist += x * x;
+        }
+      }
+      vnorm = nan_max(vnorm, sqrtf(sq));
+      dmax = nan_max(dmax, dist);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      vnorm = nan_max(vnorm, __shfl_xor_sync(0xffffffffu, vnorm, off));
+      dmax = nan_max(dmax, __shfl_xor_sync(0xffffffffu, dmax, off));
+    }
+    float rho2 = dmax < 0.f ? 0.f : dmax;
+    rho2 = sqrtf(rho2);
+    rho2 = rho2 * rho2;
+    if (lane < kChunks) {
+      float ell[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ell[i] = (rho2 * width2[i]) * 1.00390625f;
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.ellipsoid) +
+                                static_cast<size_t>(pg) * D + c16 * 8) = pack8(ell);
+    }
+    if (lane == 0) {
+      p.value_norm[pg] = vnorm;
       // Norms are >= 0 (or a positive NaN), so their bit patterns order as ints.
       atomicMax(reinterpret_cast<int*>(p.max_value_norm + h), __float_as_int(vnorm));
       if (h == 0) p.counts[b] = count;
     }
+    if (p.key_pages != nullptr) {  // zero-padded page copy (rows past the prompt read as 0)
+      uint4* kdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
+                                             static_cast<size_t>(pg) * R * D);
+      uint4* vdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
+                                             static_cast<size_t>(pg) * R * D);
+      for (int i = lane; i < R * kChunks; i += 32) {
+        const int r = i / kChunks, c = i - r * kChunks;
+        kdst[i] = *reinterpret_cast<const uint4*>(kt + swz(r, c, R));
+        vdst[i] = *reinterpret_cast<const uint4*>(vt + swz(r, c, R));
+      }
+    }
+    __syncwarp();
+    if (j + S < mine) {
+      if (lane == 0) {
+        fence_proxy_async();
+        issue(j + S);
+      }
+      ++issued;
+    }
   }
 }
 
-template <int D>
-cudaError_t launch_summarize_t(const SummarizeParams& p, cudaStream_t stream) {
-  constexpr int kChunks = D / 8;
-  constexpr int kLanes = kChunks <= 8 ? 8 : (kChunks <= 16 ? 16 : 32);
-  constexpr int kPagesPerWarp = 32 / kLanes;
-  constexpr int kWarps = 8;
-  const long long pages = static_cast<long long>(p.heads) * p.blocks;
-  const long long per_cta = static_cast<long long>(kWarps) * kPagesPerWarp;
+template <int D, int R>
+cudaError_t launch_t(const SummarizeMaps& maps, const SummarizeParams& p, int ctas, int warps,
+                     size_t smem, cudaStream_t stream) {
+  const void* kernel = reinterpret_cast<const void*>(summarize_kernel<D, R>);
+  cudaError_t err = ensure_smem_limit(kernel, smem);
+  if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>((pages + per_cta - 1) / per_cta));
-  cfg.blockDim = dim3(kWarps * 32);
-  cfg.dynamicSmemBytes = 0;
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, summarize_kernel<D>, p);
+  return cudaLaunchKernelEx(&cfg, summarize_kernel<D, R>, maps, p);
+}
+
+template <int D>
+cudaError_t launch_d(const SummarizeMaps& maps, const SummarizeParams& p, int ctas, int warps,
+                     size_t smem, cudaStream_t stream) {
+  switch (p.block_size) {
+    case 16: return launch_t<D, 16>(maps, p, ctas, warps, smem, stream);
+    case 32: return launch_t<D, 32>(maps, p, ctas, warps, smem, stream);
+    case 64: return launch_t<D, 64>(maps, p, ctas, warps, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
 
-cudaError_t launch_summarize(const SummarizeParams& p, int dim, cudaStream_t stream) {
+size_t summarize_smem_bytes(int dim, int block, int warps, int stages) {
+  return kSmemSlack + static_cast<size_t>(warps) * stages * 2 * block * dim * 2 +
+         round16(static_cast<size_t>(warps) * stages * 8) + static_cast<size_t>(warps) * 2 * dim * 4;
+}
+
+cudaError_t launch_summarize(const SummarizeMaps& maps, const SummarizeParams& p, int dim,
+                             int ctas, int warps, size_t smem, cudaStream_t stream) {
   switch (dim) {
-    case 64: return launch_summarize_t<64>(p, stream);
-    case 128: return launch_summarize_t<128>(p, stream);
-    case 192: return launch_summarize_t<192>(p, stream);
-    case 256: return launch_summarize_t<256>(p, stream);
+    case 64: return launch_d<64>(maps, p, ctas, warps, smem, stream);
+    case 128: return launch_d<128>(maps, p, ctas, warps, smem, stream);
+    case 192: return launch_d<192>(maps, p, ctas, warps, smem, stream);
+    case 256: return launch_d<256>(maps, p, ctas, warps, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
