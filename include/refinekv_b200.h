@@ -14,7 +14,7 @@
  *
  * Data types: K/V caches, pages and summaries are bf16; queries are bf16 or
  * fp32 (rounded to bf16 before use, as the reference does); outputs are in
- * the query dtype.  Head dimensions 64, 128, 192 and 256; block sizes 16,
+ * the query dtype.  Head dimensions: multiples of 32 up to 256; block sizes 16,
  * 32 and 64; GQA groups of 1..16 query rows per KV head.
  *
  * Caller-owned scratch: rkv_select and rkv_decode take a workspace whose

@@ -221,8 +221,8 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
     load_query_frags<D, NT>(
         qb,
         static_cast<const char*>(p.query) +
-            static_cast<size_t>(h) * p.group * D * (p.query_f32 ? 4 : 2),
-        p.query_f32, p.group, lane, false);
+            static_cast<size_t>(h) * p.group * p.dim * (p.query_f32 ? 4 : 2),
+        p.query_f32, p.group, p.dim, lane, false);
     float m[NT][2], l[NT][2], o[D / 16][NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     for (int w = 0; w < kWarps; ++w) s += red[(w * 32 + ln) * G8 + g];
     const float out = s / fmaxf(den[g], 1e-30f);
     const size_t row = static_cast<size_t>(h) * p.group + g;
-    const size_t o = row * D + blockIdx.y * 32 + ln;
+    const size_t o = row * p.dim + blockIdx.y * 32 + ln;
     if (p.part_o != nullptr) {  // sequence split: this rank's row partial
       p.part_o[o] = out;
       if (blockIdx.y == 0 && ln == 0) {
@@ -533,13 +533,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
 // Sequence split: out[row, d] = sum_r w_r o_r[row, d] / sum_r w_r with
 // w_r = l_r exp(m_r - max_r m_r) over the ranks whose row is non-empty.
 // One CTA per KV head, one thread per (group row, dim) element.
-template <int D>
 __global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const int h = blockIdx.x;
-  for (int i = threadIdx.x; i < p.group * D; i += blockDim.x) {
-    const int g = i / D, d = i - g * D;
+  const int dim = p.dim;
+  for (int i = threadIdx.x; i < p.group * dim; i += blockDim.x) {
+    const int g = i / dim, d = i - g * dim;
     const size_t row = static_cast<size_t>(h) * p.group + g;
     float top = -INFINITY;
     for (int r = 0; r < p.ranks; ++r) {
@@ -552,13 +552,13 @@ __global__ void __launch_bounds__(256) merge_kernel(const MergeParams p) {
       if (!(ml[1] > 0.f)) continue;
       const float w = ml[1] * __expf(ml[0] - top);
       den += w;
-      num += w * p.part_o[r * p.slab_floats + row * D + d];
+      num += w * p.part_o[r * p.slab_floats + row * dim + d];
     }
     const float out = num / fmaxf(den, 1e-30f);
     if (p.query_f32) {
-      static_cast<float*>(p.out)[row * D + d] = out;
+      static_cast<float*>(p.out)[row * dim + d] = out;
     } else {
-      static_cast<__nv_bfloat16*>(p.out)[row * D + d] = __float2bfloat16_rn(out);
+      static_cast<__nv_bfloat16*>(p.out)[row * dim + d] = __float2bfloat16_rn(out);
     }
   }
 }
@@ -614,7 +614,7 @@ cudaError_t launch_combine_t(const CombineParams& p, cudaStream_t stream, bool p
   cudaError_t err = ensure_smem_limit(kernel, smem);
   if (err != cudaSuccess) return err;
   void* args[] = {const_cast<CombineParams*>(&p)};
-  return launch_pdl(kernel, dim3(p.heads, D / 32), dim3(256), smem, stream, pdl, args);
+  return launch_pdl(kernel, dim3(p.heads, p.dim / 32), dim3(256), smem, stream, pdl, args);
 }
 
 template <int D>
@@ -623,12 +623,6 @@ cudaError_t combine_g(const CombineParams& p, cudaStream_t stream, bool pdl) {
   return launch_combine_t<D, 16>(p, stream, pdl);
 }
 
-template <int D>
-cudaError_t launch_merge_t(const MergeParams& p, cudaStream_t stream, bool pdl) {
-  void* args[] = {const_cast<MergeParams*>(&p)};
-  return launch_pdl(reinterpret_cast<const void*>(merge_kernel<D>), dim3(p.heads), dim3(256), 0,
-                    stream, pdl, args);
-}
 
 }  // namespace
 
@@ -669,13 +663,10 @@ cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream,
 }
 
 cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, bool pdl) {
-  switch (dim) {
-    case 64: return launch_merge_t<64>(p, stream, pdl);
-    case 128: return launch_merge_t<128>(p, stream, pdl);
-    case 192: return launch_merge_t<192>(p, stream, pdl);
-    case 256: return launch_merge_t<256>(p, stream, pdl);
-    default: return cudaErrorInvalidValue;
-  }
+  (void)dim;  // the merge works on the real width in p.dim
+  void* args[] = {const_cast<MergeParams*>(&p)};
+  return launch_pdl(reinterpret_cast<const void*>(merge_kernel), dim3(p.heads), dim3(256), 0,
+                    stream, pdl, args);
 }
 
 }  // namespace rkv

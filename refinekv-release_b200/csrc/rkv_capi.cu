@@ -29,7 +29,11 @@ int cuda_fail(cudaError_t err, const char* what) {
   return fail(RKV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
 }
 
-bool supported_dim(int64_t d) { return d == 64 || d == 128 || d == 192 || d == 256; }
+// Head dims: multiples of 32 up to 256 (the reference's GPU limits,
+// attention.py:29-39).  Kernels compute on the width rounded up to 64, the
+// TMA boxes' width; loads past the real width read zeros.
+bool supported_dim(int64_t d) { return d >= 32 && d <= 256 && d % 32 == 0; }
+int padded_dim(int64_t d) { return static_cast<int>((d + 63) / 64 * 64); }
 bool supported_block(int64_t b) { return b == 16 || b == 32 || b == 64; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -93,6 +97,7 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   DeviceInfo dev;
   int rc = device_info(&dev);
   if (rc != RKV_OK) return rc;
+  dim = padded_dim(dim);  // shared memory and scratch hold padded rows
   pl->tiles = static_cast<int>(cdiv(blocks, kSelectTile));
   const int64_t rows = heads * instances;
   // Phase A: about two CTAs per SM in total.
@@ -286,7 +291,7 @@ int check_summary(const rkv_summary* s) {
     return fail(RKV_ERR_UNSUPPORTED, "block_size must be 16, 32 or 64");
   }
   if (!supported_dim(s->head_dim)) {
-    return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+    return fail(RKV_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 in [32, 256]");
   }
   if (cdiv(s->prompt_length, s->block_size) != s->blocks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "blocks must equal ceil(prompt_length / block_size)");
@@ -359,6 +364,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
                  int accumulate, void* ws, bool decode, unsigned phases, cudaStream_t stream,
                  const SplitTarget* split = nullptr) {
   const int D = static_cast<int>(s->head_dim);
+  const int DP = padded_dim(D);
   if (phases & RKV_PHASE_STATS) {
     StatsMaps maps;
     int rc = summary_maps(s, &maps.key_mean, &maps.ellipsoid, nullptr);
@@ -366,6 +372,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     StatsParams p = {};
     p.query = q;
     p.query_f32 = qdtype == RKV_DTYPE_F32;
+    p.dim = D;
     p.counts = s->counts;
     p.heads = static_cast<int>(s->heads);
     p.group = static_cast<int>(group);
@@ -380,7 +387,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.delta = at<float>(ws, pl.delta);
     p.lse = split ? split->stats_slab(split->rank) : at<float>(ws, pl.lse);
     p.status = at<int>(ws, pl.status);
-    cudaError_t err = launch_stats(maps, p, D, pl.warps_a, pl.smem_a, stream, true);
+    cudaError_t err = launch_stats(maps, p, DP, pl.warps_a, pl.smem_a, stream, true);
     if (err != cudaSuccess) return cuda_fail(err, "selector stats launch");
   }
   if (phases & RKV_PHASE_FINAL) {
@@ -420,7 +427,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
       p.rep_o = at<float>(ws, pl.rep_o);
     }
     p.status = at<int>(ws, pl.status);
-    cudaError_t err = launch_final(maps, p, D, pl.warps_b, pl.smem_b, stream, true);
+    cudaError_t err = launch_final(maps, p, DP, pl.warps_b, pl.smem_b, stream, true);
     if (err != cudaSuccess) return cuda_fail(err, "selector final launch");
   }
   return RKV_OK;
@@ -488,7 +495,7 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
                   void* stream) {
   g_last_error.clear();
   if (heads <= 0 || tokens <= 0) return fail(RKV_ERR_INVALID_ARGUMENT, "empty keys/values");
-  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 in [32, 256]");
   if (!supported_block(block_size)) return fail(RKV_ERR_UNSUPPORTED, "block_size must be 16, 32 or 64");
   if (!keys || !values || !key_mean || !value_mean || !ellipsoid || !value_norm ||
       !max_value_norm || !counts) {
@@ -521,11 +528,11 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   if (rc != RKV_OK) return rc;
   // Persistent grid: one CTA per SM with about 128 KB of TMA ring per CTA,
   // as many warps as fit (3..8) with one or more stages each.
-  const int64_t stage = 2 * block_size * head_dim * 2;
+  const int64_t stage = 2 * block_size * padded_dim(head_dim) * 2;
   const int warps = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(8, 131072 / stage)));
   const int stages =
       static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, 131072 / (warps * stage))));
-  const size_t smem = summarize_smem_bytes(static_cast<int>(head_dim), static_cast<int>(block_size),
+  const size_t smem = summarize_smem_bytes(padded_dim(head_dim), static_cast<int>(block_size),
                                            warps, stages);
   if (smem > static_cast<size_t>(dev.smem_optin)) {
     return fail(RKV_ERR_UNSUPPORTED, "summarizer stages do not fit in shared memory");
@@ -542,6 +549,7 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   p.block_size = static_cast<int>(block_size);
   p.blocks = static_cast<int>(blocks);
   p.stages = stages;
+  p.dim = static_cast<int>(head_dim);
   p.key_pages = key_pages_out;
   p.value_pages = value_pages_out;
   p.key_mean = key_mean;
@@ -550,7 +558,7 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   p.value_norm = value_norm;
   p.max_value_norm = max_value_norm;
   p.counts = counts;
-  err = launch_summarize(maps, p, static_cast<int>(head_dim), ctas, warps, smem, st);
+  err = launch_summarize(maps, p, padded_dim(head_dim), ctas, warps, smem, st);
   if (err != cudaSuccess) return cuda_fail(err, "summarize launch");
   return RKV_OK;
 }
@@ -735,6 +743,7 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     AttendParams p = {};
     p.query = query;
     p.query_f32 = query_dtype == RKV_DTYPE_F32;
+    p.dim = static_cast<int>(D);
     p.counts = summary->counts;
     p.heads = static_cast<int>(H);
     p.group = static_cast<int>(group);
@@ -756,12 +765,13 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     p.stages = pl.stages_c;
     p.status = at<int>(workspace, pl.status);
     p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
-    cudaError_t err = launch_attend(maps, p, static_cast<int>(D), pl.warps_c, pl.smem_c, st, true);
+    cudaError_t err = launch_attend(maps, p, padded_dim(D), pl.warps_c, pl.smem_c, st, true);
     if (err != cudaSuccess) return cuda_fail(err, "attention launch");
   }
   if (phases & RKV_PHASE_COMBINE) {
     CombineParams c = {};
     c.query_f32 = query_dtype == RKV_DTYPE_F32;
+    c.dim = static_cast<int>(D);
     c.out = output;
     c.heads = static_cast<int>(H);
     c.group = static_cast<int>(group);
@@ -784,7 +794,7 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     c.part_ml = split ? split->output_ml(split->rank) : nullptr;
     c.part_o = split ? split->output_o(split->rank) : nullptr;
     c.status = at<int>(workspace, pl.status);
-    cudaError_t err = launch_combine(c, static_cast<int>(D), st, true);
+    cudaError_t err = launch_combine(c, padded_dim(D), st, true);
     if (err != cudaSuccess) return cuda_fail(err, "combine launch");
   }
   return RKV_OK;
@@ -817,7 +827,7 @@ int rkv_split_exchange_slabs(int64_t heads, int64_t group, int64_t max_blocks, i
       max_blocks > (1LL << 26)) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "split geometry out of range");
   }
-  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be 64, 128, 192 or 256");
+  if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 in [32, 256]");
   if (stats_slab == nullptr || output_slab == nullptr) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "null output pointer");
   }
@@ -882,6 +892,7 @@ int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dt
   if (stage & RKV_SPLIT_MERGE) {
     MergeParams m = {};
     m.query_f32 = query_dtype == RKV_DTYPE_F32;
+    m.dim = static_cast<int>(summary->head_dim);
     m.out = output;
     m.heads = static_cast<int>(summary->heads);
     m.group = static_cast<int>(group);

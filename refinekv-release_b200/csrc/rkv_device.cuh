@@ -235,7 +235,8 @@ __device__ __forceinline__ float bf16_round(float x) {
 // `square` builds the fragments of bf16(q^2) instead (the ellipsoid term).
 template <int D, int NT>
 __device__ __forceinline__ void load_query_frags(uint32_t (&qb)[D / 16][NT][2], const void* q,
-                                                 int q_is_f32, int group, int lane, bool square) {
+                                                 int q_is_f32, int group, int dim, int lane,
+                                                 bool square) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int g = nt * 8 + (lane >> 2);
@@ -245,15 +246,15 @@ __device__ __forceinline__ void load_query_frags(uint32_t (&qb)[D / 16][NT][2], 
       for (int half = 0; half < 2; ++half) {
         const int d = ks * 16 + half * 8 + 2 * (lane & 3);
         float x0 = 0.f, x1 = 0.f;
-        if (g < group) {
+        if (g < group && d < dim) {  // channels past the real width are zero
           if (q_is_f32) {
-            const float* qf = static_cast<const float*>(q) + g * D + d;
+            const float* qf = static_cast<const float*>(q) + g * dim + d;
             x0 = bf16_round(qf[0]);
             x1 = bf16_round(qf[1]);
           } else {
             const __nv_bfloat162 v =
                 *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(q) +
-                                                         g * D + d);
+                                                         g * dim + d);
             x0 = __low2float(v);
             x1 = __high2float(v);
           }

@@ -20,6 +20,7 @@ struct SummarizeMaps {
 
 struct SummarizeParams {
   int heads, tokens, blocks, block_size;
+  int dim;            // real head dim (the kernel's D is dim rounded up to 64)
   int stages;         // TMA stages per warp
   void* key_pages;    // optional (heads, blocks, block, dim) copy, zero padded
   void* value_pages;  // optional
@@ -39,6 +40,7 @@ struct StatsMaps {
 struct StatsParams {
   const void* query;  // (instances, heads, group, dim)
   int query_f32;
+  int dim;            // real head dim (the kernel's D is dim rounded up to 64)
   const int64_t* counts;
   int heads, group, blocks, instances;
   int tiles, tiles_per_cta, parts;
@@ -93,6 +95,7 @@ struct AttendMaps {
 struct AttendParams {
   const void* query;  // (heads, group, dim)
   int query_f32;
+  int dim;            // real head dim (the kernel's D is dim rounded up to 64)
   const int64_t* counts;
   int heads, group, blocks, page;
   int prompt_length;  // rows of block b: min(page, prompt_length - b * page)
@@ -117,6 +120,7 @@ struct AttendParams {
 
 struct CombineParams {
   int query_f32;
+  int dim;    // real head dim; one CTA column per 32 real channels
   void* out;  // (heads, group, dim) in the query dtype
   int heads, group, page;
   int has_suffix, suffix_capacity;
@@ -134,7 +138,7 @@ struct CombineParams {
   int max_sources;     // capacity of the shared-memory source table
   // Sequence split: when non-null, each row's merged (max, sum) goes to
   // part_ml[row * 2 + {0, 1}] and its normalised output to part_o[row * dim
-  // + d] (FP32) instead of `out`.
+  // + d] (FP32, real dim) instead of `out`.
   float* part_ml;
   float* part_o;
   int* status;
@@ -143,6 +147,7 @@ struct CombineParams {
 // LSE merge of the ranks' rows of a sequence split (rkv_decode_split).
 struct MergeParams {
   int query_f32;
+  int dim;    // real head dim
   void* out;  // (heads, group, dim) in the query dtype
   int heads, group;
   int ranks;

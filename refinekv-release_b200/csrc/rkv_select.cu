@@ -116,15 +116,15 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
   }
 
   const void* q = static_cast<const char*>(p.query) +
-                  static_cast<size_t>(ih) * p.group * D * (p.query_f32 ? 4 : 2);
+                  static_cast<size_t>(ih) * p.group * p.dim * (p.query_f32 ? 4 : 2);
   uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
   uint32_t packed[PACK4 ? 2 * D / 16 : 1][2];
   if constexpr (PACK4) {
     uint32_t q1[D / 16][1][2];
-    load_query_frags<D, 1>(q1, q, p.query_f32, p.group, lane & 15, false);
+    load_query_frags<D, 1>(q1, q, p.query_f32, p.group, p.dim, lane & 15, false);
     pack4_frags<D>(q1, packed, lane);
   } else {
-    load_query_frags<D, NT>(qk, q, p.query_f32, p.group, lane, false);
+    load_query_frags<D, NT>(qk, q, p.query_f32, p.group, p.dim, lane, false);
     square_frags<D, NT>(qk, q2);
   }
 

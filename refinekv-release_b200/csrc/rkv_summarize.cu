@@ -42,14 +42,16 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
 __device__ __forceinline__ float nan_min(float a, float b) { return (b < a || b != b) ? b : a; }
 
+// D: the tile width (the real head dim p.dim rounded up to 64; TMA fills the
+// padding columns with zeros and nothing reads them).
 template <int D, int R>
 __global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant__ SummarizeMaps maps,
                                                            const SummarizeParams p) {
   constexpr int kTile = R * D * 2;
   constexpr int kStage = 2 * kTile;
-  constexpr int kChunks = D / 8;                               // 16-byte chunks per row
-  constexpr int kLpc = 32 % kChunks == 0 ? 32 / kChunks : 1;   // lanes per chunk (row interleave)
-  constexpr int kActive = kChunks * kLpc;                      // lanes of the per-chunk pass
+  const int kChunks = p.dim / 8;                              // real 16-byte chunks per row
+  const int kLpc = 32 % kChunks == 0 ? 32 / kChunks : 1;      // lanes per chunk (row interleave)
+  const int kActive = kChunks * kLpc;                         // lanes of the per-chunk pass
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
   const int warps = blockDim.x >> 5;
@@ -134,7 +136,6 @@ __global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant
         }
       }
     }
-#pragma unroll
     for (int off = kChunks; off < kActive; off <<= 1) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant
         kmean_s[c16 * 8 + i] = kmean[i];
         rscale_s[c16 * 8 + i] = __frsqrt_rn(width2[i]);
       }
-      const size_t off = static_cast<size_t>(pg) * D + c16 * 8;
+      const size_t off = static_cast<size_t>(pg) * p.dim + c16 * 8;
       *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_mean) + off) = pack8(kmean);
       *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_mean) + off) = pack8(vmean);
     }
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant
 #pragma unroll
       for (int i = 0; i < 8; ++i) ell[i] = (rho2 * width2[i]) * 1.00390625f;
       *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.ellipsoid) +
-                                static_cast<size_t>(pg) * D + c16 * 8) = pack8(ell);
+                                static_cast<size_t>(pg) * p.dim + c16 * 8) = pack8(ell);
     }
     if (lane == 0) {
       p.value_norm[pg] = vnorm;
@@ -212,9 +213,9 @@ __global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant
     }
     if (p.key_pages != nullptr) {  // zero-padded page copy (rows past the prompt read as 0)
       uint4* kdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
-                                             static_cast<size_t>(pg) * R * D);
+                                             static_cast<size_t>(pg) * R * p.dim);
       uint4* vdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
-                                             static_cast<size_t>(pg) * R * D);
+                                             static_cast<size_t>(pg) * R * p.dim);
       for (int i = lane; i < R * kChunks; i += 32) {
         const int r = i / kChunks, c = i - r * kChunks;
         kdst[i] = *reinterpret_cast<const uint4*>(kt + swz(r, c, R));

@@ -14,7 +14,9 @@ import torch
 from . import _native
 from .config import RefineKVConfig
 
-SUPPORTED_HEAD_DIMS = (64, 128, 192, 256)
+#: Head dims of the CUDA path: multiples of 32 up to 256, as the reference's GPU backend
+#: (``attention.py:29-39``).
+SUPPORTED_HEAD_DIMS = tuple(range(32, 257, 32))
 
 
 @dataclass

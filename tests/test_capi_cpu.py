@@ -56,11 +56,13 @@ def test_status_strings(lib):
 
 
 def test_summarize_rejects_bad_arguments_before_touching_a_device(lib):
-    args = [ctypes.c_void_p(16), ctypes.c_void_p(16), 2, 64, 96, 0, 96, 0, 96, 32,
+    args = [ctypes.c_void_p(16), ctypes.c_void_p(16), 2, 64, 80, 0, 80, 0, 80, 32,
             None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
             ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), None]
-    assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # head_dim 96
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # head_dim 80
     assert b"head_dim" in lib.rkv_last_error()
+    args[4] = 288
+    assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # above 256
     args[4], args[9] = 128, 24
     assert lib.rkv_summarize(*args) == _native.RKV_ERR_UNSUPPORTED  # block 24
     args[9] = 32

@@ -101,6 +101,18 @@ def test_cuda_graph_with_dense_layers_matches_eager(family):
         assert torch.equal(model.generate(**opts), eager)
 
 
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_reference_tiny_model_head_dim_32(family):
+    """The reference's own adapter-test model (hidden 128, 4 heads: head_dim 32), graph == eager."""
+    model = _model(family, hidden=128)
+    config = RefineKVConfig(eps=0.01, anchor_tokens=2)
+    opts = _options(39)
+    with RefineKV(model, config):
+        eager = model.generate(**opts)
+    with RefineKV(model, config, cuda_graph=True):
+        assert torch.equal(model.generate(**opts), eager)
+
+
 def test_full_layers_match_native_generation():
     model = _model()
     opts = _options(39, 4)

@@ -290,6 +290,11 @@ SHAPES = [
     (3, 8, 192, 64, 777, 65, "mean", 0.01),
     (1, 2, 128, 32, 17, 1, "any", 0.0),
     (2, 12, 64, 16, 300, 17, "max", 0.1),
+    # head dims that are not multiples of 64 (TMA zero-fills the padding columns)
+    (2, 4, 32, 32, 1000, 5, "any", 0.01),
+    (4, 7, 96, 64, 2000, 9, "max", 0.005),
+    (2, 8, 160, 16, 700, 3, "mean", 0.02),
+    (1, 16, 224, 32, 900, 33, "any", 0.02),
 ]
 
 
