@@ -113,6 +113,47 @@ def test_reference_tiny_model_head_dim_32(family):
         assert torch.equal(model.generate(**opts), eager)
 
 
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+@pytest.mark.parametrize("reduction", ["any", "mean"])
+def test_greedy_tokens_match_the_reference_backend(family, reduction, monkeypatch):
+    """Same random-init model and prompt, attention by librefinekv_b200 vs the reference algorithm.
+
+    The reference side swaps the adapter's three kernel calls for the CPU
+    oracle (the reference PyTorch backend restated), moving each layer's
+    tensors to the host and the results back; everything else in the model is
+    the same GPU computation.  Greedy tokens must be identical.
+    """
+    from oracle import refinekv_oracle as ora
+    from refinekv_b200.attention import AttentionResult
+
+    model = _model(family, hidden=512, heads=8, kv_heads=2, layers=2, vocab=256)  # head_dim 64
+    config = RefineKVConfig(eps=0.05, gqa_reduction=reduction, anchor_tokens=4)
+    opts = _options(700, 12)
+    with RefineKV(model, config):
+        ours = model.generate(**opts)
+
+    def summary(keys, values, cfg):
+        return ora.build_summary(keys.cpu(), values.cpu(), block_size=cfg.block_size)
+
+    def union(queries, summ, cfg, *, workspace=None):
+        return ora.anchor_union(queries.cpu(), summ, cfg.eps, cfg.gqa_reduction).cuda()
+
+    def decode(query, summ, ks, vs, cfg, *, anchor_mask=None, workspace=None,
+               return_selected=False, suffix_length=None):
+        out, sel = ora.sparse_attention(query.cpu(), summ, ks.cpu(), vs.cpu(), cfg.eps,
+                                        cfg.gqa_reduction,
+                                        anchor_mask=None if anchor_mask is None
+                                        else anchor_mask.cpu())
+        return AttentionResult(out.cuda(), sel.cuda() if return_selected else None)
+
+    monkeypatch.setattr(adapter, "build_summary", summary)
+    monkeypatch.setattr(adapter, "select_blocks_union", union)
+    monkeypatch.setattr(adapter, "sparse_attention", decode)
+    with RefineKV(model, config):
+        reference = model.generate(**opts)
+    assert torch.equal(ours, reference)
+
+
 def test_full_layers_match_native_generation():
     model = _model()
     opts = _options(39, 4)
