@@ -26,14 +26,22 @@ namespace {
 constexpr float kInflate = 1.00390625f;  // 1 + 2^-8
 constexpr float kDeltaSplit = 10.f;
 
+// exp and log on the special-function unit (__expf / __logf): a few ulp from
+// the correctly rounded functions, far inside the 1e-3 relative eps margin
+// that decides which blocks are judged against the reference; the
+// accurate library calls cost several times as many instructions on the
+// selector's latency-bound path.
+__device__ __forceinline__ float fexp(float x) { return __expf(x); }
+__device__ __forceinline__ float flog(float x) { return __logf(x); }
+
 // NaN-propagating clamp from above (torch.clamp(max=...)).
 __device__ __forceinline__ float clamp_hi(float x, float hi) { return x > hi ? hi : x; }
 
 // log(cosh(delta)) with the reference's two branches (reference.py:19-22).
 __device__ __forceinline__ float log_cosh(float delta) {
   const float small = clamp_hi(delta, kDeltaSplit);
-  const float direct = logf((expf(small) + expf(-small)) * 0.5f);
-  const float large = delta + logf((1.f + expf(-2.f * delta)) * 0.5f);
+  const float direct = flog((fexp(small) + fexp(-small)) * 0.5f);
+  const float large = delta + flog((1.f + fexp(-2.f * delta)) * 0.5f);
   return delta <= kDeltaSplit ? direct : large;
 }
 
@@ -43,17 +51,17 @@ __device__ __forceinline__ float block_risk(float z, float delta, float log_z, f
                                             float vnorm, float vmax) {
   const bool near = delta <= kDeltaSplit;
   const float small = clamp_hi(delta, kDeltaSplit);
-  const float t = expf(small);
+  const float t = fexp(small);
   const float two_vmax = 2.f * vmax;
-  const float mass_direct = (two_vmax * expf(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
-  const float e_neg = expf(-delta);
+  const float mass_direct = (two_vmax * fexp(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
+  const float e_neg = fexp(-delta);
   float one_minus = 1.f - e_neg;
   one_minus = one_minus < 1e-30f ? 1e-30f : one_minus;
-  const float lcm1 = (delta + 2.f * logf(one_minus)) - 0.693147182464599609375f;
-  const float mass_large = two_vmax * expf((z - log_c) + lcm1);
+  const float lcm1 = (delta + 2.f * flog(one_minus)) - 0.693147182464599609375f;
+  const float mass_large = two_vmax * fexp((z - log_c) + lcm1);
   const float mass = near ? mass_direct : mass_large;
   const float tanh_half = near ? (t - 1.f) / (t + 1.f) : (1.f - e_neg) / (1.f + e_neg);
-  const float importance = ((2.f * vnorm) * expf(z - log_z)) * tanh_half;
+  const float importance = ((2.f * vnorm) * fexp(z - log_z)) * tanh_half;
   return mass + importance;
 }
 
@@ -62,7 +70,7 @@ __device__ __forceinline__ bool finite(float x) { return isfinite(x); }
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   const float top = fmaxf(m, m2);
   const float ref = top == -INFINITY ? 0.f : top;
-  s = s * expf(m - ref) + s2 * expf(m2 - ref);
+  s = s * fexp(m - ref) + s2 * fexp(m2 - ref);
   m = top;
 }
 
@@ -137,9 +145,28 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
       zs[nt][j] = cs[nt][j] = 0.f;
     }
 
+  // This lane's block rows within a tile (the C-fragment rows it finishes).
+  constexpr int kHalves = PACK4 ? 1 : 2;
+  int lane_rows[R / 16][2];
+#pragma unroll
+  for (int mt = 0; mt < R / 16; ++mt) {
+    lane_rows[mt][0] = mt * 16 + (lane >> 2) + (PACK4 && ((lane >> 1) & 1) ? 8 : 0);
+    lane_rows[mt][1] = lane_rows[mt][0] + 8;
+  }
+
   int issued = min(S, mine);
   for (int j = 0; j < mine; ++j) {
     const int s = j % S;
+    const int tile = t0 + warp + j * warps;
+    // Token counts of this lane's blocks, loaded while the tiles land.
+    long long cnt[R / 16][2];
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < kHalves; ++hf) {
+        const int b = tile * R + lane_rows[mt][hf];
+        cnt[mt][hf] = b < p.blocks ? __ldg(p.counts + b) : 1;
+      }
     if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
       if (lane == 0) atomicOr(p.status, kStatusTimeout);
       drain_pending(bars + warp * S, S, j, issued);
@@ -185,17 +212,15 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
       }
       ++issued;
     }
-    const int tile = t0 + warp + j * warps;
     // z and z + log cosh(delta) of every element first (independent), then
     // one (max, sum) update per column: no serial exp chain.
-    constexpr int kHalves = PACK4 ? 1 : 2;
     float zv[R / 16][NT][4], cv[R / 16][NT][4];
 #pragma unroll
     for (int mt = 0; mt < R / 16; ++mt) {
 #pragma unroll
       for (int hf = 0; hf < kHalves; ++hf) {
         const int b = tile * R + row_of[mt][hf];
-        const float log_count = b < p.blocks ? logf(static_cast<float>(__ldg(p.counts + b))) : 0.f;
+        const float log_count = b < p.blocks ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
 #pragma unroll
         for (int jc = 0; jc < 2; ++jc) {
           const int c = 2 * hf + jc;
@@ -239,8 +264,8 @@ __global__ void __launch_bounds__(128) stats_kernel(const __grid_constant__ Stat
         for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
           for (int hf = 0; hf < kHalves; ++hf) {
-            sz += expf(zv[mt][nt][2 * hf + jc] - rz);
-            sc2 += expf(cv[mt][nt][2 * hf + jc] - rc);
+            sz += fexp(zv[mt][nt][2 * hf + jc] - rz);
+            sc2 += fexp(cv[mt][nt][2 * hf + jc] - rc);
           }
         if (nan) sz = sc2 = NAN;  // a NaN row statistic must stay non-finite
         lse_merge(zm[nt][jc], zs[nt][jc], tz, sz);
@@ -340,6 +365,27 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   pdl_wait();
   pdl_launch_dependents();
 
+  // Pass-1 inputs of a tile (one lane per block): z and delta of every row,
+  // the value norm and the anchor bit.  The first tile's are loaded before
+  // the normalisers are merged and each next tile's before the current one
+  // is evaluated, so the loads overlap other work.
+  auto load_tile = [&](int t, float (&zr)[GM], float (&dr)[GM], float& vn, bool& anc) {
+    const int b = t * R + lane;
+    if (t < t1 && b < p.blocks) {
+      vn = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        const size_t row = static_cast<size_t>(ih) * p.group + (g < p.group ? g : 0);
+        zr[g] = p.z[row * p.blocks + b];
+        dr[g] = p.delta[row * p.blocks + b];
+      }
+      anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+    }
+  };
+  float zr[GM], dr[GM], vnorm = 0.f;
+  bool anc = false;
+  load_tile(t0 + warp, zr, dr, vnorm, anc);
+
   // Row-global normalisers from the phase-A partials (of every rank's slab
   // under a sequence split): one warp per row, lanes load partials in
   // parallel and merge them with shuffles.
@@ -363,8 +409,8 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
       lse_merge(m1, s1, pm, ps);
     }
     if (lane == 0) {
-      const float lz = m0 + logf(s0);
-      const float lc = m1 + logf(s1);
+      const float lz = m0 + flog(s0);
+      const float lc = m1 + flog(s1);
       log_z[g] = lz;
       log_c[g] = lc;
       if (!finite(lz) || !finite(lc)) atomicOr(&flags[0], 1);
@@ -374,21 +420,19 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
   const bool bad_global = flags[0] != 0;
   const float vmax = p.max_value_norm[h];
 
-  // Pass 1: decisions, one lane per block.  All rows' z and delta are
-  // loaded before any risk is evaluated so the loads overlap.
+  // Pass 1: decisions, one lane per block.
   for (int t = t0 + warp; t < t1; t += warps) {
+    float zn[GM], dn[GM], vnorm_n = 0.f;
+    bool anc_n = false;
+    load_tile(t + warps, zn, dn, vnorm_n, anc_n);  // the next tile's inputs in flight
     const int b = t * R + lane;
     const bool valid = b < p.blocks;
     bool sel = false;
     if (valid) {
-      const float vnorm = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
-      float zr[GM], dr[GM], lz[GM], lc[GM];
+      float lz[GM], lc[GM];
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
         const int gg = g < p.group ? g : 0;
-        const size_t row = static_cast<size_t>(ih) * p.group + gg;
-        zr[g] = p.z[row * p.blocks + b];
-        dr[g] = p.delta[row * p.blocks + b];
         lz[g] = log_z[gg];
         lc[g] = log_c[gg];
       }
@@ -418,8 +462,7 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
       } else {
         dec = any;
       }
-      sel = dec || bad || bad_global;
-      if (p.anchor != nullptr) sel = sel || p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+      sel = dec || bad || bad_global || anc;
       uint8_t* mk = p.mask + static_cast<size_t>(h) * p.blocks + b;
       if (p.accumulate) {
         if (sel) *mk = 1;
@@ -433,6 +476,13 @@ __global__ void __launch_bounds__(128) final_kernel(const __grid_constant__ Fina
       sel_bits[t - t0] = sb;
       rep_bits[t - t0] = vb & ~sb;
     }
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      zr[g] = zn[g];
+      dr[g] = dn[g];
+    }
+    vnorm = vnorm_n;
+    anc = anc_n;
   }
   if (!p.decode) return;
   __syncthreads();
