@@ -386,6 +386,19 @@ def run_b200(args):
     lib = _native.load()
     layers, cfg, summarize_ms = build_layers(args, plan, group, dev)
     cap = args.warmup + args.steps
+    # One tensor per step-wide quantity, each layer's a view of it (as a
+    # serving engine lays out its decode buffers): the suffix caches and the
+    # attention outputs, so a step moves its inputs and outputs in one copy.
+    G, D = args.group, args.head_dim
+    out_all = torch.empty(args.layers, plan.heads, G, D, device=dev, dtype=torch.bfloat16)
+    for li, L in enumerate(layers):
+        L.workspace["output"] = out_all[li]
+    sk_all = sv_all = None
+    if plan.holds_suffix:
+        sk_all = torch.stack([L.suffix_k for L in layers])  # (layers, heads, cap, dim)
+        sv_all = torch.stack([L.suffix_v for L in layers])
+        for li, L in enumerate(layers):
+            L.suffix_k, L.suffix_v = sk_all[li], sv_all[li]
     length = torch.zeros((), device=dev, dtype=torch.int32)
     heads_local = plan.heads
     split = plan.seq_ranks > 1
@@ -556,44 +569,48 @@ def run_b200(args):
                          "prompt K/V only, CUDA graph over all layers"}
 
     # ---- end to end through the public API with host buffers ---------------
-    # Each step copies its queries and new K/V token from pinned host memory,
-    # runs every layer's decode through the public call and copies the
-    # outputs back; the host waits for them before the next step.  As in the
-    # adapter's CUDA-graph decode, each step is one captured graph (copies
-    # included); the same steps issued eagerly, call by call, are reported
-    # beside it.
+    # Each step copies its inputs -- every layer's query and new K/V token,
+    # packed in one pinned host buffer -- to the device in one copy, places the
+    # new tokens in the suffix caches, runs every layer's decode through the
+    # public call and copies all layers' outputs back in one copy; the host
+    # waits for them before the next step.  As in the adapter's CUDA-graph
+    # decode, each step is one captured graph (copies included); the same
+    # steps issued eagerly, call by call, are reported beside it.
     e2e = None
     if not args.skip_e2e:
         pin = dict(pin_memory=True)
-        q_host = torch.stack([L.q for L in layers], 1).cpu().pin_memory()  # (cap, L, H, G, 1, D)
-        kv_host = None
-        if plan.holds_suffix:
-            kv_host = torch.stack([torch.stack([L.suffix_k, L.suffix_v]) for L in layers]).cpu()
-            kv_host = kv_host.permute(3, 0, 1, 2, 4).contiguous().pin_memory()  # (cap, L, 2, H, D)
+        q_words = plan.heads * G * D
+        kv_words = 2 * plan.heads * D if plan.holds_suffix else 0
+        host_in = torch.empty(cap, args.layers, q_words + kv_words, dtype=torch.bfloat16, **pin)
+        for li, L in enumerate(layers):
+            host_in[:, li, :q_words] = L.q.reshape(cap, q_words).cpu()
+            if plan.holds_suffix:
+                kv = torch.stack([L.suffix_k, L.suffix_v]).permute(2, 0, 1, 3)  # (cap, 2, H, D)
+                host_in[:, li, q_words:] = kv.reshape(cap, kv_words).cpu()
+        dev_in = torch.empty(args.layers, q_words + kv_words, device=dev, dtype=torch.bfloat16)
+        q_dev = [dev_in[li, :q_words].view(plan.heads, G, 1, D) for li in range(args.layers)]
+        kv_new = dev_in[:, q_words:].view(args.layers, 2, plan.heads, D) if kv_words else None
         reads_output = plan.seq_rank == 0  # every rank of a sequence group gets the output
-        out_host = torch.empty(cap, args.layers, heads_local, G, 1, D, dtype=torch.bfloat16, **pin)
-        q_dev = [torch.empty_like(L.q[0]) for L in layers]
+        out_host = torch.empty(cap, args.layers, plan.heads, G, D, dtype=torch.bfloat16, **pin)
 
         def e2e_step(s, *, graph_mode):
+            dev_in.copy_(host_in[s], non_blocking=True)
+            if kv_new is not None:
+                sk_all[:, :, s].copy_(kv_new[:, 0])
+                sv_all[:, :, s].copy_(kv_new[:, 1])
             if graph_mode:
                 length.fill_(s + 1)
             for li, L in enumerate(layers):
-                q_dev[li].copy_(q_host[s, li], non_blocking=True)
-                if kv_host is not None:
-                    L.suffix_k[:, s].copy_(kv_host[s, li, 0], non_blocking=True)
-                    L.suffix_v[:, s].copy_(kv_host[s, li, 1], non_blocking=True)
-            for li, L in enumerate(layers):
                 if graph_mode:
-                    res = decode(q_dev[li], L.summary, L.suffix_k, L.suffix_v, cfg,
-                                 anchor_mask=L.anchor, workspace=L.workspace,
-                                 suffix_length=length)
+                    decode(q_dev[li], L.summary, L.suffix_k, L.suffix_v, cfg,
+                           anchor_mask=L.anchor, workspace=L.workspace, suffix_length=length)
                 else:
-                    res = decode(q_dev[li], L.summary,
-                                 L.suffix_k[:, :s + 1] if plan.holds_suffix else None,
-                                 L.suffix_v[:, :s + 1] if plan.holds_suffix else None, cfg,
-                                 anchor_mask=L.anchor, workspace=L.workspace)
-                if reads_output:
-                    out_host[s, li].copy_(res.output, non_blocking=True)
+                    decode(q_dev[li], L.summary,
+                           L.suffix_k[:, :s + 1] if plan.holds_suffix else None,
+                           L.suffix_v[:, :s + 1] if plan.holds_suffix else None, cfg,
+                           anchor_mask=L.anchor, workspace=L.workspace)
+            if reads_output:
+                out_host[s].copy_(out_all, non_blocking=True)
 
         def timed(run_step):
             barrier(world)
@@ -619,15 +636,15 @@ def run_b200(args):
         del graph
         graph_us = timed(lambda s: e2e_graphs[s].replay())
         del e2e_graphs
-        h2d = args.layers * (q_dev[0].numel() * 2
-                             + (2 * heads_local * D * 2 if plan.holds_suffix else 0))
-        d2h = args.layers * heads_local * G * D * 2 if reads_output else 0
+        h2d = host_in[0].numel() * 2
+        d2h = out_all.numel() * 2 if reads_output else 0
         api = "refinekv_b200.parallel.SplitDecode" if split else "refinekv_b200.sparse_attention"
         e2e = {"value": round(graph_us, 1), "unit": "us/step",
                "h2d_bytes_per_step": int(sum_over_ranks(h2d, world)),
                "d2h_bytes_per_step": int(sum_over_ranks(d2h, world)),
-               "path": f"{api} via the C ABI, one CUDA graph per step (pinned-host copies "
-                       "inside), host waits for each step's outputs",
+               "path": f"{api} via the C ABI, one CUDA graph per step: one pinned-host copy of "
+                       "all layers' queries and new K/V tokens in, one copy of all outputs out, "
+                       "host waits for each step's outputs",
                "eager_value": round(eager_us, 1),
                "eager_path": f"{api}, eager call per layer, same copies and waits"}
 
