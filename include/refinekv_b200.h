@@ -276,6 +276,15 @@ RKV_API int rkv_decode_split(const rkv_summary* summary, const void* query, int 
                              int64_t max_blocks, void* exchange, size_t exchange_size,
                              unsigned stage, void* stream);
 
+/*
+ * Diagnostic: one bounded device wait on an mbarrier that nothing completes,
+ * with a limit of `limit_ns` (0 < limit_ns <= 1e9) instead of the kernels'
+ * 1 s; it ORs RKV_DEVICE_TIMEOUT into the device int32 *status and returns,
+ * the path every kernel takes when a wait runs out.  No counterpart in the
+ * reference (which has no device waits); used by the failure-handling tests.
+ */
+RKV_API int rkv_selftest_wait_timeout(int32_t* status, int64_t limit_ns, void* stream);
+
 /* Message of the last failing call on this host thread ("" if none). */
 RKV_API const char* rkv_last_error(void);
 RKV_API const char* rkv_status_string(int status);

@@ -65,13 +65,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for the phase with the given parity to complete; false after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for the phase with the given parity to complete; false after
+// `limit_ns` (1 s by default).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitLimitNs) return false;
+    if (global_ns() - start > limit_ns) return false;
   }
 }
 

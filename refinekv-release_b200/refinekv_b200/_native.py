@@ -51,6 +51,7 @@ EXPORTS = (
     "rkv_select_split",
     "rkv_split_exchange_slabs",
     "rkv_decode_split",
+    "rkv_selftest_wait_timeout",
     "rkv_last_error",
     "rkv_status_string",
     "rkv_abi_version",
@@ -113,6 +114,7 @@ _SIGNATURES = {
                                         c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
                                         c_ptr, ctypes.c_size_t, c_i64, c_i64, c_i64, c_ptr,
                                         ctypes.c_size_t, ctypes.c_uint, c_ptr]),
+    "rkv_selftest_wait_timeout": (ctypes.c_int, [c_ptr, c_i64, c_ptr]),
     "rkv_last_error": (ctypes.c_char_p, []),
     "rkv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "rkv_abi_version": (ctypes.c_int, []),
