@@ -71,6 +71,9 @@ def parse_args():
     ap.add_argument("--reduction", default="any")
     ap.add_argument("--anchors", type=int, default=32)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--query-scale", type=float, default=1.0,
+                    help="extra, not the headline workload: scale the queries (sharper "
+                         "attention, fewer refined blocks)")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
@@ -83,8 +86,9 @@ def parse_args():
 
 def workload_config(args, world, plan=None):
     return {
-        "workload": "llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
-        else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}",
+        "workload": ("llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
+                     else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}")
+                    + ("" if args.query_scale == 1.0 else f"-q{args.query_scale:g}"),
         "layers": args.layers,
         "prompt_tokens": args.tokens,
         "kv_heads": args.kv_heads,
@@ -100,6 +104,7 @@ def workload_config(args, world, plan=None):
         "cache_flush": "none needed: every layer's KV (heads x tokens x 256 B x 2) exceeds L2",
         "cuda_graph": True,
         "seed": args.seed,
+        "query_scale": args.query_scale,
     }
 
 
@@ -271,7 +276,8 @@ def run_reference(args):
                                 args.block_size, device=gen_dev)
     summary = ora.build_summary(data.keys, data.values, args.block_size)
     planted = data.planted_mean
-    anchors = synthetic.make_queries(args.seed, 0, -1, planted, args.group, args.anchors).cpu()
+    anchors = (synthetic.make_queries(args.seed, 0, -1, planted, args.group, args.anchors,
+                                      torch.float32) * args.query_scale).to(torch.bfloat16).cpu()
     anchor = ora.anchor_union(anchors, summary, args.eps, args.reduction) if args.anchors else None
     cap = args.warmup + args.steps
     tokens = [synthetic.make_decode_token(args.seed, 0, s, args.kv_heads, args.head_dim,
@@ -280,7 +286,8 @@ def run_reference(args):
     suffix_v = torch.cat([v for _, v in tokens], 1).cpu()
     times = []
     for step in range(cap):
-        q = synthetic.make_queries(args.seed, 0, step, planted, args.group)[0].cpu()
+        q = (synthetic.make_queries(args.seed, 0, step, planted, args.group, 1, torch.float32)[0]
+             * args.query_scale).to(torch.bfloat16).cpu()
         ks, vs = suffix_k[:, :step + 1], suffix_v[:, :step + 1]
         t0 = time.perf_counter()
         ora.sparse_attention(q, summary, ks, vs, args.eps, args.reduction, anchor_mask=anchor)
@@ -351,12 +358,14 @@ def build_layers(args, plan, group, dev):
         end.synchronize()
         summarize_ms.append(start.elapsed_time(end))
         parallel.merge_max_value_norm(L.summary.max_value_norm, group)
-        anchors = synthetic.make_queries(args.seed, li, -1, data.planted_mean, args.group,
-                                         args.anchors)[:, h0:h1]
+        anchors = (synthetic.make_queries(args.seed, li, -1, data.planted_mean, args.group,
+                                          args.anchors, torch.float32)[:, h0:h1]
+                   * args.query_scale).to(torch.bfloat16)
         L.anchor = (parallel.select_blocks_union_split(anchors.contiguous(), L.summary, cfg, plan,
                                                        group) if args.anchors else None)
-        L.q = torch.stack([synthetic.make_queries(args.seed, li, s, data.planted_mean,
-                                                  args.group)[0, h0:h1]
+        L.q = torch.stack([(synthetic.make_queries(args.seed, li, s, data.planted_mean,
+                                                   args.group, 1, torch.float32)[0, h0:h1]
+                            * args.query_scale).to(torch.bfloat16)
                            for s in range(cap)]).contiguous()
         L.suffix_k = L.suffix_v = None  # the generated tokens live on the group's last rank
         if plan.holds_suffix:
