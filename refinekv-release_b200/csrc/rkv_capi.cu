@@ -70,9 +70,9 @@ int device_info(DeviceInfo* info) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int tiles = 0;
-  int warps_a = 4, parts_a = 1, tpc_a = 1, stages_a = 1;
+  int warps_a = 8, parts_a = 1, tpc_a = 1, stages_a = 1;
   size_t smem_a = 0;
-  int warps_b = 4, parts_b = 1, tpc_b = 1, stages_b = 2, seg_cap = 0;
+  int warps_b = 8, parts_b = 1, tpc_b = 1, stages_b = 2, seg_cap = 0;
   size_t smem_b = 0;
   int warps_c = 4, stages_c = 2, ctas = 1;
   size_t smem_c = 0;
@@ -100,20 +100,29 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   dim = padded_dim(dim);  // shared memory and scratch hold padded rows
   pl->tiles = static_cast<int>(cdiv(blocks, kSelectTile));
   const int64_t rows = heads * instances;
-  // Phase A: about two CTAs per SM in total.
+  // Both selector kernels run one wave of at most one CTA per SM (8 warps,
+  // ~128 KB of TMA tiles each): a grid a few CTAs larger than the SM count
+  // doubles the work of the SMs that take two.  Phase A: one 16 KB stage
+  // (key-mean + ellipsoid tile) per warp.
+  const int one_wave = static_cast<int>(std::max<int64_t>(1, dev.sms / rows));
   if (fixed_parts_a > 0) {
     pl->parts_a = fixed_parts_a;
     pl->tpc_a = static_cast<int>(cdiv(pl->tiles, fixed_parts_a));
   } else {
-    split(pl->tiles, static_cast<int>(cdiv(2LL * dev.sms, rows)), &pl->parts_a, &pl->tpc_a);
+    split(pl->tiles, one_wave, &pl->parts_a, &pl->tpc_a);
   }
-  pl->stages_a = static_cast<int>(std::min<int64_t>(2, cdiv(pl->tpc_a, pl->warps_a)));
+  pl->stages_a = 1;
+  const int64_t stage_a = 2LL * kSelectTile * dim * 2;
+  pl->warps_a = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, 131072 / stage_a)));
   pl->smem_a = stats_smem_bytes(static_cast<int>(dim), pl->warps_a, pl->stages_a,
                                 static_cast<int>(group));
-  // Phase B: about one CTA per SM; segment capacity = blocks per CTA.
-  split(pl->tiles, static_cast<int>(cdiv(dev.sms, rows)), &pl->parts_b, &pl->tpc_b);
+  // Phase B: segment capacity = blocks per CTA.
+  split(pl->tiles, one_wave, &pl->parts_b, &pl->tpc_b);
   pl->seg_cap = pl->tpc_b * kSelectTile;
   pl->stages_b = decode ? 2 : 0;  // select mode stages no value tiles
+  const int64_t g8b = group <= 8 ? 8 : 16;
+  const int64_t per_warp_b = pl->stages_b * kSelectTile * dim * 2 + g8b * dim * 4;
+  pl->warps_b = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, 200000 / per_warp_b)));
   pl->smem_b = final_smem_bytes(static_cast<int>(dim), pl->warps_b, pl->stages_b,
                                 static_cast<int>(group), pl->tpc_b);
   if (pl->smem_a > static_cast<size_t>(dev.smem_optin) ||
@@ -191,7 +200,7 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
 // Sequence split: phase-A partials per row on every rank (fixed by the
 // largest rank's block count, not by the device, so that all ranks agree) and
 // the slab sizes of the exchange buffer.
-constexpr int kSplitStatsCtas = 296;
+constexpr int kSplitStatsCtas = 148;  // one wave on a B200 (fixed so that all ranks agree)
 
 struct SplitGeometry {
   int parts_a = 1;
@@ -207,7 +216,8 @@ SplitGeometry split_geometry(int64_t heads, int64_t group, int64_t max_blocks, i
   SplitGeometry g;
   int per = 1;
   split(static_cast<int>(cdiv(max_blocks, kSelectTile)),
-        static_cast<int>(cdiv(kSplitStatsCtas, heads * instances)), &g.parts_a, &per);
+        static_cast<int>(std::max<int64_t>(1, kSplitStatsCtas / (heads * instances))), &g.parts_a,
+        &per);
   const size_t rows = static_cast<size_t>(heads) * group;
   g.stats_slab = up256(rows * instances * g.parts_a * 16);
   g.ml_bytes = dim > 0 ? up256(rows * 8) : 0;
