@@ -111,13 +111,17 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   pdl_wait();
   pdl_launch_dependents();
 
+  // Key-mean and ellipsoid tiles are read once per step: evict them first so
+  // that z and delta, which the next kernel reads, stay in L2 at long
+  // contexts (the tiles of a 1M-token layer outsize L2).
+  const uint64_t stream_policy = l2_evict_first_policy();
   auto issue = [&](int j) {
     const int s = j % S;
     uint8_t* dst = tiles + (warp * S + s) * 2 * kTile;
     const int row = (t0 + warp + j * warps) * R;
     mbar_expect_tx(&bars[warp * S + s], 2 * kTile);
-    tma_tile<D>(dst, &maps.key_mean, &bars[warp * S + s], row, h, R);
-    tma_tile<D>(dst + kTile, &maps.ellipsoid, &bars[warp * S + s], row, h, R);
+    tma_tile_hint<D>(dst, &maps.key_mean, &bars[warp * S + s], row, h, R, stream_policy);
+    tma_tile_hint<D>(dst + kTile, &maps.ellipsoid, &bars[warp * S + s], row, h, R, stream_policy);
   };
   if (lane == 0) {
     for (int j = 0; j < min(S, mine); ++j) issue(j);
@@ -517,11 +521,35 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
     return;
   }
   const int mine = n_reps > warp ? (n_reps - warp + warps - 1) / warps : 0;
+  const uint64_t stream_policy = l2_evict_first_policy();
   auto issue = [&](int j) {
     const int s = j % S;
     mbar_expect_tx(&bars[warp * S + s], kTile);
-    tma_tile<D>(tiles + (warp * S + s) * kTile, &maps.value_mean, &bars[warp * S + s],
-                (t0 + rep_list[warp + j * warps]) * R, h, R);
+    tma_tile_hint<D>(tiles + (warp * S + s) * kTile, &maps.value_mean, &bars[warp * S + s],
+                     (t0 + rep_list[warp + j * warps]) * R, h, R, stream_policy);
+  };
+  // Logits (z) of the representatives of this warp's j-th tile; loaded one
+  // tile ahead so their latency overlaps the current tile's work.
+  auto load_logits = [&](int j, float (&lg)[R / 16][NT][4]) {
+    const bool have = j < mine;
+    const int k = have ? rep_list[warp + j * warps] : 0;
+    const uint32_t reps = have ? rep_bits[k] : 0u;
+    const int tile = t0 + k;
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+        const bool rep = (reps >> r) & 1u;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
+          lg[mt][nt][c] =
+              (rep && g < p.group)
+                  ? p.z[(static_cast<size_t>(ih) * p.group + g) * p.blocks + tile * R + r]
+                  : -INFINITY;
+        }
+      }
   };
   int issued = min(S, mine);
   if (lane == 0) {
@@ -535,6 +563,8 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
 #pragma unroll
     for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
   }
+  float next_logit[R / 16][NT][4];
+  load_logits(0, next_logit);
   for (int j = 0; j < mine; ++j) {
     const int s = j % S;
     if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
@@ -542,25 +572,14 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
       drain_pending(bars + warp * S, S, j, issued);
       break;
     }
-    const int k = rep_list[warp + j * warps];
-    const uint32_t reps = rep_bits[k];
-    const int tile = t0 + k;
     float logit[R / 16][NT][4];
 #pragma unroll
     for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
-        const bool rep = (reps >> r) & 1u;
+      for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
-          logit[mt][nt][c] =
-              (rep && g < p.group)
-                  ? p.z[(static_cast<size_t>(ih) * p.group + g) * p.blocks + tile * R + r]
-                  : -INFINITY;
-        }
-      }
+        for (int nt = 0; nt < NT; ++nt) logit[mt][nt][c] = next_logit[mt][nt][c];
+    load_logits(j + 1, next_logit);
     attend_tile<R, D, NT>(logit, smem_addr(tiles + (warp * S + s) * kTile), m, l, o,
                           p.split_probs != 0, lane);
     __syncwarp();
