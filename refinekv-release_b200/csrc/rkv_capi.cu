@@ -70,7 +70,7 @@ int device_info(DeviceInfo* info) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int tiles = 0;
-  int warps_a = 8, parts_a = 1, tpc_a = 1, stages_a = 1;
+  int warps_a = 8, parts_a = 1, tpc_a = 1, stages_a = 1, slots_a = 8;
   size_t smem_a = 0;
   int warps_b = 8, parts_b = 1, tpc_b = 1, stages_b = 2, seg_cap = 0;
   size_t smem_b = 0;
@@ -113,7 +113,12 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   }
   pl->stages_a = 1;
   const int64_t stage_a = 2LL * kSelectTile * dim * 2;
-  pl->warps_a = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, 131072 / stage_a)));
+  // No more warps than tiles per CTA (one head per GPU leaves one tile each).
+  pl->warps_a = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>({8, 131072 / stage_a, static_cast<int64_t>(pl->tpc_a)})));
+  // One LSE partial per warp; a sequence split fixes the count so that every
+  // rank's slab has the same layout.
+  pl->slots_a = fixed_parts_a > 0 ? kStatsSlots : pl->warps_a;
   pl->smem_a = stats_smem_bytes(static_cast<int>(dim), pl->warps_a, pl->stages_a,
                                 static_cast<int>(group));
   // Phase B: segment capacity = blocks per CTA.
@@ -122,7 +127,8 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   pl->stages_b = decode ? 2 : 0;  // select mode stages no value tiles
   const int64_t g8b = group <= 8 ? 8 : 16;
   const int64_t per_warp_b = pl->stages_b * kSelectTile * dim * 2 + g8b * dim * 4;
-  pl->warps_b = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, 200000 / per_warp_b)));
+  pl->warps_b = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>({8, 200000 / per_warp_b, static_cast<int64_t>(pl->tpc_b)})));
   pl->smem_b = final_smem_bytes(static_cast<int>(dim), pl->warps_b, pl->stages_b,
                                 static_cast<int>(group), pl->tpc_b);
   if (pl->smem_a > static_cast<size_t>(dev.smem_optin) ||
@@ -177,7 +183,8 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   const size_t rowsg = static_cast<size_t>(rows) * group;
   pl->status = take(256);
   pl->done = take(static_cast<size_t>(heads) * 4);
-  pl->lse = take(rowsg * pl->parts_a * 4 * 4);
+  // (Under a sequence split phase A writes into the exchange slab instead.)
+  pl->lse = take(fixed_parts_a > 0 ? 0 : rowsg * pl->parts_a * pl->slots_a * 4 * 4);
   pl->z = take(rowsg * blocks * 4);
   pl->delta = take(rowsg * blocks * 4);
   if (decode) {
@@ -219,7 +226,7 @@ SplitGeometry split_geometry(int64_t heads, int64_t group, int64_t max_blocks, i
         static_cast<int>(std::max<int64_t>(1, kSplitStatsCtas / (heads * instances))), &g.parts_a,
         &per);
   const size_t rows = static_cast<size_t>(heads) * group;
-  g.stats_slab = up256(rows * instances * g.parts_a * 16);
+  g.stats_slab = up256(rows * instances * g.parts_a * kStatsSlots * 16);
   g.ml_bytes = dim > 0 ? up256(rows * 8) : 0;
   g.output_slab = dim > 0 ? g.ml_bytes + up256(rows * dim * 4) : 0;
   return g;
@@ -391,6 +398,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.tiles = pl.tiles;
     p.tiles_per_cta = pl.tpc_a;
     p.parts = pl.parts_a;
+    p.slots = pl.slots_a;
     p.stages = pl.stages_a;
     p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
     p.z = at<float>(ws, pl.z);
@@ -411,7 +419,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.instances = static_cast<int>(inst);
     p.tiles = pl.tiles;
     p.tiles_per_cta = pl.tpc_b;
-    p.parts_a = pl.parts_a;
+    p.parts_a = pl.parts_a * pl.slots_a;  // phase-A partials per row
     p.parts = pl.parts_b;
     p.stages = pl.stages_b;
     p.eps = eps;

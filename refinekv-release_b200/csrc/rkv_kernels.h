@@ -10,6 +10,7 @@ namespace rkv {
 
 constexpr int kSelectTile = 32;  // summary blocks per selector tile
 constexpr int kMaxGroup = 16;    // GQA rows per KV head (two n8 tiles)
+constexpr int kStatsSlots = 8;   // phase-A partials per CTA under a sequence split (one per warp)
 
 enum Reduction { kMean = 0, kMax = 1, kAny = 2 };
 
@@ -44,11 +45,12 @@ struct StatsParams {
   const int64_t* counts;
   int heads, group, blocks, instances;
   int tiles, tiles_per_cta, parts;
+  int slots;     // partials per CTA: the warp count, or kStatsSlots under a split
   int stages;
   float scale;
   float* z;      // (instances*heads*group, blocks)
   float* delta;  // (instances*heads*group, blocks)
-  float* lse;    // (instances*heads*group, parts, 4): z max, z sum, c max, c sum
+  float* lse;    // (instances*heads*group, parts * slots, 4): z max, z sum, c max, c sum
   int* status;
 };
 
@@ -64,7 +66,8 @@ struct FinalParams {
   int reduction;
   const float* z;
   const float* delta;
-  // Phase-A partials: lse_slabs slabs of (instances*heads*group, parts_a, 4),
+  // Phase-A partials: lse_slabs slabs of (instances*heads*group, parts_a, 4)
+  // (parts_a = phase-A CTAs per row x partials per CTA),
   // lse_slab_floats apart (one slab per rank of a sequence split, else one).
   const float* lse;
   int lse_slabs;

@@ -34,33 +34,34 @@ constexpr float kDeltaSplit = 10.f;
 __device__ __forceinline__ float fexp(float x) { return __expf(x); }
 __device__ __forceinline__ float flog(float x) { return __logf(x); }
 
-// NaN-propagating clamp from above (torch.clamp(max=...)).
-__device__ __forceinline__ float clamp_hi(float x, float hi) { return x > hi ? hi : x; }
-
 // log(cosh(delta)) with the reference's two branches (reference.py:19-22).
+// Only the branch the reference selects is evaluated (a NaN takes the large
+// one, as torch.where does), so the value is the same with half the work.
 __device__ __forceinline__ float log_cosh(float delta) {
-  const float small = clamp_hi(delta, kDeltaSplit);
-  const float direct = flog((fexp(small) + fexp(-small)) * 0.5f);
-  const float large = delta + flog((1.f + fexp(-2.f * delta)) * 0.5f);
-  return delta <= kDeltaSplit ? direct : large;
+  if (delta <= kDeltaSplit) return flog((fexp(delta) + fexp(-delta)) * 0.5f);
+  return delta + flog((1.f + fexp(-2.f * delta)) * 0.5f);
 }
 
 // Risk of one (row, block): distortion ("mass") + importance ("value") terms,
 // evaluated in the same operation order as reference.py:25-34.
+// Only the branch the reference selects is evaluated (delta <= 10, else the
+// large-delta forms; a NaN takes the latter, as torch.where does).
 __device__ __forceinline__ float block_risk(float z, float delta, float log_z, float log_c,
                                             float vnorm, float vmax) {
-  const bool near = delta <= kDeltaSplit;
-  const float small = clamp_hi(delta, kDeltaSplit);
-  const float t = fexp(small);
   const float two_vmax = 2.f * vmax;
-  const float mass_direct = (two_vmax * fexp(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
-  const float e_neg = fexp(-delta);
-  float one_minus = 1.f - e_neg;
-  one_minus = one_minus < 1e-30f ? 1e-30f : one_minus;
-  const float lcm1 = (delta + 2.f * flog(one_minus)) - 0.693147182464599609375f;
-  const float mass_large = two_vmax * fexp((z - log_c) + lcm1);
-  const float mass = near ? mass_direct : mass_large;
-  const float tanh_half = near ? (t - 1.f) / (t + 1.f) : (1.f - e_neg) / (1.f + e_neg);
+  float mass, tanh_half;
+  if (delta <= kDeltaSplit) {
+    const float t = fexp(delta);
+    mass = (two_vmax * fexp(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
+    tanh_half = (t - 1.f) / (t + 1.f);
+  } else {
+    const float e_neg = fexp(-delta);
+    float one_minus = 1.f - e_neg;
+    one_minus = one_minus < 1e-30f ? 1e-30f : one_minus;
+    const float lcm1 = (delta + 2.f * flog(one_minus)) - 0.693147182464599609375f;
+    mass = two_vmax * fexp((z - log_c) + lcm1);
+    tanh_half = (1.f - e_neg) / (1.f + e_neg);
+  }
   const float importance = ((2.f * vnorm) * fexp(z - log_z)) * tanh_half;
   return mass + importance;
 }
@@ -90,8 +91,6 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   const int S = p.stages;
   uint8_t* tiles = smem;  // [warp][stage][key_mean | ellipsoid]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + warps * S * 2 * kTile);
-  float* red = reinterpret_cast<float*>(smem + warps * S * 2 * kTile +
-                                        round16(static_cast<size_t>(warps) * S * 8));
 
   const int ih = blockIdx.x;  // instance * heads + head
   const int inst = ih / p.heads, h = ih - inst * p.heads;
@@ -277,45 +276,44 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
       }
   }
 
-  // Reduce the (max, sum) pairs over the lanes that share a column (8 lanes;
-  // 16 with PACK4), then across warps.
+  // One (max, sum) pair per warp and column: reduce the maxima over the
+  // lanes that share a column (8 lanes; 16 with PACK4), rescale each lane's
+  // sum once, add the sums.  Each warp writes its own partial (slot
+  // part * slots + warp), so there is no CTA barrier; slots past the CTA's
+  // warp count (a fixed count under a sequence split) are left empty.
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
+      float mz = zm[nt][j], mc = cm[nt][j];
 #pragma unroll
       for (int off = PACK4 ? 2 : 4; off < 32; off <<= 1) {
-        const float om = __shfl_xor_sync(0xffffffffu, zm[nt][j], off);
-        const float os = __shfl_xor_sync(0xffffffffu, zs[nt][j], off);
-        lse_merge(zm[nt][j], zs[nt][j], om, os);
-        const float pm = __shfl_xor_sync(0xffffffffu, cm[nt][j], off);
-        const float ps = __shfl_xor_sync(0xffffffffu, cs[nt][j], off);
-        lse_merge(cm[nt][j], cs[nt][j], pm, ps);
+        mz = fmaxf(mz, __shfl_xor_sync(0xffffffffu, mz, off));
+        mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+      }
+      const float rz = mz == -INFINITY ? 0.f : mz, rc = mc == -INFINITY ? 0.f : mc;
+      float sz = zs[nt][j] == 0.f ? 0.f : zs[nt][j] * fexp(zm[nt][j] - rz);
+      float sc = cs[nt][j] == 0.f ? 0.f : cs[nt][j] * fexp(cm[nt][j] - rc);
+#pragma unroll
+      for (int off = PACK4 ? 2 : 4; off < 32; off <<= 1) {
+        sz += __shfl_xor_sync(0xffffffffu, sz, off);
+        sc += __shfl_xor_sync(0xffffffffu, sc, off);
       }
       const bool writer = PACK4 ? lane < 2 : lane < 4;
-      if (writer) {
-        const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
-        float* r = red + (warp * NT * 8 + g) * 4;
-        r[0] = zm[nt][j];
-        r[1] = zs[nt][j];
-        r[2] = cm[nt][j];
-        r[3] = cs[nt][j];
+      const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
+      if (writer && g < p.group) {
+        float* out = p.lse + ((static_cast<size_t>(ih) * p.group + g) * p.parts * p.slots +
+                              static_cast<size_t>(blockIdx.y) * p.slots + warp) * 4;
+        *reinterpret_cast<float4*>(out) = make_float4(mz, sz, mc, sc);
       }
     }
-  __syncthreads();
-  if (threadIdx.x < p.group) {
-    const int g = threadIdx.x;
-    float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    for (int w = 0; w < warps; ++w) {
-      const float* r = red + (w * NT * 8 + g) * 4;
-      lse_merge(m0, s0, r[0], r[1]);
-      lse_merge(m1, s1, r[2], r[3]);
+  if (warp == 0 && p.slots > warps) {
+    for (int i = lane; i < p.group * (p.slots - warps); i += 32) {
+      const int g = i / (p.slots - warps), w = warps + i % (p.slots - warps);
+      float* out = p.lse + ((static_cast<size_t>(ih) * p.group + g) * p.parts * p.slots +
+                            static_cast<size_t>(blockIdx.y) * p.slots + w) * 4;
+      *reinterpret_cast<float4*>(out) = make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
     }
-    float* out = p.lse + ((static_cast<size_t>(ih) * p.group + g) * p.parts + blockIdx.y) * 4;
-    out[0] = m0;
-    out[1] = s0;
-    out[2] = m1;
-    out[3] = s1;
   }
 }
 
@@ -641,9 +639,9 @@ cudaError_t final_dispatch(const FinalMaps& maps, const FinalParams& p, int warp
 }  // namespace
 
 size_t stats_smem_bytes(int dim, int warps, int stages, int group) {
-  const int g8 = group <= 8 ? 8 : 16;
+  (void)group;
   return kSmemSlack + static_cast<size_t>(warps) * stages * 2 * kSelectTile * dim * 2 +
-         round16(static_cast<size_t>(warps) * stages * 8) + static_cast<size_t>(warps) * g8 * 4 * 4;
+         round16(static_cast<size_t>(warps) * stages * 8);
 }
 
 size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta) {
