@@ -121,8 +121,10 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   pl->slots_a = fixed_parts_a > 0 ? kStatsSlots : pl->warps_a;
   pl->smem_a = stats_smem_bytes(static_cast<int>(dim), pl->warps_a, pl->stages_a,
                                 static_cast<int>(group));
-  // Phase B: segment capacity = blocks per CTA.
-  split(pl->tiles, one_wave, &pl->parts_b, &pl->tpc_b);
+  // Phase B: at least four tiles per CTA -- each CTA leaves one
+  // representative partial per row that the combine merges, so a few heads
+  // over many one-tile CTAs would flood it.  Segment capacity = blocks per CTA.
+  split(pl->tiles, std::min(one_wave, std::max(1, pl->tiles / 4)), &pl->parts_b, &pl->tpc_b);
   pl->seg_cap = pl->tpc_b * kSelectTile;
   pl->stages_b = decode ? 2 : 0;  // select mode stages no value tiles
   const int64_t g8b = group <= 8 ? 8 : 16;
