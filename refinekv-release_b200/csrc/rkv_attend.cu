@@ -368,10 +368,12 @@ struct CombineLayout {
 // turned into weights exp(m - M_g)) and this warp's o^T rows (every 8th
 // partial, kBatch per round, kept in registers).  The warps' sums are then
 // added in shared memory.
-template <int D, int G8>
+// QN: the 16-byte pieces of each (source, channel) o^T row that hold real
+// group rows (ceil(group / 4)); only those are loaded.
+template <int D, int G8, int QN>
 __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   constexpr int kWarps = 8;
-  constexpr int kBatch = G8 == 8 ? 12 : 6;
+  constexpr int kBatch = 24 / QN;  // sources per warp and round (24 float4 in flight)
   constexpr int kStage = 4;  // m/l entries staged per thread per round
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
@@ -425,13 +427,13 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
                                            d * G8);
   };
   // This warp's first round of o rows, issued before anything else is waited on.
-  float4 v[kBatch][G8 / 4];
+  float4 v[kBatch][QN];
   auto load_round = [&](int k0) {
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int k = k0 + u * kWarps;
 #pragma unroll
-      for (int q = 0; q < G8 / 4; ++q) {
+      for (int q = 0; q < QN; ++q) {
         v[u][q] = k < nsrc ? __ldcg(o_row(k) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
@@ -492,7 +494,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
       const int k = k0 + u * kWarps;
       if (k >= nsrc) continue;
 #pragma unroll
-      for (int q = 0; q < G8 / 4; ++q) {
+      for (int q = 0; q < QN; ++q) {
         const float* w = wgt + k * G8 + 4 * q;
         // An unused slot may hold a stale value: weight 0 must not multiply it.
         if (w[0] != 0.f) acc[4 * q + 0] += w[0] * v[u][q].x;
@@ -607,9 +609,9 @@ cudaError_t attend_dim(const AttendMaps& maps, const AttendParams& p, int dim, i
   }
 }
 
-template <int D, int G8>
+template <int D, int G8, int QN>
 cudaError_t launch_combine_t(const CombineParams& p, cudaStream_t stream, bool pdl) {
-  const void* kernel = reinterpret_cast<const void*>(combine_kernel<D, G8>);
+  const void* kernel = reinterpret_cast<const void*>(combine_kernel<D, G8, QN>);
   const size_t smem = CombineLayout(p.heads, p.parts_b, G8, p.max_sources).bytes;
   cudaError_t err = ensure_smem_limit(kernel, smem);
   if (err != cudaSuccess) return err;
@@ -619,8 +621,12 @@ cudaError_t launch_combine_t(const CombineParams& p, cudaStream_t stream, bool p
 
 template <int D>
 cudaError_t combine_g(const CombineParams& p, cudaStream_t stream, bool pdl) {
-  if (p.group <= 8) return launch_combine_t<D, 8>(p, stream, pdl);
-  return launch_combine_t<D, 16>(p, stream, pdl);
+  switch ((p.group + 3) / 4) {
+    case 1: return launch_combine_t<D, 8, 1>(p, stream, pdl);
+    case 2: return launch_combine_t<D, 8, 2>(p, stream, pdl);
+    case 3: return launch_combine_t<D, 16, 3>(p, stream, pdl);
+    default: return launch_combine_t<D, 16, 4>(p, stream, pdl);
+  }
 }
 
 
