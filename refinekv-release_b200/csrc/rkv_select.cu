@@ -384,9 +384,14 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
       anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     }
   };
+  // Two tiles ahead: the first two tiles' inputs are loaded here, and every
+  // iteration issues the loads of the tile two steps on.
   float zr[GM], dr[GM], vnorm = 0.f;
   bool anc = false;
+  float zn[GM], dn[GM], vnorm_n = 0.f;
+  bool anc_n = false;
   load_tile(t0 + warp, zr, dr, vnorm, anc);
+  load_tile(t0 + warp + warps, zn, dn, vnorm_n, anc_n);
 
   // Row-global normalisers from the phase-A partials (of every rank's slab
   // under a sequence split): one warp per row, lanes load partials in
@@ -424,9 +429,9 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
 
   // Pass 1: decisions, one lane per block.
   for (int t = t0 + warp; t < t1; t += warps) {
-    float zn[GM], dn[GM], vnorm_n = 0.f;
-    bool anc_n = false;
-    load_tile(t + warps, zn, dn, vnorm_n, anc_n);  // the next tile's inputs in flight
+    float znn[GM], dnn[GM], vnorm_nn = 0.f;
+    bool anc_nn = false;
+    load_tile(t + 2 * warps, znn, dnn, vnorm_nn, anc_nn);  // two tiles ahead
     const int b = t * R + lane;
     const bool valid = b < p.blocks;
     bool sel = false;
@@ -482,9 +487,13 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
     for (int g = 0; g < GM; ++g) {
       zr[g] = zn[g];
       dr[g] = dn[g];
+      zn[g] = znn[g];
+      dn[g] = dnn[g];
     }
     vnorm = vnorm_n;
     anc = anc_n;
+    vnorm_n = vnorm_nn;
+    anc_n = anc_nn;
   }
   if (!p.decode) return;
   __syncthreads();
