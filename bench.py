@@ -319,7 +319,7 @@ def run_reference(args):
         "e2e": {"value": round(value, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -724,14 +724,28 @@ def run_b200(args):
             "dense_attention": dense,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
         dist.destroy_process_group()
 
 
+# The result line goes to the process's original stdout; everything else the
+# process writes to file descriptor 1 (NCCL's version banner, library
+# messages) is sent to stderr, so stdout holds exactly the one JSON line.
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (json.dumps(line) + "\n").encode())
+
+
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
