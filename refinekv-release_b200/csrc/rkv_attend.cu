@@ -389,8 +389,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   float* lsum = reinterpret_cast<float*>(smem + lay.lsum);  // [sources][G8]
   float* red = reinterpret_cast<float*>(smem + lay.red);    // [warps][32][G8]
 
-  pdl_wait();
-  pdl_launch_dependents();
+  // Everything but the attention partials was complete before the attention
+  // kernel passed its own dependency wait (the suffix length, the selector's
+  // page counts and representative partials), and this grid launches only
+  // after every attention CTA has passed it: the work list and the
+  // representative rows are read before this grid's wait, off the critical
+  // path behind the attention kernel.
   const int suffix_len = visible_suffix(p.has_suffix, p.suffix_len_ptr, p.suffix_len_host,
                                         p.suffix_capacity, p.status);
   build_work_list(p.seg_count, H, PB, (suffix_len + p.page - 1) / p.page, seg_pre, hstart);
@@ -413,6 +417,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int nsrc = PB + n_att;
   if (nsrc > p.max_sources) {  // cannot happen with the host's plan; never read past the table
     if (threadIdx.x == 0) atomicOr(p.status, kStatusBadInput);
+    pdl_wait();
+    pdl_launch_dependents();
     return;
   }
   auto src_index = [&](int k) -> size_t {
@@ -426,41 +432,50 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     return reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) + src_index(k) * D * G8 +
                                            d * G8);
   };
-  // This warp's first round of o rows, issued before anything else is waited on.
+  // This warp's first round of o rows: sources [k_lo, k_hi) of it (the
+  // representative rows before the wait, the attention rows after it).
   float4 v[kBatch][QN];
-  auto load_round = [&](int k0) {
+  auto load_round = [&](int k0, int k_lo, int k_hi) {
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const int k = k0 + u * kWarps;
 #pragma unroll
       for (int q = 0; q < QN; ++q) {
-        v[u][q] = k < nsrc ? __ldcg(o_row(k) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k >= k_lo && k < k_hi) v[u][q] = __ldcg(o_row(k) + q);
+        else if (k_lo == 0) v[u][q] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
   };
-  load_round(warp);
-  // m and l of every source, loaded kStage at a time per thread.
-  for (int i0 = threadIdx.x; i0 < nsrc * G8; i0 += blockDim.x * kStage) {
-    float mv[kStage], lv[kStage];
+  // m and l of sources [k_lo, k_hi), loaded kStage at a time per thread.
+  auto stage_ml = [&](int k_lo, int k_hi) {
+    for (int i0 = k_lo * G8 + threadIdx.x; i0 < k_hi * G8; i0 += blockDim.x * kStage) {
+      float mv[kStage], lv[kStage];
 #pragma unroll
-    for (int u = 0; u < kStage; ++u) {
-      const int i = i0 + u * blockDim.x;
-      if (i < nsrc * G8) {
-        const int k = i / G8, g = i - k * G8;
-        const size_t at = src_index(k) * G8 + g;
-        mv[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + at);
-        lv[u] = __ldcg((k < PB ? p.rep_l : p.att_l) + at);
+      for (int u = 0; u < kStage; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < k_hi * G8) {
+          const int k = i / G8, g = i - k * G8;
+          const size_t at = src_index(k) * G8 + g;
+          mv[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + at);
+          lv[u] = __ldcg((k < PB ? p.rep_l : p.att_l) + at);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStage; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < k_hi * G8) {
+          wgt[i] = mv[u];
+          lsum[i] = lv[u];
+        }
       }
     }
-#pragma unroll
-    for (int u = 0; u < kStage; ++u) {
-      const int i = i0 + u * blockDim.x;
-      if (i < nsrc * G8) {
-        wgt[i] = mv[u];
-        lsum[i] = lv[u];
-      }
-    }
-  }
+  };
+  load_round(warp, 0, PB);
+  stage_ml(0, PB);
+  pdl_wait();
+  pdl_launch_dependents();
+  load_round(warp, PB, nsrc);
+  stage_ml(PB, nsrc);
   __syncthreads();
   for (int g = warp; g < G8; g += kWarps) {
     float mx = -INFINITY;
@@ -504,7 +519,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
       }
     }
     if (k0 + kBatch * kWarps >= nsrc) break;
-    load_round(k0 + kBatch * kWarps);
+    load_round(k0 + kBatch * kWarps, 0, nsrc);
   }
 #pragma unroll
   for (int g = 0; g < G8; ++g) red[(warp * 32 + lane) * G8 + g] = acc[g];

@@ -368,30 +368,30 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   pdl_launch_dependents();
 
   // Pass-1 inputs of a tile (one lane per block): z and delta of every row,
-  // the value norm and the anchor bit.  The first tile's are loaded before
-  // the normalisers are merged and each next tile's before the current one
-  // is evaluated, so the loads overlap other work.
-  auto load_tile = [&](int t, float (&zr)[GM], float (&dr)[GM], float& vn, bool& anc) {
+  // the value norm and the anchor bit.  Three buffers rotate by name through
+  // a loop unrolled three times, so the loads of the tile two steps ahead
+  // are in flight while the current tile is decided (a register copy at the
+  // end of each iteration would wait for them).
+  struct TileIn {
+    float z[GM], d[GM], vn;
+    bool anc;
+  };
+  auto load_tile = [&](int t, TileIn& in) {
     const int b = t * R + lane;
     if (t < t1 && b < p.blocks) {
-      vn = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
+      in.vn = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
         const size_t row = static_cast<size_t>(ih) * p.group + (g < p.group ? g : 0);
-        zr[g] = p.z[row * p.blocks + b];
-        dr[g] = p.delta[row * p.blocks + b];
+        in.z[g] = p.z[row * p.blocks + b];
+        in.d[g] = p.delta[row * p.blocks + b];
       }
-      anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+      in.anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     }
   };
-  // Two tiles ahead: the first two tiles' inputs are loaded here, and every
-  // iteration issues the loads of the tile two steps on.
-  float zr[GM], dr[GM], vnorm = 0.f;
-  bool anc = false;
-  float zn[GM], dn[GM], vnorm_n = 0.f;
-  bool anc_n = false;
-  load_tile(t0 + warp, zr, dr, vnorm, anc);
-  load_tile(t0 + warp + warps, zn, dn, vnorm_n, anc_n);
+  TileIn buf_a, buf_b, buf_c;
+  load_tile(t0 + warp, buf_a);
+  load_tile(t0 + warp + warps, buf_b);
 
   // Row-global normalisers from the phase-A partials (of every rank's slab
   // under a sequence split): one warp per row, lanes load partials in
@@ -428,10 +428,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   const float vmax = p.max_value_norm[h];
 
   // Pass 1: decisions, one lane per block.
-  for (int t = t0 + warp; t < t1; t += warps) {
-    float znn[GM], dnn[GM], vnorm_nn = 0.f;
-    bool anc_nn = false;
-    load_tile(t + 2 * warps, znn, dnn, vnorm_nn, anc_nn);  // two tiles ahead
+  auto decide = [&](int t, const TileIn& in) {
     const int b = t * R + lane;
     const bool valid = b < p.blocks;
     bool sel = false;
@@ -445,7 +442,8 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
       }
       float risk[GM];
 #pragma unroll
-      for (int g = 0; g < GM; ++g) risk[g] = block_risk(zr[g], dr[g], lz[g], lc[g], vnorm, vmax);
+      for (int g = 0; g < GM; ++g)
+        risk[g] = block_risk(in.z[g], in.d[g], lz[g], lc[g], in.vn, vmax);
       float agg = p.reduction == kMax ? -INFINITY : 0.f;
       bool any = false, bad = false;
 #pragma unroll
@@ -469,7 +467,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
       } else {
         dec = any;
       }
-      sel = dec || bad || bad_global || anc;
+      sel = dec || bad || bad_global || in.anc;
       uint8_t* mk = p.mask + static_cast<size_t>(h) * p.blocks + b;
       if (p.accumulate) {
         if (sel) *mk = 1;
@@ -483,17 +481,16 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
       sel_bits[t - t0] = sb;
       rep_bits[t - t0] = vb & ~sb;
     }
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      zr[g] = zn[g];
-      dr[g] = dn[g];
-      zn[g] = znn[g];
-      dn[g] = dnn[g];
-    }
-    vnorm = vnorm_n;
-    anc = anc_n;
-    vnorm_n = vnorm_nn;
-    anc_n = anc_nn;
+  };
+  for (int t = t0 + warp; t < t1; t += 3 * warps) {
+    load_tile(t + 2 * warps, buf_c);
+    decide(t, buf_a);
+    if (t + warps >= t1) break;
+    load_tile(t + 3 * warps, buf_a);
+    decide(t + warps, buf_b);
+    if (t + 2 * warps >= t1) break;
+    load_tile(t + 4 * warps, buf_b);
+    decide(t + 2 * warps, buf_c);
   }
   if (!p.decode) return;
   __syncthreads();
