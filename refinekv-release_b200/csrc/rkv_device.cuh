@@ -132,6 +132,25 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Bring one [rows x D] bf16 tile into L2 (no shared memory, no barrier, no
+// data returned): warms L2 and the address translation for a later tma_tile
+// of the same rows.  L2 is the point of coherence, so a prefetch issued
+// before a dependency wait can never make a later read stale.
+template <int D>
+__device__ __forceinline__ void tma_prefetch_tile(const CUtensorMap* map, int row, int head) {
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(i * 64), "r"(row), "r"(head)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Order this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) writes to the same buffers.
 __device__ __forceinline__ void fence_proxy_async() {

@@ -25,6 +25,9 @@ namespace {
 
 constexpr float kInflate = 1.00390625f;  // 1 + 2^-8
 constexpr float kDeltaSplit = 10.f;
+// Summary tiles per warp fetched into L2 ahead of the stats kernel's
+// dependency wait (two per warp: about 38 MB over a full B200 at D 128).
+constexpr int kStatsPrefetch = 2;
 
 // exp and log on the special-function unit (__expf / __logf): a few ulp from
 // the correctly rounded functions, far inside the 1e-3 relative eps margin
@@ -105,6 +108,14 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[warp * S + s], 1);
     mbar_fence_init();
+    // The summaries do not change during decode: this warp's first tiles go
+    // to L2 before the dependency wait, so their first-touch latency
+    // overlaps the previous kernel's tail (nothing is consumed before it).
+    for (int j = 0; j < min(kStatsPrefetch, mine); ++j) {
+      const int row = (t0 + warp + j * warps) * R;
+      tma_prefetch_tile<D>(&maps.key_mean, row, h);
+      tma_prefetch_tile<D>(&maps.ellipsoid, row, h);
+    }
   }
   __syncwarp();
   pdl_wait();
@@ -362,6 +373,19 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   if (threadIdx.x == 0) {
     flags[0] = 0;
     if (p.decode) tma_prefetch_desc(&maps.value_mean);
+  }
+  // Value norms and anchor bits do not change during decode: the lines of
+  // this warp's first two tiles go to L2 before the dependency wait (the
+  // first and last lane's addresses cover a tile's lines).
+  if (lane == 0 || lane == 31) {
+    for (int j = 0; j < 2; ++j) {
+      const int t = t0 + warp + j * warps;
+      const int b = min(t * R + lane, p.blocks - 1);
+      if (t < t1) {
+        prefetch_l2(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
+        if (p.anchor != nullptr) prefetch_l2(p.anchor + static_cast<size_t>(h) * p.blocks + b);
+      }
+    }
   }
   __syncthreads();
   pdl_wait();
