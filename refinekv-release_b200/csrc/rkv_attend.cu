@@ -117,6 +117,16 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       tma_prefetch_desc(&maps.key_suffix);
       tma_prefetch_desc(&maps.value_suffix);
     }
+    if (p.suffix_len_ptr != nullptr) prefetch_l2(p.suffix_len_ptr);
+  }
+  // The query lines (all heads', spread over the CTAs) go to L2 before the
+  // dependency wait; a prefetch returns no data, so a query the previous
+  // kernel is still writing is read correctly after the wait.
+  {
+    const int q_lines = (H * p.group * p.dim * (p.query_f32 ? 4 : 2) + 127) / 128;
+    for (int i = blockIdx.x + threadIdx.x * gridDim.x; i < q_lines; i += blockDim.x * gridDim.x) {
+      prefetch_l2(static_cast<const char*>(p.query) + static_cast<size_t>(i) * 128);
+    }
   }
   pdl_wait();
   pdl_launch_dependents();

@@ -252,41 +252,64 @@ __device__ __forceinline__ float bf16_round(float x) {
 
 // Query B fragments for S^T = tile . q^T.  Thread lane holds, for n-tile nt
 // and k-step ks, q[g][d] with g = nt*8 + lane/4 and
-// d = ks*16 + 2*(lane%4) + {0,1} (b0) and + 8 (b1).  Rows g >= group are 0.
-// `square` builds the fragments of bf16(q^2) instead (the ellipsoid term).
+// d = ks*16 + 2*(lane%4) + {0,1} (b0) and + 8 (b1).  Rows g >= group and
+// channels d >= dim are 0.  `square` builds the fragments of bf16(q^2)
+// instead (the ellipsoid term).  Every load is issued unconditionally from a
+// clamped in-range address before any value is used, so the whole query
+// arrives in one memory round trip.
 template <int D, int NT>
 __device__ __forceinline__ void load_query_frags(uint32_t (&qb)[D / 16][NT][2], const void* q,
                                                  int q_is_f32, int group, int dim, int lane,
                                                  bool square) {
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
+  auto finish = [&](int nt, int ks, int half, float x0, float x1) {
     const int g = nt * 8 + (lane >> 2);
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int d = ks * 16 + half * 8 + 2 * (lane & 3);
-        float x0 = 0.f, x1 = 0.f;
-        if (g < group && d < dim) {  // channels past the real width are zero
-          if (q_is_f32) {
-            const float* qf = static_cast<const float*>(q) + g * dim + d;
-            x0 = bf16_round(qf[0]);
-            x1 = bf16_round(qf[1]);
-          } else {
-            const __nv_bfloat162 v =
-                *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(q) +
-                                                         g * dim + d);
-            x0 = __low2float(v);
-            x1 = __high2float(v);
-          }
-          if (square) {
-            x0 = x0 * x0;
-            x1 = x1 * x1;
-          }
-        }
-        qb[ks][nt][half] = pack_bf16(x0, x1);
-      }
+    const int d = ks * 16 + half * 8 + 2 * (lane & 3);
+    if (!(g < group && d < dim)) x0 = x1 = 0.f;
+    if (square) {
+      x0 = x0 * x0;
+      x1 = x1 * x1;
     }
+    qb[ks][nt][half] = pack_bf16(x0, x1);
+  };
+  auto offset = [&](int nt, int ks, int half) {
+    const int g = min(nt * 8 + (lane >> 2), group - 1);
+    const int d = min(ks * 16 + half * 8 + 2 * (lane & 3), dim - 2);
+    return g * dim + d;
+  };
+  if (q_is_f32) {
+    const float* qf = static_cast<const float*>(q);
+    float2 raw[NT][D / 16][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+          raw[nt][ks][half] = *reinterpret_cast<const float2*>(qf + offset(nt, ks, half));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+          finish(nt, ks, half, bf16_round(raw[nt][ks][half].x), bf16_round(raw[nt][ks][half].y));
+  } else {
+    const __nv_bfloat16* qh = static_cast<const __nv_bfloat16*>(q);
+    __nv_bfloat162 raw[NT][D / 16][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+          raw[nt][ks][half] = *reinterpret_cast<const __nv_bfloat162*>(qh + offset(nt, ks, half));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+          finish(nt, ks, half, __low2float(raw[nt][ks][half]), __high2float(raw[nt][ks][half]));
   }
 }
 

@@ -117,6 +117,19 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
       tma_prefetch_tile<D>(&maps.ellipsoid, row, h);
     }
   }
+  // Token counts of the same tiles (lanes 0, 16 and 31 cover a tile's
+  // 256 bytes) and the query rows (which the previous kernel may still be
+  // writing: a prefetch only warms L2 and the translation, it returns no data).
+  if (lane == 0 || lane == 16 || lane == 31) {
+    for (int j = 0; j < min(kStatsPrefetch, mine); ++j) {
+      prefetch_l2(p.counts + min((t0 + warp + j * warps) * R + lane, p.blocks - 1));
+    }
+  }
+  const char* q = static_cast<const char*>(p.query) +
+                  static_cast<size_t>(ih) * p.group * p.dim * (p.query_f32 ? 4 : 2);
+  for (int i = threadIdx.x; i * 128 < p.group * p.dim * (p.query_f32 ? 4 : 2); i += blockDim.x) {
+    prefetch_l2(q + i * 128);
+  }
   __syncwarp();
   pdl_wait();
   pdl_launch_dependents();
@@ -137,8 +150,29 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
     for (int j = 0; j < min(S, mine); ++j) issue(j);
   }
 
-  const void* q = static_cast<const char*>(p.query) +
-                  static_cast<size_t>(ih) * p.group * p.dim * (p.query_f32 ? 4 : 2);
+  // This lane's block rows within a tile (the C-fragment rows it finishes).
+  constexpr int kHalves = PACK4 ? 1 : 2;
+  int lane_rows[R / 16][2];
+#pragma unroll
+  for (int mt = 0; mt < R / 16; ++mt) {
+    lane_rows[mt][0] = mt * 16 + (lane >> 2) + (PACK4 && ((lane >> 1) & 1) ? 8 : 0);
+    lane_rows[mt][1] = lane_rows[mt][0] + 8;
+  }
+  // Token counts of this lane's blocks in tile j; the first tile's are
+  // requested before the query, then each next tile's one step ahead.
+  auto load_counts = [&](int j, long long (&c)[R / 16][2]) {
+    const int tile = t0 + warp + j * warps;
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < kHalves; ++hf) {
+        const int b = tile * R + lane_rows[mt][hf];
+        c[mt][hf] = (j < mine && b < p.blocks) ? __ldg(p.counts + b) : 1;
+      }
+  };
+  long long cnt_next[R / 16][2];
+  load_counts(0, cnt_next);
+
   uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
   uint32_t packed[PACK4 ? 2 * D / 16 : 1][2];
   if constexpr (PACK4) {
@@ -159,28 +193,16 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
       zs[nt][j] = cs[nt][j] = 0.f;
     }
 
-  // This lane's block rows within a tile (the C-fragment rows it finishes).
-  constexpr int kHalves = PACK4 ? 1 : 2;
-  int lane_rows[R / 16][2];
-#pragma unroll
-  for (int mt = 0; mt < R / 16; ++mt) {
-    lane_rows[mt][0] = mt * 16 + (lane >> 2) + (PACK4 && ((lane >> 1) & 1) ? 8 : 0);
-    lane_rows[mt][1] = lane_rows[mt][0] + 8;
-  }
-
   int issued = min(S, mine);
   for (int j = 0; j < mine; ++j) {
     const int s = j % S;
     const int tile = t0 + warp + j * warps;
-    // Token counts of this lane's blocks, loaded while the tiles land.
     long long cnt[R / 16][2];
 #pragma unroll
     for (int mt = 0; mt < R / 16; ++mt)
 #pragma unroll
-      for (int hf = 0; hf < kHalves; ++hf) {
-        const int b = tile * R + lane_rows[mt][hf];
-        cnt[mt][hf] = b < p.blocks ? __ldg(p.counts + b) : 1;
-      }
+      for (int hf = 0; hf < kHalves; ++hf) cnt[mt][hf] = cnt_next[mt][hf];
+    load_counts(j + 1, cnt_next);
     if (!warp_wait(&bars[warp * S + s], (j / S) & 1)) {
       if (lane == 0) atomicOr(p.status, kStatusTimeout);
       drain_pending(bars + warp * S, S, j, issued);
