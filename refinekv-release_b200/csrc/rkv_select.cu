@@ -28,6 +28,8 @@ constexpr float kDeltaSplit = 10.f;
 // Summary tiles per warp fetched into L2 ahead of the stats kernel's
 // dependency wait (two per warp: about 38 MB over a full B200 at D 128).
 constexpr int kStatsPrefetch = 2;
+// Normaliser partials each lane loads before merging any of them.
+constexpr int kNormBatch = 8;
 
 // exp and log on the special-function unit (__expf / __logf): a few ulp from
 // the correctly rounded functions, far inside the 1e-3 relative eps margin
@@ -445,12 +447,22 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   for (int g = warp; g < p.group; g += warps) {
     const float* in = p.lse + (static_cast<size_t>(ih) * p.group + g) * p.parts_a * 4;
     float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    for (int k = lane; k < p.parts_a * p.lse_slabs; k += 32) {
-      const int slab = k / p.parts_a, part_k = k - slab * p.parts_a;
-      const float4 v =
-          *reinterpret_cast<const float4*>(in + slab * p.lse_slab_floats + 4 * part_k);
-      lse_merge(m0, s0, v.x, v.y);
-      lse_merge(m1, s1, v.z, v.w);
+    const int n_part = p.parts_a * p.lse_slabs;
+    for (int k0 = lane; k0 < n_part; k0 += 32 * kNormBatch) {
+      float4 v[kNormBatch];  // all of a batch's loads in flight before any merge
+#pragma unroll
+      for (int u = 0; u < kNormBatch; ++u) {
+        const int k = k0 + 32 * u;
+        const int slab = k / p.parts_a, part_k = k - slab * p.parts_a;
+        v[u] = k < n_part
+                   ? *reinterpret_cast<const float4*>(in + slab * p.lse_slab_floats + 4 * part_k)
+                   : make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kNormBatch; ++u) {
+        lse_merge(m0, s0, v[u].x, v[u].y);
+        lse_merge(m1, s1, v[u].z, v[u].w);
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
@@ -543,16 +555,32 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
 
   // Deterministic compaction: tile offsets in block order, and the list of
   // tiles holding at least one representative (rank k goes to warp k % warps).
-  if (threadIdx.x == 0) {
+  // Warp 0 scans 32 tiles at a time: a shuffle prefix sum of the selected
+  // counts and a ballot rank for the representative list.
+  if (warp == 0) {
+    const int n_t = t1 - t0;
     int acc = 0, reps = 0;
-    for (int k = 0; k < t1 - t0; ++k) {
-      offsets[k] = acc;
-      acc += __popc(sel_bits[k]);
-      if (rep_bits[k] != 0u) rep_list[reps++] = k;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int c = k < n_t ? __popc(sel_bits[k]) : 0;
+      const bool has_rep = k < n_t && rep_bits[k] != 0u;
+      int incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) offsets[k] = acc + incl - c;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
+      const uint32_t rb = __ballot_sync(0xffffffffu, has_rep);
+      if (has_rep) rep_list[reps + __popc(rb & ((1u << lane) - 1u))] = k;
+      reps += __popc(rb);
     }
-    offsets[t1 - t0] = acc;
-    flags[1] = reps;
-    p.seg_count[h * p.parts + part] = acc;
+    if (lane == 0) {
+      offsets[n_t] = acc;
+      flags[1] = reps;
+      p.seg_count[h * p.parts + part] = acc;
+    }
   }
   __syncthreads();
   int* ids = p.sel_ids + (static_cast<size_t>(h) * p.parts + part) * p.seg_cap;
