@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define RKV_ABI_VERSION 1
+#define RKV_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define RKV_API __attribute__((visibility("default")))
@@ -81,6 +81,19 @@ typedef enum rkv_status {
  *   counts: (blocks,) int64 tokens per block (block_size, tail for the last).
  *   key_mean / value_mean / ellipsoid: (heads, blocks, head_dim) bf16, contiguous.
  *   value_norm: (heads, blocks) fp32; max_value_norm: (heads,) fp32.
+ *
+ * Batched decode (no reference counterpart: the reference decodes one
+ * sequence, transformers.py:448-449).  With sequences > 1 the summary holds
+ * several prompts that decode in lockstep: the head axis is sequence-major
+ * (heads = sequences x KV heads, row = sequence * (heads / sequences) +
+ * head), prompt_lengths is a (sequences,) int64 device array, prompt_length
+ * is their maximum and blocks = ceil(prompt_length / block_size); counts is
+ * (sequences, blocks) with 0 for the blocks past a sequence's prompt, whose
+ * summary rows must be zero.  Such padding blocks are never selected,
+ * represented or read; their mask bytes are written 0.  Queries, suffix
+ * K/V, anchors, masks and outputs use the same sequence-major head axis, and
+ * every sequence sees the same suffix length.  sequences 0 or 1 is one prompt
+ * (prompt_lengths unused).
  */
 typedef struct rkv_summary {
   const void* key_pages;
@@ -98,6 +111,8 @@ typedef struct rkv_summary {
   int64_t block_size;
   int64_t head_dim;
   int64_t prompt_length;
+  int64_t sequences;              /* batched decode: see above; 0 or 1 for one prompt */
+  const int64_t* prompt_lengths;  /* (sequences,) device array when sequences > 1 */
 } rkv_summary;
 
 /*

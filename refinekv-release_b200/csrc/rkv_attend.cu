@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       }
       const int block = __ldg(p.sel_ids + (static_cast<size_t>(h) * PB + a) * p.seg_cap +
                               (pos - pre[a]));
-      d = make_int4(h, block * R, min(R, p.prompt_length - block * R), 0);
+      d = make_int4(h, block * R, min(R, p.seq.prompt(h, p.prompt_length) - block * R), 0);
     } else {
       const int c = pos - pre[PB];
       d = make_int4(h, c * R, min(R, suffix_len - c * R), 1);

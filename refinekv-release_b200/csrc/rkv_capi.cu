@@ -322,7 +322,22 @@ int check_summary(const rkv_summary* s) {
   if (s->heads > (1 << 16) || s->blocks > (1LL << 26)) {
     return fail(RKV_ERR_UNSUPPORTED, "summary is larger than the kernels index");
   }
+  if (s->sequences < 0 || s->sequences > s->heads ||
+      (s->sequences > 1 && (s->heads % s->sequences != 0 || s->prompt_lengths == nullptr))) {
+    return fail(RKV_ERR_INVALID_ARGUMENT,
+                "sequences must divide heads, with prompt_lengths for a batch");
+  }
   return RKV_OK;
+}
+
+// Row-to-sequence layout of a (possibly batched) summary for the kernels.
+SeqLayout seq_layout(const rkv_summary* s) {
+  SeqLayout l = {};
+  const bool batched = s->sequences > 1;
+  l.seq_prompt = batched ? s->prompt_lengths : nullptr;
+  l.heads_per_seq = static_cast<int>(batched ? s->heads / s->sequences : s->heads);
+  l.page = static_cast<int>(s->block_size);
+  return l;
 }
 
 int check_selection_args(const rkv_summary* s, const void* q, int qdtype, int64_t group,
@@ -393,6 +408,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     p.query_f32 = qdtype == RKV_DTYPE_F32;
     p.dim = D;
     p.counts = s->counts;
+    p.seq = seq_layout(s);
     p.heads = static_cast<int>(s->heads);
     p.group = static_cast<int>(group);
     p.blocks = static_cast<int>(s->blocks);
@@ -415,6 +431,7 @@ int run_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype
     int rc = summary_maps(s, nullptr, nullptr, &maps.value_mean);
     if (rc != RKV_OK) return rc;
     FinalParams p = {};
+    p.seq = seq_layout(s);
     p.heads = static_cast<int>(s->heads);
     p.group = static_cast<int>(group);
     p.blocks = static_cast<int>(s->blocks);
@@ -653,6 +670,9 @@ int rkv_select_split(const rkv_summary* summary, const void* queries, int query_
                      unsigned stage, void* stream) {
   g_last_error.clear();
   if (summary == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
+  if (summary->sequences > 1) {
+    return fail(RKV_ERR_UNSUPPORTED, "a sequence split takes one prompt, not a batch");
+  }
   if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");
   }
@@ -761,6 +781,7 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
       maps.value_suffix = maps.value_pages;
     }
     AttendParams p = {};
+    p.seq = seq_layout(summary);
     p.query = query;
     p.query_f32 = query_dtype == RKV_DTYPE_F32;
     p.dim = static_cast<int>(D);
@@ -869,6 +890,9 @@ int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dt
   g_last_error.clear();
   int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
   if (rc != RKV_OK) return rc;
+  if (summary->sequences > 1) {
+    return fail(RKV_ERR_UNSUPPORTED, "a sequence split takes one prompt, not a batch");
+  }
   if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");
   }

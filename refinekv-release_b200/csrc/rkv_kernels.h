@@ -14,6 +14,28 @@ constexpr int kStatsSlots = 8;   // phase-A partials per CTA under a sequence sp
 
 enum Reduction { kMean = 0, kMax = 1, kAny = 2 };
 
+// Batched decode: the KV-head rows of several prompts decoding in lockstep,
+// sequence-major (row = sequence * heads_per_seq + head), all padded to the
+// longest prompt's block count.  seq_prompt is null for a single prompt.
+struct SeqLayout {
+  const int64_t* seq_prompt;  // (sequences,) prompt lengths, or null
+  int heads_per_seq;
+  int page;  // tokens per block
+
+  __device__ __forceinline__ int sequence(int row) const {
+    return seq_prompt != nullptr ? row / heads_per_seq : 0;
+  }
+  // Prompt length of row's sequence (`single` for one prompt).
+  __device__ __forceinline__ int prompt(int row, int single) const {
+    return seq_prompt != nullptr ? static_cast<int>(__ldg(seq_prompt + row / heads_per_seq))
+                                 : single;
+  }
+  // Real blocks of row's sequence (`single` for one prompt).
+  __device__ __forceinline__ int blocks(int row, int single) const {
+    return seq_prompt != nullptr ? (prompt(row, 0) + page - 1) / page : single;
+  }
+};
+
 struct SummarizeMaps {
   CUtensorMap keys;    // (dim, tokens, heads) bf16, [block_size x 64] boxes, 128B swizzle
   CUtensorMap values;
@@ -51,6 +73,7 @@ struct StatsParams {
   float* z;      // (instances*heads*group, blocks)
   float* delta;  // (instances*heads*group, blocks)
   float* lse;    // (instances*heads*group, parts * slots, 4): z max, z sum, c max, c sum
+  SeqLayout seq;  // counts is (sequences, blocks) when batched
   int* status;
 };
 
@@ -85,6 +108,7 @@ struct FinalParams {
   float* rep_m;  // (heads, parts, G8)
   float* rep_l;
   float* rep_o;  // (heads, parts, dim, G8): o^T, group rows innermost
+  SeqLayout seq;
   int* status;
 };
 
@@ -102,6 +126,7 @@ struct AttendParams {
   const int64_t* counts;
   int heads, group, blocks, page;
   int prompt_length;  // rows of block b: min(page, prompt_length - b * page)
+  SeqLayout seq;      // batched: each row's own prompt length
   int has_suffix;
   int suffix_capacity;
   const int* suffix_len_ptr;  // device scalar or null

@@ -100,8 +100,9 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   const int ih = blockIdx.x;  // instance * heads + head
   const int inst = ih / p.heads, h = ih - inst * p.heads;
   const int t0 = blockIdx.y * p.tiles_per_cta;
-  const int t1 = min(p.tiles, t0 + p.tiles_per_cta);
-  const int mine = t1 - t0 > warp ? (t1 - t0 - warp + warps - 1) / warps : 0;
+  const int t1_all = min(p.tiles, t0 + p.tiles_per_cta);
+  const int mine_all = t1_all - t0 > warp ? (t1_all - t0 - warp + warps - 1) / warps : 0;
+  const int64_t* counts = p.counts + static_cast<size_t>(p.seq.sequence(h)) * p.blocks;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&maps.key_mean);
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
     // The summaries do not change during decode: this warp's first tiles go
     // to L2 before the dependency wait, so their first-touch latency
     // overlaps the previous kernel's tail (nothing is consumed before it).
-    for (int j = 0; j < min(kStatsPrefetch, mine); ++j) {
+    for (int j = 0; j < min(kStatsPrefetch, mine_all); ++j) {
       const int row = (t0 + warp + j * warps) * R;
       tma_prefetch_tile<D>(&maps.key_mean, row, h);
       tma_prefetch_tile<D>(&maps.ellipsoid, row, h);
@@ -123,8 +124,8 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   // 256 bytes) and the query rows (which the previous kernel may still be
   // writing: a prefetch only warms L2 and the translation, it returns no data).
   if (lane == 0 || lane == 16 || lane == 31) {
-    for (int j = 0; j < min(kStatsPrefetch, mine); ++j) {
-      prefetch_l2(p.counts + min((t0 + warp + j * warps) * R + lane, p.blocks - 1));
+    for (int j = 0; j < min(kStatsPrefetch, mine_all); ++j) {
+      prefetch_l2(counts + min((t0 + warp + j * warps) * R + lane, p.blocks - 1));
     }
   }
   const char* q = static_cast<const char*>(p.query) +
@@ -135,6 +136,11 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
   __syncwarp();
   pdl_wait();
   pdl_launch_dependents();
+  // A batched row stops at its own sequence's blocks (tiles wholly past them
+  // are skipped; their partial slots stay empty).
+  const int blocks_h = p.seq.blocks(h, p.blocks);
+  const int t1 = max(t0, min(t1_all, (blocks_h + R - 1) / R));
+  const int mine = t1 - t0 > warp ? (t1 - t0 - warp + warps - 1) / warps : 0;
 
   // Key-mean and ellipsoid tiles are read once per step: evict them first so
   // that z and delta, which the next kernel reads, stay in L2 at long
@@ -169,7 +175,7 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
 #pragma unroll
       for (int hf = 0; hf < kHalves; ++hf) {
         const int b = tile * R + lane_rows[mt][hf];
-        c[mt][hf] = (j < mine && b < p.blocks) ? __ldg(p.counts + b) : 1;
+        c[mt][hf] = (j < mine && b < blocks_h) ? __ldg(counts + b) : 1;
       }
   };
   long long cnt_next[R / 16][2];
@@ -258,7 +264,7 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
 #pragma unroll
       for (int hf = 0; hf < kHalves; ++hf) {
         const int b = tile * R + row_of[mt][hf];
-        const float log_count = b < p.blocks ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
+        const float log_count = b < blocks_h ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
 #pragma unroll
         for (int jc = 0; jc < 2; ++jc) {
           const int c = 2 * hf + jc;
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
             const int g = PACK4 ? g_base + jc : nt * 8 + 2 * (lane & 3) + jc;
             zv[mt][nt][c] = -INFINITY;
             cv[mt][nt][c] = -INFINITY;
-            if (b >= p.blocks || g >= p.group) continue;
+            if (b >= blocks_h || g >= p.group) continue;
             const float score = sc[mt][nt][c] * p.scale;
             const float proj = pr[mt][nt][c];
             const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
@@ -414,6 +420,9 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
+  // A batched row's blocks past its own prompt are padding: never selected
+  // or represented, their mask bytes written 0.
+  const int blocks_h = p.seq.blocks(h, p.blocks);
 
   // Pass-1 inputs of a tile (one lane per block): z and delta of every row,
   // the value norm and the anchor bit.  Three buffers rotate by name through
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   };
   auto load_tile = [&](int t, TileIn& in) {
     const int b = t * R + lane;
-    if (t < t1 && b < p.blocks) {
+    if (t < t1 && b < blocks_h) {
       in.vn = p.value_norm[static_cast<size_t>(h) * p.blocks + b];
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
@@ -488,7 +497,7 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
   // Pass 1: decisions, one lane per block.
   auto decide = [&](int t, const TileIn& in) {
     const int b = t * R + lane;
-    const bool valid = b < p.blocks;
+    const bool valid = b < blocks_h;
     bool sel = false;
     if (valid) {
       float lz[GM], lc[GM];
@@ -526,6 +535,8 @@ __global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ Fina
         dec = any;
       }
       sel = dec || bad || bad_global || in.anc;
+    }
+    if (b < p.blocks) {
       uint8_t* mk = p.mask + static_cast<size_t>(h) * p.blocks + b;
       if (p.accumulate) {
         if (sel) *mk = 1;

@@ -11,7 +11,7 @@ import pathlib
 import threading
 
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "_lib" / "librefinekv_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 RKV_OK = 0
 RKV_ERR_INVALID_ARGUMENT = 1
@@ -80,6 +80,8 @@ class Summary(ctypes.Structure):
         ("block_size", c_i64),
         ("head_dim", c_i64),
         ("prompt_length", c_i64),
+        ("sequences", c_i64),
+        ("prompt_lengths", c_ptr),
     ]
 
 

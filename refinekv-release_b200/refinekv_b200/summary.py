@@ -31,6 +31,13 @@ class BlockSummary:
     (kv_heads, pages, head_dim); ``value_norm`` is FP32 (kv_heads, pages) and
     ``max_value_norm`` FP32 (kv_heads,).  A summary belongs to one immutable
     prompt prefix.
+
+    A batch of prompts (``build_summary_batch``; beyond the reference, which
+    decodes one sequence) stacks them on the head axis, sequence-major
+    (``sequences * kv_heads`` rows), padded to the longest prompt's page
+    count: ``counts`` is then (sequences, pages) with 0 past each prompt,
+    ``prompt_lengths`` the (sequences,) int64 device lengths and
+    ``prompt_length`` their maximum.
     """
 
     keys: torch.Tensor
@@ -43,11 +50,13 @@ class BlockSummary:
     max_value_norm: torch.Tensor
     prompt_length: int
     block_size: int
+    sequences: int = 1
+    prompt_lengths: torch.Tensor | None = None
     _abi: object = field(default=None, repr=False, compare=False)
 
     @property
     def num_blocks(self) -> int:
-        return self.counts.numel()
+        return self.counts.shape[-1]
 
     def abi(self) -> _native.Summary:
         """The ``rkv_summary`` view handed to the C ABI (built once)."""
@@ -68,6 +77,9 @@ class BlockSummary:
                 block_size=self.block_size,
                 head_dim=self.keys.shape[-1],
                 prompt_length=self.prompt_length,
+                sequences=self.sequences,
+                prompt_lengths=(self.prompt_lengths.data_ptr()
+                                if self.prompt_lengths is not None else None),
             )
         return self._abi
 
@@ -90,6 +102,30 @@ def _page_alias(tensor: torch.Tensor, block: int):
                              (tensor.stride(0), block * dim, dim, 1))
 
 
+def _checked_prompt(keys: torch.Tensor, values: torch.Tensor):
+    """The reference's argument checks (``summary.py:46-60``) plus the CUDA path's own."""
+    if keys.ndim != 3 or keys.shape != values.shape or min(keys.shape) <= 0:
+        raise ValueError(
+            "keys and values must have the same nonempty (kv_heads, tokens, dim) shape")
+    if keys.device != values.device or keys.dtype != values.dtype:
+        raise ValueError("keys and values must have the same device and dtype")
+    if not keys.is_floating_point():
+        raise TypeError("keys and values must be floating point")
+    require_cuda_tensor(keys, "keys")
+    if keys.dtype != torch.bfloat16:
+        raise TypeError("the CUDA summarizer requires BF16 keys and values")
+    if keys.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"head_dim must be one of {SUPPORTED_HEAD_DIMS}")
+    keys, values = keys.detach(), values.detach()
+    if keys.stride(2) != 1 or keys.data_ptr() % 16 or (keys.stride(1) * 2) % 16 or (
+            keys.stride(0) * 2) % 16:
+        keys = keys.contiguous()
+    if values.stride(2) != 1 or values.data_ptr() % 16 or (values.stride(1) * 2) % 16 or (
+            values.stride(0) * 2) % 16:
+        values = values.contiguous()
+    return keys, values
+
+
 @torch.no_grad()
 def build_summary(keys: torch.Tensor, values: torch.Tensor,
                   config: RefineKVConfig | None = None) -> BlockSummary:
@@ -103,27 +139,8 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
     unsupported head dimensions and ``RuntimeError`` for CPU tensors.
     """
     config = config or RefineKVConfig()
-    if keys.ndim != 3 or keys.shape != values.shape or min(keys.shape) <= 0:
-        raise ValueError(
-            "keys and values must have the same nonempty (kv_heads, tokens, dim) shape")
-    if keys.device != values.device or keys.dtype != values.dtype:
-        raise ValueError("keys and values must have the same device and dtype")
-    if not keys.is_floating_point():
-        raise TypeError("keys and values must be floating point")
-    require_cuda_tensor(keys, "keys")
-    if keys.dtype != torch.bfloat16:
-        raise TypeError("the CUDA summarizer requires BF16 keys and values")
+    keys, values = _checked_prompt(keys, values)
     heads, tokens, dim = keys.shape
-    if dim not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"head_dim must be one of {SUPPORTED_HEAD_DIMS}")
-    keys, values = keys.detach(), values.detach()
-    if keys.stride(2) != 1 or keys.data_ptr() % 16 or (keys.stride(1) * 2) % 16 or (
-            keys.stride(0) * 2) % 16:
-        keys = keys.contiguous()
-    if values.stride(2) != 1 or values.data_ptr() % 16 or (values.stride(1) * 2) % 16 or (
-            values.stride(0) * 2) % 16:
-        values = values.contiguous()
-
     block = config.block_size
     blocks = -(-tokens // block)
     dev = keys.device
@@ -150,3 +167,64 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
             torch.cuda.current_stream(dev).cuda_stream))
     return BlockSummary(key_pages, value_pages, counts, key_mean, value_mean, ellipsoid,
                         value_norm, max_value_norm, tokens, block)
+
+
+@torch.no_grad()
+def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
+                        config: RefineKVConfig | None = None) -> BlockSummary:
+    """Summaries of several prompts that decode together, in one batched summary.
+
+    ``keys[i]``/``values[i]``: (kv_heads, tokens_i, head_dim) bf16 CUDA
+    tensors, the same heads, dim and device for every prompt.  The result
+    stacks the prompts on the head axis (row ``i * kv_heads + h``) padded to
+    the longest prompt's page count; every page, mean, ellipsoid and norm
+    past a prompt is zero and its count is 0, so the decode kernels neither
+    select, represent nor read it.  Each prompt's rows hold exactly what
+    ``build_summary`` computes for it alone (the same kernel over the same
+    pages).  No reference counterpart: the reference is batch 1
+    (``transformers.py:448-449``).
+    """
+    config = config or RefineKVConfig()
+    if len(keys) == 0 or len(keys) != len(values):
+        raise ValueError("need the same nonzero number of key and value tensors")
+    checked = [_checked_prompt(k, v) for k, v in zip(keys, values)]
+    heads, _, dim = checked[0][0].shape
+    dev, dtype = checked[0][0].device, checked[0][0].dtype
+    for k, _ in checked:
+        if k.shape[0] != heads or k.shape[2] != dim or k.device != dev:
+            raise ValueError("every prompt needs the same kv_heads, head_dim and device")
+    block = config.block_size
+    lengths = [k.shape[1] for k, _ in checked]
+    seqs, longest = len(checked), max(lengths)
+    blocks = -(-longest // block)
+    rows = seqs * heads
+    key_pages = torch.zeros(rows, blocks, block, dim, device=dev, dtype=dtype)
+    value_pages = torch.zeros_like(key_pages)
+    key_mean = torch.zeros(rows, blocks, dim, device=dev, dtype=torch.bfloat16)
+    value_mean = torch.zeros_like(key_mean)
+    ellipsoid = torch.zeros_like(key_mean)
+    value_norm = torch.zeros(rows, blocks, device=dev, dtype=torch.float32)
+    max_value_norm = torch.zeros(rows, device=dev, dtype=torch.float32)
+    counts = torch.zeros(seqs, blocks, device=dev, dtype=torch.int64)
+    lib = _native.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        for i, (k, v) in enumerate(checked):
+            tokens = k.shape[1]
+            # A prompt of the full page count writes all its heads in one call;
+            # a shorter one head by head (its rows are `blocks` pages apart).
+            groups = [range(heads)] if -(-tokens // block) == blocks else [[h] for h in range(heads)]
+            for hs in groups:
+                h0, n = hs[0], len(hs)
+                r0 = i * heads + h0
+                _native.check(lib.rkv_summarize(
+                    k[h0].data_ptr(), v[h0].data_ptr(), n, tokens, dim,
+                    k.stride(0), k.stride(1), v.stride(0), v.stride(1), block,
+                    key_pages[r0].data_ptr(), value_pages[r0].data_ptr(),
+                    key_mean[r0].data_ptr(), value_mean[r0].data_ptr(), ellipsoid[r0].data_ptr(),
+                    value_norm[r0].data_ptr(), max_value_norm[r0:].data_ptr(),
+                    counts[i].data_ptr(), stream))
+    prompt_lengths = torch.tensor(lengths, device=dev, dtype=torch.int64)
+    return BlockSummary(key_pages, value_pages, counts, key_mean, value_mean, ellipsoid,
+                        value_norm, max_value_norm, longest, block, sequences=seqs,
+                        prompt_lengths=prompt_lengths)

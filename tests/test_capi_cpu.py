@@ -93,6 +93,33 @@ def test_decode_rejects_bad_arguments_before_touching_a_device(lib):
     assert call(bad) == _native.RKV_ERR_UNSUPPORTED
 
 
+def test_batch_geometry_is_checked_before_touching_a_device(lib):
+    def summary(**kw):
+        base = dict(key_pages=16, value_pages=16, counts=16, key_mean=16, value_mean=16,
+                    ellipsoid=16, value_norm=16, max_value_norm=16, heads=4, blocks=3,
+                    block_size=32, head_dim=128, prompt_length=71, sequences=2,
+                    prompt_lengths=16)
+        base.update(kw)
+        return _native.Summary(**base)
+
+    def decode(s):
+        return lib.rkv_decode(ctypes.byref(s), 16, 0, 4, None, None, 0, 0, 0, 0, 0,
+                              None, 0, None, 0.01, 2, 16, 16, None, 0, 15, None)
+
+    assert decode(summary(sequences=3)) == _native.RKV_ERR_INVALID_ARGUMENT  # 3 does not divide 4
+    assert decode(summary(prompt_lengths=None)) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert decode(summary(sequences=-1)) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert b"sequences" in lib.rkv_last_error()
+    # a sequence split takes one prompt
+    rc = lib.rkv_select_split(ctypes.byref(summary()), 16, 0, 1, 4, 0.01, 2, 16, 0, 16, 1 << 20,
+                              2, 0, 3, 16, 1 << 20, 1, None)
+    assert rc == _native.RKV_ERR_UNSUPPORTED and b"batch" in lib.rkv_last_error()
+    rc = lib.rkv_decode_split(ctypes.byref(summary()), 16, 0, 4, None, None, 0, 0, 0, 0, 0, None,
+                              0, None, 0.01, 2, 16, 16, 16, 1 << 20, 2, 0, 3, 16, 1 << 20, 1,
+                              None)
+    assert rc == _native.RKV_ERR_UNSUPPORTED and b"batch" in lib.rkv_last_error()
+
+
 def test_workspace_size_needs_a_device(lib):
     if torch.cuda.is_available():
         pytest.skip("a device is present")
