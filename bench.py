@@ -74,6 +74,9 @@ def parse_args():
     ap.add_argument("--query-scale", type=float, default=1.0,
                     help="extra, not the headline workload: scale the queries (sharper "
                          "attention, fewer refined blocks)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="extra, not the headline workload: prompts that decode together, "
+                         "stacked on the KV-head axis (one GPU)")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
@@ -81,6 +84,8 @@ def parse_args():
     args = ap.parse_args()
     if args.warmup < 0 or args.steps < 1:
         ap.error("--steps must be >= 1 and --warmup >= 0")
+    if args.batch < 1 or (args.batch > 1 and args.gpus > 1):
+        ap.error("--batch must be >= 1, and a batch runs on one GPU")
     return args
 
 
@@ -88,7 +93,9 @@ def workload_config(args, world, plan=None):
     return {
         "workload": ("llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
                      else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}")
-                    + ("" if args.query_scale == 1.0 else f"-q{args.query_scale:g}"),
+                    + ("" if args.query_scale == 1.0 else f"-q{args.query_scale:g}")
+                    + ("" if args.batch == 1 else f"-batch{args.batch}"),
+        "batch": args.batch,
         "layers": args.layers,
         "prompt_tokens": args.tokens,
         "kv_heads": args.kv_heads,
@@ -295,10 +302,11 @@ def run_reference(args):
         if step >= args.warmup:
             times.append(dt)
     per_layer_us = statistics.median(times) * 1e6
-    value = per_layer_us * args.layers
+    # The reference decodes one sequence at a time: a batch costs batch x one sequence.
+    value = per_layer_us * args.layers * args.batch
     sample = (f"1 layer per step ({args.kv_heads} KV heads x {args.tokens} tokens, reference "
               f"PyTorch algorithm via the CPU oracle), median of {len(times)} steps, "
-              f"x{args.layers} layers")
+              f"x{args.layers} layers" + (f" x{args.batch} sequences" if args.batch > 1 else ""))
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -341,6 +349,11 @@ def build_layers(args, plan, group, dev):
     layers = []
     summarize_ms = []
     for li in range(args.layers):
+        if args.batch > 1:
+            L, ms = build_batch_layer(args, li, cfg, dev)
+            layers.append(L)
+            summarize_ms.append(ms)
+            continue
         data = synthetic.make_layer(args.seed, li, H, args.tokens, args.head_dim,
                                     args.block_size, device=dev)
         L = Layer()
@@ -382,14 +395,61 @@ def build_layers(args, plan, group, dev):
     return layers, cfg, summarize_ms
 
 
+def build_batch_layer(args, li, cfg, dev):
+    """One layer of `--batch` prompts (sequence b seeded seed + 7919 b), stacked on the
+    KV-head axis in one batched cache whose pages the batched summary aliases."""
+    from refinekv_b200 import build_summary_batch, synthetic
+    from refinekv_b200.attention import select_blocks_union
+
+    B, H, T, D = args.batch, args.kv_heads, args.tokens, args.head_dim
+    cap = args.warmup + args.steps
+    keys = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
+    values = torch.empty_like(keys)
+    means = []
+    for b in range(B):
+        data = synthetic.make_layer(args.seed + 7919 * b, li, H, T, D, args.block_size, device=dev)
+        keys[b].copy_(data.keys)
+        values[b].copy_(data.values)
+        means.append(data.planted_mean)
+        del data
+    L = Layer()
+    L.keys, L.values = keys.view(B * H, T, D), values.view(B * H, T, D)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(10_000_000)
+    start.record()
+    L.summary = build_summary_batch(list(keys), list(values), cfg)
+    end.record()
+    end.synchronize()
+
+    def queries(step, count):
+        return torch.cat([
+            (synthetic.make_queries(args.seed + 7919 * b, li, step, means[b], args.group, count,
+                                    torch.float32) * args.query_scale).to(torch.bfloat16)
+            for b in range(B)], dim=1)
+
+    L.anchor = (select_blocks_union(queries(-1, args.anchors).contiguous(), L.summary, cfg)
+                if args.anchors else None)
+    L.q = torch.stack([queries(s, 1)[0] for s in range(cap)]).contiguous()
+    ks, vs = [], []
+    for s in range(cap):
+        toks = [synthetic.make_decode_token(args.seed + 7919 * b, li, s, H, D, T + s, device=dev)
+                for b in range(B)]
+        ks.append(torch.cat([k for k, _ in toks]))
+        vs.append(torch.cat([v for _, v in toks]))
+    L.suffix_k = torch.cat(ks, 1).contiguous()
+    L.suffix_v = torch.cat(vs, 1).contiguous()
+    L.workspace = {}
+    return L, start.elapsed_time(end)
+
+
 def run_b200(args):
     rank, world, local = dist_setup()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     from refinekv_b200 import _native, parallel
 
-    plan = parallel.plan_shards(args.kv_heads, args.tokens, args.block_size, world, rank,
-                                args.seq_ranks)
+    plan = parallel.plan_shards(args.kv_heads * args.batch, args.tokens, args.block_size, world,
+                                rank, args.seq_ranks)
     group = parallel.new_seq_group(plan)
     decode = parallel.SplitDecode(plan, group)
     lib = _native.load()
@@ -463,7 +523,9 @@ def run_b200(args):
     # eager pass then counts the selected pages.
     from refinekv_b200 import sparse_attention
 
-    counts_all = [L.summary.counts for L in layers]
+    # tokens per (row, page): a batch's counts are per sequence, rows sequence-major
+    counts_all = [L.summary.counts.repeat_interleave(plan.heads // L.summary.counts.shape[0], 0)
+                  if L.summary.counts.ndim == 2 else L.summary.counts for L in layers]
     sel_tokens = torch.zeros((), device=dev, dtype=torch.int64)
     sel_pages = torch.zeros((), device=dev, dtype=torch.int64)
 
@@ -666,7 +728,7 @@ def run_b200(args):
 
     # ---- CPU baseline: the reference algorithm on the host (rank 0, N=1) ---
     cpu = None
-    if rank == 0 and world == 1 and not args.skip_cpu:
+    if rank == 0 and world == 1 and args.batch == 1 and not args.skip_cpu:
         from oracle import refinekv_oracle as ora
 
         torch.set_num_threads(os.cpu_count() or 1)

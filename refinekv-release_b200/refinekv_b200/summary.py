@@ -169,6 +169,18 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
                         value_norm, max_value_norm, tokens, block)
 
 
+def _stacked(prompts: list[torch.Tensor]) -> torch.Tensor:
+    """(sequences * heads, tokens, dim): a view when the prompts are consecutive
+    equal slices of one buffer (a batched cache), else a stacked copy."""
+    first = prompts[0]
+    step = first.shape[0] * first.stride(0) * first.element_size()
+    if all(p.stride() == first.stride() and p.data_ptr() == first.data_ptr() + i * step
+           for i, p in enumerate(prompts)):
+        return first.as_strided((len(prompts) * first.shape[0],) + tuple(first.shape[1:]),
+                                first.stride())
+    return torch.cat(prompts)
+
+
 @torch.no_grad()
 def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
                         config: RefineKVConfig | None = None) -> BlockSummary:
@@ -196,6 +208,16 @@ def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
     block = config.block_size
     lengths = [k.shape[1] for k, _ in checked]
     seqs, longest = len(checked), max(lengths)
+    if len(set(lengths)) == 1:
+        # Equal prompts: the batch is the summary of the stacked heads (one
+        # launch; pages alias a batched cache the prompts are slices of).
+        stacked_k = _stacked([k for k, _ in checked])
+        stacked_v = _stacked([v for _, v in checked])
+        one = build_summary(stacked_k, stacked_v, config)
+        one.counts = one.counts.expand(seqs, -1).contiguous()
+        one.sequences = seqs
+        one.prompt_lengths = torch.tensor(lengths, device=dev, dtype=torch.int64)
+        return one
     blocks = -(-longest // block)
     rows = seqs * heads
     key_pages = torch.zeros(rows, blocks, block, dim, device=dev, dtype=dtype)
