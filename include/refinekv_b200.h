@@ -94,6 +94,20 @@ typedef enum rkv_status {
  * K/V, anchors, masks and outputs use the same sequence-major head axis, and
  * every sequence sees the same suffix length.  sequences 0 or 1 is one prompt
  * (prompt_lengths unused).
+ *
+ * Paged K/V (no reference counterpart; the layout of a vLLM-style page
+ * pool).  With page_table non-null, key_pages / value_pages are pools of
+ * pool_pages physical pages of block_size rows: the row t of KV head h in
+ * physical page p is at p * page_stride + h * page_head_stride +
+ * t * token_stride elements (HND pools [pages, heads, block, dim]: page
+ * stride heads*block*dim, head stride block*dim, token stride dim; NHD pools
+ * [pages, block, heads, dim]: block*heads*dim, dim, heads*dim).  Logical
+ * block b of the sequence that KV-head row r belongs to is physical page
+ * page_table[(r / (heads / sequences)) * page_table_stride + b]; entries
+ * outside [0, pool_pages) set the status word's range bit and read zeros.
+ * The summaries (means, ellipsoid, norms, counts) stay per sequence in
+ * logical block order.  Only the decode attention reads pages, so
+ * rkv_select ignores the page fields.
  */
 typedef struct rkv_summary {
   const void* key_pages;
@@ -113,6 +127,14 @@ typedef struct rkv_summary {
   int64_t prompt_length;
   int64_t sequences;              /* batched decode: see above; 0 or 1 for one prompt */
   const int64_t* prompt_lengths;  /* (sequences,) device array when sequences > 1 */
+  /* Paged K/V (see below); all ignored when page_table is null. */
+  const int32_t* page_table;      /* (sequences, page_table_stride) physical page per block */
+  int64_t page_table_stride;      /* entries between sequences' rows of page_table */
+  int64_t pool_pages;             /* physical pages in the pools */
+  int64_t key_page_stride;        /* elements between consecutive physical pages */
+  int64_t value_page_stride;
+  int64_t key_token_stride;       /* elements between a page's rows (tokens) */
+  int64_t value_token_stride;
 } rkv_summary;
 
 /*

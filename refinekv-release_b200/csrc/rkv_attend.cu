@@ -145,10 +145,11 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
   const long long lo = wl.T * cta / wl.C, hi = wl.T * (cta + 1) / wl.C;
   const int count_w = hi - lo > warp ? static_cast<int>((hi - lo - warp + warps - 1) / warps) : 0;
 
-  // Item descriptors {head, first row, valid rows, is_suffix} are decoded 32
-  // at a time, one per lane, one batch ahead of use, so the loads of the
-  // selected ids are off the issue path.  Each lane's head cursor only moves
-  // forward because batches are decoded in order.
+  // Item descriptors {head, physical page or first suffix row, valid rows,
+  // is_suffix} are decoded 32 at a time, one per lane, one batch ahead of
+  // use, so the loads of the selected ids are off the issue path.  Each
+  // lane's head cursor only moves forward because batches are decoded in
+  // order.
   int lane_head = 0;
   auto decode = [&](int base) {
     const int j = base + lane;
@@ -167,7 +168,16 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       }
       const int block = __ldg(p.sel_ids + (static_cast<size_t>(h) * PB + a) * p.seg_cap +
                               (pos - pre[a]));
-      d = make_int4(h, block * R, min(R, p.seq.prompt(h, p.prompt_length) - block * R), 0);
+      int page = block;  // physical page: the page table's entry when paged
+      if (p.page_table != nullptr) {
+        page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride +
+                     block);
+        if (page < 0 || page >= p.pool_pages) {  // flag the call; read page 0 instead
+          atomicOr(p.status, kStatusBadInput);
+          page = 0;
+        }
+      }
+      d = make_int4(h, page, min(R, p.seq.prompt(h, p.prompt_length) - block * R), 0);
     } else {
       const int c = pos - pre[PB];
       d = make_int4(h, c * R, min(R, suffix_len - c * R), 1);
@@ -187,6 +197,11 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
     return make_int4(__shfl_sync(0xffffffffu, cur.x, src), __shfl_sync(0xffffffffu, cur.y, src),
                      __shfl_sync(0xffffffffu, cur.z, src), __shfl_sync(0xffffffffu, cur.w, src));
   };
+  // Head coordinate of row h in the page maps: a page pool holds each
+  // sequence's KV heads, contiguous or batched pages hold every row.
+  auto pool_head = [&](int h) {
+    return p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
+  };
   // K and V of a stage have their own barriers: K is refilled as soon as the
   // scores are computed, V after the value product.
   auto issue_k = [&](int j, const int4& d) {
@@ -195,8 +210,13 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       valid_rows[warp * S + s] = d.z;
       uint64_t* bk = &bars[(warp * S + s) * 2];
       mbar_expect_tx(bk, kTile);
-      tma_tile_hint<D>(ring + (warp * S + s) * kStage, d.w ? &maps.key_suffix : &maps.key_pages,
-                       bk, d.y, d.x, R, stream_policy);
+      if (d.w) {
+        tma_tile_hint<D>(ring + (warp * S + s) * kStage, &maps.key_suffix, bk, d.y, d.x, R,
+                         stream_policy);
+      } else {
+        tma_page_hint<D>(ring + (warp * S + s) * kStage, &maps.key_pages, bk, pool_head(d.x), d.y,
+                         R, stream_policy);
+      }
     }
   };
   auto issue_v = [&](int j, const int4& d) {
@@ -204,9 +224,13 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
       const int s = j % S;
       uint64_t* bv = &bars[(warp * S + s) * 2 + 1];
       mbar_expect_tx(bv, kTile);
-      tma_tile_hint<D>(ring + (warp * S + s) * kStage + kTile,
-                       d.w ? &maps.value_suffix : &maps.value_pages, bv, d.y, d.x, R,
-                       stream_policy);
+      if (d.w) {
+        tma_tile_hint<D>(ring + (warp * S + s) * kStage + kTile, &maps.value_suffix, bv, d.y,
+                         d.x, R, stream_policy);
+      } else {
+        tma_page_hint<D>(ring + (warp * S + s) * kStage + kTile, &maps.value_pages, bv,
+                         pool_head(d.x), d.y, R, stream_policy);
+      }
     }
   };
   const int first_fill = min(S, count_w);

@@ -301,6 +301,40 @@ int rows_map(CUtensorMap* map, const void* base, int64_t dim, int64_t rows, int6
   return RKV_OK;
 }
 
+// 4-D bf16 map of K/V pages (dim, row in page, head, page), read one
+// [block x 64] box per page and column half (the same shared-memory tile as
+// rows_map's boxes).  Contiguous pages and HND / NHD page pools are the
+// same map with different strides.
+int pages_map(CUtensorMap* map, const void* base, int64_t dim, int64_t block, int64_t heads,
+              int64_t pages, int64_t token_stride, int64_t head_stride, int64_t page_stride,
+              const char* what) {
+  EncodeTiled encode = encoder();
+  if (encode == nullptr) return fail(RKV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (!aligned16(base) || (token_stride * 2) % 16 != 0 || (head_stride * 2) % 16 != 0 ||
+      (page_stride * 2) % 16 != 0) {
+    return fail(RKV_ERR_ALIGNMENT, std::string(what) + ": base and strides must be 16-byte aligned");
+  }
+  if (token_stride <= 0 || (heads > 1 && head_stride <= 0) || (pages > 1 && page_stride <= 0)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, std::string(what) + ": strides must be positive");
+  }
+  cuuint64_t gdim[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(block),
+                        static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(pages)};
+  cuuint64_t gstride[3] = {static_cast<cuuint64_t>(token_stride * 2),
+                           static_cast<cuuint64_t>((heads > 1 ? head_stride : block * token_stride) * 2),
+                           static_cast<cuuint64_t>((pages > 1 ? page_stride : heads * block * token_stride) * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(block), 1, 1};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), gdim,
+                            gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(RKV_ERR_INVALID_ARGUMENT,
+                std::string(what) + ": cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  }
+  return RKV_OK;
+}
+
 int check_summary(const rkv_summary* s) {
   if (s == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
   if (s->heads <= 0 || s->blocks <= 0 || s->prompt_length <= 0) {
@@ -326,6 +360,13 @@ int check_summary(const rkv_summary* s) {
       (s->sequences > 1 && (s->heads % s->sequences != 0 || s->prompt_lengths == nullptr))) {
     return fail(RKV_ERR_INVALID_ARGUMENT,
                 "sequences must divide heads, with prompt_lengths for a batch");
+  }
+  if (s->page_table != nullptr &&
+      (s->pool_pages <= 0 || s->pool_pages > (1LL << 31) - 1 || s->page_table_stride < s->blocks ||
+       s->key_page_stride <= 0 || s->value_page_stride <= 0 || s->key_token_stride <= 0 ||
+       s->value_token_stride <= 0)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT,
+                "a page table needs pool_pages, a stride of at least blocks and positive strides");
   }
   return RKV_OK;
 }
@@ -670,8 +711,9 @@ int rkv_select_split(const rkv_summary* summary, const void* queries, int query_
                      unsigned stage, void* stream) {
   g_last_error.clear();
   if (summary == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
-  if (summary->sequences > 1) {
-    return fail(RKV_ERR_UNSUPPORTED, "a sequence split takes one prompt, not a batch");
+  if (summary->sequences > 1 || summary->page_table != nullptr) {
+    return fail(RKV_ERR_UNSUPPORTED,
+                "a sequence split takes one prompt in contiguous pages, not a batch or a page pool");
   }
   if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");
@@ -762,11 +804,17 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
   const int* suffix_ptr = suffix_length;
   if (phases & RKV_PHASE_ATTEND) {
     AttendMaps maps;
-    rc = rows_map(&maps.key_pages, summary->key_pages, D, summary->blocks * B, H, D,
-                  summary->key_page_head_stride, static_cast<int>(B), "key_pages");
+    const bool paged = summary->page_table != nullptr;
+    const int64_t pool_heads = paged ? H / std::max<int64_t>(1, summary->sequences) : H;
+    rc = pages_map(&maps.key_pages, summary->key_pages, D, B, pool_heads,
+                   paged ? summary->pool_pages : summary->blocks,
+                   paged ? summary->key_token_stride : D, summary->key_page_head_stride,
+                   paged ? summary->key_page_stride : B * D, "key_pages");
     if (rc != RKV_OK) return rc;
-    rc = rows_map(&maps.value_pages, summary->value_pages, D, summary->blocks * B, H, D,
-                  summary->value_page_head_stride, static_cast<int>(B), "value_pages");
+    rc = pages_map(&maps.value_pages, summary->value_pages, D, B, pool_heads,
+                   paged ? summary->pool_pages : summary->blocks,
+                   paged ? summary->value_token_stride : D, summary->value_page_head_stride,
+                   paged ? summary->value_page_stride : B * D, "value_pages");
     if (rc != RKV_OK) return rc;
     if (suffix_capacity > 0) {
       rc = rows_map(&maps.key_suffix, key_suffix, D, suffix_capacity, H, key_suffix_token_stride,
@@ -791,6 +839,9 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     p.blocks = static_cast<int>(summary->blocks);
     p.page = static_cast<int>(B);
     p.prompt_length = static_cast<int>(summary->prompt_length);
+    p.page_table = summary->page_table;
+    p.page_table_stride = static_cast<int>(paged ? summary->page_table_stride : 0);
+    p.pool_pages = static_cast<int>(paged ? summary->pool_pages : summary->blocks);
     p.has_suffix = suffix_capacity > 0;
     p.suffix_capacity = static_cast<int>(suffix_capacity);
     p.suffix_len_ptr = suffix_ptr;
@@ -890,8 +941,9 @@ int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dt
   g_last_error.clear();
   int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
   if (rc != RKV_OK) return rc;
-  if (summary->sequences > 1) {
-    return fail(RKV_ERR_UNSUPPORTED, "a sequence split takes one prompt, not a batch");
+  if (summary->sequences > 1 || summary->page_table != nullptr) {
+    return fail(RKV_ERR_UNSUPPORTED,
+                "a sequence split takes one prompt in contiguous pages, not a batch or a page pool");
   }
   if (ranks < 1 || ranks > 64 || rank < 0 || rank >= ranks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "need 1 <= ranks <= 64 and 0 <= rank < ranks");

@@ -122,6 +122,17 @@ __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// 4-D form (x = channel, y = row in page, z = head, w = page) for K/V pages.
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int x, int y, int z, int w, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(bar)),
+      "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
@@ -165,6 +176,18 @@ __device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, uint
 #pragma unroll
   for (int i = 0; i < D / 64; ++i) {
     tma_load_3d(static_cast<char*>(dst) + i * rows * 128, map, bar, i * 64, row, head);
+  }
+}
+
+// One K or V page (all `rows` rows of KV head `head` in page `page`) from a
+// 4-D page map, landing in the same swizzled layout as tma_tile.
+template <int D>
+__device__ __forceinline__ void tma_page_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                              int head, int page, int rows, uint64_t policy) {
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    tma_load_4d_hint(static_cast<char*>(dst) + i * rows * 128, map, bar, i * 64, 0, head, page,
+                     policy);
   }
 }
 

@@ -127,6 +127,10 @@ struct AttendParams {
   int heads, group, blocks, page;
   int prompt_length;  // rows of block b: min(page, prompt_length - b * page)
   SeqLayout seq;      // batched: each row's own prompt length
+  // Paged K/V: physical page of (sequence, block) (null: page = block).
+  const int32_t* page_table;
+  int page_table_stride;
+  int pool_pages;
   int has_suffix;
   int suffix_capacity;
   const int* suffix_len_ptr;  // device scalar or null

@@ -6,8 +6,9 @@ Public names mirror the reference package ``refinekv`` v0.1.2
 ``AttentionResult``, and the Transformers adapter ``RefineKV`` /
 ``make_visible_static_cache`` (imported lazily, like the reference).
 Beyond the reference: ``build_summary_batch`` (several prompts decoding in
-lockstep, stacked on the head axis) and ``refinekv_b200.parallel`` (KV-head
-sharding and sequence split over GPUs).
+lockstep, stacked on the head axis), ``attach_page_pool`` (decode from a
+vLLM-style K/V page pool through a page table) and ``refinekv_b200.parallel``
+(KV-head sharding and sequence split over GPUs).
 
 All compute runs in the CUDA library ``librefinekv_b200.so`` built from
 ``csrc/``; it is loaded on first use and a missing or unloadable library is
@@ -23,6 +24,7 @@ __all__ = [
     "RefineKVConfig",
     "build_summary",
     "build_summary_batch",
+    "attach_page_pool",
     "select_blocks",
     "sparse_attention",
     "RefineKV",
@@ -35,7 +37,7 @@ def __getattr__(name):
         from . import attention
 
         return getattr(attention, name)
-    if name in ("BlockSummary", "build_summary", "build_summary_batch"):
+    if name in ("BlockSummary", "build_summary", "build_summary_batch", "attach_page_pool"):
         from . import summary
 
         return getattr(summary, name)

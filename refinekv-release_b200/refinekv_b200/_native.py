@@ -82,6 +82,13 @@ class Summary(ctypes.Structure):
         ("prompt_length", c_i64),
         ("sequences", c_i64),
         ("prompt_lengths", c_ptr),
+        ("page_table", c_ptr),
+        ("page_table_stride", c_i64),
+        ("pool_pages", c_i64),
+        ("key_page_stride", c_i64),
+        ("value_page_stride", c_i64),
+        ("key_token_stride", c_i64),
+        ("value_token_stride", c_i64),
     ]
 
 

@@ -46,7 +46,7 @@ def _validate(query, summary, config, anchor_mask=None):
     """Shape/device checks of the reference ``_validate`` (``attention.py:43-59``)."""
     if query.ndim != 4 or query.shape[2] != 1 or min(query.shape) <= 0:
         raise ValueError("query must have shape (kv_heads, group_size, 1, head_dim)")
-    if query.shape[0] != summary.keys.shape[0] or query.shape[-1] != summary.keys.shape[-1]:
+    if query.shape[0] != summary.num_heads or query.shape[-1] != summary.keys.shape[-1]:
         raise ValueError("query heads and dimension must match the summary")
     if query.device != summary.keys.device:
         raise ValueError("query and summary must be on the same device")

@@ -52,11 +52,19 @@ class BlockSummary:
     block_size: int
     sequences: int = 1
     prompt_lengths: torch.Tensor | None = None
+    page_table: torch.Tensor | None = None
     _abi: object = field(default=None, repr=False, compare=False)
 
     @property
     def num_blocks(self) -> int:
         return self.counts.shape[-1]
+
+    @property
+    def num_heads(self) -> int:
+        """KV-head rows of the decode (sequences x KV heads for a paged batch)."""
+        if self.page_table is not None:
+            return self.sequences * self.keys.shape[0]
+        return self.keys.shape[0]
 
     def abi(self) -> _native.Summary:
         """The ``rkv_summary`` view handed to the C ABI (built once)."""
@@ -72,7 +80,7 @@ class BlockSummary:
                 ellipsoid=self.ellipsoid.data_ptr(),
                 value_norm=self.value_norm.data_ptr(),
                 max_value_norm=self.max_value_norm.data_ptr(),
-                heads=self.keys.shape[0],
+                heads=self.num_heads,
                 blocks=self.num_blocks,
                 block_size=self.block_size,
                 head_dim=self.keys.shape[-1],
@@ -81,6 +89,14 @@ class BlockSummary:
                 prompt_lengths=(self.prompt_lengths.data_ptr()
                                 if self.prompt_lengths is not None else None),
             )
+            if self.page_table is not None:
+                a = self._abi
+                a.page_table = self.page_table.data_ptr()
+                a.page_table_stride = self.page_table.stride(0)
+                a.pool_pages = self.keys.shape[1]
+                a.key_page_stride, a.value_page_stride = self.keys.stride(1), self.values.stride(1)
+                a.key_token_stride = self.keys.stride(2)
+                a.value_token_stride = self.values.stride(2)
         return self._abi
 
 
@@ -250,3 +266,44 @@ def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
     return BlockSummary(key_pages, value_pages, counts, key_mean, value_mean, ellipsoid,
                         value_norm, max_value_norm, longest, block, sequences=seqs,
                         prompt_lengths=prompt_lengths)
+
+
+def attach_page_pool(summary: BlockSummary, key_pool: torch.Tensor, value_pool: torch.Tensor,
+                     page_table: torch.Tensor, layout: str = "HND") -> BlockSummary:
+    """The summary decoding from a vLLM-style K/V page pool instead of its own pages.
+
+    ``key_pool``/``value_pool``: bf16 ``(pages, kv_heads, block, dim)``
+    (``layout="HND"``) or ``(pages, block, kv_heads, dim)`` (``"NHD"``) on the
+    summary's device; ``page_table``: int32 ``(sequences, >= blocks)`` with the
+    physical page of each logical block of each sequence (a 1-D table for one
+    sequence).  The pool must hold, at those pages, the same K/V rows the
+    summary was built from (the prompt's pages, rows past a prompt's end
+    zero); the summary's means, ellipsoid, norms and counts are used as they
+    are.  No copy is made.  No reference counterpart (the reference keeps one
+    contiguous cache per layer).
+    """
+    if layout not in ("HND", "NHD"):
+        raise ValueError("layout must be 'HND' or 'NHD'")
+    if key_pool.shape != value_pool.shape or key_pool.ndim != 4:
+        raise ValueError("key and value pools must have the same 4-D shape")
+    if key_pool.dtype != torch.bfloat16 or value_pool.dtype != torch.bfloat16:
+        raise TypeError("page pools must be bf16")
+    if key_pool.device != summary.key_mean.device or value_pool.device != key_pool.device:
+        raise ValueError("page pools must be on the summary's device")
+    keys = key_pool.permute(1, 0, 2, 3) if layout == "HND" else key_pool.permute(2, 0, 1, 3)
+    values = value_pool.permute(1, 0, 2, 3) if layout == "HND" else value_pool.permute(2, 0, 1, 3)
+    heads = summary.num_heads // summary.sequences
+    if (keys.shape[0], keys.shape[2], keys.shape[3]) != (heads, summary.block_size,
+                                                         summary.key_mean.shape[-1]):
+        raise ValueError("pool pages must be (kv_heads, block_size, head_dim) per page")
+    if keys.stride(3) != 1 or values.stride(3) != 1:
+        raise ValueError("pool rows must be contiguous in head_dim")
+    table = page_table.reshape(1, -1) if page_table.ndim == 1 else page_table
+    if (table.dtype != torch.int32 or table.device != key_pool.device
+            or table.shape[0] != summary.sequences or table.shape[1] < summary.num_blocks
+            or table.stride(1) != 1):
+        raise ValueError("page_table must be int32 (sequences, >= blocks) on the pool's device")
+    return BlockSummary(keys, values, summary.counts, summary.key_mean, summary.value_mean,
+                        summary.ellipsoid, summary.value_norm, summary.max_value_norm,
+                        summary.prompt_length, summary.block_size, sequences=summary.sequences,
+                        prompt_lengths=summary.prompt_lengths, page_table=table)

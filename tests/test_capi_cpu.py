@@ -120,6 +120,30 @@ def test_batch_geometry_is_checked_before_touching_a_device(lib):
     assert rc == _native.RKV_ERR_UNSUPPORTED and b"batch" in lib.rkv_last_error()
 
 
+def test_page_table_geometry_is_checked_before_touching_a_device(lib):
+    def summary(**kw):
+        base = dict(key_pages=16, value_pages=16, counts=16, key_mean=16, value_mean=16,
+                    ellipsoid=16, value_norm=16, max_value_norm=16, heads=2, blocks=3,
+                    block_size=32, head_dim=128, prompt_length=71, page_table=16,
+                    page_table_stride=3, pool_pages=8, key_page_stride=8192,
+                    value_page_stride=8192, key_token_stride=128, value_token_stride=128)
+        base.update(kw)
+        return _native.Summary(**base)
+
+    def decode(s):
+        return lib.rkv_decode(ctypes.byref(s), 16, 0, 4, None, None, 0, 0, 0, 0, 0,
+                              None, 0, None, 0.01, 2, 16, 16, None, 0, 15, None)
+
+    for bad in ({"pool_pages": 0}, {"page_table_stride": 2}, {"key_token_stride": 0},
+                {"value_page_stride": -8192}):
+        assert decode(summary(**bad)) == _native.RKV_ERR_INVALID_ARGUMENT, bad
+        assert b"page table" in lib.rkv_last_error()
+    rc = lib.rkv_decode_split(ctypes.byref(summary()), 16, 0, 4, None, None, 0, 0, 0, 0, 0, None,
+                              0, None, 0.01, 2, 16, 16, 16, 1 << 20, 2, 0, 3, 16, 1 << 20, 1,
+                              None)
+    assert rc == _native.RKV_ERR_UNSUPPORTED and b"page pool" in lib.rkv_last_error()
+
+
 def test_workspace_size_needs_a_device(lib):
     if torch.cuda.is_available():
         pytest.skip("a device is present")
@@ -156,6 +180,7 @@ def test_cpu_tensors_fail_loudly():
         keys = torch.zeros(2, 2, 32, 128)
         block_size = 32
         num_blocks = 2
+        num_heads = 2
 
     q = torch.zeros(2, 4, 1, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
