@@ -45,7 +45,7 @@ __device__ __forceinline__ float nan_min(float a, float b) { return (b < a || b 
 // D: the tile width (the real head dim p.dim rounded up to 64; TMA fills the
 // padding columns with zeros and nothing reads them).
 template <int D, int R>
-__global__ void __launch_bounds__(256, 1) summarize_kernel(const __grid_constant__ SummarizeMaps maps,
+__global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant__ SummarizeMaps maps,
                                                            const SummarizeParams p) {
   constexpr int kTile = R * D * 2;
   constexpr int kStage = 2 * kTile;
