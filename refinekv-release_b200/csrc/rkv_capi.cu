@@ -100,10 +100,9 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   dim = padded_dim(dim);  // shared memory and scratch hold padded rows
   pl->tiles = static_cast<int>(cdiv(blocks, kSelectTile));
   const int64_t rows = heads * instances;
-  // Both selector kernels run one wave of at most one CTA per SM (8 warps,
-  // ~128 KB of TMA tiles each): a grid a few CTAs larger than the SM count
-  // doubles the work of the SMs that take two.  Phase A: one 16 KB stage
-  // (key-mean + ellipsoid tile) per warp.
+  // Both selector kernels run one wave of at most one CTA per SM: a grid a
+  // few CTAs larger than the SM count doubles the work of the SMs that take
+  // two.  Phase A: one 16 KB stage (key-mean + ellipsoid tile) per warp.
   const int one_wave = static_cast<int>(std::max<int64_t>(1, dev.sms / rows));
   if (fixed_parts_a > 0) {
     pl->parts_a = fixed_parts_a;
@@ -113,9 +112,14 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   }
   pl->stages_a = 1;
   const int64_t stage_a = 2LL * kSelectTile * dim * 2;
-  // No more warps than tiles per CTA (one head per GPU leaves one tile each).
+  // No more warps than tiles per CTA (one head per GPU leaves one tile each);
+  // up to 12 warps (a 192 KB ring) for groups of at most 8 rows, whose
+  // kernels fit 384 threads' registers, 8 under a sequence split (its
+  // fixed partial slots per CTA).
+  const int64_t max_warps = group <= 8 ? 12 : 8;
   pl->warps_a = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>({8, 131072 / stage_a, static_cast<int64_t>(pl->tpc_a)})));
+      1, std::min<int64_t>({fixed_parts_a > 0 ? int64_t{kStatsSlots} : max_warps,
+                            196608 / stage_a, static_cast<int64_t>(pl->tpc_a)})));
   // One LSE partial per warp; a sequence split fixes the count so that every
   // rank's slab has the same layout.
   pl->slots_a = fixed_parts_a > 0 ? kStatsSlots : pl->warps_a;
@@ -126,11 +130,14 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   // over many one-tile CTAs would flood it.  Segment capacity = blocks per CTA.
   split(pl->tiles, std::min(one_wave, std::max(1, pl->tiles / 4)), &pl->parts_b, &pl->tpc_b);
   pl->seg_cap = pl->tpc_b * kSelectTile;
-  pl->stages_b = decode ? 2 : 0;  // select mode stages no value tiles
+  // One value-mean stage per warp and up to 12 warps: the decisions and the
+  // representative softmax are latency-bound, so warps beat stages (a 1M
+  // layer's final kernel measured ~3 us faster than 8 warps x 2 stages).
+  pl->stages_b = decode ? 1 : 0;  // select mode stages no value tiles
   const int64_t g8b = group <= 8 ? 8 : 16;
   const int64_t per_warp_b = pl->stages_b * kSelectTile * dim * 2 + g8b * dim * 4;
   pl->warps_b = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>({8, 200000 / per_warp_b, static_cast<int64_t>(pl->tpc_b)})));
+      1, std::min<int64_t>({max_warps, 200000 / per_warp_b, static_cast<int64_t>(pl->tpc_b)})));
   pl->smem_b = final_smem_bytes(static_cast<int>(dim), pl->warps_b, pl->stages_b,
                                 static_cast<int>(group), pl->tpc_b);
   if (pl->smem_a > static_cast<size_t>(dev.smem_optin) ||

@@ -85,7 +85,7 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
 // PACK4 (groups of at most 4 rows): q and q^2 share one n8 tile, see
 // score_tile_pair; each lane then finishes 4 (block, row) elements.
 template <int D, int NT, bool PACK4>
-__global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ StatsMaps maps,
+__global__ void __launch_bounds__(NT == 1 ? 384 : 256) stats_kernel(const __grid_constant__ StatsMaps maps,
                                                     const StatsParams p) {
   constexpr int R = kSelectTile;
   constexpr int kTile = R * D * 2;
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(256) stats_kernel(const __grid_constant__ Stat
 // padding rows repeat row 0 and are masked out of the reduction, which keeps
 // the per-row risk evaluations branch-free and independent.
 template <int D, int NT, int GM>
-__global__ void __launch_bounds__(256) final_kernel(const __grid_constant__ FinalMaps maps,
+__global__ void __launch_bounds__(NT == 1 ? 384 : 256) final_kernel(const __grid_constant__ FinalMaps maps,
                                                     const FinalParams p) {
   constexpr int R = kSelectTile;
   constexpr int kTile = R * D * 2;
