@@ -404,6 +404,12 @@ __global__ void __launch_bounds__(NT == 1 ? 384 : 256) final_kernel(const __grid
     flags[0] = 0;
     if (p.decode) tma_prefetch_desc(&maps.value_mean);
   }
+  // The value-mean tiles of the CTA's range (read by the representative
+  // softmax after the decisions) go to L2 before the dependency wait, while
+  // DRAM idles through the stats kernel's tail and the decisions.
+  if (p.decode && lane == 0) {
+    for (int t = t0 + warp; t < t1; t += warps) tma_prefetch_tile<D>(&maps.value_mean, t * R, h);
+  }
   // Value norms and anchor bits do not change during decode: the lines of
   // this warp's first two tiles go to L2 before the dependency wait (the
   // first and last lane's addresses cover a tile's lines).
