@@ -33,7 +33,9 @@ import torch
 HERE = pathlib.Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "refinekv-release_b200"))
-sys.path.insert(0, os.environ.get("REFINEKV_REFERENCE_SRC", "/root/reference/src"))
+if "REFINEKV_REFERENCE_SRC" not in os.environ:
+    sys.exit("set REFINEKV_REFERENCE_SRC to the reference source tree's src directory")
+sys.path.insert(0, os.environ["REFINEKV_REFERENCE_SRC"])
 
 import refinekv  # noqa: E402  (the reference package)
 from refinekv import RefineKVConfig, build_summary, sparse_attention  # noqa: E402
