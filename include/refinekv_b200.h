@@ -209,10 +209,10 @@ RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_
 
 /*
  * rkv_decode without a workspace, for callers that cannot allocate device
- * memory on the decode path: runtimes that record the step into a CUDA graph
- * while allocation is not allowed, hosts that reach this library only through
- * its C ABI and have no device allocator of their own, or serving stacks whose
- * device memory is partitioned before decoding starts.  This entry point has
+ * memory on the decode path: hosts that reach this library only through its
+ * C ABI (an FFI from a language with no CUDA allocator of its own), or serving
+ * stacks that hand out all device memory before decoding starts and may not
+ * allocate afterwards.  This entry point has
  * no counterpart in the reference.
  *   Same arguments and results as rkv_decode with phases = RKV_PHASE_ALL,
  *   minus the workspace.  Scratch comes from one array of

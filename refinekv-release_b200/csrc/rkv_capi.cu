@@ -79,7 +79,7 @@ struct Plan {
   int g8 = 8, max_sources = 0;
   size_t smem_d = 0;  // combine
   // workspace offsets (bytes)
-  size_t status = 0, done = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
+  size_t status = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
   size_t rep_m = 0, rep_l = 0, rep_o = 0, att_m = 0, att_l = 0, att_o = 0, bytes = 0;
 };
 
@@ -191,7 +191,6 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   };
   const size_t rowsg = static_cast<size_t>(rows) * group;
   pl->status = take(256);
-  pl->done = take(static_cast<size_t>(heads) * 4);
   // (Under a sequence split phase A writes into the exchange slab instead.)
   pl->lse = take(fixed_parts_a > 0 ? 0 : rowsg * pl->parts_a * pl->slots_a * 4 * 4);
   pl->z = take(rowsg * blocks * 4);

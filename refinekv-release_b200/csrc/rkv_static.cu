@@ -1,12 +1,12 @@
 // rkv_decode_static: rkv_decode for callers that cannot allocate device memory.
 //
 // Some callers of this library have no way to provide a device workspace:
-// runtimes that record the decode step into a CUDA graph while allocation is
-// forbidden, hosts that bind only this C ABI (for example through an FFI from a
-// language without a CUDA allocator), or serving stacks whose memory is fully
-// partitioned in advance.  This entry point runs exactly the same kernels as
-// rkv_decode but takes its scratch from a fixed array that lives in this
-// library's device image instead of a caller-supplied workspace.
+// hosts that bind only this C ABI (for example through an FFI from a language
+// without a CUDA allocator), or serving stacks that partition all device
+// memory in advance and may not allocate once decoding has started.  This
+// entry point runs exactly the same kernels as rkv_decode but takes its
+// scratch from a fixed array that lives in this library's device image
+// instead of a caller-supplied workspace.
 //
 // Limits and sharing:
 // * the array is RKV_DECODE_STATIC_SCRATCH_BYTES (32 MiB) on every GPU that loads the

@@ -1,9 +1,9 @@
 """rkv_decode_static: decode for callers that cannot allocate device memory.
 
-Some callers of this library cannot hand it a device workspace: a runtime that
-records the decode step into a CUDA graph at a point where allocation is not
-allowed, or a host that reaches the library only through its C ABI and has no
-device allocator of its own.  rkv_decode_static runs the same kernels as
+Some callers of this library cannot hand it a device workspace: a host that
+reaches the library only through its C ABI and has no device allocator of its
+own, or a serving stack that has partitioned all device memory before decoding
+starts and may not allocate afterwards.  rkv_decode_static runs the same kernels as
 rkv_decode but takes its scratch from one fixed array inside the library.
 
 These tests call it through the C ABI and require the same results as the
