@@ -8,14 +8,17 @@ refinekv_b200/synthetic.py), block_size 32, eps 0.01, GQA "any", 32 prompt
 anchors.  Following the reference's speed protocol (128 generated tokens,
 timing the last 125), the default run decodes W=3 warm-up steps and times
 K=125 steps.  A step is one decode step of all 32 layers: for each layer the
-selector (2 kernels) and the split attention with its combine (1 kernel),
-replayed from a per-step CUDA graph with the device-side suffix length.
+selector (2 kernels), the split attention (1 kernel) and its combine (1
+kernel), replayed from a per-step CUDA graph with the device-side suffix
+length.
 
 Every layer's KV (512 MiB) is larger than L2, so no flush is needed between
 steps.  value = device time per step (CUDA events, max over ranks).  e2e =
-the same step through the public Python API (sparse_attention), eager, with
-the step's queries and new K/V tokens copied from pinned host memory and the
-outputs copied back inside the timed region.
+the same step through the public Python API (sparse_attention) with the
+step's queries and new K/V tokens copied from pinned host memory and the
+outputs copied back inside the timed region, the host waiting for each
+step: one captured CUDA graph per step (copies included) for `value`, the
+same calls issued eagerly for `eager_value`.
 
 --gpus N shards the KV heads across N ranks (one process per GPU, torchrun);
 with N dividing the 8 KV heads there is no per-step collective (strong
