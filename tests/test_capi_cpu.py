@@ -189,3 +189,19 @@ def test_cpu_tensors_fail_loudly():
         select_blocks(q, _Summary(), RefineKVConfig(backend="torch"))
     with pytest.raises(ValueError, match="query must have shape"):
         select_blocks(q[:, :, 0], _Summary())
+
+
+def test_integration_stub_matches_the_abi_struct():
+    """The ctypes stub a maintainer would copy declares rkv_summary as the library does."""
+    text = (REPO / "INTEGRATION.md").read_text()
+    block = text[text.index("class _Summary(ctypes.Structure)"):text.index("def _view(s)")]
+    names = re.findall(r'\("(\w+)", ctypes\.c_\w+\)', block)
+    assert names == [name for name, _ in _native.Summary._fields_]
+    view = text[text.index("def _view(s)"):text.index("_RED = ")]
+    args = view[view.index("_Summary(") + len("_Summary("):view.rindex(")")]
+    depth, count = 0, 1
+    for ch in args:
+        depth += ch in "(["
+        depth -= ch in ")]"
+        count += ch == "," and depth == 0
+    assert count == len(_native.Summary._fields_)
