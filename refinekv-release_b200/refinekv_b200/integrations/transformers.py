@@ -25,7 +25,11 @@ here) or from the B200 design:
   the model forward): the graph cache writes at a device-side cursor;
 * ``full_attention_layers`` works under CUDA graphs (the reference refuses):
   dense layers attend over the fixed-capacity cache with a device-side mask
-  built from the visible length.
+  built from the visible length;
+* beyond the reference (batch 1 only, ``:448-449``), eager decode also takes
+  a left-padded batch of prompts: each row's summary covers its own prompt
+  (the padding excluded) and all rows decode in one batched launch set
+  (``build_summary_batch``).
 """
 
 from __future__ import annotations
@@ -45,7 +49,7 @@ except ImportError as error:  # pragma: no cover - exercised only without transf
 
 from ..attention import select_blocks_union, sparse_attention
 from ..config import RefineKVConfig
-from ..summary import BlockSummary, build_summary
+from ..summary import BlockSummary, build_summary, build_summary_batch
 
 ATTN_IMPLEMENTATION = "refinekv_b200"
 _MISSING = object()
@@ -152,6 +156,7 @@ class _LayerState:
     summary: BlockSummary | None = None
     anchor_mask: torch.Tensor | None = None
     workspace: dict = field(default_factory=dict)
+    pads: list | None = None  # left padding per row of a batch
 
 
 def _attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None,
@@ -190,6 +195,8 @@ class RefineKV:
     with one unpadded prompt; DynamicCache, ``cache_implementation="static"``
     and :func:`make_visible_static_cache` are supported.  ``cuda_graph=True``
     runs fixed-length greedy decode from one captured CUDA graph per request.
+    Beyond the reference, eager generation also takes a batch of prompts,
+    left-padded as Transformers pads decoder-only batches (``num_beams=1``).
     """
 
     def __init__(self, model, config: RefineKVConfig | None = None, *, cuda_graph=False):
@@ -203,6 +210,7 @@ class RefineKV:
         self._anchor_queries: dict[int, torch.Tensor] = {}
         self._handles = []
         self._cache = None
+        self._pads = None
         self._active = False
         self._totals = dict(accessed=0, dense=0, decode_attention_calls=0)
 
@@ -229,6 +237,7 @@ class RefineKV:
         self._anchor_queries.clear()
         self._totals = dict(accessed=0, dense=0, decode_attention_calls=0)
         self._cache = cache
+        self._pads = None
 
     # ---- context -----------------------------------------------------------
     def __enter__(self):
@@ -285,6 +294,9 @@ class RefineKV:
                 raise ValueError("stock StaticCache is unsupported; use "
                                  "cache_implementation='static' or make_visible_static_cache")
             generation = kwargs.get("generation_config") or self.model.generation_config
+            if (kwargs.get("num_beams", generation.num_beams) or 1) != 1:
+                # Beam search reorders the cache; the summaries cannot follow.
+                raise ValueError("RefineKV requires num_beams=1")
             implementation = kwargs.get("cache_implementation", generation.cache_implementation)
             if implementation == "static":
                 if kwargs.get("past_key_values") is not None:
@@ -294,7 +306,7 @@ class RefineKV:
                     inputs = args[0]
                 if not isinstance(inputs, torch.Tensor) or inputs.ndim != 2:
                     raise ValueError(
-                        "static cache generation requires input_ids of shape (1, tokens)")
+                        "static cache generation requires input_ids of shape (batch, tokens)")
                 prompt = inputs.shape[1]
                 new_tokens = kwargs.get("max_new_tokens", generation.max_new_tokens)
                 capacity = (prompt + int(new_tokens) if new_tokens is not None
@@ -479,8 +491,7 @@ class RefineKV:
             inputs = kwargs.get("inputs_embeds")
         if inputs is None and args:
             inputs = args[0]
-        if inputs is not None and inputs.shape[0] != 1:
-            raise ValueError("RefineKV requires batch_size=1 and num_beams=1")
+        batch = inputs.shape[0] if inputs is not None else 1
         if not kwargs.get("use_cache", self.model.config.use_cache):
             raise ValueError("RefineKV requires use_cache=True")
         if kwargs.get("output_attentions", False):
@@ -492,17 +503,25 @@ class RefineKV:
             mask = kwargs.get("attention_mask")
             if isinstance(mask, dict):
                 mask = mask.get("full_attention")
+            pads = None
             if mask is not None:
-                if mask.ndim == 2:
+                if mask.ndim == 2 and batch > 1:
+                    # A batch may be left-padded: every row 0...0 1...1.
+                    rows = mask.bool()
+                    valid = bool(rows[:, -1].all()) and bool((rows[:, 1:] >= rows[:, :-1]).all())
+                    pads = (~rows).sum(1).tolist()
+                elif mask.ndim == 2:
                     valid = bool(mask.all())
-                elif mask.ndim == 4 and inputs is not None:
+                elif mask.ndim == 4 and inputs is not None and batch == 1:
                     last = mask[0, 0, -1, :inputs.shape[1]]
                     valid = bool(last.all()) if mask.dtype == torch.bool else bool((last == 0).all())
                 else:
                     valid = False
                 if not valid:
-                    raise ValueError("RefineKV requires an unpadded prompt")
+                    raise ValueError("RefineKV requires an unpadded prompt (a batch may be "
+                                     "left-padded, with a 2-D attention_mask)")
             self._reset_request(cache)
+            self._pads = pads
 
     def _after_forward(self, module, args, kwargs, output):
         cache = getattr(output, "past_key_values", None)
@@ -533,7 +552,7 @@ class RefineKV:
         cos, sin = positions
         query, _ = _rotary(self.model.config.model_type)(
             query, query, cos[..., -count:, :], sin[..., -count:, :])
-        self._anchor_queries[index] = query[0].detach()
+        self._anchor_queries[index] = query.detach()  # (batch, query heads, count, dim)
 
     # ---- attention ---------------------------------------------------------
     def _prefill(self, module, index, query, key, value, mask, scaling, kwargs):
@@ -551,7 +570,8 @@ class RefineKV:
                 heads, dim = key.shape[1], query.shape[-1]
                 groups = query.shape[1] // heads
                 # (query heads, anchors, dim) -> (anchors, kv heads, group, 1, dim)
-                grouped = anchors[:, -count:].transpose(0, 1).reshape(count, heads, groups, 1, dim)
+                grouped = anchors[0, :, -count:].transpose(0, 1).reshape(
+                    count, heads, groups, 1, dim)
                 state.anchor_mask = select_blocks_union(grouped, state.summary, self.config,
                                                         workspace=state.workspace)
         self._layers[index] = state
@@ -580,7 +600,7 @@ class RefineKV:
 
     def _attention(self, module, query, key, value, mask, scaling, kwargs):
         if query.shape[0] != 1:
-            raise ValueError("RefineKV requires batch_size=1")
+            return self._attention_batch(module, query, key, value, mask, scaling, kwargs)
         index = self._module_indices[id(module)]
         state = self._layers.get(index)
         if state is None:
@@ -619,3 +639,75 @@ class RefineKV:
             accessed = accessed + query.shape[1] * (state.visible_length - state.prompt_length)
             self._record(accessed, query.shape[1] * state.visible_length)
         return result.output.reshape(query.shape[1], 1, dim).transpose(0, 1).unsqueeze(0), None
+
+    # ---- batches (beyond the reference) ------------------------------------
+    def _attention_batch(self, module, query, key, value, mask, scaling, kwargs):
+        """A left-padded batch: prompts stacked on the KV-head axis of one summary.
+
+        Row i's prompt is its last ``prompt - pads[i]`` positions; the
+        generated tokens follow the padded prompt in every row, so all rows
+        decode in lockstep with one suffix length, the layout of
+        :func:`~refinekv_b200.build_summary_batch`.
+        """
+        if self._graph_mode:
+            raise ValueError("CUDA-graph decode takes one sequence")
+        index = self._module_indices[id(module)]
+        state = self._layers.get(index)
+        rows, heads, dim = query.shape[0], key.shape[1], query.shape[-1]
+        groups = query.shape[1] // heads
+        if state is None:
+            return self._prefill_batch(module, index, query, key, value, mask, scaling, kwargs)
+        if query.shape[2] != 1:
+            raise ValueError("RefineKV supports one full prefill followed by single-token decode")
+        state.visible_length += 1
+        if key.shape[2] < state.visible_length:
+            raise ValueError("the KV cache no longer contains the full visible prefix")
+        dense = query.shape[1] * sum(state.visible_length - pad for pad in state.pads)
+        if state.summary is None:
+            if self.config.collect_stats:
+                self._record(dense, dense)
+            return self._dense_decode(module, query, key, value, mask, scaling, kwargs,
+                                      state.visible_length)
+        result = sparse_attention(
+            query.reshape(rows * heads, groups, 1, dim), state.summary,
+            key[:, :, state.prompt_length:state.visible_length].flatten(0, 1),
+            value[:, :, state.prompt_length:state.visible_length].flatten(0, 1), self.config,
+            anchor_mask=state.anchor_mask, workspace=state.workspace,
+            return_selected=self.config.collect_stats)
+        if self.config.collect_stats:
+            selected = result.selected
+            counts = state.summary.counts.repeat_interleave(heads, 0)  # per row, 0 past a prompt
+            accessed = ((selected * counts).sum() + (~selected & (counts > 0)).sum()) * groups
+            accessed = accessed + query.shape[1] * rows * (state.visible_length - state.prompt_length)
+            self._record(accessed, dense)
+        return result.output.reshape(rows, query.shape[1], 1, dim).transpose(1, 2), None
+
+    def _prefill_batch(self, module, index, query, key, value, mask, scaling, kwargs):
+        output = sdpa_attention_forward(module, query, key, value, mask, dropout=0,
+                                        scaling=scaling, **kwargs)
+        rows, prompt = query.shape[0], query.shape[2]
+        pads = self._pads if self._pads is not None else [0] * rows
+        if len(pads) != rows:
+            raise RuntimeError("the batch's padding does not match its rows")
+        state = _LayerState(prompt, prompt, pads=list(pads))
+        if index >= self.config.full_attention_layers:
+            state.summary = build_summary_batch(
+                [key[i, :, pad:prompt] for i, pad in enumerate(pads)],
+                [value[i, :, pad:prompt] for i, pad in enumerate(pads)], self.config)
+            count = min(self.config.anchor_tokens, prompt)
+            anchors = self._anchor_queries.pop(index, None)
+            if count and anchors is None:
+                raise RuntimeError(f"missing prompt anchor queries in layer {index}")
+            if count:
+                heads, dim = key.shape[1], query.shape[-1]
+                groups = query.shape[1] // heads
+                tail = anchors[:, :, -count:].clone()  # (rows, query heads, count, dim)
+                for i, pad in enumerate(pads):
+                    real = min(count, prompt - pad)
+                    if real < count:  # a short prompt: repeat a real anchor, the union is unchanged
+                        tail[i, :, :count - real] = tail[i, :, count - 1:count]
+                grouped = tail.permute(2, 0, 1, 3).reshape(count, rows * heads, groups, 1, dim)
+                state.anchor_mask = select_blocks_union(grouped, state.summary, self.config,
+                                                        workspace=state.workspace)
+        self._layers[index] = state
+        return output

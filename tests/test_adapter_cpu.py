@@ -212,3 +212,102 @@ def test_cuda_graph_arguments_are_validated_before_any_work():
                            temperature=0.5)
         with pytest.raises(ValueError, match="CUDA BF16"):  # a CPU model is refused
             model.generate(input_ids=ids, max_new_tokens=4, min_new_tokens=4, eos_token_id=None)
+
+
+class _OracleBatch:
+    """Stand-in batched summary: one oracle summary per prompt (rows stacked per prompt)."""
+
+    def __init__(self, parts):
+        self.parts = parts
+
+
+@pytest.fixture
+def oracle_batch_backend(monkeypatch, oracle_backend):
+    single_union, single_decode = adapter.select_blocks_union, adapter.sparse_attention
+    calls = {"summaries": 0, "anchor_unions": 0, "decodes": 0}
+
+    def build_summary_batch(keys, values, config):
+        calls["summaries"] += 1
+        return _OracleBatch([ora.build_summary(k.float(), v.float(), block_size=config.block_size)
+                             for k, v in zip(keys, values)])
+
+    def select_blocks_union(queries, summary, config, *, workspace=None):
+        if not isinstance(summary, _OracleBatch):
+            return single_union(queries, summary, config, workspace=workspace)
+        calls["anchor_unions"] += 1
+        h = queries.shape[1] // len(summary.parts)
+        return [ora.anchor_union(queries[:, i * h:(i + 1) * h].float(), s, config.eps,
+                                 config.gqa_reduction) for i, s in enumerate(summary.parts)]
+
+    def sparse_attention(query, summary, key_suffix, value_suffix, config, *, anchor_mask=None,
+                         workspace=None, return_selected=False, suffix_length=None):
+        if not isinstance(summary, _OracleBatch):
+            return single_decode(query, summary, key_suffix, value_suffix, config,
+                                 anchor_mask=anchor_mask, return_selected=return_selected)
+        calls["decodes"] += 1
+        h = query.shape[0] // len(summary.parts)
+        outs = []
+        for i, s in enumerate(summary.parts):
+            r = slice(i * h, (i + 1) * h)
+            out, _ = ora.sparse_attention(query[r].float(), s, key_suffix[r].float(),
+                                          value_suffix[r].float(), config.eps,
+                                          config.gqa_reduction,
+                                          anchor_mask=None if anchor_mask is None else anchor_mask[i])
+            outs.append(out)
+        return AttentionResult(torch.cat(outs).to(query.dtype), None)
+
+    monkeypatch.setattr(adapter, "build_summary_batch", build_summary_batch)
+    monkeypatch.setattr(adapter, "select_blocks_union", select_blocks_union)
+    monkeypatch.setattr(adapter, "sparse_attention", sparse_attention)
+    return calls
+
+
+def _prefill_and_step(model, ids, mask, token):
+    """Dense prefill then one decode step, positions from the padding as generate sets them."""
+    cache = transformers.DynamicCache(config=model.config)
+    positions = (mask.cumsum(1) - 1).clamp(min=0)
+    first = model(input_ids=ids, attention_mask=mask, position_ids=positions,
+                  past_key_values=cache, use_cache=True).logits[:, -1]
+    mask = torch.cat([mask, torch.ones_like(mask[:, :1])], 1)
+    step = model(input_ids=token, attention_mask=mask, position_ids=positions[:, -1:] + 1,
+                 past_key_values=cache, use_cache=True).logits[:, -1]
+    return first, step
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_left_padded_batch_decodes_like_each_prompt_alone(family, oracle_batch_backend):
+    """Beyond the reference (batch 1): a left-padded batch, one summary per row's own prompt."""
+    model = _model(family)
+    config = RefineKVConfig(eps=0.05, anchor_tokens=16, full_attention_layers=1)
+    lengths = (9, 40, 23)  # the 9-token prompt is shorter than the 16 anchors
+    width = max(lengths)
+    ids = torch.zeros(len(lengths), width, dtype=torch.long)
+    mask = torch.zeros_like(ids)
+    prompts = [torch.arange(n) % 61 + 3 + i for i, n in enumerate(lengths)]
+    for i, p in enumerate(prompts):
+        ids[i, width - len(p):] = p
+        mask[i, width - len(p):] = 1
+    token = torch.tensor([[5], [7], [11]])
+    with RefineKV(model, config):
+        first, step = _prefill_and_step(model, ids, mask, token)
+    # layer 0 dense, layer 1 through the batched summary, anchors and decode
+    assert oracle_batch_backend == {"summaries": 1, "anchor_unions": 1, "decodes": 1}
+    for i, p in enumerate(prompts):
+        with RefineKV(model, config):
+            first_i, step_i = _prefill_and_step(model, p[None], torch.ones_like(p[None]),
+                                                token[i:i + 1])
+        torch.testing.assert_close(first[i], first_i[0], atol=1e-4, rtol=1e-4)
+        torch.testing.assert_close(step[i], step_i[0], atol=1e-4, rtol=1e-4)
+
+
+def test_batch_rejects_right_padding_and_beams(oracle_batch_backend):
+    model = _model()
+    ids = torch.full((2, 6), 4, dtype=torch.long)
+    right = torch.tensor([[1, 1, 1, 1, 1, 1], [1, 1, 1, 1, 0, 0]])
+    with RefineKV(model, RefineKVConfig()):
+        with pytest.raises(ValueError, match="left-padded"):
+            model(input_ids=ids, attention_mask=right,
+                  past_key_values=transformers.DynamicCache(config=model.config), use_cache=True)
+        with pytest.raises(ValueError, match="num_beams"):
+            model.generate(input_ids=ids, attention_mask=torch.ones_like(ids), num_beams=2,
+                           max_new_tokens=2, do_sample=False)
