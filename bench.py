@@ -597,7 +597,9 @@ def run_b200(args):
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
     traffic = profiled_traffic("attend_llama8b_128k.md")
     traffic_per_launch = None
-    if traffic is not None and not split:
+    # The committed capture is of 32-token pages of 128 channels; its DRAM
+    # bytes scale with the pages a launch reads only for that page shape.
+    if traffic is not None and not split and (args.block_size, args.head_dim) == (32, 128):
         dram_bytes, pages_profiled = traffic
         traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
