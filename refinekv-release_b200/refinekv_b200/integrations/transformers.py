@@ -26,10 +26,10 @@ here) or from the B200 design:
 * ``full_attention_layers`` works under CUDA graphs (the reference refuses):
   dense layers attend over the fixed-capacity cache with a device-side mask
   built from the visible length;
-* beyond the reference (batch 1 only, ``:448-449``), eager decode also takes
-  a left-padded batch of prompts: each row's summary covers its own prompt
-  (the padding excluded) and all rows decode in one batched launch set
-  (``build_summary_batch``).
+* beyond the reference (batch 1 only, ``:448-449``), decode also takes a
+  left-padded batch of prompts, eagerly or from one captured CUDA graph:
+  each row's summary covers its own prompt (the padding excluded) and all
+  rows decode in one batched launch set (``build_summary_batch``).
 """
 
 from __future__ import annotations
@@ -157,6 +157,7 @@ class _LayerState:
     anchor_mask: torch.Tensor | None = None
     workspace: dict = field(default_factory=dict)
     pads: list | None = None  # left padding per row of a batch
+    pad_rows: torch.Tensor | None = None  # the same, (rows, 1, 1, 1) on the device
 
 
 def _attention_forward(module, query, key, value, attention_mask, dropout=0.0, scaling=None,
@@ -195,8 +196,9 @@ class RefineKV:
     with one unpadded prompt; DynamicCache, ``cache_implementation="static"``
     and :func:`make_visible_static_cache` are supported.  ``cuda_graph=True``
     runs fixed-length greedy decode from one captured CUDA graph per request.
-    Beyond the reference, eager generation also takes a batch of prompts,
-    left-padded as Transformers pads decoder-only batches (``num_beams=1``).
+    Beyond the reference, generation (eager or CUDA graph) also takes a batch
+    of prompts, left-padded as Transformers pads decoder-only batches
+    (``num_beams=1``).
     """
 
     def __init__(self, model, config: RefineKVConfig | None = None, *, cuda_graph=False):
@@ -378,8 +380,8 @@ class RefineKV:
         else:
             input_ids = kwargs.get("input_ids")
         if (not isinstance(input_ids, torch.Tensor) or input_ids.ndim != 2
-                or input_ids.shape[0] != 1 or input_ids.dtype != torch.long):
-            raise ValueError("CUDA Graph generation requires one input_ids sequence")
+                or input_ids.dtype != torch.long):
+            raise ValueError("CUDA Graph generation requires an input_ids tensor (batch, tokens)")
         max_new_tokens = kwargs.get("max_new_tokens")
         if not isinstance(max_new_tokens, int) or max_new_tokens < 4:
             raise ValueError("CUDA Graph generation requires max_new_tokens >= 4")
@@ -410,21 +412,33 @@ class RefineKV:
                 or self.config.collect_stats):
             raise ValueError("CUDA Graph requires a CUDA BF16 model, the CUDA backend and no stats")
         mask = kwargs.get("attention_mask")
-        if mask is not None and (not isinstance(mask, torch.Tensor) or mask.shape != input_ids.shape
-                                 or mask.device != input_ids.device or not bool(mask.all())):
-            raise ValueError("CUDA Graph generation requires an unpadded prompt")
+        if mask is not None:
+            if (not isinstance(mask, torch.Tensor) or mask.shape != input_ids.shape
+                    or mask.device != input_ids.device):
+                raise ValueError("attention_mask must match input_ids")
+            rows = mask.bool()
+            left_padded = bool(rows[:, -1].all()) and bool((rows[:, 1:] >= rows[:, :-1]).all())
+            if not (bool(rows.all()) or (input_ids.shape[0] > 1 and left_padded)):
+                raise ValueError("CUDA Graph generation requires an unpadded prompt "
+                                 "(a batch may be left-padded)")
         return input_ids, max_new_tokens, penalty, mask
 
     def _generate_cuda_graph(self, *args, **kwargs):
         """Prefill eagerly, capture one greedy decode step, replay it (``transformers.py:302-440``)."""
         input_ids, max_new_tokens, penalty, mask = self._graph_arguments(args, kwargs)
         device = input_ids.device
-        prompt_length = input_ids.shape[1]
+        rows, prompt_length = input_ids.shape
         cursor = _GraphCursor(device)
         capacity = prompt_length + max_new_tokens
         cache = Cache(layers=[_GraphStaticLayer(capacity, cursor) for _ in self.model.model.layers])
-        prefill = self.model(input_ids=input_ids, attention_mask=mask, past_key_values=cache,
-                             use_cache=True, logits_to_keep=1)
+        # Left padding (a batch): each row's positions count its real tokens only.
+        pads = torch.zeros(rows, 1, device=device, dtype=torch.long)
+        positions = None
+        if mask is not None and not bool(mask.all()):
+            pads = (mask == 0).sum(1, keepdim=True)
+            positions = (mask.long().cumsum(1) - 1).clamp(min=0)
+        prefill = self.model(input_ids=input_ids, attention_mask=mask, position_ids=positions,
+                             past_key_values=cache, use_cache=True, logits_to_keep=1)
         seen = None
         if penalty != 1.0:
             seen = torch.zeros_like(prefill.logits[:, -1], dtype=torch.bool)
@@ -437,9 +451,9 @@ class RefineKV:
                 scores = torch.where(seen, adjusted, scores)
             return scores.argmax(-1, keepdim=True)
 
-        token = greedy(prefill.logits[:, -1]).clone()
-        output_tokens = torch.empty(max_new_tokens, device=device, dtype=input_ids.dtype)
-        output_tokens[:1].copy_(token.reshape(1))
+        token = greedy(prefill.logits[:, -1]).clone()  # (rows, 1)
+        output_tokens = torch.empty(max_new_tokens, rows, device=device, dtype=input_ids.dtype)
+        output_tokens[:1].copy_(token.reshape(1, rows))
         del prefill
         for layer in cache.layers:
             layer.graph_decode = True
@@ -454,10 +468,10 @@ class RefineKV:
             if seen is not None:
                 seen.scatter_(1, token, True)
             result = self.model(input_ids=token, attention_mask=None, past_key_values=cache,
-                                position_ids=cursor.position.unsqueeze(0), use_cache=True,
+                                position_ids=cursor.position.view(1, 1) - pads, use_cache=True,
                                 logits_to_keep=1)
             following = greedy(result.logits[:, -1])
-            output_tokens.index_copy_(0, output_index, following.reshape(1))
+            output_tokens.index_copy_(0, output_index, following.reshape(1, rows))
             token.copy_(following)
             cursor.position.add_(1)
             output_index.add_(1)
@@ -478,7 +492,7 @@ class RefineKV:
             for _ in range(max_new_tokens - 1 - warmup_steps):
                 graph.replay()
             torch.cuda.synchronize(device)
-            return torch.cat((input_ids, output_tokens.view(1, -1)), dim=1)
+            return torch.cat((input_ids, output_tokens.t()), dim=1)
         finally:
             del graph
             self._graph_mode = False
@@ -592,9 +606,12 @@ class RefineKV:
     def _dense_graph_decode(self, module, query, key, value, scaling, kwargs, state):
         """Dense layer under CUDA graphs: the whole fixed-capacity cache, masked on the device."""
         visible = state.prompt_length + self._graph_suffix_length
-        live = torch.arange(key.shape[2], device=key.device) < visible
-        mask = query.new_zeros((1, 1, 1, key.shape[2])).masked_fill(
-            ~live.view(1, 1, 1, -1), torch.finfo(query.dtype).min)
+        columns = torch.arange(key.shape[2], device=key.device)
+        live = (columns < visible).view(1, 1, 1, -1)
+        if state.pad_rows is not None:  # a left-padded batch: skip each row's padding
+            live = live & (columns.view(1, 1, 1, -1) >= state.pad_rows)
+        mask = query.new_zeros((live.shape[0], 1, 1, key.shape[2])).masked_fill(
+            ~live, torch.finfo(query.dtype).min)
         return sdpa_attention_forward(module, query, key, value, mask, dropout=0, scaling=scaling,
                                       **kwargs)
 
@@ -649,8 +666,6 @@ class RefineKV:
         decode in lockstep with one suffix length, the layout of
         :func:`~refinekv_b200.build_summary_batch`.
         """
-        if self._graph_mode:
-            raise ValueError("CUDA-graph decode takes one sequence")
         index = self._module_indices[id(module)]
         state = self._layers.get(index)
         rows, heads, dim = query.shape[0], key.shape[1], query.shape[-1]
@@ -659,6 +674,16 @@ class RefineKV:
             return self._prefill_batch(module, index, query, key, value, mask, scaling, kwargs)
         if query.shape[2] != 1:
             raise ValueError("RefineKV supports one full prefill followed by single-token decode")
+        if self._graph_mode:
+            if state.summary is None:
+                return self._dense_graph_decode(module, query, key, value, scaling, kwargs, state)
+            result = sparse_attention(
+                query.reshape(rows * heads, groups, 1, dim), state.summary,
+                key[:, :, state.prompt_length:].flatten(0, 1),
+                value[:, :, state.prompt_length:].flatten(0, 1), self.config,
+                anchor_mask=state.anchor_mask, workspace=state.workspace,
+                suffix_length=self._graph_suffix_length)
+            return result.output.reshape(rows, query.shape[1], 1, dim).transpose(1, 2), None
         state.visible_length += 1
         if key.shape[2] < state.visible_length:
             raise ValueError("the KV cache no longer contains the full visible prefix")
@@ -690,6 +715,8 @@ class RefineKV:
         if len(pads) != rows:
             raise RuntimeError("the batch's padding does not match its rows")
         state = _LayerState(prompt, prompt, pads=list(pads))
+        if any(pads):
+            state.pad_rows = torch.tensor(pads, device=key.device).view(-1, 1, 1, 1)
         if index >= self.config.full_attention_layers:
             state.summary = build_summary_batch(
                 [key[i, :, pad:prompt] for i, pad in enumerate(pads)],

@@ -4,7 +4,8 @@ Beyond the reference adapter, which decodes one sequence
 (``transformers.py:448-449``).  Each row of a batch keeps a summary of its
 own prompt (the padding excluded), so one batched decode step must give every
 row the logits of that prompt decoded alone, to bf16 rounding (the padded
-prefill and the stacked kernels round differently in the last bits).
+prefill and the stacked kernels round differently in the last bits); a
+captured decode step gives the eager batch's tokens exactly.
 """
 
 from __future__ import annotations
@@ -80,10 +81,30 @@ def test_batch_generate_dynamic_and_static_caches_agree(family):
     assert torch.equal(dynamic, static)
 
 
-def test_batch_is_refused_by_cuda_graph_decode():
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+@pytest.mark.parametrize("dense_layers", [0, 1])
+def test_batch_cuda_graph_decode_matches_eager(family, dense_layers):
+    """One captured step for a left-padded batch gives the eager batch's tokens."""
+    model = _model(family, layers=3)
+    if family == "qwen2":
+        model.generation_config.repetition_penalty = 1.05
+    config = RefineKVConfig(eps=0.01, anchor_tokens=4, full_attention_layers=dense_layers)
+    ids, mask, _ = _batch(LENGTHS)
+    opts = dict(input_ids=ids, attention_mask=mask, max_new_tokens=8, min_new_tokens=8,
+                do_sample=False, eos_token_id=None, pad_token_id=0)
+    with RefineKV(model, config):
+        eager = model.generate(**opts)
+    with RefineKV(model, config, cuda_graph=True):
+        graph = model.generate(**opts)
+    assert torch.equal(graph, eager)
+
+
+def test_cuda_graph_refuses_right_padding():
     model = _model()
-    ids, mask, _ = _batch((8, 8))
+    ids = torch.full((2, 8), 4, dtype=torch.long, device="cuda")
+    right = torch.ones_like(ids)
+    right[1, -2:] = 0
     with RefineKV(model, cuda_graph=True):
-        with pytest.raises(ValueError, match="one input_ids sequence"):
-            model.generate(input_ids=ids, attention_mask=mask, max_new_tokens=4,
+        with pytest.raises(ValueError, match="left-padded"):
+            model.generate(input_ids=ids, attention_mask=right, max_new_tokens=4,
                            min_new_tokens=4, eos_token_id=None)
