@@ -157,6 +157,26 @@ RKV_API int rkv_summarize(const void* keys, const void* values, int64_t heads, i
                   void* stream);
 
 /*
+ * rkv_summarize fused with the prefill's cache write (replaces the
+ * reference's prefill sequence transformers.py:529-536, which writes the
+ * prompt into the cache and then summarises it from there with
+ * summary.py:46-113): reads the prompt K/V once and writes them, as the
+ * zero-padded page copy, into rows [0, ceil(tokens / block_size) *
+ * block_size) of each head of a cache whose head h starts
+ * h * *_cache_head_stride elements after its base (rows of head_dim
+ * elements, contiguous), plus the summaries.  The cache then holds the
+ * prompt and is the summary's page view.  The head strides must hold the
+ * padded prompt; rows past the prompt are written as zeros.
+ */
+RKV_API int rkv_summarize_into(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                       int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                       int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                       void* key_cache, int64_t key_cache_head_stride, void* value_cache,
+                       int64_t value_cache_head_stride, void* key_mean, void* value_mean,
+                       void* ellipsoid, float* value_norm, float* max_value_norm,
+                       int64_t* counts, void* stream);
+
+/*
  * Workspace bytes for rkv_select with `queries` query instances.
  */
 RKV_API size_t rkv_select_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,

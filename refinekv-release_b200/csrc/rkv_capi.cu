@@ -571,13 +571,20 @@ const char* rkv_status_string(int status) {
   }
 }
 
-int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t tokens,
-                  int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
-                  int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
-                  void* key_pages_out, void* value_pages_out, void* key_mean, void* value_mean,
-                  void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
-                  void* stream) {
-  g_last_error.clear();
+}  // extern "C"
+
+namespace rkv {
+namespace {
+
+// rkv_summarize and rkv_summarize_into: the page copy of head h starts
+// `*_pages_head_stride` elements after head h - 1's (0: packed pages).
+int summarize_impl(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                   int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                   int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                   void* key_pages_out, int64_t key_pages_head_stride, void* value_pages_out,
+                   int64_t value_pages_head_stride, void* key_mean, void* value_mean,
+                   void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
+                   void* stream) {
   if (heads <= 0 || tokens <= 0) return fail(RKV_ERR_INVALID_ARGUMENT, "empty keys/values");
   if (!supported_dim(head_dim)) return fail(RKV_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 in [32, 256]");
   if (!supported_block(block_size)) return fail(RKV_ERR_UNSUPPORTED, "block_size must be 16, 32 or 64");
@@ -640,6 +647,9 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   p.dim = static_cast<int>(head_dim);
   p.key_pages = key_pages_out;
   p.value_pages = value_pages_out;
+  const int64_t packed = blocks * block_size * head_dim;
+  p.key_pages_head_stride = key_pages_head_stride > 0 ? key_pages_head_stride : packed;
+  p.value_pages_head_stride = value_pages_head_stride > 0 ? value_pages_head_stride : packed;
   p.key_mean = key_mean;
   p.value_mean = value_mean;
   p.ellipsoid = ellipsoid;
@@ -649,6 +659,50 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
   err = launch_summarize(maps, p, padded_dim(head_dim), ctas, warps, smem, st);
   if (err != cudaSuccess) return cuda_fail(err, "summarize launch");
   return RKV_OK;
+}
+
+}  // namespace
+}  // namespace rkv
+
+extern "C" {
+
+int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                  int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                  int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                  void* key_pages_out, void* value_pages_out, void* key_mean, void* value_mean,
+                  void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
+                  void* stream) {
+  g_last_error.clear();
+  return summarize_impl(keys, values, heads, tokens, head_dim, key_head_stride,
+                        key_token_stride, value_head_stride, value_token_stride, block_size,
+                        key_pages_out, 0, value_pages_out, 0, key_mean, value_mean, ellipsoid,
+                        value_norm, max_value_norm, counts, stream);
+}
+
+int rkv_summarize_into(const void* keys, const void* values, int64_t heads, int64_t tokens,
+                       int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                       int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                       void* key_cache, int64_t key_cache_head_stride, void* value_cache,
+                       int64_t value_cache_head_stride, void* key_mean, void* value_mean,
+                       void* ellipsoid, float* value_norm, float* max_value_norm,
+                       int64_t* counts, void* stream) {
+  g_last_error.clear();
+  if (key_cache == nullptr || value_cache == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "null cache");
+  }
+  if (block_size > 0 && head_dim > 0 && tokens > 0) {
+    const int64_t rows = cdiv(tokens, block_size) * block_size * head_dim;
+    if (key_cache_head_stride < rows || value_cache_head_stride < rows ||
+        (key_cache_head_stride * 2) % 16 || (value_cache_head_stride * 2) % 16) {
+      return fail(RKV_ERR_INVALID_ARGUMENT,
+                  "cache head strides must hold the padded prompt and be 16-byte multiples");
+    }
+  }
+  return summarize_impl(keys, values, heads, tokens, head_dim, key_head_stride,
+                        key_token_stride, value_head_stride, value_token_stride, block_size,
+                        key_cache, key_cache_head_stride, value_cache, value_cache_head_stride,
+                        key_mean, value_mean, ellipsoid, value_norm, max_value_norm, counts,
+                        stream);
 }
 
 size_t rkv_select_workspace_size(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,

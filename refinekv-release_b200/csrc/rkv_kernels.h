@@ -47,6 +47,8 @@ struct SummarizeParams {
   int stages;         // TMA stages per warp
   void* key_pages;    // optional (heads, blocks, block, dim) copy, zero padded
   void* value_pages;  // optional
+  int64_t key_pages_head_stride;    // elements between heads' page copies
+  int64_t value_pages_head_stride;
   void* key_mean;     // bf16 (heads, blocks, dim)
   void* value_mean;
   void* ellipsoid;

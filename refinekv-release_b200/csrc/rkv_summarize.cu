@@ -212,10 +212,11 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
       if (h == 0) p.counts[b] = count;
     }
     if (p.key_pages != nullptr) {  // zero-padded page copy (rows past the prompt read as 0)
+      const size_t row0 = static_cast<size_t>(b) * R * p.dim;  // page b of head h
       uint4* kdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
-                                             static_cast<size_t>(pg) * R * p.dim);
+                                             h * p.key_pages_head_stride + row0);
       uint4* vdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.value_pages) +
-                                             static_cast<size_t>(pg) * R * p.dim);
+                                             h * p.value_pages_head_stride + row0);
       for (int i = lane; i < R * kChunks; i += 32) {
         const int r = i / kChunks, c = i - r * kChunks;
         kdst[i] = *reinterpret_cast<const uint4*>(kt + swz(r, c, R));

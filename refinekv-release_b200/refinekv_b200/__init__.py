@@ -6,7 +6,8 @@ Public names mirror the reference package ``refinekv`` v0.1.2
 ``AttentionResult``, and the Transformers adapter ``RefineKV`` /
 ``make_visible_static_cache`` (imported lazily, like the reference).
 Beyond the reference: ``build_summary_batch`` (several prompts decoding in
-lockstep, stacked on the head axis), ``attach_page_pool`` (decode from a
+lockstep, stacked on the head axis), ``build_summary_into`` (the prefill's
+cache write and the summary in one pass), ``attach_page_pool`` (decode from a
 vLLM-style K/V page pool through a page table) and ``refinekv_b200.parallel``
 (KV-head sharding and sequence split over GPUs).
 
@@ -24,6 +25,7 @@ __all__ = [
     "RefineKVConfig",
     "build_summary",
     "build_summary_batch",
+    "build_summary_into",
     "attach_page_pool",
     "select_blocks",
     "sparse_attention",
@@ -37,7 +39,8 @@ def __getattr__(name):
         from . import attention
 
         return getattr(attention, name)
-    if name in ("BlockSummary", "build_summary", "build_summary_batch", "attach_page_pool"):
+    if name in ("BlockSummary", "build_summary", "build_summary_batch", "build_summary_into",
+                "attach_page_pool"):
         from . import summary
 
         return getattr(summary, name)

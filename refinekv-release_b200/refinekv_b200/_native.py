@@ -41,6 +41,7 @@ SPLIT_FINAL = 2
 #: Every symbol the header declares.
 EXPORTS = (
     "rkv_summarize",
+    "rkv_summarize_into",
     "rkv_select_workspace_size",
     "rkv_select",
     "rkv_decode_workspace_size",
@@ -96,6 +97,9 @@ _SIGNATURES = {
     "rkv_summarize": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                      c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                                      c_ptr, c_ptr, c_ptr]),
+    "rkv_summarize_into": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                          c_i64, c_i64, c_ptr, c_i64, c_ptr, c_i64, c_ptr, c_ptr,
+                                          c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
     "rkv_select_workspace_size": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64, c_i64]),
     "rkv_select": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64, c_i64,
                                   ctypes.c_float, ctypes.c_int, c_ptr, ctypes.c_int, c_ptr,

@@ -49,7 +49,7 @@ except ImportError as error:  # pragma: no cover - exercised only without transf
 
 from ..attention import select_blocks_union, sparse_attention
 from ..config import RefineKVConfig
-from ..summary import BlockSummary, build_summary, build_summary_batch
+from ..summary import BlockSummary, build_summary, build_summary_batch, build_summary_into
 
 ATTN_IMPLEMENTATION = "refinekv_b200"
 _MISSING = object()
@@ -58,6 +58,24 @@ _MISSING = object()
 # ---------------------------------------------------------------------------
 # caches
 # ---------------------------------------------------------------------------
+
+def _write_prompt(layer, key_states, value_states, end):
+    """A static layer's prefill write, fused with the layer's summary when asked for.
+
+    The session sets ``summary_config`` on the layers it summarises; for one
+    sequence on the GPU whose padded last page fits the capacity, the prompt
+    reaches the cache through ``build_summary_into``, which summarises it in
+    the same pass (``fused_summary``, picked up by the session's prefill).
+    """
+    config = getattr(layer, "summary_config", None)
+    if (config is not None and key_states.shape[0] == 1 and key_states.is_cuda
+            and key_states.dtype == torch.bfloat16
+            and -(-end // config.block_size) * config.block_size <= layer.max_cache_len):
+        layer.fused_summary = build_summary_into(key_states[0], value_states[0], layer.keys[0],
+                                                 layer.values[0], config)
+        return
+    layer.keys[:, :, :end].copy_(key_states)
+    layer.values[:, :, :end].copy_(value_states)
 
 class _VisibleStaticLayer(StaticLayer):
     """Preallocated KV that exposes only the tokens written so far (``:25-62`` of the reference)."""
@@ -83,8 +101,11 @@ class _VisibleStaticLayer(StaticLayer):
         end = self.visible + key_states.shape[-2]
         if end > self.max_cache_len:
             raise ValueError("visible KV cache capacity exceeded")
-        self.keys[:, :, self.visible:end].copy_(key_states)
-        self.values[:, :, self.visible:end].copy_(value_states)
+        if self.visible == 0:  # the prompt
+            _write_prompt(self, key_states, value_states, end)
+        else:
+            self.keys[:, :, self.visible:end].copy_(key_states)
+            self.values[:, :, self.visible:end].copy_(value_states)
         self.visible = end
         return self.keys[:, :, :end], self.values[:, :, :end]
 
@@ -130,8 +151,7 @@ class _GraphStaticLayer(StaticLayer):
             end = key_states.shape[-2]
             if self.visible or end > self.max_cache_len:
                 raise ValueError("the graph cache takes one complete prompt prefill")
-            self.keys[:, :, :end].copy_(key_states)
-            self.values[:, :, :end].copy_(value_states)
+            _write_prompt(self, key_states, value_states, end)
             self.visible = end
             return self.keys[:, :, :end], self.values[:, :, :end]
         self.keys.index_copy_(2, self.cursor.position, key_states)
@@ -536,6 +556,11 @@ class RefineKV:
                                      "left-padded, with a 2-D attention_mask)")
             self._reset_request(cache)
             self._pads = pads
+            for i, layer in enumerate(getattr(cache, "layers", None) or []):
+                if isinstance(layer, (_VisibleStaticLayer, _GraphStaticLayer)):
+                    layer.summary_config = (self.config if i >= self.config.full_attention_layers
+                                            else None)
+                    layer.fused_summary = None
 
     def _after_forward(self, module, args, kwargs, output):
         cache = getattr(output, "past_key_values", None)
@@ -575,7 +600,14 @@ class RefineKV:
         prompt = query.shape[2]
         state = _LayerState(prompt, prompt)
         if index >= self.config.full_attention_layers:
-            state.summary = build_summary(key[0, :, :prompt], value[0, :, :prompt], self.config)
+            layers = getattr(self._cache, "layers", None) or []
+            fused = getattr(layers[index], "fused_summary", None) if index < len(layers) else None
+            if fused is not None:  # summarised while the prompt was written to the cache
+                layers[index].fused_summary = None
+                state.summary = fused
+            else:
+                state.summary = build_summary(key[0, :, :prompt], value[0, :, :prompt],
+                                              self.config)
             count = min(self.config.anchor_tokens, prompt)
             anchors = self._anchor_queries.pop(index, None)
             if count and anchors is None:

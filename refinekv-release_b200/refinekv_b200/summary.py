@@ -307,3 +307,54 @@ def attach_page_pool(summary: BlockSummary, key_pool: torch.Tensor, value_pool: 
                         summary.ellipsoid, summary.value_norm, summary.max_value_norm,
                         summary.prompt_length, summary.block_size, sequences=summary.sequences,
                         prompt_lengths=summary.prompt_lengths, page_table=table)
+
+
+@torch.no_grad()
+def build_summary_into(keys: torch.Tensor, values: torch.Tensor, key_cache: torch.Tensor,
+                       value_cache: torch.Tensor,
+                       config: RefineKVConfig | None = None) -> BlockSummary:
+    """Write a prompt into its KV cache and summarise it in the same pass.
+
+    ``keys``/``values``: the prompt's (kv_heads, tokens, head_dim) bf16 K/V
+    (the attention layer's fresh projections); ``key_cache``/``value_cache``:
+    the (kv_heads, capacity, head_dim) bf16 cache of the same device, rows
+    contiguous, with capacity at least the prompt rounded up to whole
+    pages.  Rows [0, tokens) of the caches receive the prompt, the rest of
+    its last page zeros, and the returned summary's page views alias the
+    caches.  The same summaries as ``build_summary(keys, values)``; the
+    prompt is read once instead of once for the cache write and once more
+    for the summary (the reference's prefill, ``transformers.py:529-536``).
+    """
+    config = config or RefineKVConfig()
+    keys, values = _checked_prompt(keys, values)
+    heads, tokens, dim = keys.shape
+    block = config.block_size
+    blocks = -(-tokens // block)
+    for cache in (key_cache, value_cache):
+        if (cache.ndim != 3 or cache.shape[0] != heads or cache.shape[2] != dim
+                or cache.dtype != torch.bfloat16 or cache.device != keys.device):
+            raise ValueError("caches must be bf16 (kv_heads, capacity, head_dim) on the keys' device")
+        if cache.shape[1] < blocks * block:
+            raise ValueError("cache capacity must hold the prompt rounded up to whole pages")
+        if cache.stride(2) != 1 or cache.stride(1) != dim:
+            raise ValueError("cache rows must be contiguous")
+    dev = keys.device
+    key_mean = torch.empty(heads, blocks, dim, device=dev, dtype=torch.bfloat16)
+    value_mean = torch.empty_like(key_mean)
+    ellipsoid = torch.empty_like(key_mean)
+    value_norm = torch.empty(heads, blocks, device=dev, dtype=torch.float32)
+    max_value_norm = torch.empty(heads, device=dev, dtype=torch.float32)
+    counts = torch.empty(blocks, device=dev, dtype=torch.int64)
+    lib = _native.load()
+    with torch.cuda.device(dev):
+        _native.check(lib.rkv_summarize_into(
+            keys.data_ptr(), values.data_ptr(), heads, tokens, dim,
+            keys.stride(0), keys.stride(1), values.stride(0), values.stride(1), block,
+            key_cache.data_ptr(), key_cache.stride(0), value_cache.data_ptr(),
+            value_cache.stride(0), key_mean.data_ptr(), value_mean.data_ptr(),
+            ellipsoid.data_ptr(), value_norm.data_ptr(), max_value_norm.data_ptr(),
+            counts.data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+    pages = lambda cache: cache.as_strided((heads, blocks, block, dim),  # noqa: E731
+                                           (cache.stride(0), block * dim, dim, 1))
+    return BlockSummary(pages(key_cache), pages(value_cache), counts, key_mean, value_mean,
+                        ellipsoid, value_norm, max_value_norm, tokens, block)

@@ -41,8 +41,9 @@ def _options(length, new_tokens=8):
 
 @pytest.fixture
 def counted(monkeypatch):
-    calls = {"decode": 0, "summaries": 0}
+    calls = {"decode": 0, "summaries": 0, "fused": 0}
     real_decode, real_summary = adapter.sparse_attention, adapter.build_summary
+    real_into = adapter.build_summary_into
 
     def decode(*args, **kwargs):
         calls["decode"] += 1
@@ -52,8 +53,14 @@ def counted(monkeypatch):
         calls["summaries"] += 1
         return real_summary(*args, **kwargs)
 
+    def summary_into(*args, **kwargs):
+        calls["summaries"] += 1
+        calls["fused"] += 1
+        return real_into(*args, **kwargs)
+
     monkeypatch.setattr(adapter, "sparse_attention", decode)
     monkeypatch.setattr(adapter, "build_summary", summary)
+    monkeypatch.setattr(adapter, "build_summary_into", summary_into)
     return calls
 
 
@@ -70,6 +77,24 @@ def test_dynamic_and_static_caches_give_the_same_tokens(family, counted):
         static = model.generate(**opts, cache_implementation="static")
     assert torch.equal(dynamic, static)
     assert counted["decode"] == 12 and counted["summaries"] == 4
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2"])
+def test_static_prefill_summarises_while_writing_the_cache(family, counted):
+    """Static and graph caches take the prompt and its summary in one pass (same tokens)."""
+    model = _model(family)
+    config = RefineKVConfig(eps=0.01, anchor_tokens=4)
+    opts = _options(300, 24)  # capacity 324 holds the prompt's padded last page (320)
+    with RefineKV(model, config):
+        dynamic = model.generate(**opts)
+    assert counted["fused"] == 0 and counted["summaries"] == 2
+    with RefineKV(model, config):
+        static = model.generate(**opts, cache_implementation="static")
+    assert counted["fused"] == 2  # both sparse layers
+    with RefineKV(model, config, cuda_graph=True):
+        graph = model.generate(**opts)
+    assert counted["fused"] == 4
+    assert torch.equal(static, dynamic) and torch.equal(graph, dynamic)
 
 
 @pytest.mark.parametrize("family", ["llama", "qwen2"])

@@ -15,7 +15,8 @@ import torch.nn.functional as F
 
 from helpers import bf16_ulp_diff, checksum, reference_inputs
 from oracle import refinekv_oracle as ora
-from refinekv_b200 import RefineKVConfig, build_summary, select_blocks, sparse_attention, synthetic
+from refinekv_b200 import (RefineKVConfig, build_summary, build_summary_into, select_blocks,
+                           sparse_attention, synthetic)
 from refinekv_b200.attention import device_status, select_blocks_union
 
 pytestmark = pytest.mark.gpu
@@ -89,6 +90,35 @@ def test_summary_aliases_aligned_cache_and_keeps_inputs():
     assert not s2.keys.reshape(2, -1, 128)[:, 67:].any()
     assert torch.equal(cache_k, ck) and torch.equal(cache_v, cv)
     assert_summary_close(s2, ora.build_summary(cache_k[:, :67].cpu(), cache_v[:, :67].cpu(), 32))
+
+
+@pytest.mark.parametrize("tokens", [64, 67, 1000])
+def test_summary_into_cache_equals_build_summary(tokens):
+    """The prefill's cache write fused with the summary: the same summaries, the prompt in the cache."""
+    gen = torch.Generator(device=DEV).manual_seed(23)
+    big_k = torch.randn(2, tokens + 5, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    big_v = torch.randn(2, tokens + 5, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    keys, values = big_k[:, 2:2 + tokens], big_v[:, 2:2 + tokens]  # strided prompt
+    padded = -(-tokens // 32) * 32
+    cache_k = torch.randn(2, padded + 40, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    cache_v = torch.randn(2, padded + 40, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    before_k, before_v = cache_k.clone(), cache_v.clone()
+    fused = build_summary_into(keys, values, cache_k, cache_v)
+    plain = build_summary(keys, values)
+    for name in ("counts", "key_mean", "value_mean", "ellipsoid", "value_norm", "max_value_norm"):
+        assert torch.equal(getattr(fused, name), getattr(plain, name)), name
+    for cache, src, before in ((cache_k, keys, before_k), (cache_v, values, before_v)):
+        assert torch.equal(cache[:, :tokens], src)
+        assert not cache[:, tokens:padded].any()
+        assert torch.equal(cache[:, padded:], before[:, padded:])
+    assert fused.keys.data_ptr() == cache_k.data_ptr()
+    assert torch.equal(fused.keys, plain.keys.contiguous())
+    q = torch.randn(2, 4, 1, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    suffix = torch.randn(2, 3, 128, device=DEV, generator=gen).to(torch.bfloat16)
+    a = sparse_attention(q, fused, suffix, suffix, return_selected=True)
+    b = sparse_attention(q, plain, suffix, suffix, return_selected=True)
+    assert torch.equal(a.selected, b.selected)
+    assert torch.equal(a.output.view(torch.int16), b.output.view(torch.int16))
 
 
 def test_summary_rejects_fp32_cache():
