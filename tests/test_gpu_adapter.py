@@ -3,9 +3,11 @@
 Tiny random-init Llama/Qwen2 models as in the reference (hidden 128, head_dim
 32) and with head_dim 64 (hidden 256, 4 query / 2 KV heads): the CUDA kernels
 cover head dimensions 32-256 in steps of 32.  Checks: dynamic and static caches give the same tokens;
-CUDA-graph decode gives the eager tokens (including a repetition penalty and,
-beyond the reference, dense ``full_attention_layers`` under the graph); the
-decode really runs through librefinekv_b200 (call counts and stats).
+static and graph caches summarise the prompt while writing it (rkv_summarize_into)
+with the same tokens; CUDA-graph decode gives the eager tokens (including a
+repetition penalty and, beyond the reference, dense ``full_attention_layers``
+under the graph); the decode really runs through librefinekv_b200 (call counts
+and stats).
 """
 
 from __future__ import annotations
