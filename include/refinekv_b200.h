@@ -166,7 +166,11 @@ RKV_API int rkv_summarize(const void* keys, const void* values, int64_t heads, i
  * h * *_cache_head_stride elements after its base (rows of head_dim
  * elements, contiguous), plus the summaries.  The cache then holds the
  * prompt and is the summary's page view.  The head strides must hold the
- * padded prompt; rows past the prompt are written as zeros.
+ * padded prompt.  Rows past the prompt in its last page are written as
+ * zeros by this call, but they are cache rows: a decoder that appends its
+ * generated tokens to the cache overwrites them later.  The decode kernels
+ * never read them as prompt rows (each page's valid rows come from its
+ * count), so nothing may rely on them staying zero.
  */
 RKV_API int rkv_summarize_into(const void* keys, const void* values, int64_t heads, int64_t tokens,
                        int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
@@ -243,8 +247,11 @@ RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_
  *   the last call's contents (the status word is cleared at the start of each
  *   call), so calls that can overlap on the GPU race: order them on one
  *   stream.  The first call on each device looks up the array's address, with
- *   that device current; make it before any stream capture.  Allocates
- *   nothing.
+ *   that device current; make it before any stream capture.  The address is
+ *   kept for the life of the process and belongs to the context current at
+ *   that first call: after cudaDeviceReset, or any other teardown of the
+ *   device's primary context, do not call this entry point on that device
+ *   again.  Allocates nothing.
  */
 #define RKV_DECODE_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
 RKV_API int rkv_decode_static(const rkv_summary* summary, const void* query, int query_dtype,
@@ -254,6 +261,17 @@ RKV_API int rkv_decode_static(const rkv_summary* summary, const void* query, int
                               int64_t value_suffix_token_stride, const int32_t* suffix_length,
                               int64_t suffix_length_host, const uint8_t* anchor_mask, float eps,
                               int reduction, void* output, uint8_t* selected, void* stream);
+
+/*
+ * Device status word of the last rkv_decode_static call on the current device
+ * (0, or the RKV_DEVICE_* bits: a bounded wait that ran out, a device-side
+ * input out of range), copied to `out` -- a host or device int32 -- on
+ * `stream`, ordered after the calls already issued on it.  With a host
+ * pointer, read `*out` after synchronising the stream.  Like
+ * rkv_decode_static it allocates nothing and has no counterpart in the
+ * reference.
+ */
+RKV_API int rkv_decode_static_status(int32_t* out, void* stream);
 
 /* Kernel launches one rkv_decode call makes for the given phases. */
 RKV_API int rkv_decode_launch_count(unsigned phases);

@@ -17,7 +17,13 @@
 //   without ordering between them) race and must not be issued;
 // * the array's device address is looked up once per device, on the first
 //   call made with that device current; make that first call before any
-//   stream capture begins.
+//   stream capture begins.  The address belongs to the CUDA context current
+//   at that call: after cudaDeviceReset (or any teardown of the device's
+//   primary context) the cached address is stale, so a process that resets
+//   a device must not call these entry points on it again;
+// * the device status word (timeouts of the kernels' bounded waits, range
+//   errors in device-side inputs) lives in the array too; read it with
+//   rkv_decode_static_status after the call.
 // Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
 #include <cuda_runtime.h>
 
@@ -45,9 +51,14 @@ void* g_scratch_ptr[kMaxDevices] = {};
 int scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  if (err != cudaSuccess) {
     rkv::set_last_error(std::string("cudaGetDevice failed: ") + cudaGetErrorString(err));
     return RKV_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    rkv::set_last_error("device index " + std::to_string(dev) + " is beyond the " +
+                        std::to_string(kMaxDevices) + " devices the static array supports");
+    return RKV_ERR_UNSUPPORTED;
   }
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_scratch_ptr[dev] == nullptr) {
@@ -75,7 +86,10 @@ int rkv_decode_static(const rkv_summary* summary, const void* query, int query_d
                       int64_t value_suffix_token_stride, const int32_t* suffix_length,
                       int64_t suffix_length_host, const uint8_t* anchor_mask, float eps,
                       int reduction, void* output, uint8_t* selected, void* stream) {
-  if (summary == nullptr) return RKV_ERR_INVALID_ARGUMENT;
+  if (summary == nullptr) {
+    rkv::set_last_error("summary is null");
+    return RKV_ERR_INVALID_ARGUMENT;
+  }
   const size_t need = rkv_decode_workspace_size(summary->heads, group, summary->blocks,
                                                 summary->head_dim, summary->block_size);
   if (need == 0) return rkv_decode(summary, query, query_dtype, group, key_suffix, value_suffix,
@@ -105,6 +119,25 @@ int rkv_decode_static(const rkv_summary* summary, const void* query, int query_d
                     value_suffix_head_stride, value_suffix_token_stride, suffix_length,
                     suffix_length_host, anchor_mask, eps, reduction, output, selected, scratch,
                     kStaticScratchBytes, RKV_PHASE_ALL, stream);
+}
+
+int rkv_decode_static_status(int32_t* out, void* stream) {
+  if (out == nullptr) {
+    rkv::set_last_error("out is null");
+    return RKV_ERR_INVALID_ARGUMENT;
+  }
+  void* scratch = nullptr;
+  const int rc = scratch_for_current_device(&scratch);
+  if (rc != RKV_OK) return rc;
+  // Word 0 of the array is the status word of the last rkv_decode_static
+  // call on this device; the copy is ordered after that call on `stream`.
+  const cudaError_t err = cudaMemcpyAsync(out, scratch, sizeof(int32_t), cudaMemcpyDefault,
+                                          static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) {
+    rkv::set_last_error(std::string("cudaMemcpyAsync failed: ") + cudaGetErrorString(err));
+    return RKV_ERR_CUDA;
+  }
+  return RKV_OK;
 }
 
 }  // extern "C"

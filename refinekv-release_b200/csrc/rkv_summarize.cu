@@ -211,7 +211,10 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
       atomicMax(reinterpret_cast<int*>(p.max_value_norm + h), __float_as_int(vnorm));
       if (h == 0) p.counts[b] = count;
     }
-    if (p.key_pages != nullptr) {  // zero-padded page copy (rows past the prompt read as 0)
+    // Zero-padded page copy: the rows past the prompt are written as zeros
+    // here; a decoder may later append generated tokens there, and the
+    // decode kernels mask them out by the page's count, never by their value.
+    if (p.key_pages != nullptr) {
       const size_t row0 = static_cast<size_t>(b) * R * p.dim;  // page b of head h
       uint4* kdst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.key_pages) +
                                              h * p.key_pages_head_stride + row0);

@@ -47,6 +47,7 @@ EXPORTS = (
     "rkv_decode_workspace_size",
     "rkv_decode",
     "rkv_decode_static",
+    "rkv_decode_static_status",
     "rkv_decode_launch_count",
     "rkv_select_split_slab",
     "rkv_select_split",
@@ -113,6 +114,7 @@ _SIGNATURES = {
                                          c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr,
                                          c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
                                          c_ptr]),
+    "rkv_decode_static_status": (ctypes.c_int, [c_ptr, c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
     "rkv_select_split_slab": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64]),
     "rkv_select_split": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64, c_i64,

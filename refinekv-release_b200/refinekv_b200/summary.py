@@ -55,6 +55,13 @@ class BlockSummary:
     page_table: torch.Tensor | None = None
     _abi: object = field(default=None, repr=False, compare=False)
 
+    def __setattr__(self, name, value):
+        # The C view holds raw pointers and sizes of the fields: any change to
+        # a field drops it, and the next abi() call rebuilds it.
+        if name != "_abi":
+            object.__setattr__(self, "_abi", None)
+        object.__setattr__(self, name, value)
+
     @property
     def num_blocks(self) -> int:
         return self.counts.shape[-1]
@@ -67,7 +74,12 @@ class BlockSummary:
         return self.keys.shape[0]
 
     def abi(self) -> _native.Summary:
-        """The ``rkv_summary`` view handed to the C ABI (built once)."""
+        """The ``rkv_summary`` view handed to the C ABI (built once per set of fields).
+
+        Reassigning any field drops the cached view.  Changing a tensor in
+        place (``summary.counts.copy_(...)``) keeps it valid, since the view
+        holds the same storage; swapping the storage (``.set_()``) does not.
+        """
         if self._abi is None:
             self._abi = _native.Summary(
                 key_pages=self.keys.data_ptr(),
@@ -324,6 +336,12 @@ def build_summary_into(keys: torch.Tensor, values: torch.Tensor, key_cache: torc
     caches.  The same summaries as ``build_summary(keys, values)``; the
     prompt is read once instead of once for the cache write and once more
     for the summary (the reference's prefill, ``transformers.py:529-536``).
+
+    The zeroed rows after the prompt are ordinary cache rows: a decoder that
+    appends generated tokens to the same cache writes them there, so the
+    summary's last page may later hold those tokens past the prompt.  The
+    decode kernels take each page's valid rows from ``counts`` and never
+    read those rows as prompt rows; do not rely on them staying zero.
     """
     config = config or RefineKVConfig()
     keys, values = _checked_prompt(keys, values)

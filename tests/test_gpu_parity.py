@@ -118,6 +118,36 @@ def test_summary_into_cache_equals_build_summary(tokens):
     a = sparse_attention(q, fused, suffix, suffix, return_selected=True)
     b = sparse_attention(q, plain, suffix, suffix, return_selected=True)
     assert torch.equal(a.selected, b.selected)
+
+
+@pytest.mark.parametrize("tokens", [1020, 67])
+def test_fused_summary_decodes_after_generated_tokens_fill_the_last_page(tokens):
+    """A decoder appends its tokens to the cache the fused summary aliases: the rows
+    after the prompt in its last page stop being zero, and decode must not notice."""
+    gen = torch.Generator(device=DEV).manual_seed(29)
+    heads, dim, steps = 4, 128, 12
+    keys = torch.randn(heads, tokens, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    values = torch.randn(heads, tokens, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    new_k = torch.randn(heads, steps, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    new_v = torch.randn(heads, steps, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    assert tokens % 32  # the prompt ends inside a page; 1020 + 12 also crosses into the next
+    cache_k = torch.zeros(heads, tokens + steps + 64, dim, device=DEV, dtype=torch.bfloat16)
+    cache_v = torch.zeros_like(cache_k)
+    cfg = RefineKVConfig(eps=0.02)
+    fused = build_summary_into(keys, values, cache_k, cache_v, cfg)
+    plain = build_summary(keys, values, cfg)
+    ws_fused, ws_plain = {}, {}
+    for step in range(steps):
+        cache_k[:, tokens + step] = new_k[:, step]  # the decoder's cache write
+        cache_v[:, tokens + step] = new_v[:, step]
+        q = torch.randn(heads, 4, 1, dim, device=DEV, generator=gen).to(torch.bfloat16)
+        ks, vs = cache_k[:, tokens:tokens + step + 1], cache_v[:, tokens:tokens + step + 1]
+        a = sparse_attention(q, fused, ks, vs, cfg, workspace=ws_fused, return_selected=True)
+        b = sparse_attention(q, plain, new_k[:, :step + 1], new_v[:, :step + 1], cfg,
+                             workspace=ws_plain, return_selected=True)
+        assert torch.equal(a.selected, b.selected), step
+        assert torch.equal(a.output, b.output), step
+    assert device_status(ws_fused) == 0 and device_status(ws_plain) == 0
     assert torch.equal(a.output.view(torch.int16), b.output.view(torch.int16))
 
 

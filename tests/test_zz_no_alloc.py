@@ -24,6 +24,15 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+def _static_status():
+    """The device status word of the last rkv_decode_static call, read without allocating in C."""
+    lib = _native.load()
+    word = torch.full((1,), -1, device=DEV, dtype=torch.int32)
+    _native.check(lib.rkv_decode_static_status(word.data_ptr(),
+                                               torch.cuda.current_stream().cuda_stream))
+    return int(word.item())
+
+
 def _decode_static(q, summary, ks, vs, cfg, out, selected):
     lib = _native.load()
     heads, group, _, dim = q.shape
@@ -52,6 +61,7 @@ def test_static_scratch_matches_workspace_entry_point_twice(qdtype):
         selected = torch.full((heads, summary.num_blocks), 7, device=DEV, dtype=torch.uint8)
         _decode_static(q, summary, ks, vs, cfg, out, selected)
         torch.cuda.synchronize()
+        assert _static_status() == 0  # no bounded wait ran out, no device input out of range
         assert torch.equal(selected.bool(), want.selected)
         tol = dict(atol=1e-4, rtol=0) if qdtype == torch.float32 else dict(atol=4e-3, rtol=2e-2)
         torch.testing.assert_close(out, want.output, **tol)
@@ -75,3 +85,8 @@ def test_static_scratch_rejects_geometry_larger_than_the_array():
                                t.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == _native.RKV_ERR_WORKSPACE
     assert b"static array" in lib.rkv_last_error()
+    rc = lib.rkv_decode_static(None, t.data_ptr(), _native.DTYPE_BF16, group, None, None, 0, 0, 0,
+                               0, 0, None, 0, None, 0.01, 2, t.data_ptr(), t.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream)
+    assert rc == _native.RKV_ERR_INVALID_ARGUMENT
+    assert lib.rkv_last_error() == b"summary is null"
