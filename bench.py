@@ -28,8 +28,10 @@ exchange the selector normalisers and the (max, sum, output) rows of each
 step over NCCL (refinekv_b200.parallel).
 
 --impl reference times the reference algorithm on the host CPU (the oracle
-restatement of the reference PyTorch backend, all host threads), one layer
-per step at the same geometry, scaled to 32 layers.
+restatement of the reference PyTorch backend, all host threads): every step
+runs all 32 layers, unless that would exceed a few minutes of CPU time, in
+which case each step runs a rotating subset of the layers and the line says
+how many.
 """
 
 from __future__ import annotations
@@ -39,7 +41,6 @@ import datetime
 import json
 import os
 import pathlib
-import re
 import statistics
 import sys
 import threading
@@ -92,10 +93,25 @@ def parse_args():
     return args
 
 
+def geometry_name(args):
+    """The model whose attention geometry the arguments describe."""
+    if (args.kv_heads, args.group, args.head_dim) == (4, 7, 128):
+        return "qwen2.5-7b", 28
+    return "llama3.1-8b", 32
+
+
 def workload_config(args, world, plan=None):
+    """The `config` object; identical in both arms for the same arguments."""
+    if plan is None:
+        from refinekv_b200 import parallel
+
+        plan = parallel.plan_shards(args.kv_heads * args.batch, args.tokens, args.block_size,
+                                    world, 0, args.seq_ranks)
+    model, full_layers = geometry_name(args)
+    size = f"{args.tokens // 1024}k" if args.tokens % 1024 == 0 else str(args.tokens)
     return {
-        "workload": ("llama3.1-8b-attention-phase-128k" if args.tokens == 131072 and args.layers == 32
-                     else f"llama3.1-8b-attention-phase-{args.layers}L-{args.tokens}")
+        "workload": (f"{model}-attention-phase-{size}" if args.layers == full_layers
+                     else f"{model}-attention-phase-{args.layers}L-{size}")
                     + ("" if args.query_scale == 1.0 else f"-q{args.query_scale:g}")
                     + ("" if args.batch == 1 else f"-batch{args.batch}"),
         "batch": args.batch,
@@ -109,10 +125,8 @@ def workload_config(args, world, plan=None):
         "gqa_reduction": args.reduction,
         "anchor_tokens": args.anchors,
         "decode_steps": args.warmup + args.steps,
-        "parallelism": (f"kv-head shard x{plan.head_shards}, sequence split x{plan.seq_ranks}"
-                        if plan is not None else f"kv-head shard x{world}"),
+        "parallelism": f"kv-head shard x{plan.head_shards}, sequence split x{plan.seq_ranks}",
         "cache_flush": "none needed: every layer's KV (heads x tokens x 256 B x 2) exceeds L2",
-        "cuda_graph": True,
         "seed": args.seed,
         "query_scale": args.query_scale,
     }
@@ -128,16 +142,13 @@ def measured_hbm_peak():
 
 
 def profiled_traffic(kernel_file: str):
-    """dram bytes per launch and the pages it covered, from a committed ncu summary."""
+    """dram bytes per launch and the pages it covered, from a committed ncu figure (JSON)."""
     path = REPO / "profiles" / kernel_file
-    if not path.exists():
+    try:
+        figures = json.loads(path.read_text())
+        return float(figures["dram_bytes_per_launch"]), float(figures["pages_per_launch"])
+    except (OSError, KeyError, ValueError):
         return None
-    text = path.read_text()
-    b = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
-    u = re.search(r"pages_per_launch:\s*([0-9.eE+]+)", text)
-    if not b or not u:
-        return None
-    return float(b.group(1)), float(u.group(1))
 
 
 # ---------------------------------------------------------------------------
@@ -270,64 +281,109 @@ def sum_over_ranks(value: float, world: int) -> float:
 # ---------------------------------------------------------------------------
 # reference arm: the reference algorithm on the host CPU
 # ---------------------------------------------------------------------------
+REFERENCE_BUDGET_S = 240.0  # timed CPU work of the reference arm, warm-up included
+
+
 def run_reference(args):
+    """The reference algorithm on the host CPU, one decode step = every layer of the step.
+
+    Each layer's prompt K/V comes from the same generator as the B200 arm
+    (drawn on the GPU when there is one, then copied to host memory), is
+    summarised by the CPU oracle (the reference PyTorch backend restated,
+    ``summary.py:46-113``) and gets its 32-anchor union; every step then
+    runs ``reference.py:50-73`` (selection and the mixed softmax) for each
+    layer with that step's query and the suffix so far.  When the requested
+    steps of all layers would exceed REFERENCE_BUDGET_S of timed work, each
+    step runs a rotating subset of the layers and the line says so
+    (``layers_timed_per_step``; ``value`` is then that subset's time scaled
+    to all layers).
+    """
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import refinekv_oracle as ora
     from refinekv_b200 import synthetic
 
+    torch.set_num_threads(max(torch.get_num_threads(), os.cpu_count() or 1))
     cores = torch.get_num_threads()
-    torch.set_num_threads(max(cores, os.cpu_count() or cores))
-    cores = torch.get_num_threads()
-    # Same generator and device as the B200 arm, so both time the same data.
     gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
-    data = synthetic.make_layer(args.seed, 0, args.kv_heads, args.tokens, args.head_dim,
-                                args.block_size, device=gen_dev)
-    summary = ora.build_summary(data.keys, data.values, args.block_size)
-    planted = data.planted_mean
-    anchors = (synthetic.make_queries(args.seed, 0, -1, planted, args.group, args.anchors,
-                                      torch.float32) * args.query_scale).to(torch.bfloat16).cpu()
-    anchor = ora.anchor_union(anchors, summary, args.eps, args.reduction) if args.anchors else None
     cap = args.warmup + args.steps
-    tokens = [synthetic.make_decode_token(args.seed, 0, s, args.kv_heads, args.head_dim,
-                                          args.tokens + s, device=gen_dev) for s in range(cap)]
-    suffix_k = torch.cat([k for k, _ in tokens], 1).cpu()
-    suffix_v = torch.cat([v for _, v in tokens], 1).cpu()
+    H, D, B, G, N = args.kv_heads * args.batch, args.head_dim, args.block_size, args.group, args.tokens
+    layers = []
+    for li in range(args.layers):
+        seqs = []
+        for b in range(args.batch):
+            seed = args.seed + 7919 * b if args.batch > 1 else args.seed
+            data = synthetic.make_layer(seed, li, args.kv_heads, N, D, B, device=gen_dev)
+            seqs.append((seed, data.keys.cpu(), data.values.cpu(), data.planted_mean))
+            del data
+        L = Layer()
+        L.keys = torch.cat([k for _, k, _, _ in seqs])
+        L.values = torch.cat([v for _, _, v, _ in seqs])
+        L.summary = ora.build_summary(L.keys, L.values, B)
+
+        def queries(step, count, seqs=seqs, li=li):
+            return torch.cat([(synthetic.make_queries(seed, li, step, mean, G, count, torch.float32)
+                               * args.query_scale).to(torch.bfloat16).cpu()
+                              for seed, _, _, mean in seqs], dim=1)
+
+        L.anchor = (ora.anchor_union(queries(-1, args.anchors), L.summary, args.eps,
+                                     args.reduction) if args.anchors else None)
+        L.q = [queries(s, 1)[0] for s in range(cap)]
+        toks = [[synthetic.make_decode_token(seed, li, s, args.kv_heads, D, N + s, device=gen_dev)
+                 for seed, _, _, _ in seqs] for s in range(cap)]
+        L.suffix_k = torch.cat([torch.cat([k for k, _ in t]) for t in toks], 1).cpu()
+        L.suffix_v = torch.cat([torch.cat([v for _, v in t]) for t in toks], 1).cpu()
+        layers.append(L)
+
+    def run_layer(L, step):
+        ora.sparse_attention(L.q[step], L.summary, L.suffix_k[:, :step + 1],
+                             L.suffix_v[:, :step + 1], args.eps, args.reduction,
+                             anchor_mask=L.anchor)
+
+    t0 = time.perf_counter()
+    run_layer(layers[0], 0)  # untimed: sizes the sample
+    per_layer_s = time.perf_counter() - t0
+    per_step = len(layers)
+    if cap * len(layers) * per_layer_s > REFERENCE_BUDGET_S:
+        per_step = max(1, min(len(layers), int(REFERENCE_BUDGET_S / (cap * per_layer_s))))
     times = []
     for step in range(cap):
-        q = (synthetic.make_queries(args.seed, 0, step, planted, args.group, 1, torch.float32)[0]
-             * args.query_scale).to(torch.bfloat16).cpu()
-        ks, vs = suffix_k[:, :step + 1], suffix_v[:, :step + 1]
+        chosen = [layers[(step * per_step + j) % len(layers)] for j in range(per_step)]
         t0 = time.perf_counter()
-        ora.sparse_attention(q, summary, ks, vs, args.eps, args.reduction, anchor_mask=anchor)
+        for L in chosen:
+            run_layer(L, step)
         dt = time.perf_counter() - t0
         if step >= args.warmup:
             times.append(dt)
-    per_layer_us = statistics.median(times) * 1e6
-    # The reference decodes one sequence at a time: a batch costs batch x one sequence.
-    value = per_layer_us * args.layers * args.batch
-    sample = (f"1 layer per step ({args.kv_heads} KV heads x {args.tokens} tokens, reference "
-              f"PyTorch algorithm via the CPU oracle), median of {len(times)} steps, "
-              f"x{args.layers} layers" + (f" x{args.batch} sequences" if args.batch > 1 else ""))
+    timed_ms = statistics.median(times) * 1e3
+    value_us = timed_ms * 1e3 * len(layers) / per_step
+    full = per_step == len(layers)
+    sample = (f"every step runs all {len(layers)} layers ({H} KV-head rows x {N} tokens each) "
+              "through the CPU oracle (the reference PyTorch backend restated); median over the "
+              f"{len(times)} timed steps" if full else
+              f"{per_step} of {len(layers)} layers per step (rotating), scaled x{len(layers)}/"
+              f"{per_step}: all layers' {cap} steps would exceed {REFERENCE_BUDGET_S:.0f} s")
     line = {
         "impl": "reference",
         "metric": METRIC,
-        "value": round(value, 1),
+        "value": round(value_us, 1),
         "unit": "us/step",
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(value / 1e3, 3),
+        "ms_per_step": round(timed_ms, 3),
+        "layers_timed_per_step": per_step,
         "higher_is_better": False,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32 math on bf16 data",
         "data": "synthetic",
         "config": workload_config(args, 1),
-        "cpu_baseline": {"value": round(value, 1), "unit": "us/step", "cores": cores,
+        "execution": {"device": "cpu", "threads": cores, "cuda_graph": False},
+        "cpu_baseline": {"value": round(value_us, 1), "unit": "us/step", "cores": cores,
                          "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
+        "e2e": {"value": round(value_us, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -595,7 +651,7 @@ def run_b200(args):
                      + heads_local * nb * (2 if args.anchors else 1))
     step_bytes = args.layers * (summary_bytes + qo_bytes) + (
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
-    traffic = profiled_traffic("attend_llama8b_128k.md")
+    traffic = profiled_traffic("attend_llama8b_128k.json")
     traffic_per_launch = None
     # The committed capture is of 32-token pages of 128 channels; its DRAM
     # bytes scale with the pages a launch reads only for that page shape.
@@ -603,7 +659,8 @@ def run_b200(args):
         dram_bytes, pages_profiled = traffic
         traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
-    step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9
+    step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9  # whole job
+    step_gbs_per_gpu = step_gbs / world
 
     # ---- dense decode attention over the same prompt KV (reference point) --
     # The dense alternative RefineKV competes with: one query token against
@@ -732,28 +789,53 @@ def run_b200(args):
                "eager_path": f"{api}, eager call per layer, same copies and waits"}
 
     # ---- CPU baseline: the reference algorithm on the host (rank 0, N=1) ---
-    cpu = None
+    # A bounded sample: `cpu_samples` (layer, step) pairs spread over the
+    # layers, each one layer's decode step through the CPU oracle (the
+    # reference PyTorch backend restated), timed, median scaled to all
+    # layers.  The same pairs double as a parity record: the GPU's mask and
+    # output for that layer and step (one eager call, untimed) against the
+    # oracle's, masks compared outside the eps margin.
+    cpu = parity = None
     if rank == 0 and world == 1 and args.batch == 1 and not args.skip_cpu:
         from oracle import refinekv_oracle as ora
 
         torch.set_num_threads(os.cpu_count() or 1)
-        L = layers[0]
-        s_cpu = ora.as_cpu_summary(L.summary)
-        anchor = L.anchor.cpu() if L.anchor is not None else None
         times = []
+        parity = {"layer_steps": 0, "mask_mismatch_outside_margin": 0, "margin_blocks": 0,
+                  "max_abs_out_err": 0.0, "tolerance_max_abs": 2e-2,
+                  "judge": "the CPU oracle on the GPU's summary; margin = blocks whose "
+                           "decisive risk lies within 1e-3 (relative) of eps"}
+        check_ws = {}
         for i in range(args.cpu_samples):
+            L = layers[i * args.layers // args.cpu_samples]
             s = args.warmup + i % args.steps
+            s_cpu = ora.as_cpu_summary(L.summary)
+            anchor = L.anchor.cpu() if L.anchor is not None else None
             q = L.q[s].cpu()
             ks, vs = L.suffix_k[:, :s + 1].cpu(), L.suffix_v[:, :s + 1].cpu()
             t0 = time.perf_counter()
-            ora.sparse_attention(q, s_cpu, ks, vs, args.eps, args.reduction, anchor_mask=anchor)
+            want_out, want_mask = ora.sparse_attention(q, s_cpu, ks, vs, args.eps,
+                                                       args.reduction, anchor_mask=anchor)
             times.append(time.perf_counter() - t0)
+            got = sparse_attention(L.q[s], L.summary, L.suffix_k[:, :s + 1],
+                                   L.suffix_v[:, :s + 1], cfg, anchor_mask=L.anchor,
+                                   workspace=check_ws, return_selected=True)
+            margin = ora.margin_blocks(q, s_cpu, args.eps, args.reduction)
+            if anchor is not None:
+                margin &= ~anchor
+            parity["layer_steps"] += 1
+            parity["margin_blocks"] += int(margin.sum())
+            parity["mask_mismatch_outside_margin"] += int(
+                ((got.selected.cpu() != want_mask) & ~margin).sum())
+            parity["max_abs_out_err"] = max(parity["max_abs_out_err"], float(
+                (got.output.float().cpu() - want_out.float()).abs().max()))
+            del s_cpu
         cpu_us = statistics.median(times[1:] or times) * 1e6 * args.layers
         cpu = {"value": round(cpu_us, 1), "unit": "us/step", "cores": torch.get_num_threads(),
                "kind": "port",
-               "sample": f"layer 0, {args.cpu_samples} decode steps of the same workload through "
-                         f"the CPU oracle (reference PyTorch algorithm), median x{args.layers} "
-                         "layers"}
+               "sample": f"{args.cpu_samples} (layer, decode step) pairs spread over the layers, "
+                         "each one layer's step through the CPU oracle (reference PyTorch "
+                         f"algorithm), median x{args.layers} layers"}
 
     if rank == 0:
         line = {
@@ -771,9 +853,13 @@ def run_b200(args):
             "data": "synthetic (seeded: LogNormal-scaled RoPE keys, N(0,1) values, 6 planted "
                     "blocks per layer; stands in for the paper's LongBench prompts)",
             "config": workload_config(args, world, plan),
-            "hbm": {"achieved_gbs": round(step_gbs, 1), "peak_gbs": peak,
-                    "frac": round(step_gbs / peak, 4), "bytes_per_step": int(step_bytes_all),
-                    "note": peak_note},
+            "execution": {"device": "cuda", "cuda_graph": True},
+            "hbm": {"achieved_gbs": round(step_gbs, 1),
+                    "achieved_gbs_per_gpu": round(step_gbs_per_gpu, 1), "peak_gbs": peak,
+                    "frac": round(step_gbs_per_gpu / peak, 4),
+                    "bytes_per_step": int(step_bytes_all),
+                    "note": peak_note + "; frac is per GPU (job bytes / GPUs / step time "
+                                        "/ one GPU's peak)"},
             "roofline": {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
                          "traffic": None if traffic_per_launch is None else int(traffic_per_launch),
@@ -797,6 +883,7 @@ def run_b200(args):
             "e2e": e2e,
             "dense_attention": dense,
             "cpu_baseline": cpu,
+            "parity": parity,
         }
         emit(line)
     if world > 1:

@@ -77,6 +77,21 @@ def _write_prompt(layer, key_states, value_states, end):
     layer.keys[:, :, :end].copy_(key_states)
     layer.values[:, :, :end].copy_(value_states)
 
+def decode_access_counts(selected, counts, groups, query_heads, suffix_tokens):
+    """K/V rows one decode step of a layer reads, the reference's access counter.
+
+    ``integrations/transformers.py:590-594``: every row of a selected block and
+    one representative of every other block, for each of the ``groups`` query
+    rows of a KV head, plus the visible suffix for every one of the
+    ``query_heads``.  ``counts`` (tokens per block) broadcasts against the
+    (kv_heads, blocks) mask ``selected``; a batch's padding blocks (count 0)
+    cost nothing.  Returns a 0-d device tensor (no host sync).
+    """
+    real = counts > 0
+    accessed = ((selected * counts).sum() + (~selected & real).sum()) * groups
+    return accessed + query_heads * suffix_tokens
+
+
 class _VisibleStaticLayer(StaticLayer):
     """Preallocated KV that exposes only the tokens written so far (``:25-62`` of the reference)."""
 
@@ -683,9 +698,9 @@ class RefineKV:
             anchor_mask=state.anchor_mask, workspace=state.workspace,
             return_selected=self.config.collect_stats)
         if self.config.collect_stats:
-            selected = result.selected
-            accessed = ((selected * state.summary.counts).sum() + (~selected).sum()) * groups
-            accessed = accessed + query.shape[1] * (state.visible_length - state.prompt_length)
+            accessed = decode_access_counts(result.selected, state.summary.counts, groups,
+                                            query.shape[1],
+                                            state.visible_length - state.prompt_length)
             self._record(accessed, query.shape[1] * state.visible_length)
         return result.output.reshape(query.shape[1], 1, dim).transpose(0, 1).unsqueeze(0), None
 
@@ -732,10 +747,10 @@ class RefineKV:
             anchor_mask=state.anchor_mask, workspace=state.workspace,
             return_selected=self.config.collect_stats)
         if self.config.collect_stats:
-            selected = result.selected
             counts = state.summary.counts.repeat_interleave(heads, 0)  # per row, 0 past a prompt
-            accessed = ((selected * counts).sum() + (~selected & (counts > 0)).sum()) * groups
-            accessed = accessed + query.shape[1] * rows * (state.visible_length - state.prompt_length)
+            accessed = decode_access_counts(result.selected, counts, groups,
+                                            query.shape[1] * rows,
+                                            state.visible_length - state.prompt_length)
             self._record(accessed, dense)
         return result.output.reshape(rows, query.shape[1], 1, dim).transpose(1, 2), None
 

@@ -1,0 +1,161 @@
+"""Parity at the full sizes of the benchmark configurations (needs a B200).
+
+Config 1 of the benchmark: 32 independent layers of Llama-3.1-8B attention
+geometry (8 KV heads, group 4, head_dim 128) over a 32768-token bf16 prompt
+each, block_size 32, eps 0.01, GQA "any", 32 prompt anchors, 128 decode steps
+(one fresh K/V token per step), seed 0, the synthetic generator of
+``refinekv_b200.synthetic``.  Every layer decodes all 128 steps through the
+CUDA path; at steps 0, 1, 63 and 127 of every layer the step is judged
+against the CPU oracle (a restatement of the reference PyTorch backend
+pinned to the reference's own outputs):
+
+* summaries: counts exact, bf16 means / ellipsoid within 2 bf16 ulp on under
+  2 % of elements, norms within 2e-6 relative, against the oracle's own
+  summary of the same K/V;
+* masks: equal to the oracle's outside the eps margin (blocks whose decisive
+  risk lies within 1e-3 relative of eps), with the oracle deciding from the
+  GPU's summary; margin blocks are counted and reported;
+* access counters (the adapter's ``decode_access_counts``, the reference's
+  ``transformers.py:590-594``): equal to the oracle's once margin blocks
+  take the oracle's decision; the raw difference is reported;
+* outputs: within 2e-2 max-abs of the oracle's mixed softmax (bf16 queries),
+  also against the oracle's end-to-end result from its own summary.
+
+Half the layers decode with the suffix length read from device memory (the
+CUDA-graph path), half with the host length.  With ``RKV_PARITY_REPORT`` set,
+the counts are written there as JSON.
+"""
+
+import json
+import os
+
+import pytest
+import torch
+
+from helpers import bf16_ulp_diff
+from oracle import refinekv_oracle as ora
+from refinekv_b200 import RefineKVConfig, build_summary, sparse_attention, synthetic
+from refinekv_b200.attention import device_status, select_blocks_union
+from refinekv_b200.integrations.transformers import decode_access_counts
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+CONFIG1 = dict(layers=32, tokens=32768, heads=8, group=4, dim=128, block=32, eps=0.01,
+               reduction="any", anchors=32, steps=128, seed=0)
+CHECK_STEPS = (0, 1, 63, 127)
+
+
+def _report(name, payload):
+    path = os.environ.get("RKV_PARITY_REPORT")
+    print(name, json.dumps(payload))
+    if path:
+        try:
+            existing = json.loads(open(path).read())
+        except (OSError, ValueError):
+            existing = {}
+        existing[name] = payload
+        with open(path, "w") as f:
+            json.dump(existing, f, indent=1)
+
+
+def _summary_ulps(gpu, want):
+    worst = {}
+    assert torch.equal(gpu.counts.cpu(), want.counts)
+    for name in ("key_mean", "value_mean", "ellipsoid"):
+        ulp = bf16_ulp_diff(getattr(gpu, name).cpu(), getattr(want, name))
+        worst[name] = (int(ulp.max()), float((ulp > 0).float().mean()))
+        assert worst[name][0] <= 2 and worst[name][1] < 0.02, (name, worst[name])
+    torch.testing.assert_close(gpu.value_norm.cpu(), want.value_norm, rtol=2e-6, atol=1e-6)
+    torch.testing.assert_close(gpu.max_value_norm.cpu(), want.max_value_norm, rtol=2e-6,
+                               atol=1e-6)
+    return worst
+
+
+def test_config1_32_layers_32k_128_steps_layer_by_layer():
+    c = CONFIG1
+    H, G, D, N, B, S = c["heads"], c["group"], c["dim"], c["tokens"], c["block"], c["steps"]
+    cfg = RefineKVConfig(block_size=B, eps=c["eps"], gqa_reduction=c["reduction"],
+                         anchor_tokens=c["anchors"])
+    totals = dict(layer_steps=0, margin_blocks=0, mask_mismatch_outside_margin=0,
+                  mask_mismatch_vs_own_summary=0, counter_diff_raw=0, max_abs_out_err=0.0,
+                  max_abs_out_err_vs_own_summary=0.0, selected_fraction_sum=0.0,
+                  summary_ulp_max=0, summary_ulp_frac_max=0.0)
+    for li in range(c["layers"]):
+        data = synthetic.make_layer(c["seed"], li, H, N, D, B, device=DEV)
+        s = build_summary(data.keys, data.values, cfg)
+        anchor_q = synthetic.make_queries(c["seed"], li, -1, data.planted_mean, G, c["anchors"])
+        anchor = select_blocks_union(anchor_q, s, cfg)
+        suffix_k = torch.zeros(H, S, D, device=DEV, dtype=torch.bfloat16)
+        suffix_v = torch.zeros_like(suffix_k)
+        length = torch.zeros((), device=DEV, dtype=torch.int32)
+        device_length = li % 2 == 1
+        ws = {}
+        checks = []
+        for step in range(S):
+            k, v = synthetic.make_decode_token(c["seed"], li, step, H, D, N + step, device=DEV)
+            suffix_k[:, step:step + 1] = k
+            suffix_v[:, step:step + 1] = v
+            q = synthetic.make_queries(c["seed"], li, step, data.planted_mean, G, 1)[0]
+            if device_length:
+                length.fill_(step + 1)
+                res = sparse_attention(q, s, suffix_k, suffix_v, cfg, anchor_mask=anchor,
+                                       workspace=ws, return_selected=True, suffix_length=length)
+            else:
+                res = sparse_attention(q, s, suffix_k[:, :step + 1], suffix_v[:, :step + 1], cfg,
+                                       anchor_mask=anchor, workspace=ws, return_selected=True)
+            if step in CHECK_STEPS:
+                checks.append((step, q.cpu(), res.selected.cpu(), res.output.float().cpu(),
+                               int(decode_access_counts(res.selected, s.counts, G, H * G,
+                                                        step + 1))))
+        assert device_status(ws) == 0
+        # ---- the oracle, on the CPU ------------------------------------------
+        keys, values = data.keys.cpu(), data.values.cpu()
+        own = ora.build_summary(keys, values, B)
+        worst = _summary_ulps(s, own)
+        totals["summary_ulp_max"] = max(totals["summary_ulp_max"],
+                                        max(w[0] for w in worst.values()))
+        totals["summary_ulp_frac_max"] = max(totals["summary_ulp_frac_max"],
+                                             max(w[1] for w in worst.values()))
+        s_gpu = ora.as_cpu_summary(s)
+        anchor_cpu = anchor.cpu()
+        a_margin = torch.zeros_like(anchor_cpu)
+        for a in anchor_q.cpu():
+            a_margin |= ora.margin_blocks(a, s_gpu, cfg.eps, cfg.gqa_reduction)
+        want_anchor = ora.anchor_union(anchor_q.cpu(), s_gpu, cfg.eps, cfg.gqa_reduction)
+        assert not ((anchor_cpu != want_anchor) & ~a_margin).any(), f"layer {li} anchors"
+        own_anchor = ora.anchor_union(anchor_q.cpu(), own, cfg.eps, cfg.gqa_reduction)
+        for step, q, got_mask, got_out, got_access in checks:
+            ks, vs = suffix_k[:, :step + 1].cpu(), suffix_v[:, :step + 1].cpu()
+            want, z = ora.select_blocks(q, s_gpu, cfg.eps, cfg.gqa_reduction)
+            margin = ora.margin_blocks(q, s_gpu, cfg.eps, cfg.gqa_reduction) & ~anchor_cpu
+            want = want | anchor_cpu
+            diff = (got_mask != want) & ~margin
+            assert not diff.any(), f"layer {li} step {step}: {int(diff.sum())} blocks"
+            # counters: exact once the margin blocks take the oracle's decision
+            settled = torch.where(margin, want, got_mask)
+            acc_settled = int(decode_access_counts(settled, s_gpu.counts, G, H * G, step + 1))
+            acc_want, dense = ora.access_counters(want, s_gpu.counts, G, H * G, step + 1, N)
+            assert acc_settled == acc_want, (li, step, acc_settled, acc_want)
+            assert dense == H * G * (N + step + 1)
+            # outputs against the oracle's softmax for the GPU's mask
+            ref = ora.mixed_attention(q, s_gpu, ks, vs, got_mask, z)
+            err = float((got_out - ref).abs().max())
+            assert err <= 2e-2, (li, step, err)
+            # end to end against the oracle's own summary and decisions
+            own_out, own_mask = ora.sparse_attention(q, own, ks, vs, cfg.eps, cfg.gqa_reduction,
+                                                     anchor_mask=own_anchor)
+            err_own = float((got_out - own_out.float()).abs().max())
+            assert err_own <= 2e-2, (li, step, err_own)
+            totals["layer_steps"] += 1
+            totals["margin_blocks"] += int(margin.sum())
+            totals["mask_mismatch_outside_margin"] += int(diff.sum())
+            totals["mask_mismatch_vs_own_summary"] += int((got_mask != own_mask).sum())
+            totals["counter_diff_raw"] += abs(got_access - acc_want)
+            totals["max_abs_out_err"] = max(totals["max_abs_out_err"], err)
+            totals["max_abs_out_err_vs_own_summary"] = max(
+                totals["max_abs_out_err_vs_own_summary"], err_own)
+            totals["selected_fraction_sum"] += float(got_mask.float().mean())
+        del data, keys, values, own, s_gpu
+    totals["selected_fraction"] = totals.pop("selected_fraction_sum") / totals["layer_steps"]
+    _report("config1", dict(config=c, check_steps=list(CHECK_STEPS), **totals))
