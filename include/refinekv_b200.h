@@ -12,7 +12,8 @@
  * given stream (no host synchronisation), so every call can be captured in a
  * CUDA graph.
  *
- * Data types: K/V caches, pages and summaries are bf16; queries are bf16 or
+ * Data types: K/V pages and summaries are bf16 (an fp32 K/V cache is
+ * summarised by rkv_summarize_f32 into bf16 pages); queries are bf16 or
  * fp32 (rounded to bf16 before use, as the reference does); outputs are in
  * the query dtype.  Head dimensions: multiples of 32 up to 256; block sizes 16,
  * 32 and 64; GQA groups of 1..16 query rows per KV head.
@@ -155,6 +156,26 @@ RKV_API int rkv_summarize(const void* keys, const void* values, int64_t heads, i
                   void* key_pages_out, void* value_pages_out, void* key_mean, void* value_mean,
                   void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
                   void* stream);
+
+/*
+ * rkv_summarize for an fp32 K/V cache (the reference's build_summary takes any
+ * floating cache, summary.py:46-60; config 0 of its benchmarks is fp32).
+ *   keys / values: (heads, tokens, head_dim) fp32, element strides given,
+ *     innermost stride 1, 16-byte aligned rows.  The summaries are computed
+ *     from the fp32 values, exactly as rkv_summarize does from bf16 ones.
+ *   key_pages_out / value_pages_out: required (heads, blocks, block_size,
+ *     head_dim) bf16 destinations for the zero-padded page copy rounded to
+ *     bf16 -- the values the reference's attention uses, since it rounds the
+ *     prompt K/V to bf16 before use (reference.py:57, :63-66).  The summary
+ *     handed to rkv_select / rkv_decode points at these bf16 pages.
+ */
+RKV_API int rkv_summarize_f32(const float* keys, const float* values, int64_t heads,
+                              int64_t tokens, int64_t head_dim, int64_t key_head_stride,
+                              int64_t key_token_stride, int64_t value_head_stride,
+                              int64_t value_token_stride, int64_t block_size, void* key_pages_out,
+                              void* value_pages_out, void* key_mean, void* value_mean,
+                              void* ellipsoid, float* value_norm, float* max_value_norm,
+                              int64_t* counts, void* stream);
 
 /*
  * rkv_summarize fused with the prefill's cache write (replaces the

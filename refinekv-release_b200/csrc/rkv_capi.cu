@@ -277,13 +277,16 @@ EncodeTiled encoder() {
   return fn;
 }
 
-// 3-D bf16 map (dim, rows, heads) read in [box_rows x 64] boxes, 128B swizzle.
+// 3-D map (dim, rows, heads) of bf16 (elem_bytes 2) or fp32 (4) elements read
+// in [box_rows x 128 bytes] boxes (64 bf16 or 32 fp32 columns), 128B swizzle.
 int rows_map(CUtensorMap* map, const void* base, int64_t dim, int64_t rows, int64_t heads,
-             int64_t row_stride, int64_t head_stride, int box_rows, const char* what) {
+             int64_t row_stride, int64_t head_stride, int box_rows, const char* what,
+             int elem_bytes = 2) {
   EncodeTiled encode = encoder();
   if (encode == nullptr) return fail(RKV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  if (!aligned16(base) || (row_stride * 2) % 16 != 0 ||
-      (heads > 1 && (head_stride * 2) % 16 != 0)) {
+  const int64_t w = elem_bytes;
+  if (!aligned16(base) || (row_stride * w) % 16 != 0 ||
+      (heads > 1 && (head_stride * w) % 16 != 0)) {
     return fail(RKV_ERR_ALIGNMENT, std::string(what) + ": base and strides must be 16-byte aligned");
   }
   if (heads > 1 && head_stride <= 0) {
@@ -291,12 +294,14 @@ int rows_map(CUtensorMap* map, const void* base, int64_t dim, int64_t rows, int6
   }
   cuuint64_t gdim[3] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(heads)};
-  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(row_stride * 2),
-                           static_cast<cuuint64_t>(heads > 1 ? head_stride * 2
-                                                             : rows * row_stride * 2)};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(row_stride * w),
+                           static_cast<cuuint64_t>(heads > 1 ? head_stride * w
+                                                             : rows * row_stride * w)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / w), static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estride[3] = {1, 1, 1};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim,
+  const CUresult r = encode(map,
+                            w == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                            3, const_cast<void*>(base), gdim,
                             gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -578,7 +583,7 @@ namespace {
 
 // rkv_summarize and rkv_summarize_into: the page copy of head h starts
 // `*_pages_head_stride` elements after head h - 1's (0: packed pages).
-int summarize_impl(const void* keys, const void* values, int64_t heads, int64_t tokens,
+int summarize_impl(const void* keys, const void* values, bool f32, int64_t heads, int64_t tokens,
                    int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
                    int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
                    void* key_pages_out, int64_t key_pages_head_stride, void* value_pages_out,
@@ -595,9 +600,13 @@ int summarize_impl(const void* keys, const void* values, int64_t heads, int64_t 
   if ((key_pages_out == nullptr) != (value_pages_out == nullptr)) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "pass both page copies or neither");
   }
-  if (!aligned16(keys) || !aligned16(values) || (key_token_stride * 2) % 16 ||
-      (value_token_stride * 2) % 16 || (key_head_stride * 2) % 16 ||
-      (value_head_stride * 2) % 16) {
+  if (f32 && key_pages_out == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "an fp32 cache needs the bf16 page copies");
+  }
+  const int64_t w = f32 ? 4 : 2;
+  if (!aligned16(keys) || !aligned16(values) || (key_token_stride * w) % 16 ||
+      (value_token_stride * w) % 16 || (key_head_stride * w) % 16 ||
+      (value_head_stride * w) % 16) {
     return fail(RKV_ERR_ALIGNMENT, "keys/values rows must be 16-byte aligned");
   }
   if ((key_pages_out && !aligned16(key_pages_out)) || (value_pages_out && !aligned16(value_pages_out)) ||
@@ -612,23 +621,24 @@ int summarize_impl(const void* keys, const void* values, int64_t heads, int64_t 
   if (rc != RKV_OK) return rc;
   SummarizeMaps maps;
   rc = rows_map(&maps.keys, keys, head_dim, tokens, heads, key_token_stride, key_head_stride,
-                static_cast<int>(block_size), "keys");
+                static_cast<int>(block_size), "keys", static_cast<int>(w));
   if (rc != RKV_OK) return rc;
   rc = rows_map(&maps.values, values, head_dim, tokens, heads, value_token_stride,
-                value_head_stride, static_cast<int>(block_size), "values");
+                value_head_stride, static_cast<int>(block_size), "values", static_cast<int>(w));
   if (rc != RKV_OK) return rc;
   // Persistent grid: one CTA per SM with about 192 KB of TMA ring per CTA,
   // as many warps as fit (3..12) with one or more stages each.  The pages
   // cost ~2K instructions each, so the kernel is bound by instruction
   // latency: 12 warps at 128 dims measured 182 us per 128K-token layer of 8
-  // heads against 208 us for 8 warps (and 199 us for 13).
-  const int64_t stage = 2 * block_size * padded_dim(head_dim) * 2;
+  // heads against 208 us for 8 warps (and 199 us for 13).  (fp32 caches
+  // have twice the stage bytes, so fewer warps; that path is not tuned.)
+  const int64_t stage = 2 * block_size * padded_dim(head_dim) * w;
   const int64_t ring = 192 * 1024;
-  const int warps = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(12, ring / stage)));
+  const int warps = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(12, ring / stage)));
   const int stages =
       static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, ring / (warps * stage))));
   const size_t smem = summarize_smem_bytes(padded_dim(head_dim), static_cast<int>(block_size),
-                                           warps, stages);
+                                           warps, stages, static_cast<int>(w));
   if (smem > static_cast<size_t>(dev.smem_optin)) {
     return fail(RKV_ERR_UNSUPPORTED, "summarizer stages do not fit in shared memory");
   }
@@ -643,6 +653,7 @@ int summarize_impl(const void* keys, const void* values, int64_t heads, int64_t 
   p.tokens = static_cast<int>(tokens);
   p.block_size = static_cast<int>(block_size);
   p.blocks = static_cast<int>(blocks);
+  p.f32 = f32 ? 1 : 0;
   p.stages = stages;
   p.dim = static_cast<int>(head_dim);
   p.key_pages = key_pages_out;
@@ -673,7 +684,20 @@ int rkv_summarize(const void* keys, const void* values, int64_t heads, int64_t t
                   void* ellipsoid, float* value_norm, float* max_value_norm, int64_t* counts,
                   void* stream) {
   g_last_error.clear();
-  return summarize_impl(keys, values, heads, tokens, head_dim, key_head_stride,
+  return summarize_impl(keys, values, false, heads, tokens, head_dim, key_head_stride,
+                        key_token_stride, value_head_stride, value_token_stride, block_size,
+                        key_pages_out, 0, value_pages_out, 0, key_mean, value_mean, ellipsoid,
+                        value_norm, max_value_norm, counts, stream);
+}
+
+int rkv_summarize_f32(const float* keys, const float* values, int64_t heads, int64_t tokens,
+                      int64_t head_dim, int64_t key_head_stride, int64_t key_token_stride,
+                      int64_t value_head_stride, int64_t value_token_stride, int64_t block_size,
+                      void* key_pages_out, void* value_pages_out, void* key_mean,
+                      void* value_mean, void* ellipsoid, float* value_norm,
+                      float* max_value_norm, int64_t* counts, void* stream) {
+  g_last_error.clear();
+  return summarize_impl(keys, values, true, heads, tokens, head_dim, key_head_stride,
                         key_token_stride, value_head_stride, value_token_stride, block_size,
                         key_pages_out, 0, value_pages_out, 0, key_mean, value_mean, ellipsoid,
                         value_norm, max_value_norm, counts, stream);
@@ -698,7 +722,7 @@ int rkv_summarize_into(const void* keys, const void* values, int64_t heads, int6
                   "cache head strides must hold the padded prompt and be 16-byte multiples");
     }
   }
-  return summarize_impl(keys, values, heads, tokens, head_dim, key_head_stride,
+  return summarize_impl(keys, values, false, heads, tokens, head_dim, key_head_stride,
                         key_token_stride, value_head_stride, value_token_stride, block_size,
                         key_cache, key_cache_head_stride, value_cache, value_cache_head_stride,
                         key_mean, value_mean, ellipsoid, value_norm, max_value_norm, counts,

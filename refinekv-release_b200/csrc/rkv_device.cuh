@@ -201,6 +201,20 @@ __device__ __forceinline__ void tma_tile_hint(void* dst, const CUtensorMap* map,
   }
 }
 
+// Same for a tile of `W`-byte-wide elements: W == 2 is tma_tile_hint, W == 4
+// (fp32) loads D / 32 boxes of [rows x 32] (128-byte rows, the same
+// swizzled layout; box i lands at dst + i * rows * 128).
+template <int D, int W>
+__device__ __forceinline__ void tma_tile_hint_w(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                int row, int head, int rows, uint64_t policy) {
+  constexpr int kBoxCols = 128 / W;
+#pragma unroll
+  for (int i = 0; i < D / kBoxCols; ++i) {
+    tma_load_3d_hint(static_cast<char*>(dst) + i * rows * 128, map, bar, i * kBoxCols, row, head,
+                     policy);
+  }
+}
+
 // Byte offset of the 16-byte chunk `c16` (= column / 8) of row `r` inside a
 // swizzled tile of `rows` rows.
 __device__ __forceinline__ uint32_t swz(int r, int c16, int rows) {

@@ -37,12 +37,13 @@ struct SeqLayout {
 };
 
 struct SummarizeMaps {
-  CUtensorMap keys;    // (dim, tokens, heads) bf16, [block_size x 64] boxes, 128B swizzle
+  CUtensorMap keys;    // (dim, tokens, heads), [block_size x 128 bytes] boxes, 128B swizzle
   CUtensorMap values;
 };
 
 struct SummarizeParams {
   int heads, tokens, blocks, block_size;
+  int f32;            // the caches are fp32 (else bf16); pages are copied out as bf16
   int dim;            // real head dim (the kernel's D is dim rounded up to 64)
   int stages;         // TMA stages per warp
   void* key_pages;    // optional (heads, blocks, block, dim) copy, zero padded
@@ -208,7 +209,7 @@ cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, boo
 cudaError_t ensure_smem_limit(const void* func, size_t bytes);
 
 // Shared-memory footprint of each kernel for a given stage count.
-size_t summarize_smem_bytes(int dim, int block, int warps, int stages);
+size_t summarize_smem_bytes(int dim, int block, int warps, int stages, int elem_bytes);
 size_t stats_smem_bytes(int dim, int warps, int stages, int group);
 size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per_cta);
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,

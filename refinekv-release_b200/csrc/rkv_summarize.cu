@@ -14,6 +14,12 @@
 //     zero-padded page copy, counts and the per-head maximum value norm.
 // Statistics over rows are reduced in a different order than the reference's
 // torch reductions (FP32); the bf16 outputs agree to an ulp.
+//
+// K/V caches may be bf16 or fp32 (the reference's build_summary takes any
+// floating cache, summary.py:46-60).  An fp32 cache is summarised from its
+// fp32 values, and its pages are always copied out rounded to bf16: the
+// reference's attention rounds the prompt K/V to bf16 before use
+// (reference.py:57, :63-66), so the decode kernels read the same values.
 #include "rkv_device.cuh"
 #include "rkv_kernels.h"
 
@@ -38,18 +44,51 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
+// Eight consecutive channels (8 * v .. 8 * v + 7) of row r of a swizzled
+// tile: one 16-byte chunk of bf16, two of fp32.
+template <typename T>
+__device__ __forceinline__ void load8(const uint8_t* tile, int r, int v, int rows, float (&f)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const uint8_t* tile, int r, int v, int rows,
+                                                     float (&f)[8]) {
+  unpack8(*reinterpret_cast<const uint4*>(tile + swz(r, v, rows)), f);
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const uint8_t* tile, int r, int v, int rows,
+                                             float (&f)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(tile + swz(r, 2 * v, rows));
+  const float4 b = *reinterpret_cast<const float4*>(tile + swz(r, 2 * v + 1, rows));
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
+// The same eight channels as a bf16 page-copy chunk (bf16: the stored bits).
+template <typename T>
+__device__ __forceinline__ uint4 page_chunk(const uint8_t* tile, int r, int v, int rows) {
+  if constexpr (sizeof(T) == 2) {
+    return *reinterpret_cast<const uint4*>(tile + swz(r, v, rows));
+  } else {
+    float f[8];
+    load8<T>(tile, r, v, rows, f);
+    return pack8(f);
+  }
+}
+
 // max/min that keep a NaN once seen, like torch.amax / torch.maximum.
 __device__ __forceinline__ float nan_max(float a, float b) { return (b > a || b != b) ? b : a; }
 __device__ __forceinline__ float nan_min(float a, float b) { return (b < a || b != b) ? b : a; }
 
 // D: the tile width (the real head dim p.dim rounded up to 64; TMA fills the
-// padding columns with zeros and nothing reads them).
-template <int D, int R>
+// padding columns with zeros and nothing reads them).  T: the cache's element
+// type (bf16 or fp32); each lane of the per-channel pass owns 8 channels.
+template <int D, int R, typename T>
 __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant__ SummarizeMaps maps,
                                                            const SummarizeParams p) {
-  constexpr int kTile = R * D * 2;
+  constexpr int kTile = R * D * static_cast<int>(sizeof(T));
   constexpr int kStage = 2 * kTile;
-  const int kChunks = p.dim / 8;                              // real 16-byte chunks per row
+  const int kChunks = p.dim / 8;                              // real 8-channel chunks per row
   const int kLpc = 32 % kChunks == 0 ? 32 / kChunks : 1;      // lanes per chunk (row interleave)
   const int kActive = kChunks * kLpc;                         // lanes of the per-chunk pass
   extern __shared__ uint8_t smem_raw[];
@@ -89,8 +128,9 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
     const int s = j % S;
     uint8_t* dst = ring + static_cast<size_t>(warp * S + s) * kStage;
     mbar_expect_tx(&bars[warp * S + s], kStage);
-    tma_tile_hint<D>(dst, &maps.keys, &bars[warp * S + s], b * R, h, R, policy);
-    tma_tile_hint<D>(dst + kTile, &maps.values, &bars[warp * S + s], b * R, h, R, policy);
+    tma_tile_hint_w<D, sizeof(T)>(dst, &maps.keys, &bars[warp * S + s], b * R, h, R, policy);
+    tma_tile_hint_w<D, sizeof(T)>(dst + kTile, &maps.values, &bars[warp * S + s], b * R, h, R,
+                                  policy);
   };
   const int first = min(S, mine);
   if (lane == 0) {
@@ -125,8 +165,8 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
     if (lane < kActive) {
       for (int r = lane / kChunks; r < count; r += kLpc) {
         float kf[8], vf[8];
-        unpack8(*reinterpret_cast<const uint4*>(kt + swz(r, c16, R)), kf);
-        unpack8(*reinterpret_cast<const uint4*>(vt + swz(r, c16, R)), vf);
+        load8<T>(kt, r, c16, R, kf);
+        load8<T>(vt, r, c16, R, vf);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           ksum[i] += kf[i];
@@ -172,8 +212,8 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
 #pragma unroll 4
       for (int c = 0; c < kChunks; ++c) {
         float kf[8], vf[8];
-        unpack8(*reinterpret_cast<const uint4*>(kt + swz(r, c, R)), kf);
-        unpack8(*reinterpret_cast<const uint4*>(vt + swz(r, c, R)), vf);
+        load8<T>(kt, r, c, R, kf);
+        load8<T>(vt, r, c, R, vf);
         const float4 m0 = *reinterpret_cast<const float4*>(kmean_s + c * 8);
         const float4 m1 = *reinterpret_cast<const float4*>(kmean_s + c * 8 + 4);
         const float4 s0 = *reinterpret_cast<const float4*>(rscale_s + c * 8);
@@ -222,8 +262,8 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
                                              h * p.value_pages_head_stride + row0);
       for (int i = lane; i < R * kChunks; i += 32) {
         const int r = i / kChunks, c = i - r * kChunks;
-        kdst[i] = *reinterpret_cast<const uint4*>(kt + swz(r, c, R));
-        vdst[i] = *reinterpret_cast<const uint4*>(vt + swz(r, c, R));
+        kdst[i] = page_chunk<T>(kt, r, c, R);
+        vdst[i] = page_chunk<T>(vt, r, c, R);
       }
     }
     __syncwarp();
@@ -237,10 +277,10 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
   }
 }
 
-template <int D, int R>
+template <int D, int R, typename T>
 cudaError_t launch_t(const SummarizeMaps& maps, const SummarizeParams& p, int ctas, int warps,
                      size_t smem, cudaStream_t stream) {
-  const void* kernel = reinterpret_cast<const void*>(summarize_kernel<D, R>);
+  const void* kernel = reinterpret_cast<const void*>(summarize_kernel<D, R, T>);
   cudaError_t err = ensure_smem_limit(kernel, smem);
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
@@ -253,24 +293,31 @@ cudaError_t launch_t(const SummarizeMaps& maps, const SummarizeParams& p, int ct
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, summarize_kernel<D, R>, maps, p);
+  return cudaLaunchKernelEx(&cfg, summarize_kernel<D, R, T>, maps, p);
+}
+
+template <int D, typename T>
+cudaError_t launch_r(const SummarizeMaps& maps, const SummarizeParams& p, int ctas, int warps,
+                     size_t smem, cudaStream_t stream) {
+  switch (p.block_size) {
+    case 16: return launch_t<D, 16, T>(maps, p, ctas, warps, smem, stream);
+    case 32: return launch_t<D, 32, T>(maps, p, ctas, warps, smem, stream);
+    case 64: return launch_t<D, 64, T>(maps, p, ctas, warps, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <int D>
 cudaError_t launch_d(const SummarizeMaps& maps, const SummarizeParams& p, int ctas, int warps,
                      size_t smem, cudaStream_t stream) {
-  switch (p.block_size) {
-    case 16: return launch_t<D, 16>(maps, p, ctas, warps, smem, stream);
-    case 32: return launch_t<D, 32>(maps, p, ctas, warps, smem, stream);
-    case 64: return launch_t<D, 64>(maps, p, ctas, warps, smem, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  return p.f32 ? launch_r<D, float>(maps, p, ctas, warps, smem, stream)
+               : launch_r<D, __nv_bfloat16>(maps, p, ctas, warps, smem, stream);
 }
 
 }  // namespace
 
-size_t summarize_smem_bytes(int dim, int block, int warps, int stages) {
-  return kSmemSlack + static_cast<size_t>(warps) * stages * 2 * block * dim * 2 +
+size_t summarize_smem_bytes(int dim, int block, int warps, int stages, int elem_bytes) {
+  return kSmemSlack + static_cast<size_t>(warps) * stages * 2 * block * dim * elem_bytes +
          round16(static_cast<size_t>(warps) * stages * 8) + static_cast<size_t>(warps) * 2 * dim * 4;
 }
 

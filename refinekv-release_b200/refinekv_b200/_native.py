@@ -41,6 +41,7 @@ SPLIT_FINAL = 2
 #: Every symbol the header declares.
 EXPORTS = (
     "rkv_summarize",
+    "rkv_summarize_f32",
     "rkv_summarize_into",
     "rkv_select_workspace_size",
     "rkv_select",
@@ -96,6 +97,9 @@ class Summary(ctypes.Structure):
 
 _SIGNATURES = {
     "rkv_summarize": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                     c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
+                                     c_ptr, c_ptr, c_ptr]),
+    "rkv_summarize_f32": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                      c_i64, c_i64, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, c_ptr,
                                      c_ptr, c_ptr, c_ptr]),
     "rkv_summarize_into": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,

@@ -168,9 +168,17 @@ def sparse_attention(
         if (suffix_length.shape != () or suffix_length.device != query.device
                 or suffix_length.dtype != torch.int32):
             raise ValueError("suffix_length must be a scalar int32 tensor on the query device")
-    if key_suffix.shape[1] and (key_suffix.dtype != torch.bfloat16
-                                or value_suffix.dtype != torch.bfloat16):
-        raise TypeError("the CUDA backend requires BF16 suffix K/V")
+    if key_suffix.shape[1] and (key_suffix.dtype not in (torch.bfloat16, torch.float32)
+                                or value_suffix.dtype != key_suffix.dtype):
+        raise TypeError("the CUDA backend requires BF16 or FP32 suffix K/V")
+    if key_suffix.dtype == torch.float32 and key_suffix.shape[1]:
+        # The reference rounds the suffix to bf16 before use (reference.py:63-66);
+        # the kernels read bf16 rows, so an fp32 suffix is rounded once here,
+        # into workspace buffers reused while the shape stays the same.
+        key_suffix = _buffer(workspace, "suffix_k_bf16", key_suffix.shape, key_suffix.device,
+                             torch.bfloat16).copy_(key_suffix)
+        value_suffix = _buffer(workspace, "suffix_v_bf16", value_suffix.shape,
+                               value_suffix.device, torch.bfloat16).copy_(value_suffix)
 
     heads, group, _, dim = query.shape
     dev = query.device

@@ -140,16 +140,17 @@ def _checked_prompt(keys: torch.Tensor, values: torch.Tensor):
     if not keys.is_floating_point():
         raise TypeError("keys and values must be floating point")
     require_cuda_tensor(keys, "keys")
-    if keys.dtype != torch.bfloat16:
-        raise TypeError("the CUDA summarizer requires BF16 keys and values")
+    if keys.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("the CUDA summarizer requires BF16 or FP32 keys and values")
     if keys.shape[-1] not in SUPPORTED_HEAD_DIMS:
         raise ValueError(f"head_dim must be one of {SUPPORTED_HEAD_DIMS}")
     keys, values = keys.detach(), values.detach()
-    if keys.stride(2) != 1 or keys.data_ptr() % 16 or (keys.stride(1) * 2) % 16 or (
-            keys.stride(0) * 2) % 16:
+    w = keys.element_size()
+    if keys.stride(2) != 1 or keys.data_ptr() % 16 or (keys.stride(1) * w) % 16 or (
+            keys.stride(0) * w) % 16:
         keys = keys.contiguous()
-    if values.stride(2) != 1 or values.data_ptr() % 16 or (values.stride(1) * 2) % 16 or (
-            values.stride(0) * 2) % 16:
+    if values.stride(2) != 1 or values.data_ptr() % 16 or (values.stride(1) * w) % 16 or (
+            values.stride(0) * w) % 16:
         values = values.contiguous()
     return keys, values
 
@@ -159,12 +160,18 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
                   config: RefineKVConfig | None = None) -> BlockSummary:
     """Build BF16 block summaries in one pass over the prompt K/V.
 
-    ``keys``/``values``: (kv_heads, tokens, head_dim) bf16 CUDA tensors (any
-    head/token strides, innermost stride 1).  Raises the reference's
-    ``ValueError``/``TypeError`` for bad shapes, devices and dtypes
-    (``summary.py:46-60``), ``TypeError`` for non-bf16 caches (the CUDA path
-    is bf16-only, like the reference's Triton backend), ``ValueError`` for
-    unsupported head dimensions and ``RuntimeError`` for CPU tensors.
+    ``keys``/``values``: (kv_heads, tokens, head_dim) bf16 or fp32 CUDA
+    tensors (any head/token strides, innermost stride 1).  Raises the
+    reference's ``ValueError``/``TypeError`` for bad shapes, devices and
+    dtypes (``summary.py:46-60``), ``TypeError`` for caches other than bf16
+    and fp32, ``ValueError`` for unsupported head dimensions and
+    ``RuntimeError`` for CPU tensors.
+
+    An fp32 cache is summarised from its fp32 values, like the reference's
+    ``build_summary``; its page views (``keys``/``values`` of the result)
+    are a bf16 copy, not fp32 views of the cache as in the reference:
+    the reference's attention rounds the pages to bf16 before using them
+    (``reference.py:57``, ``:63-66``), so the decode reads the same values.
     """
     config = config or RefineKVConfig()
     keys, values = _checked_prompt(keys, values)
@@ -172,10 +179,13 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
     block = config.block_size
     blocks = -(-tokens // block)
     dev = keys.device
-    key_pages, value_pages = _page_alias(keys, block), _page_alias(values, block)
+    f32 = keys.dtype == torch.float32
+    key_pages = value_pages = None
+    if not f32:
+        key_pages, value_pages = _page_alias(keys, block), _page_alias(values, block)
     copy_pages = key_pages is None or value_pages is None
     if copy_pages:
-        key_pages = torch.empty(heads, blocks, block, dim, device=dev, dtype=keys.dtype)
+        key_pages = torch.empty(heads, blocks, block, dim, device=dev, dtype=torch.bfloat16)
         value_pages = torch.empty_like(key_pages)
     key_mean = torch.empty(heads, blocks, dim, device=dev, dtype=torch.bfloat16)
     value_mean = torch.empty_like(key_mean)
@@ -184,8 +194,9 @@ def build_summary(keys: torch.Tensor, values: torch.Tensor,
     max_value_norm = torch.empty(heads, device=dev, dtype=torch.float32)
     counts = torch.empty(blocks, device=dev, dtype=torch.int64)
     lib = _native.load()
+    summarize = lib.rkv_summarize_f32 if f32 else lib.rkv_summarize
     with torch.cuda.device(dev):
-        _native.check(lib.rkv_summarize(
+        _native.check(summarize(
             keys.data_ptr(), values.data_ptr(), heads, tokens, dim,
             keys.stride(0), keys.stride(1), values.stride(0), values.stride(1), block,
             key_pages.data_ptr() if copy_pages else None,
@@ -248,7 +259,7 @@ def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
         return one
     blocks = -(-longest // block)
     rows = seqs * heads
-    key_pages = torch.zeros(rows, blocks, block, dim, device=dev, dtype=dtype)
+    key_pages = torch.zeros(rows, blocks, block, dim, device=dev, dtype=torch.bfloat16)
     value_pages = torch.zeros_like(key_pages)
     key_mean = torch.zeros(rows, blocks, dim, device=dev, dtype=torch.bfloat16)
     value_mean = torch.zeros_like(key_mean)
@@ -257,6 +268,7 @@ def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
     max_value_norm = torch.zeros(rows, device=dev, dtype=torch.float32)
     counts = torch.zeros(seqs, blocks, device=dev, dtype=torch.int64)
     lib = _native.load()
+    summarize = lib.rkv_summarize_f32 if dtype == torch.float32 else lib.rkv_summarize
     stream = torch.cuda.current_stream(dev).cuda_stream
     with torch.cuda.device(dev):
         for i, (k, v) in enumerate(checked):
@@ -267,7 +279,7 @@ def build_summary_batch(keys: list[torch.Tensor], values: list[torch.Tensor],
             for hs in groups:
                 h0, n = hs[0], len(hs)
                 r0 = i * heads + h0
-                _native.check(lib.rkv_summarize(
+                _native.check(summarize(
                     k[h0].data_ptr(), v[h0].data_ptr(), n, tokens, dim,
                     k.stride(0), k.stride(1), v.stride(0), v.stride(1), block,
                     key_pages[r0].data_ptr(), value_pages[r0].data_ptr(),
@@ -345,6 +357,8 @@ def build_summary_into(keys: torch.Tensor, values: torch.Tensor, key_cache: torc
     """
     config = config or RefineKVConfig()
     keys, values = _checked_prompt(keys, values)
+    if keys.dtype != torch.bfloat16:
+        raise TypeError("build_summary_into writes a bf16 cache from bf16 keys and values")
     heads, tokens, dim = keys.shape
     block = config.block_size
     blocks = -(-tokens // block)

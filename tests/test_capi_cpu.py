@@ -72,6 +72,22 @@ def test_summarize_rejects_bad_arguments_before_touching_a_device(lib):
     assert lib.rkv_summarize(*args) == _native.RKV_ERR_INVALID_ARGUMENT
 
 
+def test_fp32_summarize_requires_bf16_page_copies_before_touching_a_device(lib):
+    args = [ctypes.c_void_p(16), ctypes.c_void_p(16), 2, 64, 128, 64 * 128, 128, 64 * 128, 128,
+            32, None, None, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16),
+            ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), None]
+    assert lib.rkv_summarize_f32(*args) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert b"page copies" in lib.rkv_last_error()
+    args[10], args[11] = ctypes.c_void_p(16), ctypes.c_void_p(16)
+    args[7] = 64 * 128 + 2  # fp32 head stride of 8 bytes past a 16-byte multiple
+    assert lib.rkv_summarize_f32(*args) == _native.RKV_ERR_ALIGNMENT
+
+
+def test_static_status_rejects_a_null_destination(lib):
+    assert lib.rkv_decode_static_status(None, None) == _native.RKV_ERR_INVALID_ARGUMENT
+    assert lib.rkv_last_error() == b"out is null"
+
+
 def test_decode_rejects_bad_arguments_before_touching_a_device(lib):
     s = _native.Summary(key_pages=16, value_pages=16, counts=16, key_mean=16, value_mean=16,
                         ellipsoid=16, value_norm=16, max_value_norm=16, heads=2, blocks=3,
@@ -191,17 +207,29 @@ def test_cpu_tensors_fail_loudly():
         select_blocks(q[:, :, 0], _Summary())
 
 
-def test_integration_stub_matches_the_abi_struct():
-    """The ctypes stub a maintainer would copy declares rkv_summary as the library does."""
-    text = (REPO / "INTEGRATION.md").read_text()
-    block = text[text.index("class _Summary(ctypes.Structure)"):text.index("def _view(s)")]
-    names = re.findall(r'\("(\w+)", ctypes\.c_\w+\)', block)
-    assert names == [name for name, _ in _native.Summary._fields_]
-    view = text[text.index("def _view(s)"):text.index("_RED = ")]
-    args = view[view.index("_Summary(") + len("_Summary("):view.rindex(")")]
-    depth, count = 0, 1
-    for ch in args:
-        depth += ch in "(["
-        depth -= ch in ")]"
-        count += ch == "," and depth == 0
-    assert count == len(_native.Summary._fields_)
+def test_reference_backend_stub_matches_the_abi():
+    """The ctypes module a maintainer copies into the reference declares rkv_summary as the
+    library does and builds the view with every field."""
+    import importlib.util
+    import inspect
+    import os
+
+    os.environ["RKV_LIBRARY"] = str(_native.LIB_PATH)
+    path = REPO / "refinekv-release_b200" / "integration" / "reference_backend_stub.py"
+    spec = importlib.util.spec_from_file_location("reference_backend_stub", path)
+    stub = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(stub)
+    assert [n for n, _ in stub._Summary._fields_] == [n for n, _ in _native.Summary._fields_]
+    assert [t for _, t in stub._Summary._fields_] == [t for _, t in _native.Summary._fields_]
+    fake = type("S", (), {})()
+    t = torch.zeros(2, 3, 4, 128)
+    fake.keys = fake.values = fake.key_mean = fake.value_mean = fake.ellipsoid = t
+    fake.counts = torch.zeros(3, dtype=torch.int64)
+    fake.value_norm, fake.max_value_norm = torch.zeros(2, 3), torch.zeros(2)
+    fake.block_size, fake.prompt_length = 4, 12
+    view = stub._view(fake)
+    assert (view.heads, view.blocks, view.block_size, view.head_dim, view.prompt_length,
+            view.sequences) == (2, 3, 4, 128, 12, 1)
+    ref_args = inspect.signature(stub.sparse_attention_b200).parameters
+    assert list(ref_args) == ["query", "summary", "key_suffix", "value_suffix", "config",
+                              "anchor_mask", "workspace", "return_selected", "suffix_length"]

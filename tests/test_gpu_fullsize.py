@@ -22,8 +22,16 @@ pinned to the reference's own outputs):
   also against the oracle's end-to-end result from its own summary.
 
 Half the layers decode with the suffix length read from device memory (the
-CUDA-graph path), half with the host length.  With ``RKV_PARITY_REPORT`` set,
-the counts are written there as JSON.
+CUDA-graph path), half with the host length.
+
+Config 0 (the reference's CPU configuration) exactly: one layer, the same
+geometry over an 8192-token fp32 prompt drawn on the CPU, fp32 queries, 32
+anchors, 16 decode steps with fp32 suffix tokens, seed 0.  The GPU
+summarises the fp32 cache itself; every step is judged against the oracle
+run end to end on the CPU from the same fp32 cache (its own summary):
+masks outside the eps margin, counters, outputs within 1e-4 ("fp32 mode").
+
+With ``RKV_PARITY_REPORT`` set, the counts are written there as JSON.
 """
 
 import json
@@ -44,6 +52,8 @@ DEV = "cuda"
 CONFIG1 = dict(layers=32, tokens=32768, heads=8, group=4, dim=128, block=32, eps=0.01,
                reduction="any", anchors=32, steps=128, seed=0)
 CHECK_STEPS = (0, 1, 63, 127)
+CONFIG0 = dict(tokens=8192, heads=8, group=4, dim=128, block=32, eps=0.01, reduction="any",
+               anchors=32, steps=16, seed=0, layer=0)
 
 
 def _report(name, payload):
@@ -159,3 +169,65 @@ def test_config1_32_layers_32k_128_steps_layer_by_layer():
         del data, keys, values, own, s_gpu
     totals["selected_fraction"] = totals.pop("selected_fraction_sum") / totals["layer_steps"]
     _report("config1", dict(config=c, check_steps=list(CHECK_STEPS), **totals))
+
+
+def test_config0_fp32_cache_8k_16_steps_every_step():
+    c = CONFIG0
+    H, G, D, N, B = c["heads"], c["group"], c["dim"], c["tokens"], c["block"]
+    cfg = RefineKVConfig(block_size=B, eps=c["eps"], gqa_reduction=c["reduction"],
+                         anchor_tokens=c["anchors"])
+    data = synthetic.make_layer(c["seed"], c["layer"], H, N, D, B, dtype=torch.float32)
+    s = build_summary(data.keys.to(DEV), data.values.to(DEV), cfg)
+    own = ora.build_summary(data.keys, data.values, B)  # the reference's fp32-cache summary
+    worst = _summary_ulps(s, own)
+    anchor_q = synthetic.make_queries(c["seed"], c["layer"], -1, data.planted_mean, G,
+                                      c["anchors"], torch.float32)
+    anchor = select_blocks_union(anchor_q.to(DEV), s, cfg)
+    own_anchor = ora.anchor_union(anchor_q, own, cfg.eps, cfg.gqa_reduction)
+    a_margin = torch.zeros_like(own_anchor)
+    for a in anchor_q:
+        a_margin |= ora.margin_blocks(a, own, cfg.eps, cfg.gqa_reduction)
+    assert not ((anchor.cpu() != own_anchor) & ~a_margin).any()
+    totals = dict(steps=0, margin_blocks=0, mask_mismatch_outside_margin=0, counter_diff_raw=0,
+                  max_abs_out_err=0.0, max_abs_out_err_end_to_end=0.0, selected_fraction_sum=0.0)
+    ws = {}
+    ks, vs = [], []
+    for step in range(c["steps"]):
+        k, v = synthetic.make_decode_token(c["seed"], c["layer"], step, H, D, N + step,
+                                           dtype=torch.float32)
+        ks.append(k)
+        vs.append(v)
+        kk, vv = torch.cat(ks, 1), torch.cat(vs, 1)
+        q = synthetic.make_queries(c["seed"], c["layer"], step, data.planted_mean, G, 1,
+                                   torch.float32)[0]
+        res = sparse_attention(q.to(DEV), s, kk.to(DEV), vv.to(DEV), cfg,
+                               anchor_mask=anchor, workspace=ws, return_selected=True)
+        got_mask, got_out = res.selected.cpu(), res.output.cpu()
+        assert got_out.dtype == torch.float32
+        want, z = ora.select_blocks(q, own, cfg.eps, cfg.gqa_reduction)
+        margin = ora.margin_blocks(q, own, cfg.eps, cfg.gqa_reduction) & ~own_anchor
+        want = want | own_anchor
+        diff = (got_mask != want) & ~margin
+        assert not diff.any(), f"step {step}: {int(diff.sum())} blocks"
+        got_access = int(decode_access_counts(res.selected, s.counts, G, H * G, step + 1))
+        settled = torch.where(margin, want, got_mask)
+        acc_settled = int(decode_access_counts(settled, own.counts, G, H * G, step + 1))
+        acc_want, _ = ora.access_counters(want, own.counts, G, H * G, step + 1, N)
+        assert acc_settled == acc_want, (step, acc_settled, acc_want)
+        ref = ora.mixed_attention(q, own, kk, vv, got_mask, z)
+        err = float((got_out - ref).abs().max())
+        assert err <= 1e-4, (step, err)
+        e2e_out, e2e_mask = ora.sparse_attention(q, own, kk, vv, cfg.eps, cfg.gqa_reduction,
+                                                 anchor_mask=own_anchor)
+        err_e2e = float((got_out - e2e_out).abs().max())
+        assert err_e2e <= (1e-4 if torch.equal(got_mask, e2e_mask) else 2e-2), (step, err_e2e)
+        totals["steps"] += 1
+        totals["margin_blocks"] += int(margin.sum())
+        totals["mask_mismatch_outside_margin"] += int(diff.sum())
+        totals["counter_diff_raw"] += abs(got_access - acc_want)
+        totals["max_abs_out_err"] = max(totals["max_abs_out_err"], err)
+        totals["max_abs_out_err_end_to_end"] = max(totals["max_abs_out_err_end_to_end"], err_e2e)
+        totals["selected_fraction_sum"] += float(got_mask.float().mean())
+    assert device_status(ws) == 0
+    totals["selected_fraction"] = totals.pop("selected_fraction_sum") / totals["steps"]
+    _report("config0", dict(config=c, summary_ulps=worst, **totals))
