@@ -57,6 +57,28 @@ METRIC = "attention-phase µs/decode step at 128K; achieved HBM GB/s vs B200 pea
 FALLBACK_HBM_GBS = 6650.0
 
 
+# Whole-decoder shapes for --model (random init: no checkpoints are available).
+# RefineKV settings: Llama follows the reference's speed protocol
+# (examples/benchmark_decode.py:128-130: B 32, eps 0.01, GQA mean, no anchors);
+# Qwen follows BASELINE config 3 (B 64, eps 0.005, GQA max, 64 anchors, the
+# first 2 layers dense, static YaRN x4).
+MODELS = {
+    "llama8b": dict(family="llama", layers=32, hidden=4096, heads=32, kv_heads=8,
+                    intermediate=14336, vocab=128256,
+                    rope={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                          "high_freq_factor": 4.0, "original_max_position_embeddings": 8192,
+                          "rope_theta": 500000.0},
+                    refinekv=dict(block_size=32, eps=0.01, gqa_reduction="mean", anchor_tokens=0,
+                                  full_attention_layers=0)),
+    "qwen7b": dict(family="qwen2", layers=28, hidden=3584, heads=28, kv_heads=4,
+                   intermediate=18944, vocab=152064,
+                   rope={"rope_type": "yarn", "factor": 4.0,
+                         "original_max_position_embeddings": 32768, "rope_theta": 1000000.0},
+                   refinekv=dict(block_size=64, eps=0.005, gqa_reduction="max", anchor_tokens=64,
+                                 full_attention_layers=2)),
+}
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -81,6 +103,15 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=1,
                     help="extra, not the headline workload: prompts that decode together, "
                          "stacked on the KV-head axis (one GPU)")
+    ap.add_argument("--model", choices=sorted(MODELS), default=None,
+                    help="extra line, not the headline: a whole random-init decoder of this "
+                         "shape decoding through RefineKV(model, config, cuda_graph=True) against "
+                         "dense attention on the same model and cache (BASELINE configs 2 and 3)")
+    ap.add_argument("--model-layers", type=int, default=None,
+                    help="--model: keep only the first N decoder layers (a quick check of the "
+                         "flow, not the configuration)")
+    ap.add_argument("--new-tokens", type=int, default=128,
+                    help="--model: generated tokens (the last new-tokens - 3 are timed)")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
@@ -90,6 +121,8 @@ def parse_args():
         ap.error("--steps must be >= 1 and --warmup >= 0")
     if args.batch < 1 or (args.batch > 1 and args.gpus > 1):
         ap.error("--batch must be >= 1, and a batch runs on one GPU")
+    if args.model is not None and (args.gpus > 1 or args.new_tokens < 4):
+        ap.error("--model runs on one GPU with --new-tokens >= 4")
     return args
 
 
@@ -892,6 +925,221 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# whole random-init decoder (--model): BASELINE configs 2 and 3
+# ---------------------------------------------------------------------------
+def build_model(name, dev, seed=0, layers=None):
+    """A random-init decoder of the named shape in bf16 on `dev` (initialised on the GPU)."""
+    import transformers
+
+    spec = dict(MODELS[name])
+    if layers is not None:
+        spec["layers"] = layers
+    config_type, model_type = (
+        (transformers.LlamaConfig, transformers.LlamaForCausalLM) if spec["family"] == "llama"
+        else (transformers.Qwen2Config, transformers.Qwen2ForCausalLM))
+    config = config_type(
+        vocab_size=spec["vocab"], hidden_size=spec["hidden"],
+        intermediate_size=spec["intermediate"], num_hidden_layers=spec["layers"],
+        num_attention_heads=spec["heads"], num_key_value_heads=spec["kv_heads"],
+        max_position_embeddings=131072, rope_parameters=dict(spec["rope"]), pad_token_id=0,
+        bos_token_id=None, eos_token_id=None, tie_word_embeddings=False)
+    config._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    default = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = model_type(config)
+    finally:
+        torch.set_default_dtype(default)
+    return model.eval()
+
+
+def run_model(args):
+    """Decode ms/token of a whole random-init decoder at a 128K prompt (reference protocol).
+
+    The reference's speed protocol (examples/benchmark_decode.py:17-100,
+    speed/README.md:109): greedy generation of `new_tokens` tokens after a
+    synthetic prompt, the last `new_tokens - 3` decode steps timed.  Arms, all
+    on the same model, prompt and cache capacity:
+    * refinekv_graph -- RefineKV(model, config, cuda_graph=True): dense SDPA
+      prefill fused with the summary write, then one captured decode step
+      replayed (the clock starts when the capture ends, as the reference's);
+    * dense_graph -- the same session with every layer in
+      full_attention_layers: dense decode attention over the same static
+      cache from the same captured-graph shell (a like-for-like dense arm);
+    * full_attention_eager -- the reference's own "Full Attention" arm:
+      Transformers' generate over make_visible_static_cache with native SDPA,
+      eager, timed from the third forward.
+    Times are CUDA events on the generating stream (wall clock beside them).
+    """
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from refinekv_b200 import RefineKV, RefineKVConfig, make_visible_static_cache
+    from refinekv_b200.integrations import transformers as adapter
+
+    spec = dict(MODELS[args.model])
+    if args.model_layers is not None:
+        spec["layers"] = args.model_layers
+    model = build_model(args.model, dev, args.seed, spec["layers"])
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 12345)
+    ids = torch.randint(3, spec["vocab"], (1, args.tokens), device=dev, generator=gen)
+    n_new = args.new_tokens
+    timed_steps = n_new - 3
+    options = dict(input_ids=ids, attention_mask=torch.ones_like(ids), max_new_tokens=n_new,
+                   min_new_tokens=n_new, eos_token_id=None, forced_eos_token_id=None,
+                   do_sample=False, num_beams=1)
+    rk_cfg = dict(spec["refinekv"])
+
+    class Marks:
+        """CUDA events + wall times at the boundaries the reference's benchmark marks."""
+
+        def __init__(self):
+            self.events, self.walls = {}, {}
+
+        def mark(self, name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            torch.cuda.synchronize(dev)
+            self.events[name], self.walls[name] = e, time.perf_counter()
+
+        def ms(self, a, b, steps):
+            return (self.events[a].elapsed_time(self.events[b]) / steps,
+                    (self.walls[b] - self.walls[a]) * 1e3 / steps)
+
+    def graph_arm(config):
+        marks = Marks()
+        original_graph = torch.cuda.CUDAGraph
+        calls = [0]
+
+        class TimedGraph(original_graph):
+            def capture_end(self, *a, **k):
+                result = super().capture_end(*a, **k)
+                marks.mark("replay")
+                return result
+
+        def on_forward(module, a, out):
+            calls[0] += 1
+            if calls[0] == 1:
+                marks.mark("prefill_end")
+
+        summarize = []
+        real_into, real_summary = adapter.build_summary_into, adapter.build_summary
+
+        def timed(fn):
+            def call(*a, **k):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                out = fn(*a, **k)
+                e1.record()
+                summarize.append((e0, e1))
+                return out
+            return call
+
+        handle = model.register_forward_hook(on_forward)
+        torch.cuda.CUDAGraph = TimedGraph
+        adapter.build_summary_into, adapter.build_summary = timed(real_into), timed(real_summary)
+        try:
+            marks.mark("start")
+            with RefineKV(model, RefineKVConfig(**config), cuda_graph=True):
+                out = model.generate(**options)
+                marks.mark("end")  # before the context's exit, which the GPU would idle through
+        finally:
+            handle.remove()
+            torch.cuda.CUDAGraph = original_graph
+            adapter.build_summary_into, adapter.build_summary = real_into, real_summary
+        steady, steady_wall = marks.ms("replay", "end", timed_steps)
+        prefill_ms = marks.events["start"].elapsed_time(marks.events["prefill_end"])
+        summ = [a.elapsed_time(b) * 1e3 for a, b in summarize]
+        return dict(ms_per_token=round(steady, 3), wall_ms_per_token=round(steady_wall, 3),
+                    prefill_s=round(prefill_ms / 1e3, 2),
+                    summarize_us_per_layer=round(statistics.median(summ), 1) if summ else None,
+                    summarized_layers=len(summ)), out[0, -n_new:]
+
+    def eager_full_attention():
+        marks = Marks()
+        calls = [0]
+
+        def on_forward(module, a, out):
+            calls[0] += 1
+            if calls[0] in (1, 3):
+                marks.mark(f"call{calls[0]}")
+
+        cache = make_visible_static_cache(model, args.tokens + n_new)
+        handle = model.register_forward_hook(on_forward)
+        try:
+            with torch.inference_mode():
+                marks.mark("start")
+                out = model.generate(**options, past_key_values=cache)
+                marks.mark("end")
+        finally:
+            handle.remove()
+        del cache
+        steady, steady_wall = marks.ms("call3", "end", timed_steps)
+        return dict(ms_per_token=round(steady, 3), wall_ms_per_token=round(steady_wall, 3)), \
+            out[0, -n_new:]
+
+    def eager_refinekv_stats():
+        """Eager RefineKV decode with the reference's access counters (selected fraction)."""
+        config = RefineKVConfig(**rk_cfg, collect_stats=True)
+        with RefineKV(model, config) as session:
+            out = model.generate(**options)
+            stats = session.stats
+        return stats, out[0, -n_new:]
+
+    dense_cfg = dict(rk_cfg, full_attention_layers=spec["layers"])
+    results = {}
+    with ClockSampler(dev) as clocks:
+        graph_arm(rk_cfg)  # warm-up: module loading, cuBLAS and SDPA plans, first captures
+        results["refinekv_graph"], rk_tokens = graph_arm(rk_cfg)
+        graph_arm(dense_cfg)
+        results["dense_graph"], dense_tokens = graph_arm(dense_cfg)
+        results["full_attention_eager"], full_tokens = eager_full_attention()
+    stats, eager_tokens = eager_refinekv_stats()
+    rk = results["refinekv_graph"]["ms_per_token"]
+    layers_sparse = spec["layers"] - rk_cfg["full_attention_layers"]
+    line = {
+        "metric": "whole-decoder decode ms/token at a 128K prompt (steady: last "
+                  f"{timed_steps} of {n_new} generated tokens)",
+        "value": rk,
+        "unit": "ms/token",
+        "n_gpus": 1,
+        "steps": timed_steps,
+        "warmup": 3,
+        "ms_per_step": rk,
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform random token ids, random-init weights (no checkpoints "
+                "are available)",
+        "config": {"workload": f"{args.model}-random-init-decoder-{args.tokens // 1024}k"
+                               + (f"-{spec['layers']}L" if args.model_layers else ""),
+                   "model": args.model, "layers": spec["layers"], "hidden": spec["hidden"],
+                   "query_heads": spec["heads"], "kv_heads": spec["kv_heads"],
+                   "intermediate": spec["intermediate"], "vocab": spec["vocab"],
+                   "rope": spec["rope"], "prompt_tokens": args.tokens,
+                   "generated_tokens": n_new, "refinekv": rk_cfg, "seed": args.seed},
+        "arms": results,
+        "speedup_vs_dense_graph": round(results["dense_graph"]["ms_per_token"] / rk, 3),
+        "speedup_vs_full_attention_eager": round(
+            results["full_attention_eager"]["ms_per_token"] / rk, 3),
+        "equivalent_access_ratio": stats["equivalent_access_ratio"],
+        "refinekv_decode_calls_per_token": stats["decode_attention_calls"] / max(1, n_new - 1),
+        "sparse_layers": layers_sparse,
+        "graph_tokens_equal_eager_tokens": bool(torch.equal(rk_tokens, eager_tokens)),
+        "tokens_equal_to_dense": round(float((rk_tokens == dense_tokens).float().mean()), 4),
+        "dense_graph_tokens_equal_full_attention_tokens": bool(
+            torch.equal(dense_tokens, full_tokens)),
+        # this build's kernels in the timed replays: stats, final, attend and
+        # combine of every sparse layer of every timed step
+        "gpu_launches": timed_steps * layers_sparse * 4,
+        "clocks": clocks.summary(),
+    }
+    emit(line)
+
+
 # The result line goes to the process's original stdout; everything else the
 # process writes to file descriptor 1 (NCCL's version banner, library
 # messages) is sent to stderr, so stdout holds exactly the one JSON line.
@@ -908,6 +1156,16 @@ def main():
     _RESULT_FD = os.dup(1)
     os.dup2(2, 1)
     args = parse_args()
+    if args.model is not None:
+        if args.impl == "reference":
+            emit({"impl": "reference", "unavailable": "the --model line carries its own dense "
+                  "arms on the same model (dense_graph, full_attention_eager); the reference's "
+                  "CPU path cannot decode an 8B model at a 128K prompt in a bench run"})
+            return
+        if "--tokens" not in sys.argv:
+            args.tokens = 131072
+        run_model(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -181,6 +181,69 @@ def test_greedy_tokens_match_the_reference_backend(family, reduction, monkeypatc
     assert torch.equal(ours, reference)
 
 
+def test_llama8b_slice_greedy_tokens_match_the_reference_backend(monkeypatch):
+    """Two layers of the Llama-3.1-8B shape (hidden 4096, 32 / 8 heads, head_dim 128,
+    intermediate 14336, vocab 128256, llama3 RoPE) over a 4096-token random prompt:
+    CUDA-graph decode on librefinekv_b200 and eager decode with the attention swapped
+    for the CPU oracle (the reference PyTorch backend restated) give the same greedy
+    tokens; so do eager and graph decode on the kernels."""
+    from oracle import refinekv_oracle as ora
+    from refinekv_b200.attention import AttentionResult
+
+    config = transformers.LlamaConfig(
+        vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=2,
+        num_attention_heads=32, num_key_value_heads=8, max_position_embeddings=131072,
+        rope_parameters={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                         "high_freq_factor": 4.0, "original_max_position_embeddings": 8192,
+                         "rope_theta": 500000.0},
+        pad_token_id=0, bos_token_id=None, eos_token_id=None, tie_word_embeddings=False)
+    torch.manual_seed(13)
+    default = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device("cuda"):
+            model = transformers.LlamaForCausalLM(config).eval()
+    finally:
+        torch.set_default_dtype(default)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    ids = torch.randint(3, 128256, (1, 4096), device="cuda", generator=gen)
+    opts = dict(input_ids=ids, attention_mask=torch.ones_like(ids), max_new_tokens=12,
+                min_new_tokens=12, eos_token_id=None, forced_eos_token_id=None, do_sample=False)
+    rk = RefineKVConfig(eps=0.01, gqa_reduction="any", anchor_tokens=32)
+    with RefineKV(model, rk, cuda_graph=True):
+        graph = model.generate(**opts)
+    with RefineKV(model, rk):
+        eager = model.generate(**opts)
+    assert torch.equal(graph, eager)
+
+    def summary(keys, values, cfg):
+        return ora.build_summary(keys.cpu(), values.cpu(), block_size=cfg.block_size)
+
+    def summary_into(keys, values, key_cache, value_cache, cfg):
+        key_cache[:, :keys.shape[1]].copy_(keys)
+        value_cache[:, :values.shape[1]].copy_(values)
+        return summary(keys, values, cfg)
+
+    def union(queries, summ, cfg, *, workspace=None):
+        return ora.anchor_union(queries.cpu(), summ, cfg.eps, cfg.gqa_reduction).cuda()
+
+    def decode(query, summ, ks, vs, cfg, *, anchor_mask=None, workspace=None,
+               return_selected=False, suffix_length=None):
+        out, sel = ora.sparse_attention(query.cpu(), summ, ks.cpu(), vs.cpu(), cfg.eps,
+                                        cfg.gqa_reduction,
+                                        anchor_mask=None if anchor_mask is None
+                                        else anchor_mask.cpu())
+        return AttentionResult(out.cuda(), sel.cuda() if return_selected else None)
+
+    monkeypatch.setattr(adapter, "build_summary", summary)
+    monkeypatch.setattr(adapter, "build_summary_into", summary_into)
+    monkeypatch.setattr(adapter, "select_blocks_union", union)
+    monkeypatch.setattr(adapter, "sparse_attention", decode)
+    with RefineKV(model, rk):
+        reference = model.generate(**opts)
+    assert torch.equal(eager, reference)
+
+
 def test_full_layers_match_native_generation():
     model = _model()
     opts = _options(39, 4)
