@@ -294,6 +294,33 @@ RKV_API int rkv_decode_static(const rkv_summary* summary, const void* query, int
  */
 RKV_API int rkv_decode_static_status(int32_t* out, void* stream);
 
+/*
+ * Dense decode attention over every page of a prompt plus the suffix, on the
+ * same streaming kernel as rkv_decode's refinement (no selector, no
+ * representatives): the attention of the adapter's full_attention_layers
+ * (reference transformers.py:510-520, dense SDPA over the visible cache)
+ * without a mask over a fixed-capacity cache, so that dense layers decode
+ * from a CUDA graph at streaming speed.
+ *   pages: only the page fields of rkv_summary are read -- key_pages /
+ *     value_pages and their strides (contiguous pages, a page pool, or a
+ *     batch), heads, blocks, block_size, head_dim, prompt_length, sequences /
+ *     prompt_lengths; every row of block b past the prompt is ignored, so the
+ *     pages may be a page view of a KV cache whose later rows hold other
+ *     tokens.  The summary pointers may be null.
+ *   Other arguments as rkv_decode (phases are attention + combine); the
+ *   workspace comes from rkv_decode_dense_workspace_size and follows the
+ *   same rules.  Results: output (heads, group, head_dim) in query_dtype.
+ */
+RKV_API size_t rkv_decode_dense_workspace_size(int64_t heads, int64_t group, int64_t blocks,
+                                               int64_t head_dim, int64_t block_size);
+RKV_API int rkv_decode_dense(const rkv_summary* pages, const void* query, int query_dtype,
+                             int64_t group, const void* key_suffix, const void* value_suffix,
+                             int64_t suffix_capacity, int64_t key_suffix_head_stride,
+                             int64_t key_suffix_token_stride, int64_t value_suffix_head_stride,
+                             int64_t value_suffix_token_stride, const int32_t* suffix_length,
+                             int64_t suffix_length_host, void* output, void* workspace,
+                             size_t workspace_size, void* stream);
+
 /* Kernel launches one rkv_decode call makes for the given phases. */
 RKV_API int rkv_decode_launch_count(unsigned phases);
 

@@ -59,17 +59,27 @@ __device__ __forceinline__ int visible_suffix(int has_suffix, const int* len_ptr
 
 // seg_pre[h][0..PB] = prefix sums of the selected-page counts over the
 // selector segments of head h; hstart[0..H] = first global item of each
-// head.  Called by every thread of the CTA.
+// head.  Called by every thread of the CTA.  Dense decode (`dense_blocks`
+// non-null): one segment per row holding all of its blocks (PB must be 1).
 __device__ __forceinline__ void build_work_list(const int* seg_count, int H, int PB, int n_suffix,
-                                                int* seg_pre, long long* hstart) {
-  for (int i = threadIdx.x; i < H * PB; i += blockDim.x) {
-    seg_pre[(i / PB) * (PB + 1) + (i % PB) + 1] = __ldcg(seg_count + i);
-  }
-  __syncthreads();
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    int* pre = seg_pre + h * (PB + 1);
-    pre[0] = 0;
-    for (int k = 1; k <= PB; ++k) pre[k] += pre[k - 1];
+                                                int* seg_pre, long long* hstart,
+                                                const SeqLayout* dense_blocks = nullptr,
+                                                int blocks = 0) {
+  if (dense_blocks != nullptr) {
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+      seg_pre[2 * h] = 0;
+      seg_pre[2 * h + 1] = dense_blocks->blocks(h, blocks);
+    }
+  } else {
+    for (int i = threadIdx.x; i < H * PB; i += blockDim.x) {
+      seg_pre[(i / PB) * (PB + 1) + (i % PB) + 1] = __ldcg(seg_count + i);
+    }
+    __syncthreads();
+    for (int h = threadIdx.x; h < H; h += blockDim.x) {
+      int* pre = seg_pre + h * (PB + 1);
+      pre[0] = 0;
+      for (int k = 1; k <= PB; ++k) pre[k] += pre[k - 1];
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -136,7 +146,8 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
 
   const int suffix_len = visible_suffix(p.has_suffix, p.suffix_len_ptr, p.suffix_len_host,
                                         p.suffix_capacity, p.status);
-  build_work_list(p.seg_count, H, PB, (suffix_len + R - 1) / R, seg_pre, hstart);
+  build_work_list(p.seg_count, H, PB, (suffix_len + R - 1) / R, seg_pre, hstart,
+                  p.dense ? &p.seq : nullptr, p.blocks);
   WorkList wl;
   wl.T = hstart[H];
   wl.C = wl.T < p.ctas ? wl.T : p.ctas;
@@ -166,8 +177,9 @@ __global__ void __launch_bounds__(256, 1) attend_kernel(const __grid_constant__ 
         const int mid = (a + b) >> 1;
         if (pre[mid] <= pos) a = mid; else b = mid;
       }
-      const int block = __ldg(p.sel_ids + (static_cast<size_t>(h) * PB + a) * p.seg_cap +
-                              (pos - pre[a]));
+      const int block = p.dense ? pos
+                                : __ldg(p.sel_ids + (static_cast<size_t>(h) * PB + a) * p.seg_cap +
+                                        (pos - pre[a]));
       int page = block;  // physical page: the page table's entry when paged
       if (p.page_table != nullptr) {
         page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride +
@@ -414,6 +426,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x, d = blockIdx.y * 32 + lane;
   const int H = p.heads, PB = p.parts_b;
+  const int n_rep = p.dense ? 0 : PB;  // representative sources (none in dense decode)
   const CombineLayout lay(H, PB, G8, p.max_sources);
   long long* hstart = reinterpret_cast<long long*>(smem + lay.hstart);
   int* seg_pre = reinterpret_cast<int*>(smem + lay.seg_pre);
@@ -431,7 +444,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
   // path behind the attention kernel.
   const int suffix_len = visible_suffix(p.has_suffix, p.suffix_len_ptr, p.suffix_len_host,
                                         p.suffix_capacity, p.status);
-  build_work_list(p.seg_count, H, PB, (suffix_len + p.page - 1) / p.page, seg_pre, hstart);
+  build_work_list(p.seg_count, H, PB, (suffix_len + p.page - 1) / p.page, seg_pre, hstart,
+                  p.dense ? &p.seq : nullptr, p.blocks);
   WorkList wl;
   wl.T = hstart[H];
   wl.C = wl.T < p.ctas ? wl.T : p.ctas;
@@ -448,7 +462,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     n_merged = static_cast<int>(last - first);
     n_att = n_merged + (last_hi > hstart[h + 1] ? p.warps : 1);
   }
-  const int nsrc = PB + n_att;
+  const int nsrc = n_rep + n_att;
   if (nsrc > p.max_sources) {  // cannot happen with the host's plan; never read past the table
     if (threadIdx.x == 0) atomicOr(p.status, kStatusBadInput);
     pdl_wait();
@@ -456,14 +470,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
     return;
   }
   auto src_index = [&](int k) -> size_t {
-    if (k < PB) return static_cast<size_t>(h) * PB + k;
-    const int a = k - PB;  // merged CTAs first, then the last CTA's slots
+    if (k < n_rep) return static_cast<size_t>(h) * PB + k;
+    const int a = k - n_rep;  // merged CTAs first, then the last CTA's slots
     const long long c = first + (a < n_merged ? a : n_merged);
     const int w = a < n_merged ? 0 : a - n_merged;
     return pair_slot(h, c) * p.warps + w;
   };
   auto o_row = [&](int k) {
-    return reinterpret_cast<const float4*>((k < PB ? p.rep_o : p.att_o) + src_index(k) * D * G8 +
+    return reinterpret_cast<const float4*>((k < n_rep ? p.rep_o : p.att_o) + src_index(k) * D * G8 +
                                            d * G8);
   };
   // This warp's first round of o rows: sources [k_lo, k_hi) of it (the
@@ -490,8 +504,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
         if (i < k_hi * G8) {
           const int k = i / G8, g = i - k * G8;
           const size_t at = src_index(k) * G8 + g;
-          mv[u] = __ldcg((k < PB ? p.rep_m : p.att_m) + at);
-          lv[u] = __ldcg((k < PB ? p.rep_l : p.att_l) + at);
+          mv[u] = __ldcg((k < n_rep ? p.rep_m : p.att_m) + at);
+          lv[u] = __ldcg((k < n_rep ? p.rep_l : p.att_l) + at);
         }
       }
 #pragma unroll
@@ -504,12 +518,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineParams p) {
       }
     }
   };
-  load_round(warp, 0, PB);
-  stage_ml(0, PB);
+  load_round(warp, 0, n_rep);
+  stage_ml(0, n_rep);
   pdl_wait();
   pdl_launch_dependents();
-  load_round(warp, PB, nsrc);
-  stage_ml(PB, nsrc);
+  load_round(warp, n_rep, nsrc);
+  stage_ml(n_rep, nsrc);
   __syncthreads();
   for (int g = warp; g < G8; g += kWarps) {
     float mx = -INFINITY;

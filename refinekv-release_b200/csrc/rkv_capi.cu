@@ -89,6 +89,74 @@ void split(int tiles, int target_parts, int* parts, int* per) {
   *parts = static_cast<int>(cdiv(tiles, *per));
 }
 
+// Attention and combine launch shapes for a plan whose parts_b is set (the
+// selector's segment count, or 1 for dense decode).  `dim` is padded.
+int plan_attention(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, int64_t dim,
+                   int64_t block_size) {
+  // Attention: one CTA per SM with about 128 KB of TMA ring, split over as
+  // many warps as possible (3..8) with one stage each (more for small
+  // stages).  Measured on B200: fewer bytes in flight per SM and more
+  // warps beat deeper per-warp rings (6-8 warps x 1 stage: ~91 us per
+  // 128K layer vs ~101 us for 4 warps x 3 stages).
+  const int64_t stage = 2 * block_size * dim * 2;
+  const int64_t ring = 128 * 1024;
+  pl->warps_c = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(8, ring / stage)));
+  pl->stages_c =
+      static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, ring / (pl->warps_c * stage))));
+  // The CTA merge parks each warp's (m, l, o^T) in that warp's ring slice.
+  const int64_t g8 = group <= 8 ? 8 : 16;
+  const int64_t stash = (2 * g8 + g8 * dim) * 4;
+  while (pl->stages_c * stage < stash) ++pl->stages_c;
+  while (attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), pl->warps_c,
+                           pl->stages_c, static_cast<int>(group), static_cast<int>(heads),
+                           pl->parts_b) > static_cast<size_t>(dev.smem_optin)) {
+    if (pl->stages_c > 1 && (pl->stages_c - 1) * stage >= stash) {
+      --pl->stages_c;
+    } else if (pl->warps_c > 1) {
+      --pl->warps_c;
+    } else {
+      return fail(RKV_ERR_UNSUPPORTED, "attention stages do not fit");
+    }
+  }
+  pl->smem_c = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
+                                 pl->warps_c, pl->stages_c, static_cast<int>(group),
+                                 static_cast<int>(heads), pl->parts_b);
+  pl->ctas = dev.sms;
+  pl->g8 = group <= 8 ? 8 : 16;
+  pl->max_sources = pl->parts_b + pl->ctas * pl->warps_c;
+  pl->smem_d = combine_smem_bytes(static_cast<int>(heads), pl->parts_b, static_cast<int>(group),
+                                  pl->max_sources);
+  if (pl->smem_d > static_cast<size_t>(dev.smem_optin)) {
+    return fail(RKV_ERR_UNSUPPORTED, "combine source table does not fit in shared memory");
+  }
+  return RKV_OK;
+}
+
+// rkv_decode_dense: attention and combine only (one segment per row, no
+// representatives); workspace = status word + attention partials.
+int make_dense_plan(Plan* pl, int64_t heads, int64_t group, int64_t dim, int64_t block_size) {
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc != RKV_OK) return rc;
+  dim = padded_dim(dim);
+  pl->parts_b = 1;
+  rc = plan_attention(pl, dev, heads, group, dim, block_size);
+  if (rc != RKV_OK) return rc;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = up256(off + bytes);
+    return at;
+  };
+  const size_t slots_c = static_cast<size_t>(heads + pl->ctas) * pl->warps_c;
+  pl->status = take(256);
+  pl->att_m = take(slots_c * pl->g8 * 4);
+  pl->att_l = take(slots_c * pl->g8 * 4);
+  pl->att_o = take(slots_c * pl->g8 * dim * 4);
+  pl->bytes = off;
+  return RKV_OK;
+}
+
 // `decode` plans rkv_decode (one query instance); otherwise rkv_select.
 // `fixed_parts_a` > 0 pins the phase-A grid (a sequence split needs the same
 // partial count on every rank; CTAs past the last tile write empty partials).
@@ -145,42 +213,8 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
     return fail(RKV_ERR_UNSUPPORTED, "selector tiles do not fit in shared memory");
   }
   if (decode) {
-    // Attention: one CTA per SM with about 128 KB of TMA ring, split over as
-    // many warps as possible (3..8) with one stage each (more for small
-    // stages).  Measured on B200: fewer bytes in flight per SM and more
-    // warps beat deeper per-warp rings (6-8 warps x 1 stage: ~91 us per
-    // 128K layer vs ~101 us for 4 warps x 3 stages).
-    const int64_t stage = 2 * block_size * dim * 2;
-    const int64_t ring = 128 * 1024;
-    pl->warps_c = static_cast<int>(std::max<int64_t>(3, std::min<int64_t>(8, ring / stage)));
-    pl->stages_c =
-        static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4, ring / (pl->warps_c * stage))));
-    // The CTA merge parks each warp's (m, l, o^T) in that warp's ring slice.
-    const int64_t g8 = group <= 8 ? 8 : 16;
-    const int64_t stash = (2 * g8 + g8 * dim) * 4;
-    while (pl->stages_c * stage < stash) ++pl->stages_c;
-    while (attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), pl->warps_c,
-                             pl->stages_c, static_cast<int>(group), static_cast<int>(heads),
-                             pl->parts_b) > static_cast<size_t>(dev.smem_optin)) {
-      if (pl->stages_c > 1 && (pl->stages_c - 1) * stage >= stash) {
-        --pl->stages_c;
-      } else if (pl->warps_c > 1) {
-        --pl->warps_c;
-      } else {
-        return fail(RKV_ERR_UNSUPPORTED, "attention stages do not fit");
-      }
-    }
-    pl->smem_c = attend_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size),
-                                   pl->warps_c, pl->stages_c, static_cast<int>(group),
-                                   static_cast<int>(heads), pl->parts_b);
-    pl->ctas = dev.sms;
-    pl->g8 = group <= 8 ? 8 : 16;
-    pl->max_sources = pl->parts_b + pl->ctas * pl->warps_c;
-    pl->smem_d = combine_smem_bytes(static_cast<int>(heads), pl->parts_b, static_cast<int>(group),
-                                    pl->max_sources);
-    if (pl->smem_d > static_cast<size_t>(dev.smem_optin)) {
-      return fail(RKV_ERR_UNSUPPORTED, "combine source table does not fit in shared memory");
-    }
+    rc = plan_attention(pl, dev, heads, group, dim, block_size);
+    if (rc != RKV_OK) return rc;
   }
   // Workspace layout.
   size_t off = 0;
@@ -346,7 +380,9 @@ int pages_map(CUtensorMap* map, const void* base, int64_t dim, int64_t block, in
   return RKV_OK;
 }
 
-int check_summary(const rkv_summary* s) {
+// The page geometry of a summary (all that rkv_decode_dense reads);
+// check_summary adds the summary fields.
+int check_pages(const rkv_summary* s) {
   if (s == nullptr) return fail(RKV_ERR_INVALID_ARGUMENT, "summary is null");
   if (s->heads <= 0 || s->blocks <= 0 || s->prompt_length <= 0) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "summary sizes must be positive");
@@ -360,9 +396,8 @@ int check_summary(const rkv_summary* s) {
   if (cdiv(s->prompt_length, s->block_size) != s->blocks) {
     return fail(RKV_ERR_INVALID_ARGUMENT, "blocks must equal ceil(prompt_length / block_size)");
   }
-  if (!s->key_pages || !s->value_pages || !s->counts || !s->key_mean || !s->value_mean ||
-      !s->ellipsoid || !s->value_norm || !s->max_value_norm) {
-    return fail(RKV_ERR_INVALID_ARGUMENT, "summary has a null pointer");
+  if (!s->key_pages || !s->value_pages) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "summary has a null page pointer");
   }
   if (s->heads > (1 << 16) || s->blocks > (1LL << 26)) {
     return fail(RKV_ERR_UNSUPPORTED, "summary is larger than the kernels index");
@@ -378,6 +413,16 @@ int check_summary(const rkv_summary* s) {
        s->value_token_stride <= 0)) {
     return fail(RKV_ERR_INVALID_ARGUMENT,
                 "a page table needs pool_pages, a stride of at least blocks and positive strides");
+  }
+  return RKV_OK;
+}
+
+int check_summary(const rkv_summary* s) {
+  int rc = check_pages(s);
+  if (rc != RKV_OK) return rc;
+  if (!s->counts || !s->key_mean || !s->value_mean || !s->ellipsoid || !s->value_norm ||
+      !s->max_value_norm) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "summary has a null pointer");
   }
   return RKV_OK;
 }
@@ -853,41 +898,17 @@ int rkv_decode_launch_count(unsigned phases) {
 
 namespace {
 
-// rkv_decode, and one rank's share of a sequence-split step when `split` is
-// given (phase A into the rank's stats slab, phase B over all slabs, combine
-// into the rank's output slab).
-int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
-                const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
-                int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
-                int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
-                const int32_t* suffix_length, int64_t suffix_length_host,
-                const uint8_t* anchor_mask, float eps, int reduction, void* output,
-                uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
-                void* stream, const SplitTarget* split) {
-  int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
-  if (rc != RKV_OK) return rc;
-  if (output == nullptr || selected == nullptr) {
-    return fail(RKV_ERR_INVALID_ARGUMENT, "output and selected must be non-null");
-  }
-  if (suffix_capacity < 0 || suffix_capacity > (1LL << 30)) {
-    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_capacity out of range");
-  }
-  if (suffix_capacity > 0 && (key_suffix == nullptr || value_suffix == nullptr)) {
-    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix K/V are null");
-  }
-  if (suffix_length == nullptr && (suffix_length_host < 0 || suffix_length_host > suffix_capacity)) {
-    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_length_host must be in [0, suffix_capacity]");
-  }
-  if (phases == 0 || phases > RKV_PHASE_ALL) return fail(RKV_ERR_INVALID_ARGUMENT, "bad phases");
-  Plan pl;
-  rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
-                 summary->block_size, 1, true, split ? split->geo.parts_a : 0);
-  if (rc != RKV_OK) return rc;
-  if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
-                    selected, 0, workspace, true, phases, st, split);
-  if (rc != RKV_OK) return rc;
+// The attention and combine launches of rkv_decode (after the selector) and
+// of rkv_decode_dense (no selector: every block attended).
+int attend_and_combine(const Plan& pl, const rkv_summary* summary, const void* query,
+                       int query_dtype, int64_t group, const void* key_suffix,
+                       const void* value_suffix, int64_t suffix_capacity,
+                       int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+                       int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+                       const int32_t* suffix_length, int64_t suffix_length_host, void* output,
+                       void* workspace, unsigned phases, bool dense, cudaStream_t st,
+                       const SplitTarget* split) {
+  int rc = RKV_OK;
   const int64_t H = summary->heads, D = summary->head_dim, B = summary->block_size;
   const int* suffix_ptr = suffix_length;
   if (phases & RKV_PHASE_ATTEND) {
@@ -938,6 +959,7 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     p.sel_ids = at<int>(workspace, pl.sel_ids);
     p.parts_b = pl.parts_b;
     p.seg_cap = pl.seg_cap;
+    p.dense = dense ? 1 : 0;
     p.att_m = at<float>(workspace, pl.att_m);
     p.att_l = at<float>(workspace, pl.att_l);
     p.att_o = at<float>(workspace, pl.att_o);
@@ -962,6 +984,9 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     c.suffix_len_host = static_cast<int>(suffix_length_host);
     c.seg_count = at<int>(workspace, pl.seg_count);
     c.parts_b = pl.parts_b;
+    c.dense = dense ? 1 : 0;
+    c.seq = seq_layout(summary);
+    c.blocks = static_cast<int>(summary->blocks);
     c.rep_m = at<float>(workspace, pl.rep_m);
     c.rep_l = at<float>(workspace, pl.rep_l);
     c.rep_o = at<float>(workspace, pl.rep_o);
@@ -978,6 +1003,47 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
     if (err != cudaSuccess) return cuda_fail(err, "combine launch");
   }
   return RKV_OK;
+}
+
+// rkv_decode, and one rank's share of a sequence-split step when `split` is
+// given (phase A into the rank's stats slab, phase B over all slabs, combine
+// into the rank's output slab).
+int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
+                const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+                int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+                int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+                const int32_t* suffix_length, int64_t suffix_length_host,
+                const uint8_t* anchor_mask, float eps, int reduction, void* output,
+                uint8_t* selected, void* workspace, size_t workspace_size, unsigned phases,
+                void* stream, const SplitTarget* split) {
+  int rc = check_selection_args(summary, query, query_dtype, group, eps, reduction);
+  if (rc != RKV_OK) return rc;
+  if (output == nullptr || selected == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "output and selected must be non-null");
+  }
+  if (suffix_capacity < 0 || suffix_capacity > (1LL << 30)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_capacity out of range");
+  }
+  if (suffix_capacity > 0 && (key_suffix == nullptr || value_suffix == nullptr)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix K/V are null");
+  }
+  if (suffix_length == nullptr && (suffix_length_host < 0 || suffix_length_host > suffix_capacity)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_length_host must be in [0, suffix_capacity]");
+  }
+  if (phases == 0 || phases > RKV_PHASE_ALL) return fail(RKV_ERR_INVALID_ARGUMENT, "bad phases");
+  Plan pl;
+  rc = make_plan(&pl, summary->heads, group, summary->blocks, summary->head_dim,
+                 summary->block_size, 1, true, split ? split->geo.parts_a : 0);
+  if (rc != RKV_OK) return rc;
+  if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
+                    selected, 0, workspace, true, phases, st, split);
+  if (rc != RKV_OK) return rc;
+  return attend_and_combine(pl, summary, query, query_dtype, group, key_suffix, value_suffix,
+                            suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                            value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                            suffix_length_host, output, workspace, phases, false, st, split);
 }
 
 }  // namespace
@@ -1089,6 +1155,57 @@ int rkv_decode_split(const rkv_summary* summary, const void* query, int query_dt
     if (err != cudaSuccess) return cuda_fail(err, "split merge launch");
   }
   return RKV_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+size_t rkv_decode_dense_workspace_size(int64_t heads, int64_t group, int64_t blocks,
+                                       int64_t head_dim, int64_t block_size) {
+  if (heads <= 0 || group <= 0 || group > kMaxGroup || blocks <= 0 || !supported_dim(head_dim) ||
+      !supported_block(block_size))
+    return 0;
+  Plan pl;
+  if (make_dense_plan(&pl, heads, group, head_dim, block_size) != RKV_OK) return 0;
+  return pl.bytes;
+}
+
+int rkv_decode_dense(const rkv_summary* pages, const void* query, int query_dtype, int64_t group,
+                     const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
+                     int64_t key_suffix_head_stride, int64_t key_suffix_token_stride,
+                     int64_t value_suffix_head_stride, int64_t value_suffix_token_stride,
+                     const int32_t* suffix_length, int64_t suffix_length_host, void* output,
+                     void* workspace, size_t workspace_size, void* stream) {
+  g_last_error.clear();
+  int rc = check_pages(pages);
+  if (rc != RKV_OK) return rc;
+  if (query == nullptr || output == nullptr) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "query and output must be non-null");
+  }
+  if (query_dtype != RKV_DTYPE_BF16 && query_dtype != RKV_DTYPE_F32) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "query dtype must be bf16 or fp32");
+  }
+  if (group < 1 || group > kMaxGroup) return fail(RKV_ERR_UNSUPPORTED, "group must be 1..16");
+  if (suffix_capacity < 0 || suffix_capacity > (1LL << 30)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_capacity out of range");
+  }
+  if (suffix_capacity > 0 && (key_suffix == nullptr || value_suffix == nullptr)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix K/V are null");
+  }
+  if (suffix_length == nullptr && (suffix_length_host < 0 || suffix_length_host > suffix_capacity)) {
+    return fail(RKV_ERR_INVALID_ARGUMENT, "suffix_length_host must be in [0, suffix_capacity]");
+  }
+  Plan pl;
+  rc = make_dense_plan(&pl, pages->heads, group, pages->head_dim, pages->block_size);
+  if (rc != RKV_OK) return rc;
+  if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
+  return attend_and_combine(pl, pages, query, query_dtype, group, key_suffix, value_suffix,
+                            suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                            value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                            suffix_length_host, output, workspace,
+                            RKV_PHASE_ATTEND | RKV_PHASE_COMBINE, true,
+                            static_cast<cudaStream_t>(stream), nullptr);
 }
 
 }  // extern "C"

@@ -141,6 +141,9 @@ struct AttendParams {
   const int* seg_count;
   const int* sel_ids;
   int parts_b, seg_cap;
+  // Dense decode (rkv_decode_dense): every block of a row is attended, in
+  // order, with no selector (seg_count / sel_ids unused, parts_b 1).
+  int dense;
   // One partial per (head, CTA, warp), (head, CTA) pairs indexed by head +
   // cta: m, l ((heads + ctas) * warps, G8) and o^T ((heads + ctas) * warps,
   // dim, G8).
@@ -163,6 +166,9 @@ struct CombineParams {
   int suffix_len_host;
   const int* seg_count;
   int parts_b;
+  int dense;           // rkv_decode_dense: no representatives; every block of a row attended
+  SeqLayout seq;       // dense: each row's own block count
+  int blocks;          // dense: blocks of a single prompt
   const float* rep_m;  // (heads, parts_b, G8)
   const float* rep_l;
   const float* rep_o;  // (heads, parts_b, dim, G8)

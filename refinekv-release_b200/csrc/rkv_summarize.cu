@@ -12,8 +12,10 @@
 //     distance of every real K row -> the page's value norm and radius;
 //   * the bf16 ellipsoid (radius^2 * width^2 * (1 + 2^-8)), the optional
 //     zero-padded page copy, counts and the per-head maximum value norm.
-// Statistics over rows are reduced in a different order than the reference's
-// torch reductions (FP32); the bf16 outputs agree to an ulp.
+// The K/V sums follow the reference's FP32 summation order (bit-identical
+// means); the centred radius and the value norms reduce over channels in a
+// different order than torch's vectorised CPU kernels, so the ellipsoid can
+// differ from the reference's by an ulp and the norms by an FP32 rounding.
 //
 // K/V caches may be bf16 or fp32 (the reference's build_summary takes any
 // floating cache, summary.py:46-60).  An fp32 cache is summarised from its
@@ -153,36 +155,72 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
     const uint8_t* kt = ring + static_cast<size_t>(warp * S + s) * kStage;
     const uint8_t* vt = kt + kTile;
 
-    // Lane per channel chunk: sums and K range over the real rows.
-    float ksum[8], vsum[8], kmax[8], kmin[8];
+    // Lane per channel chunk: sums and K range over the real rows.  The sums
+    // follow the reference's order exactly: torch's CPU sum over the rows of
+    // a page (summary.py:72-74) adds 16-row chunks one after another, each
+    // summed row by row from zero (padding rows add +0).  Lane group u of a
+    // chunk of channels sums row chunks u, u + kLpc, ...; the chunk sums are
+    // then added in chunk order, so the FP32 sums -- and the bf16 means --
+    // are bit-identical to the reference's for bf16 and fp32 caches alike.
+    constexpr int kRowChunks = R / 16;
+    float kpart[kRowChunks][8], vpart[kRowChunks][8], kmax[8], kmin[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      ksum[i] = vsum[i] = 0.f;
       kmax[i] = -INFINITY;
       kmin[i] = INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < kRowChunks; ++s2) kpart[s2][i] = vpart[s2][i] = 0.f;
     }
     const int c16 = lane % kChunks;
     if (lane < kActive) {
-      for (int r = lane / kChunks; r < count; r += kLpc) {
-        float kf[8], vf[8];
-        load8<T>(kt, r, c16, R, kf);
-        load8<T>(vt, r, c16, R, vf);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          ksum[i] += kf[i];
-          vsum[i] += vf[i];
-          kmax[i] = nan_max(kmax[i], kf[i]);
-          kmin[i] = nan_min(kmin[i], kf[i]);
+      for (int s2 = 0; s2 < kRowChunks; ++s2) {
+        const int chunk = lane / kChunks + s2 * kLpc;
+        if (chunk >= kRowChunks) break;
+        const int r_end = min(chunk * 16 + 16, count);
+        for (int r = chunk * 16; r < r_end; ++r) {
+          float kf[8], vf[8];
+          load8<T>(kt, r, c16, R, kf);
+          load8<T>(vt, r, c16, R, vf);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kpart[s2][i] += kf[i];
+            vpart[s2][i] += vf[i];
+            kmax[i] = nan_max(kmax[i], kf[i]);
+            kmin[i] = nan_min(kmin[i], kf[i]);
+          }
+        }
+        if (r_end < chunk * 16 + 16) {  // zero padding rows: x + 0 turns a -0 sum into +0
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            kpart[s2][i] += 0.f;
+            vpart[s2][i] += 0.f;
+          }
         }
       }
     }
     for (int off = kChunks; off < kActive; off <<= 1) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        ksum[i] += __shfl_xor_sync(0xffffffffu, ksum[i], off);
-        vsum[i] += __shfl_xor_sync(0xffffffffu, vsum[i], off);
         kmax[i] = nan_max(kmax[i], __shfl_xor_sync(0xffffffffu, kmax[i], off));
         kmin[i] = nan_min(kmin[i], __shfl_xor_sync(0xffffffffu, kmin[i], off));
+      }
+    }
+    // Chunk k lives in slot k / kLpc of lane group k % kLpc.
+    float ksum[8], vsum[8];
+#pragma unroll
+    for (int s2 = 0; s2 < kRowChunks; ++s2) {
+      for (int g = 0; g < kLpc; ++g) {
+        const int chunk = s2 * kLpc + g;
+        if (chunk >= kRowChunks) break;
+        const int src = g * kChunks + c16;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float kv = __shfl_sync(0xffffffffu, kpart[s2][i], src);
+          const float vv = __shfl_sync(0xffffffffu, vpart[s2][i], src);
+          ksum[i] = chunk == 0 ? kv : ksum[i] + kv;
+          vsum[i] = chunk == 0 ? vv : vsum[i] + vv;
+        }
       }
     }
     const float cnt = static_cast<float>(count);

@@ -8,8 +8,10 @@ Public names mirror the reference package ``refinekv`` v0.1.2
 Beyond the reference: ``build_summary_batch`` (several prompts decoding in
 lockstep, stacked on the head axis), ``build_summary_into`` (the prefill's
 cache write and the summary in one pass), ``attach_page_pool`` (decode from a
-vLLM-style K/V page pool through a page table) and ``refinekv_b200.parallel``
-(KV-head sharding and sequence split over GPUs).
+vLLM-style K/V page pool through a page table), ``page_view`` and
+``dense_attention`` (dense decode of the full-attention layers on the same
+kernel) and ``refinekv_b200.parallel`` (KV-head sharding and sequence split
+over GPUs).
 
 All compute runs in the CUDA library ``librefinekv_b200.so`` built from
 ``csrc/``; it is loaded on first use and a missing or unloadable library is
@@ -27,6 +29,9 @@ __all__ = [
     "build_summary_batch",
     "build_summary_into",
     "attach_page_pool",
+    "page_view",
+    "PageView",
+    "dense_attention",
     "select_blocks",
     "sparse_attention",
     "RefineKV",
@@ -35,12 +40,12 @@ __all__ = [
 
 
 def __getattr__(name):
-    if name in ("AttentionResult", "select_blocks", "sparse_attention"):
+    if name in ("AttentionResult", "select_blocks", "sparse_attention", "dense_attention"):
         from . import attention
 
         return getattr(attention, name)
     if name in ("BlockSummary", "build_summary", "build_summary_batch", "build_summary_into",
-                "attach_page_pool"):
+                "attach_page_pool", "page_view", "PageView"):
         from . import summary
 
         return getattr(summary, name)

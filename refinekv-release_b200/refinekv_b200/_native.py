@@ -49,6 +49,8 @@ EXPORTS = (
     "rkv_decode",
     "rkv_decode_static",
     "rkv_decode_static_status",
+    "rkv_decode_dense_workspace_size",
+    "rkv_decode_dense",
     "rkv_decode_launch_count",
     "rkv_select_split_slab",
     "rkv_select_split",
@@ -119,6 +121,10 @@ _SIGNATURES = {
                                          c_i64, c_ptr, ctypes.c_float, ctypes.c_int, c_ptr, c_ptr,
                                          c_ptr]),
     "rkv_decode_static_status": (ctypes.c_int, [c_ptr, c_ptr]),
+    "rkv_decode_dense_workspace_size": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "rkv_decode_dense": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64,
+                                        c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr,
+                                        c_i64, c_ptr, c_ptr, ctypes.c_size_t, c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
     "rkv_select_split_slab": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64]),
     "rkv_select_split": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64, c_i64,

@@ -15,7 +15,7 @@ import torch
 
 from . import _native
 from .config import RefineKVConfig
-from .summary import SUPPORTED_HEAD_DIMS, BlockSummary, require_cuda_tensor
+from .summary import SUPPORTED_HEAD_DIMS, BlockSummary, PageView, require_cuda_tensor
 
 MAX_GROUP = 16
 
@@ -214,3 +214,56 @@ def sparse_attention(
     # The reference returns a fresh mask (``mask.bool()``, runtime.py:226); keep that ownership.
     return AttentionResult(output.view(heads, group, 1, dim),
                            selected.view(torch.bool).clone() if return_selected else None)
+
+
+@torch.no_grad()
+def dense_attention(query: torch.Tensor, pages: PageView, key_suffix: torch.Tensor,
+                    value_suffix: torch.Tensor, *, workspace: dict | None = None,
+                    suffix_length: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact attention of ``query`` over every prompt page and the visible suffix.
+
+    The dense decode of the adapter's ``full_attention_layers`` (reference
+    ``integrations/transformers.py:510-520``, SDPA over the visible cache)
+    on the refinement kernel: no selector, no mask, graph-capturable with a
+    device ``suffix_length`` over a fixed-capacity suffix buffer.  Shapes as
+    ``sparse_attention``; returns the (kv_heads, group, 1, head_dim) output
+    in the query dtype, backed by ``workspace``.
+    """
+    if query.ndim != 4 or query.shape[2] != 1 or min(query.shape) <= 0:
+        raise ValueError("query must have shape (kv_heads, group_size, 1, head_dim)")
+    if query.shape[0] != pages.num_heads or query.shape[-1] != pages.keys.shape[-1]:
+        raise ValueError("query heads and dimension must match the pages")
+    if key_suffix.ndim != 3 or key_suffix.shape != value_suffix.shape:
+        raise ValueError("suffix K/V must have matching (kv_heads, tokens, head_dim) shapes")
+    if (key_suffix.shape[0], key_suffix.shape[-1]) != (query.shape[0], query.shape[-1]):
+        raise ValueError("suffix heads and dimension must match the query")
+    _check_backend(query, RefineKVConfig(block_size=pages.block_size))
+    if key_suffix.shape[1] and (key_suffix.dtype != torch.bfloat16
+                                or value_suffix.dtype != torch.bfloat16):
+        raise TypeError("the CUDA backend requires BF16 suffix K/V")
+    if suffix_length is not None and (suffix_length.shape != () or
+                                      suffix_length.dtype != torch.int32 or
+                                      suffix_length.device != query.device):
+        raise ValueError("suffix_length must be a scalar int32 tensor on the query device")
+    heads, group, _, dim = query.shape
+    dev = query.device
+    q = query.reshape(heads, group, dim)
+    if not q.is_contiguous():
+        q = q.contiguous()
+    capacity = key_suffix.shape[1]
+    output = _buffer(workspace, "dense_output", (heads, group, dim), dev, query.dtype)
+    lib = _native.load()
+    with torch.cuda.device(dev):
+        nbytes = lib.rkv_decode_dense_workspace_size(heads, group, pages.num_blocks, dim,
+                                                     pages.block_size)
+        scratch = _scratch(workspace, "rkv_dense_scratch", nbytes, dev)
+        _native.check(lib.rkv_decode_dense(
+            pages.abi(), q.data_ptr(), _query_code(q), group,
+            key_suffix.data_ptr() if capacity else None,
+            value_suffix.data_ptr() if capacity else None, capacity,
+            key_suffix.stride(0), key_suffix.stride(1),
+            value_suffix.stride(0), value_suffix.stride(1),
+            suffix_length.data_ptr() if suffix_length is not None else None, capacity,
+            output.data_ptr(), scratch.data_ptr(), scratch.numel(),
+            torch.cuda.current_stream(dev).cuda_stream))
+    return output.view(heads, group, 1, dim)

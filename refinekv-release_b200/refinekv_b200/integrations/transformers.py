@@ -24,8 +24,10 @@ here) or from the B200 design:
 * CUDA-graph decode no longer needs ``cache_position`` (5.5 dropped it from
   the model forward): the graph cache writes at a device-side cursor;
 * ``full_attention_layers`` works under CUDA graphs (the reference refuses):
-  dense layers attend over the fixed-capacity cache with a device-side mask
-  built from the visible length;
+  a dense layer of one sequence decodes with ``dense_attention`` (the
+  refinement kernel over all of the prompt's pages and the suffix up to the
+  device length, no mask); a left-padded batch's dense layers attend over the
+  fixed-capacity cache with a device-side mask;
 * beyond the reference (batch 1 only, ``:448-449``), decode also takes a
   left-padded batch of prompts, eagerly or from one captured CUDA graph:
   each row's summary covers its own prompt (the padding excluded) and all
@@ -47,9 +49,10 @@ try:
 except ImportError as error:  # pragma: no cover - exercised only without transformers
     raise ImportError("the Transformers adapter needs the `transformers` package") from error
 
-from ..attention import select_blocks_union, sparse_attention
+from ..attention import dense_attention, select_blocks_union, sparse_attention
 from ..config import RefineKVConfig
-from ..summary import BlockSummary, build_summary, build_summary_batch, build_summary_into
+from ..summary import (BlockSummary, PageView, build_summary, build_summary_batch,
+                       build_summary_into, page_view)
 
 ATTN_IMPLEMENTATION = "refinekv_b200"
 _MISSING = object()
@@ -191,6 +194,7 @@ class _LayerState:
     summary: BlockSummary | None = None
     anchor_mask: torch.Tensor | None = None
     workspace: dict = field(default_factory=dict)
+    pages: PageView | None = None  # a dense layer's page view of the graph cache
     pads: list | None = None  # left padding per row of a batch
     pad_rows: torch.Tensor | None = None  # the same, (rows, 1, 1, 1) on the device
 
@@ -464,7 +468,9 @@ class RefineKV:
         device = input_ids.device
         rows, prompt_length = input_ids.shape
         cursor = _GraphCursor(device)
-        capacity = prompt_length + max_new_tokens
+        # Whole 64-token pages: a dense layer's page view of the cache (any
+        # block size) must stay inside the allocation.
+        capacity = -(-(prompt_length + max_new_tokens) // 64) * 64
         cache = Cache(layers=[_GraphStaticLayer(capacity, cursor) for _ in self.model.model.layers])
         # Left padding (a batch): each row's positions count its real tokens only.
         pads = torch.zeros(rows, 1, device=device, dtype=torch.long)
@@ -651,7 +657,25 @@ class RefineKV:
                                       **kwargs)
 
     def _dense_graph_decode(self, module, query, key, value, scaling, kwargs, state):
-        """Dense layer under CUDA graphs: the whole fixed-capacity cache, masked on the device."""
+        """Dense layer under CUDA graphs.
+
+        One sequence: ``dense_attention`` over the prompt's pages of the cache
+        and the suffix up to the device length (the refinement kernel with no
+        selector: no mask over the fixed capacity, no KV-head repetition).
+        A left-padded batch: SDPA over the whole fixed-capacity cache with a
+        device-side mask that also hides each row's padding.
+        """
+        if query.shape[0] == 1 and state.pad_rows is None:
+            heads, dim = key.shape[1], query.shape[-1]
+            groups = query.shape[1] // heads
+            if state.pages is None:
+                state.pages = page_view(key[0], value[0], state.prompt_length,
+                                        self.config.block_size)
+            out = dense_attention(query[0].reshape(heads, groups, 1, dim), state.pages,
+                                  key[0, :, state.prompt_length:],
+                                  value[0, :, state.prompt_length:], workspace=state.workspace,
+                                  suffix_length=self._graph_suffix_length)
+            return out.reshape(query.shape[1], 1, dim).transpose(0, 1).unsqueeze(0), None
         visible = state.prompt_length + self._graph_suffix_length
         columns = torch.arange(key.shape[2], device=key.device)
         live = (columns < visible).view(1, 1, 1, -1)

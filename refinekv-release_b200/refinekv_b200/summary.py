@@ -112,6 +112,60 @@ class BlockSummary:
         return self._abi
 
 
+@dataclass(frozen=True)
+class PageView:
+    """A prompt's K/V pages with no summaries, for dense decode (``dense_attention``).
+
+    ``keys``/``values``: (kv_heads, pages, block_size, head_dim) bf16 page
+    views (``page_view`` makes them from a KV cache without copying); rows of
+    the last page past ``prompt_length`` are never read as prompt rows.
+    """
+
+    keys: torch.Tensor
+    values: torch.Tensor
+    prompt_length: int
+    block_size: int
+
+    @property
+    def num_blocks(self) -> int:
+        return self.keys.shape[1]
+
+    @property
+    def num_heads(self) -> int:
+        return self.keys.shape[0]
+
+    def abi(self) -> _native.Summary:
+        return _native.Summary(
+            key_pages=self.keys.data_ptr(), value_pages=self.values.data_ptr(),
+            key_page_head_stride=self.keys.stride(0), value_page_head_stride=self.values.stride(0),
+            heads=self.num_heads, blocks=self.num_blocks, block_size=self.block_size,
+            head_dim=self.keys.shape[-1], prompt_length=self.prompt_length, sequences=1)
+
+
+def page_view(key_cache: torch.Tensor, value_cache: torch.Tensor, prompt_length: int,
+              block_size: int = 32) -> PageView:
+    """Pages of the first ``prompt_length`` rows of a (kv_heads, capacity, head_dim) cache.
+
+    No copy: the cache's rows must be contiguous and its capacity must hold
+    the prompt rounded up to whole pages (the rows after the prompt may hold
+    anything, e.g. the generated tokens).
+    """
+    heads, capacity, dim = key_cache.shape
+    blocks = -(-int(prompt_length) // block_size)
+    for cache in (key_cache, value_cache):
+        if cache.shape != key_cache.shape or cache.dtype != torch.bfloat16:
+            raise ValueError("caches must be bf16 with the same (kv_heads, capacity, head_dim)")
+        if cache.stride(2) != 1 or cache.stride(1) != dim:
+            raise ValueError("cache rows must be contiguous")
+        if cache.data_ptr() % 16 or (cache.stride(0) * 2) % 16:
+            raise ValueError("cache heads must start on 16-byte boundaries")
+    if prompt_length <= 0 or blocks * block_size > capacity:
+        raise ValueError("cache capacity must hold the prompt rounded up to whole pages")
+    pages = lambda cache: cache.as_strided((heads, blocks, block_size, dim),  # noqa: E731
+                                           (cache.stride(0), block_size * dim, dim, 1))
+    return PageView(pages(key_cache), pages(value_cache), int(prompt_length), block_size)
+
+
 def require_cuda_tensor(tensor: torch.Tensor, what: str) -> None:
     if not tensor.is_cuda:
         raise RuntimeError(

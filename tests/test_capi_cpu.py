@@ -233,3 +233,20 @@ def test_reference_backend_stub_matches_the_abi():
     ref_args = inspect.signature(stub.sparse_attention_b200).parameters
     assert list(ref_args) == ["query", "summary", "key_suffix", "value_suffix", "config",
                               "anchor_mask", "workspace", "return_selected", "suffix_length"]
+
+
+def test_page_view_and_dense_attention_validate_before_touching_a_device():
+    from refinekv_b200 import dense_attention, page_view
+
+    cache = torch.zeros(2, 100, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="whole pages"):
+        page_view(cache, cache, 90, 64)  # 2 pages of 64 rows need 128
+    with pytest.raises(ValueError, match="bf16"):
+        page_view(cache.float(), cache.float(), 10)
+    pages = page_view(cache, cache, 90, 32)
+    assert pages.keys.shape == (2, 3, 32, 128) and pages.keys.data_ptr() == cache.data_ptr()
+    q = torch.zeros(2, 4, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        dense_attention(q, pages, cache[:, 90:], cache[:, 90:])
+    with pytest.raises(ValueError, match="query heads"):
+        dense_attention(q[:1], pages, cache[:, 90:], cache[:, 90:])
