@@ -112,6 +112,9 @@ def parse_args():
                          "flow, not the configuration)")
     ap.add_argument("--new-tokens", type=int, default=128,
                     help="--model: generated tokens (the last new-tokens - 3 are timed)")
+    ap.add_argument("--two-kernel-selector", action="store_true",
+                    help="run the selector as its two kernels (stats, final) with every selected "
+                         "page in the attention kernel, instead of the fused selector (A/B)")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
@@ -540,6 +543,8 @@ def run_b200(args):
     torch.cuda.set_device(dev)
     from refinekv_b200 import _native, parallel
 
+    if args.two_kernel_selector:
+        _native.load().rkv_set_fused_selector(0)
     plan = parallel.plan_shards(args.kv_heads * args.batch, args.tokens, args.block_size, world,
                                 rank, args.seq_ranks)
     group = parallel.new_seq_group(plan)
@@ -620,6 +625,13 @@ def run_b200(args):
                   if L.summary.counts.ndim == 2 else L.summary.counts for L in layers]
     sel_tokens = torch.zeros((), device=dev, dtype=torch.int64)
     sel_pages = torch.zeros((), device=dev, dtype=torch.int64)
+    # Tokens of the anchored blocks of each layer (fixed for the whole decode):
+    # with the fused selector those pages are streamed by the selector launch.
+    anchored_tokens = sum(int((L.anchor.to(torch.int64) * counts).sum())
+                          for L, counts in zip(layers, counts_all) if L.anchor is not None)
+    anchored_pages = sum(int(L.anchor.sum()) for L in layers if L.anchor is not None)
+    fused = (not split and lib.rkv_decode_kernel_count(
+        plan.heads, args.group, plan.blocks, args.head_dim, args.block_size) == 3)
 
     def count_selected():
         nonlocal sel_pages, sel_tokens
@@ -675,22 +687,39 @@ def run_b200(args):
     suffix_total = (args.layers * heads_local * sum(s + 1 for s in range(args.warmup, cap))
                     if plan.holds_suffix else 0)
     qo_bytes = 2 * heads_local * G * D * 2
-    attend_bytes = (tokens_refined + suffix_total) * D * 2 * 2 / launches + qo_bytes
-    attend_avg_ms = statistics.mean(attend_ms)
-    peak, peak_note = measured_hbm_peak()
-    attend_gbs = attend_bytes / (attend_avg_ms * 1e-3) / 1e9
     unselected = launches * heads_local * nb - pages
     summary_bytes = (heads_local * nb * D * 2 * 2 + nb * 8 + heads_local * nb * 4 + heads_local * 4
                      + heads_local * nb * (2 if args.anchors else 1))
     step_bytes = args.layers * (summary_bytes + qo_bytes) + (
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
-    traffic = profiled_traffic("attend_llama8b_128k.json")
+    # Per launch: the selector launch reads the summaries, the value means of
+    # the unselected blocks and -- fused -- the anchored pages; the attention
+    # launch (+ combine) the other selected pages and the suffix.
+    streamed_tokens = anchored_tokens * args.steps if fused else 0  # over all timed launches
+    select_bytes = (summary_bytes + heads_local * G * D * 2
+                    + (unselected * D * 2 + streamed_tokens * D * 4) / launches)
+    attend_bytes = ((tokens_refined - streamed_tokens + suffix_total) * D * 2 * 2 / launches
+                    + qo_bytes)
+    attend_avg_ms = statistics.mean(attend_ms)
+    select_avg_ms = statistics.mean(select_ms) if select_ms else None
+    peak, peak_note = measured_hbm_peak()
+    attend_gbs = attend_bytes / (attend_avg_ms * 1e-3) / 1e9
+    select_gbs = select_bytes / (select_avg_ms * 1e-3) / 1e9 if select_avg_ms else None
+    # The dominant kernel: the fused selector when it streams most of the
+    # pages, else the attention kernel.
+    dominant_is_select = fused and select_avg_ms is not None and select_avg_ms > attend_avg_ms
+    traffic = profiled_traffic("fused_llama8b_128k.json" if dominant_is_select
+                               else "attend_llama8b_128k.json")
     traffic_per_launch = None
-    # The committed capture is of 32-token pages of 128 channels; its DRAM
+    # A committed capture is of 32-token pages of 128 channels; its DRAM
     # bytes scale with the pages a launch reads only for that page shape.
     if traffic is not None and not split and (args.block_size, args.head_dim) == (32, 128):
         dram_bytes, pages_profiled = traffic
-        traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
+        if dominant_is_select:  # the anchored pages one selector launch streams
+            pages_per_launch = anchored_pages / args.layers
+        else:  # the pages one attention launch streams
+            pages_per_launch = pages / launches - (anchored_pages / args.layers if fused else 0)
+        traffic_per_launch = dram_bytes * pages_per_launch / pages_profiled
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
     step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9  # whole job
     step_gbs_per_gpu = step_gbs / world
@@ -893,25 +922,44 @@ def run_b200(args):
                     "bytes_per_step": int(step_bytes_all),
                     "note": peak_note + "; frac is per GPU (job bytes / GPUs / step time "
                                         "/ one GPU's peak)"},
-            "roofline": {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
-                         "traffic": None if traffic_per_launch is None else int(traffic_per_launch),
-                         "kernel": ("rkv split decode step (selector, attention, exchanges, "
-                                    "merge)" if split else
-                                    f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}>"),
-                         "algorithmic_bytes_per_launch": int(attend_bytes),
-                         "avg_launch_us": round(attend_avg_ms * 1e3, 2),
-                         "peak_note": peak_note},
-            "phase_us_per_layer": ({"split_step": round(attend_avg_ms * 1e3, 2)} if split else
-                                   {"select": round(statistics.mean(select_ms) * 1e3, 2),
-                                    "attend": round(attend_avg_ms * 1e3, 2)}),
+            "roofline": ({"bound": "hbm", "achieved": round(select_gbs, 1), "peak": peak,
+                          "unit": "GB/s", "frac": round(select_gbs / peak, 4),
+                          "traffic": (None if traffic_per_launch is None
+                                      else int(traffic_per_launch)),
+                          "kernel": f"rkv fused_kernel<{D},{B}> (selector + anchored pages)",
+                          "algorithmic_bytes_per_launch": int(select_bytes),
+                          "avg_launch_us": round(select_avg_ms * 1e3, 2),
+                          "peak_note": peak_note} if dominant_is_select else
+                         {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
+                          "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
+                          "traffic": (None if traffic_per_launch is None
+                                      else int(traffic_per_launch)),
+                          "kernel": ("rkv split decode step (selector, attention, exchanges, "
+                                     "merge)" if split else
+                                     f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}> + combine"),
+                          "algorithmic_bytes_per_launch": int(attend_bytes),
+                          "avg_launch_us": round(attend_avg_ms * 1e3, 2),
+                          "peak_note": peak_note}),
+            "phase_us_per_layer": (
+                {"split_step": round(attend_avg_ms * 1e3, 2)} if split else
+                {"select" + ("_and_anchored_pages" if fused else ""):
+                     round(select_avg_ms * 1e3, 2),
+                 "select_achieved_gbs": round(select_gbs, 1),
+                 "attend_and_combine": round(attend_avg_ms * 1e3, 2),
+                 "attend_achieved_gbs": round(attend_gbs, 1)}),
+            "fused_selector": fused,
+            "anchored_fraction": round(anchored_pages / (args.layers * heads_local * nb), 5),
             "selected_fraction": round(pages / (launches * heads_local * nb), 5),
             # median over layers (layer 0 carries one-time module loading)
             "summarize_us_per_layer": round(statistics.median(summarize_ms) * 1e3, 1),
             # our kernels per layer-step: 4 (stats, final, attend, combine), or 5 under a
             # sequence split (the same four plus the rank merge; NCCL's kernels not counted)
+            # our kernels per layer-step: 3 with the fused selector (selector +
+            # anchored pages, attention, combine), 4 with the two selector kernels,
+            # 5 under a sequence split (+ the rank merge; NCCL's kernels not counted)
             "gpu_launches": args.steps * args.layers * (
-                lib.rkv_decode_launch_count(_native.PHASE_ALL) + (1 if split else 0)),
+                (3 if fused else lib.rkv_decode_launch_count(_native.PHASE_ALL))
+                + (1 if split else 0)),
             "clocks": clocks.summary(),
             "e2e": e2e,
             "dense_attention": dense,
@@ -976,7 +1024,7 @@ def run_model(args):
     """
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    from refinekv_b200 import RefineKV, RefineKVConfig, make_visible_static_cache
+    from refinekv_b200 import RefineKV, RefineKVConfig, _native, make_visible_static_cache
     from refinekv_b200.integrations import transformers as adapter
 
     spec = dict(MODELS[args.model])
@@ -1132,9 +1180,11 @@ def run_model(args):
         "tokens_equal_to_dense": round(float((rk_tokens == dense_tokens).float().mean()), 4),
         "dense_graph_tokens_equal_full_attention_tokens": bool(
             torch.equal(dense_tokens, full_tokens)),
-        # this build's kernels in the timed replays: stats, final, attend and
-        # combine of every sparse layer of every timed step
-        "gpu_launches": timed_steps * layers_sparse * 4,
+        # this build's kernels in the timed replays: the decode kernels of every
+        # sparse layer of every timed step
+        "gpu_launches": timed_steps * layers_sparse * _native.load().rkv_decode_kernel_count(
+            spec["kv_heads"], spec["heads"] // spec["kv_heads"], -(-args.tokens // rk_cfg["block_size"]),
+            spec["hidden"] // spec["heads"], rk_cfg["block_size"]),
         "clocks": clocks.summary(),
     }
     emit(line)

@@ -321,8 +321,29 @@ RKV_API int rkv_decode_dense(const rkv_summary* pages, const void* query, int qu
                              int64_t suffix_length_host, void* output, void* workspace,
                              size_t workspace_size, void* stream);
 
-/* Kernel launches one rkv_decode call makes for the given phases. */
+/* Kernel launches one rkv_decode call makes for the given phases on the
+ * two-kernel selector path (4 for RKV_PHASE_ALL). */
 RKV_API int rkv_decode_launch_count(unsigned phases);
+
+/*
+ * Kernel launches of one rkv_decode call (RKV_PHASE_ALL) for this geometry on
+ * the current device: 3 when the fused selector runs (one kernel for phases
+ * STATS and FINAL that also attends the anchored pages; then attention and
+ * combine), else 4; 0 for an unsupported geometry.  With the fused selector,
+ * RKV_PHASE_STATS and RKV_PHASE_FINAL must be requested together.
+ */
+RKV_API int rkv_decode_kernel_count(int64_t heads, int64_t group, int64_t blocks,
+                                    int64_t head_dim, int64_t block_size);
+
+/*
+ * Process-wide switch of rkv_decode's fused selector (on by default).  With 0,
+ * rkv_decode runs the two selector kernels (stats, final) and the attention
+ * kernel streams every selected page, anchored or not -- for measurement and
+ * cross-checks; the results agree within the summation-order tolerance.
+ * Set it before planning a workspace: workspace sizes depend on it.  No
+ * reference counterpart.
+ */
+RKV_API void rkv_set_fused_selector(int enable);
 
 /*
  * Sequence split: the prompt blocks of each KV head are spread over `ranks`

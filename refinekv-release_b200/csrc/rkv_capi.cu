@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <mutex>
@@ -38,6 +39,12 @@ bool supported_block(int64_t b) { return b == 16 || b == 32 || b == 64; }
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Workspace header: status word at 0; the fused selector's per-row barrier
+// words (arrivals, then generations) from kRowWords, for up to kMaxFusedRows rows.
+constexpr size_t kHeaderBytes = 4096;
+constexpr size_t kRowWords = 256;
+constexpr int64_t kMaxFusedRows = 480;
 
 struct DeviceInfo {
   int sms = 0;
@@ -78,6 +85,12 @@ struct Plan {
   size_t smem_c = 0;
   int g8 = 8, max_sources = 0;
   size_t smem_d = 0;  // combine
+  // Fused selector (rkv_fused.cu): one kernel for phases A and B plus the
+  // anchored pages; parts_b CTAs per row, tpc_b the largest tile range.
+  bool fused = false;
+  int warps_f = 8;
+  size_t smem_f = 0;
+  size_t rows_words = 0;  // per-row barrier words (arrivals, generations)
   // workspace offsets (bytes)
   size_t status = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
   size_t rep_m = 0, rep_l = 0, rep_o = 0, att_m = 0, att_l = 0, att_o = 0, bytes = 0;
@@ -149,12 +162,43 @@ int make_dense_plan(Plan* pl, int64_t heads, int64_t group, int64_t dim, int64_t
     return at;
   };
   const size_t slots_c = static_cast<size_t>(heads + pl->ctas) * pl->warps_c;
-  pl->status = take(256);
+  pl->status = take(kHeaderBytes);
   pl->att_m = take(slots_c * pl->g8 * 4);
   pl->att_l = take(slots_c * pl->g8 * 4);
   pl->att_o = take(slots_c * pl->g8 * dim * 4);
   pl->bytes = off;
   return RKV_OK;
+}
+
+// Whether rkv_decode runs the fused selector (switched off process-wide by
+// rkv_set_fused_selector(0), for measurement and cross-checks).
+std::atomic<int> g_fused_selector{1};
+
+// The fused selector's shape: rows x parts CTAs, never more than one per SM
+// unless each row has a single part (then no CTA waits for another), warps
+// of one slice each (a K|V page or a key-mean|ellipsoid tile pair).
+bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, int64_t dim,
+                int64_t block_size) {
+  if (!g_fused_selector.load() || heads > kMaxFusedRows) return false;
+  const int parts = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(pl->tiles, dev.sms / std::max<int64_t>(1, heads))));
+  const int tcap = static_cast<int>(cdiv(pl->tiles, parts));
+  if (tcap > 128) return false;  // the per-part tables live in shared memory
+  const int64_t slice = std::max<int64_t>(2LL * kSelectTile * dim * 2, 2LL * block_size * dim * 2);
+  const int warps = static_cast<int>(std::min<int64_t>(8, 196608 / slice));
+  if (warps < 2) return false;
+  const size_t smem = fused_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), warps,
+                                       static_cast<int>(group), tcap);
+  if (smem > static_cast<size_t>(dev.smem_optin)) return false;
+  pl->fused = true;
+  pl->warps_f = warps;
+  pl->smem_f = smem;
+  pl->parts_a = parts;
+  pl->slots_a = warps;
+  pl->parts_b = parts;
+  pl->tpc_b = tcap;
+  pl->seg_cap = tcap * kSelectTile;
+  return true;
 }
 
 // `decode` plans rkv_decode (one query instance); otherwise rkv_select.
@@ -212,6 +256,9 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
       pl->smem_b > static_cast<size_t>(dev.smem_optin)) {
     return fail(RKV_ERR_UNSUPPORTED, "selector tiles do not fit in shared memory");
   }
+  if (decode && fixed_parts_a == 0 && instances == 1) {
+    plan_fused(pl, dev, heads, group, dim, block_size);
+  }
   if (decode) {
     rc = plan_attention(pl, dev, heads, group, dim, block_size);
     if (rc != RKV_OK) return rc;
@@ -224,7 +271,12 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
     return at;
   };
   const size_t rowsg = static_cast<size_t>(rows) * group;
-  pl->status = take(256);
+  // A fixed 4 KB header for every geometry: the status word, and the fused
+  // selector's per-row barrier words at a fixed place, where no other region
+  // of any geometry writes (they clean themselves after every round, so a
+  // workspace reused for another geometry finds them consistent).
+  pl->status = take(kHeaderBytes);
+  if (pl->fused) pl->rows_words = kRowWords;
   // (Under a sequence split phase A writes into the exchange slab instead.)
   pl->lse = take(fixed_parts_a > 0 ? 0 : rowsg * pl->parts_a * pl->slots_a * 4 * 4);
   pl->z = take(rowsg * blocks * 4);
@@ -485,6 +537,70 @@ int check_workspace(const Plan& pl, void* ws, size_t size) {
 template <typename T>
 T* at(void* ws, size_t off) {
   return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
+}
+
+// rkv_decode's selector as one fused launch (phases A and B and the anchored
+// pages; see rkv_fused.cu).
+int run_fused_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype,
+                       int64_t group, float eps, int reduction, const uint8_t* anchor,
+                       uint8_t* mask, void* ws, cudaStream_t stream) {
+  const int D = static_cast<int>(s->head_dim);
+  const int DP = padded_dim(D);
+  const int64_t H = s->heads, B = s->block_size;
+  FusedMaps maps;
+  int rc = summary_maps(s, &maps.key_mean, &maps.ellipsoid, &maps.value_mean);
+  if (rc != RKV_OK) return rc;
+  const bool paged = s->page_table != nullptr;
+  const int64_t pool_heads = paged ? H / std::max<int64_t>(1, s->sequences) : H;
+  rc = pages_map(&maps.key_pages, s->key_pages, D, B, pool_heads, paged ? s->pool_pages : s->blocks,
+                 paged ? s->key_token_stride : D, s->key_page_head_stride,
+                 paged ? s->key_page_stride : B * D, "key_pages");
+  if (rc != RKV_OK) return rc;
+  rc = pages_map(&maps.value_pages, s->value_pages, D, B, pool_heads,
+                 paged ? s->pool_pages : s->blocks, paged ? s->value_token_stride : D,
+                 s->value_page_head_stride, paged ? s->value_page_stride : B * D, "value_pages");
+  if (rc != RKV_OK) return rc;
+  FusedParams p = {};
+  p.query = q;
+  p.query_f32 = qdtype == RKV_DTYPE_F32;
+  p.dim = D;
+  p.counts = s->counts;
+  p.heads = static_cast<int>(H);
+  p.group = static_cast<int>(group);
+  p.blocks = static_cast<int>(s->blocks);
+  p.tiles = pl.tiles;
+  p.parts = pl.parts_b;
+  p.tcap = pl.tpc_b;
+  p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
+  p.eps = eps;
+  p.reduction = reduction;
+  p.z = at<float>(ws, pl.z);
+  p.delta = at<float>(ws, pl.delta);
+  p.lse = at<float>(ws, pl.lse);
+  p.value_norm = s->value_norm;
+  p.max_value_norm = s->max_value_norm;
+  p.anchor = anchor;
+  p.mask = mask;
+  p.split_probs = qdtype == RKV_DTYPE_F32;
+  p.stream_anchors = anchor != nullptr ? 1 : 0;
+  p.seg_count = at<int>(ws, pl.seg_count);
+  p.sel_ids = at<int>(ws, pl.sel_ids);
+  p.seg_cap = pl.seg_cap;
+  p.rep_m = at<float>(ws, pl.rep_m);
+  p.rep_l = at<float>(ws, pl.rep_l);
+  p.rep_o = at<float>(ws, pl.rep_o);
+  p.row_arrive = at<unsigned>(ws, pl.rows_words);
+  p.row_gen = p.row_arrive + kMaxFusedRows;
+  p.seq = seq_layout(s);
+  p.page = static_cast<int>(B);
+  p.prompt_length = static_cast<int>(s->prompt_length);
+  p.page_table = s->page_table;
+  p.page_table_stride = static_cast<int>(paged ? s->page_table_stride : 0);
+  p.pool_pages = static_cast<int>(paged ? s->pool_pages : s->blocks);
+  p.status = at<int>(ws, pl.status);
+  const cudaError_t err = launch_fused(maps, p, DP, pl.warps_f, pl.smem_f, stream, true);
+  if (err != cudaSuccess) return cuda_fail(err, "fused selector launch");
+  return RKV_OK;
 }
 
 // Phases A and B shared by rkv_select and rkv_decode.
@@ -1037,9 +1153,23 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
   if (rc != RKV_OK) return rc;
   if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
-                    selected, 0, workspace, true, phases, st, split);
-  if (rc != RKV_OK) return rc;
+  if (pl.fused) {
+    // One launch serves phases A and B; they are requested together.
+    const unsigned sel = phases & (RKV_PHASE_STATS | RKV_PHASE_FINAL);
+    if (sel == RKV_PHASE_STATS || sel == RKV_PHASE_FINAL) {
+      return fail(RKV_ERR_INVALID_ARGUMENT,
+                  "the fused selector runs phases STATS and FINAL together");
+    }
+    if (sel != 0) {
+      rc = run_fused_selector(pl, summary, query, query_dtype, group, eps, reduction,
+                              anchor_mask, selected, workspace, st);
+      if (rc != RKV_OK) return rc;
+    }
+  } else {
+    rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
+                      selected, 0, workspace, true, phases, st, split);
+    if (rc != RKV_OK) return rc;
+  }
   return attend_and_combine(pl, summary, query, query_dtype, group, key_suffix, value_suffix,
                             suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
                             value_suffix_head_stride, value_suffix_token_stride, suffix_length,
@@ -1206,6 +1336,22 @@ int rkv_decode_dense(const rkv_summary* pages, const void* query, int query_dtyp
                             suffix_length_host, output, workspace,
                             RKV_PHASE_ATTEND | RKV_PHASE_COMBINE, true,
                             static_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+void rkv_set_fused_selector(int enable) { g_fused_selector.store(enable ? 1 : 0); }
+
+int rkv_decode_kernel_count(int64_t heads, int64_t group, int64_t blocks, int64_t head_dim,
+                            int64_t block_size) {
+  if (heads <= 0 || group <= 0 || group > kMaxGroup || blocks <= 0 || !supported_dim(head_dim) ||
+      !supported_block(block_size))
+    return 0;
+  Plan pl;
+  if (make_plan(&pl, heads, group, blocks, head_dim, block_size, 1, true) != RKV_OK) return 0;
+  return pl.fused ? 3 : 4;
 }
 
 }  // extern "C"

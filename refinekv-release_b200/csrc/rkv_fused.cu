@@ -1,0 +1,732 @@
+// Fused selector with in-kernel streaming of the anchored pages
+// (reference: src/refinekv/reference.py:10-73 for the math; the reference's
+// GPU form runs it as separate Triton kernels, kernels/selection.py:47-223
+// and kernels/attention.py:13-329).
+//
+// One CTA per (KV-head row, part); part k owns the tiles
+// [tiles*k/parts, tiles*(k+1)/parts) of its row, and rows x parts never
+// exceeds the SM count, so every CTA of the grid is resident at once (the
+// host checks it).  A CTA runs, for its tiles:
+//   1. phase A: z and delta of every (group row, block) from the key-mean and
+//      ellipsoid tiles (TMA, mma.sync), stored for phase B, and one log-sum-
+//      exp partial per warp;
+//   2. a per-row barrier (arrival counter + generation word in the
+//      workspace; bounded wait) until every part of the row has written its
+//      partials;
+//   3. phase B: row-global log Z / log C, risk and GQA decision of every
+//      block, the mask, and the compacted list of the selected blocks that
+//      the attention kernel reads -- minus the anchored blocks;
+//   4. the anchored pages of its tiles (they are selected whatever the
+//      decision: selected |= anchor, reference.py:54-55) and the
+//      representatives of its unselected blocks, both into one running
+//      softmax partial per warp, merged into the CTA's partial.
+// The attention kernel then streams only the non-anchored selected pages and
+// the suffix, and the combine merges everything as before.  Anchored pages
+// are attended by the same arithmetic as the attention kernel's
+// (attend-tile helpers of rkv_device.cuh); only the order in which the
+// partials are summed differs.
+#include "rkv_device.cuh"
+#include "rkv_kernels.h"
+#include "rkv_risk.cuh"
+
+namespace rkv {
+namespace {
+
+// Shared-memory layout (also sized by the host): a TMA slice per warp, two
+// mbarriers per warp, row normalisers, per-tile bit masks and lists, the
+// anchored-block list.  The warps' final partials are parked in the slices.
+struct FusedLayout {
+  size_t bars, norms, flags, bits, anchored, bytes;
+  __host__ __device__ FusedLayout(int warps, int slice, int tcap) {
+    size_t off = static_cast<size_t>(warps) * slice;
+    bars = off;
+    off += round16(static_cast<size_t>(warps) * 2 * 8);
+    norms = off;
+    off += 2 * kMaxGroup * 4;
+    flags = off;
+    off += 8 * 4;
+    bits = off;  // sel, rep, anc bits [tcap] each; offsets [tcap+1]; rep list [tcap]; anc offsets [tcap+1]
+    off += round16(static_cast<size_t>(tcap) * 4 * 5 + 8);
+    anchored = off;
+    off += round16(static_cast<size_t>(tcap) * kSelectTile * 4);
+    bytes = off + kSmemSlack;
+  }
+};
+
+template <int D, int R>
+struct FusedShape {
+  static constexpr int kSel = kSelectTile * D * 2;  // one key-mean / ellipsoid / value-mean tile
+  static constexpr int kPage = R * D * 2;           // one K or V page
+  static constexpr int kSlice = (2 * kSel > 2 * kPage ? 2 * kSel : 2 * kPage);
+};
+
+// Bounded wait for a generation word to move past `seen`; false on timeout.
+__device__ __forceinline__ bool wait_generation(const unsigned* word, unsigned seen) {
+  const unsigned long long start = global_ns();
+  while (true) {
+    unsigned now;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(now) : "l"(word) : "memory");
+    if (now != seen) return true;
+    if (global_ns() - start > kWaitLimitNs) return false;
+    __nanosleep(64);
+  }
+}
+
+// PACK4: group of at most 4 rows (q and q^2 share one n8 tile); GM: group
+// rows evaluated per block in phase B (padded to 4, 8 or 16).
+template <int D, int R, int NT, bool PACK4, int GM>
+__global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ FusedMaps maps,
+                                                       const FusedParams p) {
+  constexpr int T = kSelectTile;
+  constexpr int kSel = FusedShape<D, R>::kSel;
+  constexpr int kPage = FusedShape<D, R>::kPage;
+  constexpr int kSlice = FusedShape<D, R>::kSlice;
+  constexpr int G8 = NT * 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const FusedLayout lay(W, kSlice, p.tcap);
+  uint8_t* slice = smem + static_cast<size_t>(warp) * kSlice;
+  uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + lay.bars) + warp * 2;
+  uint64_t* bar_b = bar_a + 1;
+  float* lz = reinterpret_cast<float*>(smem + lay.norms);
+  float* lc = lz + kMaxGroup;
+  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 anchored
+  uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.bits);
+  uint32_t* rep_bits = sel_bits + p.tcap;
+  uint32_t* anc_bits = rep_bits + p.tcap;
+  int* offsets = reinterpret_cast<int*>(anc_bits + p.tcap);  // [tcap + 1]
+  int* rep_list = offsets + p.tcap + 1;                     // [tcap]
+  int* anc_off = rep_list + p.tcap;                         // [tcap + 1]
+  int* anchored = reinterpret_cast<int*>(smem + lay.anchored);
+
+  const int h = blockIdx.x, part = blockIdx.y;
+  const int t_lo = static_cast<int>(static_cast<long long>(p.tiles) * part / p.parts);
+  const int t_hi = static_cast<int>(static_cast<long long>(p.tiles) * (part + 1) / p.parts);
+  const int n_t = t_hi - t_lo;
+  const int64_t* counts = p.counts + static_cast<size_t>(p.seq.sequence(h)) * p.blocks;
+  const char* q = static_cast<const char*>(p.query) +
+                  static_cast<size_t>(h) * p.group * p.dim * (p.query_f32 ? 4 : 2);
+
+  if (lane == 0) {
+    mbar_init(bar_a, 1);
+    mbar_init(bar_b, 1);
+    mbar_fence_init();
+    // The summaries do not change during decode: this warp's first tile goes
+    // to L2 before the dependency wait.
+    if (warp < n_t) {
+      tma_prefetch_tile<D>(&maps.key_mean, (t_lo + warp) * T, h);
+      tma_prefetch_tile<D>(&maps.ellipsoid, (t_lo + warp) * T, h);
+    }
+  }
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&maps.key_mean);
+    tma_prefetch_desc(&maps.ellipsoid);
+    tma_prefetch_desc(&maps.value_mean);
+    tma_prefetch_desc(&maps.key_pages);
+    tma_prefetch_desc(&maps.value_pages);
+    for (int i = 0; i < 8; ++i) flags[i] = 0;
+  }
+  for (int i = threadIdx.x; i * 128 < p.group * p.dim * (p.query_f32 ? 4 : 2); i += blockDim.x) {
+    prefetch_l2(q + i * 128);
+  }
+  __syncthreads();
+  pdl_wait();
+  // This row's barrier generation before our arrival (it can only move once
+  // every part, this one included, has arrived).
+  unsigned seen_gen = 0;
+  if (threadIdx.x == 0) {
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(seen_gen) : "l"(p.row_gen + h)
+                 : "memory");
+  }
+  const int blocks_h = p.seq.blocks(h, p.blocks);
+  const int n_stat = max(0, min(t_hi, (blocks_h + T - 1) / T) - t_lo);  // tiles with real blocks
+  const uint64_t policy = l2_evict_first_policy();
+  uint32_t uses_a = 0, uses_b = 0;  // completed waits per barrier (parity = uses & 1)
+  bool aborted = false;
+  auto timeout = [&]() {
+    if (lane == 0) atomicOr(p.status, kStatusTimeout);
+    aborted = true;
+  };
+
+  // Anchored blocks of the range, one bit per block (known before any statistics).
+  const bool stream = p.stream_anchors != 0 && p.anchor != nullptr;
+  for (int k = warp; k < n_t; k += W) {
+    const int b = (t_lo + k) * T + lane;
+    const bool a = stream && b < blocks_h && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+    const uint32_t bits = __ballot_sync(0xffffffffu, a);
+    if (lane == 0) anc_bits[k] = bits;
+  }
+
+  // ---------------- phase A: statistics of this warp's tiles ----------------
+  {
+    int lane_rows[T / 16][2];
+    constexpr int kHalves = PACK4 ? 1 : 2;
+#pragma unroll
+    for (int mt = 0; mt < T / 16; ++mt) {
+      lane_rows[mt][0] = mt * 16 + (lane >> 2) + (PACK4 && ((lane >> 1) & 1) ? 8 : 0);
+      lane_rows[mt][1] = lane_rows[mt][0] + 8;
+    }
+    uint32_t qk[D / 16][NT][2], q2[D / 16][NT][2];
+    uint32_t packed[PACK4 ? 2 * D / 16 : 1][2];
+    if constexpr (PACK4) {
+      uint32_t q1[D / 16][1][2];
+      load_query_frags<D, 1>(q1, q, p.query_f32, p.group, p.dim, lane & 15, false);
+      pack4_frags<D>(q1, packed, lane);
+    } else {
+      load_query_frags<D, NT>(qk, q, p.query_f32, p.group, p.dim, lane, false);
+      square_frags<D, NT>(qk, q2);
+    }
+    float zm[NT][2], zs[NT][2], cm[NT][2], cs[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        zm[nt][j] = cm[nt][j] = -INFINITY;
+        zs[nt][j] = cs[nt][j] = 0.f;
+      }
+    for (int k = warp; k < n_stat && !aborted; k += W) {
+      const int tile = t_lo + k;
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(bar_a, 2 * kSel);
+        tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
+        tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
+        if (k + W < n_stat) {  // one stage per warp: warm L2 with the next tile meanwhile
+          tma_prefetch_tile<D>(&maps.key_mean, (tile + W) * T, h);
+          tma_prefetch_tile<D>(&maps.ellipsoid, (tile + W) * T, h);
+        }
+      }
+      long long cnt[T / 16][2];
+#pragma unroll
+      for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+        for (int hf = 0; hf < kHalves; ++hf) {
+          const int b = tile * T + lane_rows[mt][hf];
+          cnt[mt][hf] = b < blocks_h ? __ldg(counts + b) : 1;
+        }
+      if (!warp_wait(bar_a, uses_a & 1)) {
+        timeout();
+        mbar_wait(bar_a, uses_a & 1);  // bounded: the copy must land before the CTA exits
+        break;
+      }
+      ++uses_a;
+      const uint32_t base = smem_addr(slice);
+      float sc[T / 16][NT][4], pr[T / 16][NT][4];
+      int row_of[T / 16][2];
+      int g_base;
+      if constexpr (PACK4) {
+        float acc[T / 16][4];
+        score_tile_pair<T, D>(base, base + kSel, packed, acc, lane);
+        const bool upper = (lane >> 1) & 1;
+#pragma unroll
+        for (int mt = 0; mt < T / 16; ++mt) {
+          const float send0 = upper ? acc[mt][0] : acc[mt][2];
+          const float send1 = upper ? acc[mt][1] : acc[mt][3];
+          const float recv0 = __shfl_xor_sync(0xffffffffu, send0, 2);
+          const float recv1 = __shfl_xor_sync(0xffffffffu, send1, 2);
+          sc[mt][0][0] = upper ? recv0 : acc[mt][0];
+          sc[mt][0][1] = upper ? recv1 : acc[mt][1];
+          pr[mt][0][0] = upper ? acc[mt][2] : recv0;
+          pr[mt][0][1] = upper ? acc[mt][3] : recv1;
+          row_of[mt][0] = mt * 16 + (lane >> 2) + (upper ? 8 : 0);
+        }
+        g_base = 2 * (lane & 1);
+      } else {
+        score_tile<T, D, NT>(base, qk, sc, lane);
+        score_tile<T, D, NT>(base + kSel, q2, pr, lane);
+#pragma unroll
+        for (int mt = 0; mt < T / 16; ++mt) {
+          row_of[mt][0] = mt * 16 + (lane >> 2);
+          row_of[mt][1] = row_of[mt][0] + 8;
+        }
+        g_base = 0;
+      }
+      __syncwarp();
+      float zv[T / 16][NT][4], cv[T / 16][NT][4];
+#pragma unroll
+      for (int mt = 0; mt < T / 16; ++mt) {
+#pragma unroll
+        for (int hf = 0; hf < kHalves; ++hf) {
+          const int b = tile * T + row_of[mt][hf];
+          const float log_count = b < blocks_h ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
+#pragma unroll
+          for (int jc = 0; jc < 2; ++jc) {
+            const int c = 2 * hf + jc;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const int g = PACK4 ? g_base + jc : nt * 8 + 2 * (lane & 3) + jc;
+              zv[mt][nt][c] = -INFINITY;
+              cv[mt][nt][c] = -INFINITY;
+              if (b >= blocks_h || g >= p.group) continue;
+              const float score = sc[mt][nt][c] * p.scale;
+              const float proj = pr[mt][nt][c];
+              const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
+              const float z = score + log_count;
+              const size_t rowg = static_cast<size_t>(h) * p.group + g;
+              p.z[rowg * p.blocks + b] = z;
+              p.delta[rowg * p.blocks + b] = delta;
+              zv[mt][nt][c] = z;
+              cv[mt][nt][c] = z + log_cosh(delta);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int jc = 0; jc < 2; ++jc) {
+          float tz = -INFINITY, tc = -INFINITY;
+          bool nan = false;
+#pragma unroll
+          for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+            for (int hf = 0; hf < kHalves; ++hf) {
+              const float a = zv[mt][nt][2 * hf + jc], b = cv[mt][nt][2 * hf + jc];
+              tz = fmaxf(tz, a);
+              tc = fmaxf(tc, b);
+              nan |= (a != a) || (b != b);
+            }
+          float sz = 0.f, sc2 = 0.f;
+          const float rz = tz == -INFINITY ? 0.f : tz, rc = tc == -INFINITY ? 0.f : tc;
+#pragma unroll
+          for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+            for (int hf = 0; hf < kHalves; ++hf) {
+              sz += fexp(zv[mt][nt][2 * hf + jc] - rz);
+              sc2 += fexp(cv[mt][nt][2 * hf + jc] - rc);
+            }
+          if (nan) sz = sc2 = NAN;
+          lse_merge(zm[nt][jc], zs[nt][jc], tz, sz);
+          lse_merge(cm[nt][jc], cs[nt][jc], tc, sc2);
+        }
+    }
+    // One (max, sum) pair per warp and row (empty for a warp without tiles).
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float mz = zm[nt][j], mc = cm[nt][j];
+#pragma unroll
+        for (int off = PACK4 ? 2 : 4; off < 32; off <<= 1) {
+          mz = fmaxf(mz, __shfl_xor_sync(0xffffffffu, mz, off));
+          mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+        }
+        const float rz = mz == -INFINITY ? 0.f : mz, rc = mc == -INFINITY ? 0.f : mc;
+        float sz = zs[nt][j] == 0.f ? 0.f : zs[nt][j] * fexp(zm[nt][j] - rz);
+        float sc = cs[nt][j] == 0.f ? 0.f : cs[nt][j] * fexp(cm[nt][j] - rc);
+#pragma unroll
+        for (int off = PACK4 ? 2 : 4; off < 32; off <<= 1) {
+          sz += __shfl_xor_sync(0xffffffffu, sz, off);
+          sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        }
+        const bool writer = PACK4 ? lane < 2 : lane < 4;
+        const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
+        if (writer && g < p.group) {
+          float* out = p.lse + ((static_cast<size_t>(h) * p.group + g) * p.parts * W +
+                                static_cast<size_t>(part) * W + warp) * 4;
+          *reinterpret_cast<float4*>(out) = make_float4(mz, sz, mc, sc);
+        }
+      }
+  }
+  __syncthreads();
+
+  // ---------------- per-row barrier ----------------------------------------
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's z, delta and partials before the arrival
+    const unsigned before = atomicAdd(p.row_arrive + h, 1u);
+    if (before == static_cast<unsigned>(p.parts) - 1u) {
+      atomicExch(p.row_arrive + h, 0u);
+      __threadfence();
+      atomicAdd(p.row_gen + h, 1u);
+    }
+    if (!wait_generation(p.row_gen + h, seen_gen)) {
+      atomicOr(p.status, kStatusTimeout);
+      flags[3] = 1;
+    }
+  }
+  __syncthreads();
+  // Every CTA that gets here was resident; the attention grid may launch once
+  // all have (it then waits for this grid's completion before reading).
+  pdl_launch_dependents();
+
+  // ---------------- phase B: row normalisers, decisions ---------------------
+  for (int g = warp; g < p.group; g += W) {
+    const float* in = p.lse + (static_cast<size_t>(h) * p.group + g) * p.parts * W * 4;
+    float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
+    const int n_part = p.parts * W;
+    for (int k0 = lane; k0 < n_part; k0 += 32 * 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int k = k0 + 32 * u;
+        v[u] = k < n_part ? __ldcg(reinterpret_cast<const float4*>(in + 4 * k))
+                          : make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        lse_merge(m0, s0, v[u].x, v[u].y);
+        lse_merge(m1, s1, v[u].z, v[u].w);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m0, off);
+      const float os = __shfl_xor_sync(0xffffffffu, s0, off);
+      const float pm = __shfl_xor_sync(0xffffffffu, m1, off);
+      const float ps = __shfl_xor_sync(0xffffffffu, s1, off);
+      lse_merge(m0, s0, om, os);
+      lse_merge(m1, s1, pm, ps);
+    }
+    if (lane == 0) {
+      const float zl = m0 + flog(s0), cl = m1 + flog(s1);
+      lz[g] = zl;
+      lc[g] = cl;
+      if (!finite(zl) || !finite(cl)) atomicOr(&flags[0], 1);
+    }
+  }
+  __syncthreads();
+  const bool bad_global = flags[0] != 0;
+  const float vmax = __ldg(p.max_value_norm + h);
+  for (int k = warp; k < n_t; k += W) {
+    const int t = t_lo + k;
+    const int b = t * T + lane;
+    const bool valid = b < blocks_h;
+    bool sel = false, anc = false;
+    if (valid) {
+      float zr[GM], dr[GM];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        const size_t row = static_cast<size_t>(h) * p.group + (g < p.group ? g : 0);
+        zr[g] = __ldcg(p.z + row * p.blocks + b);
+        dr[g] = __ldcg(p.delta + row * p.blocks + b);
+      }
+      const float vn = __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
+      anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+      float agg = p.reduction == kMax ? -INFINITY : 0.f;
+      bool any = false, bad = false;
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g >= p.group) continue;
+        const float r = block_risk(zr[g], dr[g], lz[g], lc[g], vn, vmax);
+        bad |= !finite(r);
+        if (p.reduction == kMean) {
+          agg += r;
+        } else if (p.reduction == kMax) {
+          agg = (r > agg || r != r) ? r : agg;
+        } else {
+          any |= r > p.eps;
+        }
+      }
+      bool dec;
+      if (p.reduction == kMean) {
+        dec = agg / static_cast<float>(p.group) > p.eps;
+      } else if (p.reduction == kMax) {
+        dec = agg > p.eps;
+      } else {
+        dec = any;
+      }
+      sel = dec || bad || bad_global || anc;
+    }
+    if (b < p.blocks) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
+    const uint32_t listed = __ballot_sync(0xffffffffu, sel && !(stream && anc));
+    const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
+    if (lane == 0) {
+      sel_bits[k] = listed;
+      rep_bits[k] = reps;
+    }
+  }
+  __syncthreads();
+
+  // Compaction: warp 0 the attention list and the tiles with representatives,
+  // warp 1 (or 0) the anchored list; deterministic (block order).
+  if (warp == 0) {
+    int acc = 0, nreps = 0;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int c = k < n_t ? __popc(sel_bits[k]) : 0;
+      const bool has_rep = k < n_t && rep_bits[k] != 0u;
+      int incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) offsets[k] = acc + incl - c;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
+      const uint32_t rb = __ballot_sync(0xffffffffu, has_rep);
+      if (has_rep) rep_list[nreps + __popc(rb & ((1u << lane) - 1u))] = k;
+      nreps += __popc(rb);
+    }
+    if (lane == 0) {
+      flags[1] = nreps;
+      p.seg_count[h * p.parts + part] = acc;
+    }
+  }
+  if (warp == (W > 1 ? 1 : 0)) {
+    int acc = 0;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int c = k < n_t ? __popc(anc_bits[k]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) anc_off[k] = acc + incl - c;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) flags[2] = acc;
+  }
+  __syncthreads();
+  {
+    int* ids = p.sel_ids + (static_cast<size_t>(h) * p.parts + part) * p.seg_cap;
+    for (int k = warp; k < n_t; k += W) {
+      const uint32_t below = (1u << lane) - 1u;
+      const uint32_t sb = sel_bits[k], ab = anc_bits[k];
+      const int b = (t_lo + k) * T + lane;
+      if ((sb >> lane) & 1u) ids[offsets[k] + __popc(sb & below)] = b;
+      if ((ab >> lane) & 1u) anchored[anc_off[k] + __popc(ab & below)] = b;
+    }
+  }
+  __syncthreads();
+
+  // ---------------- anchored pages, then representatives --------------------
+  const int n_anc = flags[2], n_reps = flags[1];
+  float m[NT][2], l[NT][2], o[D / 16][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = -INFINITY;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
+  }
+  const bool split = p.split_probs != 0;
+  const int my_anc = n_anc > warp ? (n_anc - warp + W - 1) / W : 0;
+  if (my_anc > 0) {
+    uint32_t qb[D / 16][NT][2];
+    load_query_frags<D, NT>(qb, q, p.query_f32, p.group, p.dim, lane, false);
+    const int prompt_h = p.seq.prompt(h, p.prompt_length);
+    const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
+    // item j of this warp: block, physical page, valid rows
+    auto item = [&](int j, int& page, int& valid) {
+      const int block = anchored[warp + j * W];
+      page = block;
+      if (p.page_table != nullptr) {
+        page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride +
+                     block);
+        if (page < 0 || page >= p.pool_pages) {
+          if (lane == 0) atomicOr(p.status, kStatusBadInput);
+          page = 0;
+        }
+      }
+      valid = min(R, prompt_h - block * R);
+    };
+    auto issue_k = [&](int page) {
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(bar_a, kPage);
+        tma_page_hint<D>(slice, &maps.key_pages, bar_a, pool_head, page, R, policy);
+      }
+    };
+    auto issue_v = [&](int page) {
+      if (lane == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(bar_b, kPage);
+        tma_page_hint<D>(slice + kPage, &maps.value_pages, bar_b, pool_head, page, R, policy);
+      }
+    };
+    int page, valid;
+    item(0, page, valid);
+    issue_k(page);
+    issue_v(page);
+    int issued_a = 1, issued_b = 1;
+    for (int j = 0; j < my_anc && !aborted; ++j) {
+      if (!warp_wait(bar_a, uses_a & 1)) {
+        timeout();
+        break;
+      }
+      ++uses_a;
+      float logit[R / 16][NT][4];
+      score_tile<R, D, NT>(smem_addr(slice), qb, logit, lane);
+#pragma unroll
+      for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            logit[mt][nt][c] = r < valid ? logit[mt][nt][c] * p.scale : -INFINITY;
+        }
+      __syncwarp();
+      int next_page = 0, next_valid = 0;
+      const bool more = j + 1 < my_anc;
+      if (more) {
+        item(j + 1, next_page, next_valid);
+        issue_k(next_page);
+        ++issued_a;
+      }
+      softmax_update<R, D, NT>(logit, m, l, o);
+      uint32_t hi[R / 16][NT][2], lo[R / 16][NT][2];
+      prob_frags<R, NT>(logit, hi, lo, split);
+      if (!warp_wait(bar_b, uses_b & 1)) {
+        timeout();
+        break;
+      }
+      ++uses_b;
+      accumulate_values<R, D, NT>(smem_addr(slice + kPage), hi, o, lane);
+      if (split) accumulate_values<R, D, NT>(smem_addr(slice + kPage), lo, o, lane);
+      __syncwarp();
+      if (more) {
+        issue_v(next_page);
+        ++issued_b;
+      }
+      valid = next_valid;
+    }
+    // Copies still in flight after a timeout must land before the slice is reused.
+    for (; uses_a < static_cast<uint32_t>(issued_a); ++uses_a) mbar_wait(bar_a, uses_a & 1);
+    for (; uses_b < static_cast<uint32_t>(issued_b); ++uses_b) mbar_wait(bar_b, uses_b & 1);
+  }
+  // Representatives of this warp's tiles (value-mean tiles double-buffered
+  // on the two barriers); logit z, value the block's value mean.
+  const int my_reps = n_reps > warp ? (n_reps - warp + W - 1) / W : 0;
+  if (my_reps > 0 && !aborted) {
+    auto issue_rep = [&](int j) {
+      if (lane == 0) {
+        uint64_t* bar = (j & 1) ? bar_b : bar_a;
+        fence_proxy_async();
+        mbar_expect_tx(bar, kSel);
+        tma_tile_hint<D>(slice + (j & 1) * kSel, &maps.value_mean, bar,
+                         (t_lo + rep_list[warp + j * W]) * T, h, T, policy);
+      }
+    };
+    auto load_logits = [&](int j, float (&lg)[T / 16][NT][4]) {
+      const bool have = j < my_reps;
+      const int k = have ? rep_list[warp + j * W] : 0;
+      const uint32_t reps = have ? rep_bits[k] : 0u;
+      const int tile = t_lo + k;
+#pragma unroll
+      for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+          const bool rep = (reps >> r) & 1u;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
+            lg[mt][nt][c] =
+                (rep && g < p.group)
+                    ? __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r)
+                    : -INFINITY;
+          }
+        }
+    };
+    int issued_a = uses_a, issued_b = uses_b;
+    issue_rep(0);
+    ++issued_a;
+    if (my_reps > 1) {
+      issue_rep(1);
+      ++issued_b;
+    }
+    float next_logit[T / 16][NT][4];
+    load_logits(0, next_logit);
+    for (int j = 0; j < my_reps; ++j) {
+      const bool odd = j & 1;
+      uint64_t* bar = odd ? bar_b : bar_a;
+      uint32_t& uses = odd ? uses_b : uses_a;
+      if (!warp_wait(bar, uses & 1)) {
+        timeout();
+        break;
+      }
+      ++uses;
+      float logit[T / 16][NT][4];
+#pragma unroll
+      for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) logit[mt][nt][c] = next_logit[mt][nt][c];
+      load_logits(j + 1, next_logit);
+      attend_tile<T, D, NT>(logit, smem_addr(slice + (odd ? kSel : 0)), m, l, o, split, lane);
+      __syncwarp();
+      if (j + 2 < my_reps) {
+        issue_rep(j + 2);
+        if (odd) ++issued_b; else ++issued_a;
+      }
+    }
+    for (; uses_a < static_cast<uint32_t>(issued_a); ++uses_a) mbar_wait(bar_a, uses_a & 1);
+    for (; uses_b < static_cast<uint32_t>(issued_b); ++uses_b) mbar_wait(bar_b, uses_b & 1);
+  }
+  reduce_l<NT>(l);
+  __syncthreads();  // every slice is idle: park the warps' partials there
+  float* st_m = reinterpret_cast<float*>(smem);
+  float* st_l = st_m + W * G8;
+  float* st_o = st_l + W * G8;
+  stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
+  __syncthreads();
+  const size_t slot = static_cast<size_t>(h) * p.parts + part;
+  merge_stashed<D>(st_m, st_l, st_o, W, G8, p.rep_m + slot * G8, p.rep_l + slot * G8,
+                   p.rep_o + slot * G8 * D, threadIdx.x, blockDim.x);
+}
+
+template <int D, int R, int NT, bool PACK4, int GM>
+cudaError_t launch_t(const FusedMaps& maps, const FusedParams& p, int warps, size_t smem,
+                     cudaStream_t stream, bool pdl) {
+  auto kernel = fused_kernel<D, R, NT, PACK4, GM>;
+  cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
+  if (err != cudaSuccess) return err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.heads, p.parts);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, maps, p);
+}
+
+template <int D, int R>
+cudaError_t launch_g(const FusedMaps& maps, const FusedParams& p, int warps, size_t smem,
+                     cudaStream_t stream, bool pdl) {
+  if (p.group <= 4) return launch_t<D, R, 1, true, 4>(maps, p, warps, smem, stream, pdl);
+  if (p.group <= 8) return launch_t<D, R, 1, false, 8>(maps, p, warps, smem, stream, pdl);
+  return launch_t<D, R, 2, false, 16>(maps, p, warps, smem, stream, pdl);
+}
+
+template <int D>
+cudaError_t launch_r(const FusedMaps& maps, const FusedParams& p, int warps, size_t smem,
+                     cudaStream_t stream, bool pdl) {
+  switch (p.page) {
+    case 16: return launch_g<D, 16>(maps, p, warps, smem, stream, pdl);
+    case 32: return launch_g<D, 32>(maps, p, warps, smem, stream, pdl);
+    case 64: return launch_g<D, 64>(maps, p, warps, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap) {
+  (void)group;
+  const int sel = kSelectTile * dim * 2, pg = page * dim * 2;
+  const int slice = 2 * sel > 2 * pg ? 2 * sel : 2 * pg;
+  return FusedLayout(warps, slice, tcap).bytes;
+}
+
+cudaError_t launch_fused(const FusedMaps& maps, const FusedParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl) {
+  switch (dim) {
+    case 64: return launch_r<64>(maps, p, warps, smem, stream, pdl);
+    case 128: return launch_r<128>(maps, p, warps, smem, stream, pdl);
+    case 192: return launch_r<192>(maps, p, warps, smem, stream, pdl);
+    case 256: return launch_r<256>(maps, p, warps, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace rkv

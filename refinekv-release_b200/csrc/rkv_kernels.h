@@ -115,6 +115,53 @@ struct FinalParams {
   int* status;
 };
 
+// Fused selector (rkv_fused.cu): phases A and B of one (row, part) tile
+// range in one CTA with a per-row barrier between them, plus the exact
+// attention of the range's anchored pages, folded into the CTA's
+// representative partial.
+struct FusedMaps {
+  CUtensorMap key_mean;     // [32 x 64] bf16 boxes, like StatsMaps / FinalMaps
+  CUtensorMap ellipsoid;
+  CUtensorMap value_mean;
+  CUtensorMap key_pages;    // 4-D page maps, like AttendMaps
+  CUtensorMap value_pages;
+};
+
+struct FusedParams {
+  const void* query;  // (heads, group, dim)
+  int query_f32;
+  int dim;            // real head dim
+  const int64_t* counts;
+  int heads, group, blocks, tiles;
+  int parts;          // CTAs per row; part k owns tiles [tiles*k/parts, tiles*(k+1)/parts)
+  int tcap;           // the largest tile count of a part (shared-memory tables)
+  float scale, eps;
+  int reduction;
+  float* z;           // (heads*group, blocks)
+  float* delta;
+  float* lse;         // (heads*group, parts * warps, 4)
+  const float* value_norm;
+  const float* max_value_norm;
+  const uint8_t* anchor;  // (heads, blocks) or null
+  uint8_t* mask;
+  int split_probs;
+  int stream_anchors;     // anchored pages attended here; the attention list omits them
+  int* seg_count;         // (heads, parts): blocks of the attention list per part
+  int* sel_ids;           // (heads, parts, seg_cap)
+  int seg_cap;
+  float* rep_m;           // (heads, parts, G8): representatives and anchored pages
+  float* rep_l;
+  float* rep_o;           // (heads, parts, dim, G8)
+  unsigned* row_arrive;   // (heads,) per-row barrier: arrivals of this call
+  unsigned* row_gen;      // (heads,) per-row barrier: completed generations
+  SeqLayout seq;
+  int page, prompt_length;
+  const int32_t* page_table;
+  int page_table_stride;
+  int pool_pages;
+  int* status;
+};
+
 struct AttendMaps {
   CUtensorMap key_pages;
   CUtensorMap value_pages;
@@ -207,6 +254,8 @@ cudaError_t launch_final(const FinalMaps& maps, const FinalParams& p, int dim, i
 cudaError_t launch_attend(const AttendMaps& maps, const AttendParams& p, int dim, int warps,
                           size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_combine(const CombineParams& p, int dim, cudaStream_t stream, bool pdl);
+cudaError_t launch_fused(const FusedMaps& maps, const FusedParams& p, int dim, int warps,
+                         size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_merge(const MergeParams& p, int dim, cudaStream_t stream, bool pdl);
 
 // Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
@@ -221,5 +270,6 @@ size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
                          int parts_b);
 size_t combine_smem_bytes(int heads, int parts_b, int group, int max_sources);
+size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap);
 
 }  // namespace rkv

@@ -52,6 +52,8 @@ EXPORTS = (
     "rkv_decode_dense_workspace_size",
     "rkv_decode_dense",
     "rkv_decode_launch_count",
+    "rkv_decode_kernel_count",
+    "rkv_set_fused_selector",
     "rkv_select_split_slab",
     "rkv_select_split",
     "rkv_split_exchange_slabs",
@@ -126,6 +128,8 @@ _SIGNATURES = {
                                         c_ptr, c_ptr, c_i64, c_i64, c_i64, c_i64, c_i64, c_ptr,
                                         c_i64, c_ptr, c_ptr, ctypes.c_size_t, c_ptr]),
     "rkv_decode_launch_count": (ctypes.c_int, [ctypes.c_uint]),
+    "rkv_decode_kernel_count": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "rkv_set_fused_selector": (None, [ctypes.c_int]),
     "rkv_select_split_slab": (ctypes.c_size_t, [c_i64, c_i64, c_i64, c_i64]),
     "rkv_select_split": (ctypes.c_int, [ctypes.POINTER(Summary), c_ptr, ctypes.c_int, c_i64, c_i64,
                                         ctypes.c_float, ctypes.c_int, c_ptr, ctypes.c_int, c_ptr,

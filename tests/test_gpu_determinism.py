@@ -1,7 +1,8 @@
 """Decode is deterministic and free of launch-order races (needs a B200).
 
-The four decode kernels are chained with programmatic dependent launch: each
-may start while its predecessor drains, and the combine reads the
+The decode kernels (the fused selector or the two selector kernels, the
+attention, the combine) are chained with programmatic dependent launch:
+each may start while its predecessor drains, and the combine reads the
 selector's partials before its own dependency wait.  Whatever the overlap,
 the result must be the same bits as running the phases one call at a time
 with the device synchronised in between, and repeated calls (same or fresh
@@ -16,8 +17,17 @@ from refinekv_b200.attention import device_status, select_blocks_union
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-PHASES = (_native.PHASE_STATS, _native.PHASE_FINAL, _native.PHASE_ATTEND,
-          _native.PHASE_COMBINE)
+
+
+def _phases(summary, group):
+    """The launches of one decode, one call each: the fused selector is one launch."""
+    lib = _native.load()
+    if lib.rkv_decode_kernel_count(summary.num_heads, group, summary.num_blocks,
+                                   summary.keys.shape[-1], summary.block_size) == 3:
+        return (_native.PHASE_STATS | _native.PHASE_FINAL, _native.PHASE_ATTEND,
+                _native.PHASE_COMBINE)
+    return (_native.PHASE_STATS, _native.PHASE_FINAL, _native.PHASE_ATTEND,
+            _native.PHASE_COMBINE)
 
 
 def _layer(heads, tokens, dim, group, scale):
@@ -54,7 +64,7 @@ def test_chained_decode_equals_synchronised_phases(heads, tokens, dim, group, sc
     layer = _layer(heads, tokens, dim, group, scale)
     length = torch.full((), 33, device=DEV, dtype=torch.int32)
     ws = {}
-    ref_out, ref_sel = _run(layer, ws, length, PHASES, sync=True)
+    ref_out, ref_sel = _run(layer, ws, length, _phases(layer[0], group), sync=True)
     assert 0 < int(ref_sel.sum()) <= ref_sel.numel()
     for _ in range(3):  # same workspace, back to back without a sync
         out, sel = _run(layer, ws, length)
