@@ -36,19 +36,26 @@ namespace {
 // mbarriers per warp, row normalisers, per-tile bit masks and lists, the
 // anchored-block list.  The warps' final partials are parked in the slices.
 struct FusedLayout {
-  size_t bars, norms, flags, bits, anchored, bytes;
+  size_t bars, norms, flags, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off, anchored,
+      bytes;
   __host__ __device__ FusedLayout(int warps, int slice, int tcap) {
+    const size_t t = static_cast<size_t>(tcap);
     size_t off = static_cast<size_t>(warps) * slice;
-    bars = off;
-    off += round16(static_cast<size_t>(warps) * 2 * 8);
-    norms = off;
-    off += 2 * kMaxGroup * 4;
-    flags = off;
-    off += 8 * 4;
-    bits = off;  // sel, rep, anc bits [tcap] each; offsets [tcap+1]; rep list [tcap]; anc offsets [tcap+1]
-    off += round16(static_cast<size_t>(tcap) * 4 * 5 + 8);
-    anchored = off;
-    off += round16(static_cast<size_t>(tcap) * kSelectTile * 4);
+    auto take = [&](size_t bytes_) {
+      const size_t at_ = off;
+      off += round16(bytes_);
+      return at_;
+    };
+    bars = take(static_cast<size_t>(warps) * 2 * 8);
+    norms = take(2 * kMaxGroup * 4);
+    flags = take(8 * 4);
+    sel_bits = take(t * 4);        // [tcap] uint32
+    rep_bits = take(t * 4);        // [tcap] uint32
+    anc_bits = take(t * 4);        // [tcap] uint32
+    offsets = take((t + 1) * 4);   // [tcap + 1] int
+    rep_list = take(t * 4);        // [tcap] int
+    anc_off = take((t + 1) * 4);   // [tcap + 1] int
+    anchored = take(t * kSelectTile * 4);  // [tcap * 32] int
     bytes = off + kSmemSlack;
   }
 };
@@ -93,13 +100,13 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   float* lz = reinterpret_cast<float*>(smem + lay.norms);
   float* lc = lz + kMaxGroup;
   int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 anchored
-  uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.bits);
-  uint32_t* rep_bits = sel_bits + p.tcap;
-  uint32_t* anc_bits = rep_bits + p.tcap;
-  int* offsets = reinterpret_cast<int*>(anc_bits + p.tcap);  // [tcap + 1]
-  int* rep_list = offsets + p.tcap + 1;                     // [tcap]
-  int* anc_off = rep_list + p.tcap;                         // [tcap + 1]
-  int* anchored = reinterpret_cast<int*>(smem + lay.anchored);
+  uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.sel_bits);  // [tcap]
+  uint32_t* rep_bits = reinterpret_cast<uint32_t*>(smem + lay.rep_bits);  // [tcap]
+  uint32_t* anc_bits = reinterpret_cast<uint32_t*>(smem + lay.anc_bits);  // [tcap]
+  int* offsets = reinterpret_cast<int*>(smem + lay.offsets);             // [tcap + 1]
+  int* rep_list = reinterpret_cast<int*>(smem + lay.rep_list);           // [tcap]
+  int* anc_off = reinterpret_cast<int*>(smem + lay.anc_off);             // [tcap + 1]
+  int* anchored = reinterpret_cast<int*>(smem + lay.anchored);           // [tcap * 32]
 
   const int h = blockIdx.x, part = blockIdx.y;
   const int t_lo = static_cast<int>(static_cast<long long>(p.tiles) * part / p.parts);
