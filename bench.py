@@ -112,9 +112,9 @@ def parse_args():
                          "flow, not the configuration)")
     ap.add_argument("--new-tokens", type=int, default=128,
                     help="--model: generated tokens (the last new-tokens - 3 are timed)")
-    ap.add_argument("--two-kernel-selector", action="store_true",
-                    help="run the selector as its two kernels (stats, final) with every selected "
-                         "page in the attention kernel, instead of the fused selector (A/B)")
+    ap.add_argument("--four-kernel-decode", action="store_true",
+                    help="run each layer-step as the four kernels (selector stats and final, "
+                         "attention, combine) instead of the one-kernel decode (A/B)")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
@@ -543,7 +543,7 @@ def run_b200(args):
     torch.cuda.set_device(dev)
     from refinekv_b200 import _native, parallel
 
-    if args.two_kernel_selector:
+    if args.four_kernel_decode:
         _native.load().rkv_set_fused_selector(0)
     plan = parallel.plan_shards(args.kv_heads * args.batch, args.tokens, args.block_size, world,
                                 rank, args.seq_ranks)
@@ -625,13 +625,11 @@ def run_b200(args):
                   if L.summary.counts.ndim == 2 else L.summary.counts for L in layers]
     sel_tokens = torch.zeros((), device=dev, dtype=torch.int64)
     sel_pages = torch.zeros((), device=dev, dtype=torch.int64)
-    # Tokens of the anchored blocks of each layer (fixed for the whole decode):
-    # with the fused selector those pages are streamed by the selector launch.
-    anchored_tokens = sum(int((L.anchor.to(torch.int64) * counts).sum())
-                          for L, counts in zip(layers, counts_all) if L.anchor is not None)
+    # Anchored blocks of all layers (fixed for the whole decode; the one-kernel
+    # decode streams them before its decisions).
     anchored_pages = sum(int(L.anchor.sum()) for L in layers if L.anchor is not None)
     fused = (not split and lib.rkv_decode_kernel_count(
-        plan.heads, args.group, plan.blocks, args.head_dim, args.block_size) == 3)
+        plan.heads, args.group, plan.blocks, args.head_dim, args.block_size) == 1)
 
     def count_selected():
         nonlocal sel_pages, sel_tokens
@@ -649,6 +647,31 @@ def run_b200(args):
                        workspace=L.workspace, suffix_length=length)
             count_selected()
         attend_ms = [us_per_step / 1e3 / args.layers]
+    elif fused:
+        # One kernel per layer: the per-step graph of all layers' launches,
+        # replayed between CUDA events (no host launch gaps).
+        step_graphs = []
+        for s in range(args.warmup, cap):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for L in layers:
+                    sparse_attention(L.q[s], L.summary, L.suffix_k, L.suffix_v, cfg,
+                                     anchor_mask=L.anchor, workspace=L.workspace,
+                                     suffix_length=length)
+            step_graphs.append((s, graph))
+        del graph
+        events = []
+        for s, graph in step_graphs:
+            length.fill_(s + 1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            events.append((e0, e1))
+            count_selected()
+        torch.cuda.synchronize(dev)
+        attend_ms = [a.elapsed_time(b) / args.layers for a, b in events]
+        del step_graphs
     else:
         phase_graphs = []
         for s in range(args.warmup, cap):
@@ -692,34 +715,28 @@ def run_b200(args):
                      + heads_local * nb * (2 if args.anchors else 1))
     step_bytes = args.layers * (summary_bytes + qo_bytes) + (
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
-    # Per launch: the selector launch reads the summaries, the value means of
-    # the unselected blocks and -- fused -- the anchored pages; the attention
-    # launch (+ combine) the other selected pages and the suffix.
-    streamed_tokens = anchored_tokens * args.steps if fused else 0  # over all timed launches
-    select_bytes = (summary_bytes + heads_local * G * D * 2
-                    + (unselected * D * 2 + streamed_tokens * D * 4) / launches)
-    attend_bytes = ((tokens_refined - streamed_tokens + suffix_total) * D * 2 * 2 / launches
-                    + qo_bytes)
+    # Per launch.  One-kernel decode: the whole layer-step (summaries, value
+    # means of the unselected blocks, every selected page, the suffix, q and
+    # the output).  Four kernels: the attention launch (+ combine) streams the
+    # selected pages and the suffix; the selector reads the summaries.
     attend_avg_ms = statistics.mean(attend_ms)
     select_avg_ms = statistics.mean(select_ms) if select_ms else None
+    if fused:
+        attend_bytes = step_bytes / args.layers
+    else:
+        attend_bytes = (tokens_refined + suffix_total) * D * 2 * 2 / launches + qo_bytes
+    select_bytes = summary_bytes + heads_local * G * D * 2 + unselected * D * 2 / launches
     peak, peak_note = measured_hbm_peak()
     attend_gbs = attend_bytes / (attend_avg_ms * 1e-3) / 1e9
     select_gbs = select_bytes / (select_avg_ms * 1e-3) / 1e9 if select_avg_ms else None
-    # The dominant kernel: the fused selector when it streams most of the
-    # pages, else the attention kernel.
-    dominant_is_select = fused and select_avg_ms is not None and select_avg_ms > attend_avg_ms
-    traffic = profiled_traffic("fused_llama8b_128k.json" if dominant_is_select
+    traffic = profiled_traffic("decode_llama8b_128k.json" if fused
                                else "attend_llama8b_128k.json")
     traffic_per_launch = None
     # A committed capture is of 32-token pages of 128 channels; its DRAM
     # bytes scale with the pages a launch reads only for that page shape.
     if traffic is not None and not split and (args.block_size, args.head_dim) == (32, 128):
         dram_bytes, pages_profiled = traffic
-        if dominant_is_select:  # the anchored pages one selector launch streams
-            pages_per_launch = anchored_pages / args.layers
-        else:  # the pages one attention launch streams
-            pages_per_launch = pages / launches - (anchored_pages / args.layers if fused else 0)
-        traffic_per_launch = dram_bytes * pages_per_launch / pages_profiled
+        traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
     step_gbs = step_bytes_all / (us_per_step * 1e-6) / 1e9  # whole job
     step_gbs_per_gpu = step_gbs / world
@@ -922,43 +939,37 @@ def run_b200(args):
                     "bytes_per_step": int(step_bytes_all),
                     "note": peak_note + "; frac is per GPU (job bytes / GPUs / step time "
                                         "/ one GPU's peak)"},
-            "roofline": ({"bound": "hbm", "achieved": round(select_gbs, 1), "peak": peak,
-                          "unit": "GB/s", "frac": round(select_gbs / peak, 4),
-                          "traffic": (None if traffic_per_launch is None
-                                      else int(traffic_per_launch)),
-                          "kernel": f"rkv fused_kernel<{D},{B}> (selector + anchored pages)",
-                          "algorithmic_bytes_per_launch": int(select_bytes),
-                          "avg_launch_us": round(select_avg_ms * 1e3, 2),
-                          "peak_note": peak_note} if dominant_is_select else
-                         {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
-                          "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
-                          "traffic": (None if traffic_per_launch is None
-                                      else int(traffic_per_launch)),
-                          "kernel": ("rkv split decode step (selector, attention, exchanges, "
-                                     "merge)" if split else
-                                     f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}> + combine"),
-                          "algorithmic_bytes_per_launch": int(attend_bytes),
-                          "avg_launch_us": round(attend_avg_ms * 1e3, 2),
-                          "peak_note": peak_note}),
+            "roofline": {"bound": "hbm", "achieved": round(attend_gbs, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(attend_gbs / peak, 4),
+                         "traffic": (None if traffic_per_launch is None
+                                     else int(traffic_per_launch)),
+                         "kernel": ("rkv split decode step (selector, attention, exchanges, "
+                                    "merge)" if split else
+                                    f"rkv fused_kernel<{D},{B}> (one kernel per layer-step)"
+                                    if fused else
+                                    f"rkv attend_kernel<{B},{D},{1 if G <= 8 else 2}> + combine"),
+                         "algorithmic_bytes_per_launch": int(attend_bytes),
+                         "avg_launch_us": round(attend_avg_ms * 1e3, 2),
+                         "peak_note": peak_note},
             "phase_us_per_layer": (
                 {"split_step": round(attend_avg_ms * 1e3, 2)} if split else
-                {"select" + ("_and_anchored_pages" if fused else ""):
-                     round(select_avg_ms * 1e3, 2),
+                {"decode_kernel": round(attend_avg_ms * 1e3, 2)} if fused else
+                {"select": round(select_avg_ms * 1e3, 2),
                  "select_achieved_gbs": round(select_gbs, 1),
                  "attend_and_combine": round(attend_avg_ms * 1e3, 2),
                  "attend_achieved_gbs": round(attend_gbs, 1)}),
-            "fused_selector": fused,
+            "one_kernel_decode": fused,
             "anchored_fraction": round(anchored_pages / (args.layers * heads_local * nb), 5),
             "selected_fraction": round(pages / (launches * heads_local * nb), 5),
             # median over layers (layer 0 carries one-time module loading)
             "summarize_us_per_layer": round(statistics.median(summarize_ms) * 1e3, 1),
             # our kernels per layer-step: 4 (stats, final, attend, combine), or 5 under a
             # sequence split (the same four plus the rank merge; NCCL's kernels not counted)
-            # our kernels per layer-step: 3 with the fused selector (selector +
-            # anchored pages, attention, combine), 4 with the two selector kernels,
-            # 5 under a sequence split (+ the rank merge; NCCL's kernels not counted)
+            # our kernels per layer-step: 1 with the one-kernel decode, 4 with the
+            # selector, attention and combine kernels, 5 under a sequence split (+ the
+            # rank merge; NCCL's kernels not counted)
             "gpu_launches": args.steps * args.layers * (
-                (3 if fused else lib.rkv_decode_launch_count(_native.PHASE_ALL))
+                (1 if fused else lib.rkv_decode_launch_count(_native.PHASE_ALL))
                 + (1 if split else 0)),
             "clocks": clocks.summary(),
             "e2e": e2e,

@@ -241,7 +241,16 @@ RKV_API size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t b
  *   output: (heads, group, head_dim) in query_dtype.
  *   selected: (heads, blocks) uint8 mask written by the call.
  *   phases: RKV_PHASE_ALL, or a subset for timing individual kernels (the
- *     phases must still run in order on the stream).
+ *     phases must still run in order on the stream; with the fused selector
+ *     STATS and FINAL go together, see rkv_decode_kernel_count).
+ * The fused selector (the default for up to 480 KV-head rows) runs
+ * heads x parts CTAs, at most one per SM, whose parts of a row wait for one
+ * another at a bounded barrier.  Decode calls that run concurrently on
+ * different streams of one GPU can keep each other's CTAs from becoming
+ * resident; their barriers then give up after 1 s with RKV_DEVICE_TIMEOUT in
+ * the status word.  Order such calls on one stream (one decode step of a
+ * batch of sequences is one call: see the batched summary above), or switch
+ * the fused selector off with rkv_set_fused_selector(0).
  */
 RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
                const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,

@@ -40,9 +40,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 size_t up256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Workspace header: status word at 0; the fused selector's per-row barrier
-// words (arrivals, then generations) from kRowWords, for up to kMaxFusedRows rows.
-constexpr size_t kHeaderBytes = 4096;
+// Workspace header: status word at 0; the one-kernel decode's per-row barrier
+// words from kRowWords -- arrivals A, generations A, arrivals B, generations B,
+// kMaxFusedRows words each -- at a fixed place for every geometry.
+constexpr size_t kHeaderBytes = 8192;
 constexpr size_t kRowWords = 256;
 constexpr int64_t kMaxFusedRows = 480;
 
@@ -85,12 +86,13 @@ struct Plan {
   size_t smem_c = 0;
   int g8 = 8, max_sources = 0;
   size_t smem_d = 0;  // combine
-  // Fused selector (rkv_fused.cu): one kernel for phases A and B plus the
-  // anchored pages; parts_b CTAs per row, tpc_b the largest tile range.
+  // One-kernel decode (rkv_fused.cu), used for RKV_PHASE_ALL: parts_base /
+  // parts_extra parts per row, tcap_f the largest tile range of a part; its
+  // own workspace regions (the same allocation, another layout).
   bool fused = false;
-  int warps_f = 8;
+  int warps_f = 8, parts_base = 1, parts_extra = 0, tcap_f = 1, grid_f = 0;
   size_t smem_f = 0;
-  size_t rows_words = 0;  // per-row barrier words (arrivals, generations)
+  size_t f_lse = 0, f_z = 0, f_delta = 0, f_part_m = 0, f_part_l = 0, f_part_o = 0;
   // workspace offsets (bytes)
   size_t status = 0, lse = 0, z = 0, delta = 0, seg_count = 0, sel_ids = 0;
   size_t rep_m = 0, rep_l = 0, rep_o = 0, att_m = 0, att_l = 0, att_o = 0, bytes = 0;
@@ -170,19 +172,31 @@ int make_dense_plan(Plan* pl, int64_t heads, int64_t group, int64_t dim, int64_t
   return RKV_OK;
 }
 
-// Whether rkv_decode runs the fused selector (switched off process-wide by
+// Whether rkv_decode runs the one-kernel decode (switched off process-wide by
 // rkv_set_fused_selector(0), for measurement and cross-checks).
 std::atomic<int> g_fused_selector{1};
 
-// The fused selector's shape: rows x parts CTAs, never more than one per SM
-// unless each row has a single part (then no CTA waits for another), warps
-// of one slice each (a K|V page or a key-mean|ellipsoid tile pair).
+// The one-kernel decode's shape: every SM gets one CTA (uneven parts per row:
+// the first `extra` rows one more), never more CTAs than SMs unless each row
+// has a single part (then no CTA waits for another); warps of one slice each
+// (a K|V page or a key-mean|ellipsoid tile pair).
 bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, int64_t dim,
                 int64_t block_size) {
   if (!g_fused_selector.load() || heads > kMaxFusedRows) return false;
-  const int parts = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(pl->tiles, dev.sms / std::max<int64_t>(1, heads))));
-  const int tcap = static_cast<int>(cdiv(pl->tiles, parts));
+  int base, extra;
+  if (heads >= dev.sms) {
+    base = 1;
+    extra = 0;
+  } else {
+    base = static_cast<int>(dev.sms / heads);
+    extra = static_cast<int>(dev.sms % heads);
+    if (base >= pl->tiles) {  // no part without a tile
+      base = pl->tiles;
+      extra = 0;
+    }
+  }
+  const int most = base + (extra > 0 ? 1 : 0);
+  const int tcap = static_cast<int>(cdiv(pl->tiles, base));
   if (tcap > 128) return false;  // the per-part tables live in shared memory
   const int64_t slice = std::max<int64_t>(2LL * kSelectTile * dim * 2, 2LL * block_size * dim * 2);
   const int warps = static_cast<int>(std::min<int64_t>(8, 196608 / slice));
@@ -193,11 +207,11 @@ bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, i
   pl->fused = true;
   pl->warps_f = warps;
   pl->smem_f = smem;
-  pl->parts_a = parts;
-  pl->slots_a = warps;
-  pl->parts_b = parts;
-  pl->tpc_b = tcap;
-  pl->seg_cap = tcap * kSelectTile;
+  pl->parts_base = base;
+  pl->parts_extra = extra;
+  pl->tcap_f = tcap;
+  pl->grid_f = fused_grid(static_cast<int>(heads), base, extra);
+  (void)most;
   return true;
 }
 
@@ -256,12 +270,10 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
       pl->smem_b > static_cast<size_t>(dev.smem_optin)) {
     return fail(RKV_ERR_UNSUPPORTED, "selector tiles do not fit in shared memory");
   }
-  if (decode && fixed_parts_a == 0 && instances == 1) {
-    plan_fused(pl, dev, heads, group, dim, block_size);
-  }
   if (decode) {
     rc = plan_attention(pl, dev, heads, group, dim, block_size);
     if (rc != RKV_OK) return rc;
+    if (fixed_parts_a == 0 && instances == 1) plan_fused(pl, dev, heads, group, dim, block_size);
   }
   // Workspace layout.
   size_t off = 0;
@@ -276,7 +288,6 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   // of any geometry writes (they clean themselves after every round, so a
   // workspace reused for another geometry finds them consistent).
   pl->status = take(kHeaderBytes);
-  if (pl->fused) pl->rows_words = kRowWords;
   // (Under a sequence split phase A writes into the exchange slab instead.)
   pl->lse = take(fixed_parts_a > 0 ? 0 : rowsg * pl->parts_a * pl->slots_a * 4 * 4);
   pl->z = take(rowsg * blocks * 4);
@@ -295,6 +306,17 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
     pl->att_o = take(slots_c * pl->g8 * dim * 4);
   }
   pl->bytes = off;
+  if (pl->fused) {  // the one-kernel decode's regions, after the same header
+    off = kHeaderBytes;
+    const int most = pl->parts_base + (pl->parts_extra > 0 ? 1 : 0);
+    pl->f_lse = take(rowsg * most * pl->warps_f * 4 * 4);
+    pl->f_z = take(rowsg * blocks * 4);
+    pl->f_delta = take(rowsg * blocks * 4);
+    pl->f_part_m = take(static_cast<size_t>(pl->grid_f) * pl->g8 * 4);
+    pl->f_part_l = take(static_cast<size_t>(pl->grid_f) * pl->g8 * 4);
+    pl->f_part_o = take(static_cast<size_t>(pl->grid_f) * pl->g8 * dim * 4);
+    pl->bytes = std::max(pl->bytes, off);
+  }
   return RKV_OK;
 }
 
@@ -539,11 +561,15 @@ T* at(void* ws, size_t off) {
   return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
 }
 
-// rkv_decode's selector as one fused launch (phases A and B and the anchored
-// pages; see rkv_fused.cu).
-int run_fused_selector(const Plan& pl, const rkv_summary* s, const void* q, int qdtype,
-                       int64_t group, float eps, int reduction, const uint8_t* anchor,
-                       uint8_t* mask, void* ws, cudaStream_t stream) {
+// rkv_decode (RKV_PHASE_ALL) as one launch: selector, every page, the
+// representatives and the combine (rkv_fused.cu).
+int run_fused_decode(const Plan& pl, const rkv_summary* s, const void* q, int qdtype,
+                     int64_t group, const void* key_suffix, const void* value_suffix,
+                     int64_t suffix_capacity, int64_t key_suffix_head_stride,
+                     int64_t key_suffix_token_stride, int64_t value_suffix_head_stride,
+                     int64_t value_suffix_token_stride, const int32_t* suffix_length,
+                     int64_t suffix_length_host, float eps, int reduction, const uint8_t* anchor,
+                     uint8_t* mask, void* output, void* ws, cudaStream_t stream) {
   const int D = static_cast<int>(s->head_dim);
   const int DP = padded_dim(D);
   const int64_t H = s->heads, B = s->block_size;
@@ -560,46 +586,60 @@ int run_fused_selector(const Plan& pl, const rkv_summary* s, const void* q, int 
                  paged ? s->pool_pages : s->blocks, paged ? s->value_token_stride : D,
                  s->value_page_head_stride, paged ? s->value_page_stride : B * D, "value_pages");
   if (rc != RKV_OK) return rc;
+  if (suffix_capacity > 0) {
+    rc = rows_map(&maps.key_suffix, key_suffix, D, suffix_capacity, H, key_suffix_token_stride,
+                  key_suffix_head_stride, static_cast<int>(B), "key_suffix");
+    if (rc != RKV_OK) return rc;
+    rc = rows_map(&maps.value_suffix, value_suffix, D, suffix_capacity, H,
+                  value_suffix_token_stride, value_suffix_head_stride, static_cast<int>(B),
+                  "value_suffix");
+    if (rc != RKV_OK) return rc;
+  } else {
+    maps.key_suffix = maps.key_pages;
+    maps.value_suffix = maps.value_pages;
+  }
   FusedParams p = {};
   p.query = q;
   p.query_f32 = qdtype == RKV_DTYPE_F32;
   p.dim = D;
+  p.out = output;
   p.counts = s->counts;
   p.heads = static_cast<int>(H);
   p.group = static_cast<int>(group);
   p.blocks = static_cast<int>(s->blocks);
   p.tiles = pl.tiles;
-  p.parts = pl.parts_b;
-  p.tcap = pl.tpc_b;
+  p.parts_base = pl.parts_base;
+  p.parts_extra = pl.parts_extra;
+  p.tcap = pl.tcap_f;
   p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
   p.eps = eps;
   p.reduction = reduction;
-  p.z = at<float>(ws, pl.z);
-  p.delta = at<float>(ws, pl.delta);
-  p.lse = at<float>(ws, pl.lse);
+  p.z = at<float>(ws, pl.f_z);
+  p.delta = at<float>(ws, pl.f_delta);
+  p.lse = at<float>(ws, pl.f_lse);
   p.value_norm = s->value_norm;
   p.max_value_norm = s->max_value_norm;
   p.anchor = anchor;
   p.mask = mask;
   p.split_probs = qdtype == RKV_DTYPE_F32;
-  p.stream_anchors = anchor != nullptr ? 1 : 0;
-  p.seg_count = at<int>(ws, pl.seg_count);
-  p.sel_ids = at<int>(ws, pl.sel_ids);
-  p.seg_cap = pl.seg_cap;
-  p.rep_m = at<float>(ws, pl.rep_m);
-  p.rep_l = at<float>(ws, pl.rep_l);
-  p.rep_o = at<float>(ws, pl.rep_o);
-  p.row_arrive = at<unsigned>(ws, pl.rows_words);
-  p.row_gen = p.row_arrive + kMaxFusedRows;
+  p.part_m = at<float>(ws, pl.f_part_m);
+  p.part_l = at<float>(ws, pl.f_part_l);
+  p.part_o = at<float>(ws, pl.f_part_o);
+  p.bar_words = at<unsigned>(ws, kRowWords);
+  p.bar_stride = static_cast<int>(kMaxFusedRows);
   p.seq = seq_layout(s);
   p.page = static_cast<int>(B);
   p.prompt_length = static_cast<int>(s->prompt_length);
   p.page_table = s->page_table;
   p.page_table_stride = static_cast<int>(paged ? s->page_table_stride : 0);
   p.pool_pages = static_cast<int>(paged ? s->pool_pages : s->blocks);
+  p.has_suffix = suffix_capacity > 0;
+  p.suffix_capacity = static_cast<int>(suffix_capacity);
+  p.suffix_len_ptr = suffix_length;
+  p.suffix_len_host = static_cast<int>(suffix_length_host);
   p.status = at<int>(ws, pl.status);
   const cudaError_t err = launch_fused(maps, p, DP, pl.warps_f, pl.smem_f, stream, true);
-  if (err != cudaSuccess) return cuda_fail(err, "fused selector launch");
+  if (err != cudaSuccess) return cuda_fail(err, "decode launch");
   return RKV_OK;
 }
 
@@ -1153,23 +1193,16 @@ int decode_impl(const rkv_summary* summary, const void* query, int query_dtype, 
   if (rc != RKV_OK) return rc;
   if ((rc = check_workspace(pl, workspace, workspace_size)) != RKV_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pl.fused) {
-    // One launch serves phases A and B; they are requested together.
-    const unsigned sel = phases & (RKV_PHASE_STATS | RKV_PHASE_FINAL);
-    if (sel == RKV_PHASE_STATS || sel == RKV_PHASE_FINAL) {
-      return fail(RKV_ERR_INVALID_ARGUMENT,
-                  "the fused selector runs phases STATS and FINAL together");
-    }
-    if (sel != 0) {
-      rc = run_fused_selector(pl, summary, query, query_dtype, group, eps, reduction,
-                              anchor_mask, selected, workspace, st);
-      if (rc != RKV_OK) return rc;
-    }
-  } else {
-    rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
-                      selected, 0, workspace, true, phases, st, split);
-    if (rc != RKV_OK) return rc;
+  if (pl.fused && phases == RKV_PHASE_ALL && split == nullptr) {
+    return run_fused_decode(pl, summary, query, query_dtype, group, key_suffix, value_suffix,
+                            suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
+                            value_suffix_head_stride, value_suffix_token_stride, suffix_length,
+                            suffix_length_host, eps, reduction, anchor_mask, selected, output,
+                            workspace, st);
   }
+  rc = run_selector(pl, summary, query, query_dtype, 1, group, eps, reduction, anchor_mask,
+                    selected, 0, workspace, true, phases, st, split);
+  if (rc != RKV_OK) return rc;
   return attend_and_combine(pl, summary, query, query_dtype, group, key_suffix, value_suffix,
                             suffix_capacity, key_suffix_head_stride, key_suffix_token_stride,
                             value_suffix_head_stride, value_suffix_token_stride, suffix_length,
@@ -1351,7 +1384,7 @@ int rkv_decode_kernel_count(int64_t heads, int64_t group, int64_t blocks, int64_
     return 0;
   Plan pl;
   if (make_plan(&pl, heads, group, blocks, head_dim, block_size, 1, true) != RKV_OK) return 0;
-  return pl.fused ? 3 : 4;
+  return pl.fused ? 1 : 4;
 }
 
 }  // extern "C"

@@ -1,30 +1,29 @@
-// Fused selector with in-kernel streaming of the anchored pages
-// (reference: src/refinekv/reference.py:10-73 for the math; the reference's
-// GPU form runs it as separate Triton kernels, kernels/selection.py:47-223
+// One-kernel decode step of a layer (reference: src/refinekv/reference.py:10-73;
+// the reference's GPU form is six Triton kernels, kernels/selection.py:47-223
 // and kernels/attention.py:13-329).
 //
-// One CTA per (KV-head row, part); part k owns the tiles
-// [tiles*k/parts, tiles*(k+1)/parts) of its row, and rows x parts never
-// exceeds the SM count, so every CTA of the grid is resident at once (the
-// host checks it).  A CTA runs, for its tiles:
-//   1. phase A: z and delta of every (group row, block) from the key-mean and
-//      ellipsoid tiles (TMA, mma.sync), stored for phase B, and one log-sum-
-//      exp partial per warp;
-//   2. a per-row barrier (arrival counter + generation word in the
-//      workspace; bounded wait) until every part of the row has written its
-//      partials;
-//   3. phase B: row-global log Z / log C, risk and GQA decision of every
-//      block, the mask, and the compacted list of the selected blocks that
-//      the attention kernel reads -- minus the anchored blocks;
-//   4. the anchored pages of its tiles (they are selected whatever the
-//      decision: selected |= anchor, reference.py:54-55) and the
-//      representatives of its unselected blocks, both into one running
-//      softmax partial per warp, merged into the CTA's partial.
-// The attention kernel then streams only the non-anchored selected pages and
-// the suffix, and the combine merges everything as before.  Anchored pages
-// are attended by the same arithmetic as the attention kernel's
-// (attend-tile helpers of rkv_device.cuh); only the order in which the
-// partials are summed differs.
+// One CTA per (KV-head row, part); a row's parts split its selector tiles
+// into contiguous ranges, and the grid never has more CTAs than SMs (unless
+// every row has a single part), so all parts of a row are resident together
+// (the host sizes it; one CTA per SM by shared memory).  A CTA:
+//   1. phase A: z and delta of every (group row, block) of its tiles from the
+//      key-mean and ellipsoid tiles (TMA, mma.sync), stored for phase B, and
+//      one log-sum-exp partial per warp; arrives at the row's barrier A;
+//   2. streams, without waiting, the pages whose attention is known before
+//      any decision: its anchored blocks (selected whatever the risk,
+//      reference.py:54-55) and its share of the generated suffix;
+//   3. waits at barrier A (by then normally passed), merges the row's
+//      partials into log Z / log C, decides every block of its tiles (risk,
+//      GQA reduction, non-finite override, anchors), writes the mask, and
+//      streams its selected non-anchored pages and the representatives of
+//      its unselected blocks (value means, logit z);
+//   4. merges its warps into one softmax partial, arrives at barrier B, and
+//      once every part of the row is there writes its slice of the row's
+//      output channels from all parts' partials.
+// Every wait is bounded (status bit on timeout).  The order of the work is
+// static (block order, warps round-robin), so results are deterministic.
+// The page arithmetic is the attention kernel's (rkv_attend.cu): the same
+// helpers of rkv_device.cuh; only the order in which partials merge differs.
 #include "rkv_device.cuh"
 #include "rkv_kernels.h"
 #include "rkv_risk.cuh"
@@ -33,8 +32,9 @@ namespace rkv {
 namespace {
 
 // Shared-memory layout (also sized by the host): a TMA slice per warp, two
-// mbarriers per warp, row normalisers, per-tile bit masks and lists, the
-// anchored-block list.  The warps' final partials are parked in the slices.
+// mbarriers per warp, row normalisers, per-tile bit masks and lists, and one
+// block list (anchored blocks, then the selected non-anchored ones).  The
+// warps' final partials, then the parts' (max, sum), are parked in the slices.
 struct FusedLayout {
   size_t bars, norms, flags, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off, anchored,
       bytes;
@@ -79,6 +79,107 @@ __device__ __forceinline__ bool wait_generation(const unsigned* word, unsigned s
   }
 }
 
+// Arrival of one part at a row barrier (thread 0, after the CTA's writes and a
+// CTA barrier): the last of `parts` arrivals resets the count and moves the
+// generation on, so the words are clean for the next call.
+__device__ __forceinline__ void arrive(unsigned* count, unsigned* gen, int parts) {
+  __threadfence();
+  const unsigned before = atomicAdd(count, 1u);
+  if (before == static_cast<unsigned>(parts) - 1u) {
+    atomicExch(count, 0u);
+    __threadfence();
+    atomicAdd(gen, 1u);
+  }
+}
+
+__device__ __forceinline__ unsigned read_generation(const unsigned* word) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+  return v;
+}
+
+// Streams `count` items of one warp -- K|V pages or suffix chunks of R rows --
+// through the warp's slice with separate K and V barriers (K refilled as soon
+// as the scores are done), into the running softmax (m, l, o).  item(j)
+// returns {suffix?, page or first suffix row, valid rows, head coordinate}.
+// False on a timeout, after the copies in flight have landed.
+template <int R, int D, int NT, typename ItemFn>
+__device__ __forceinline__ bool stream_items(int count, ItemFn item, const FusedMaps& maps,
+                                             uint8_t* slice, uint64_t* bar_a, uint64_t* bar_b,
+                                             uint32_t& uses_a, uint32_t& uses_b,
+                                             const uint32_t (&qb)[D / 16][NT][2], float scale,
+                                             bool split, float (&m)[NT][2], float (&l)[NT][2],
+                                             float (&o)[D / 16][NT][4], uint64_t policy,
+                                             int lane) {
+  if (count <= 0) return true;
+  constexpr int kPage = R * D * 2;
+  auto issue = [&](const int4& it, bool value) {
+    if (lane == 0) {
+      uint64_t* bar = value ? bar_b : bar_a;
+      uint8_t* dst = slice + (value ? kPage : 0);
+      fence_proxy_async();
+      mbar_expect_tx(bar, kPage);
+      if (it.x) {
+        tma_tile_hint<D>(dst, value ? &maps.value_suffix : &maps.key_suffix, bar, it.y, it.w, R,
+                         policy);
+      } else {
+        tma_page_hint<D>(dst, value ? &maps.value_pages : &maps.key_pages, bar, it.w, it.y, R,
+                         policy);
+      }
+    }
+  };
+  int4 cur = item(0);
+  issue(cur, false);
+  issue(cur, true);
+  uint32_t issued_a = uses_a + 1, issued_b = uses_b + 1;
+  bool ok = true;
+  for (int j = 0; j < count; ++j) {
+    if (!warp_wait(bar_a, uses_a & 1)) {
+      ok = false;
+      break;
+    }
+    ++uses_a;
+    float logit[R / 16][NT][4];
+    score_tile<R, D, NT>(smem_addr(slice), qb, logit, lane);
+#pragma unroll
+    for (int mt = 0; mt < R / 16; ++mt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          logit[mt][nt][c] = r < cur.z ? logit[mt][nt][c] * scale : -INFINITY;
+      }
+    __syncwarp();
+    int4 next = make_int4(0, 0, 0, 0);
+    const bool more = j + 1 < count;
+    if (more) {
+      next = item(j + 1);
+      issue(next, false);
+      ++issued_a;
+    }
+    softmax_update<R, D, NT>(logit, m, l, o);
+    uint32_t hi[R / 16][NT][2], lo[R / 16][NT][2];
+    prob_frags<R, NT>(logit, hi, lo, split);
+    if (!warp_wait(bar_b, uses_b & 1)) {
+      ok = false;
+      break;
+    }
+    ++uses_b;
+    accumulate_values<R, D, NT>(smem_addr(slice + kPage), hi, o, lane);
+    if (split) accumulate_values<R, D, NT>(smem_addr(slice + kPage), lo, o, lane);
+    __syncwarp();
+    if (more) {
+      issue(next, true);
+      ++issued_b;
+    }
+    cur = next;
+  }
+  for (; uses_a < issued_a; ++uses_a) mbar_wait(bar_a, uses_a & 1);
+  for (; uses_b < issued_b; ++uses_b) mbar_wait(bar_b, uses_b & 1);
+  return ok;
+}
+
 // PACK4: group of at most 4 rows (q and q^2 share one n8 tile); GM: group
 // rows evaluated per block in phase B (padded to 4, 8 or 16).
 template <int D, int R, int NT, bool PACK4, int GM>
@@ -86,7 +187,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                                                        const FusedParams p) {
   constexpr int T = kSelectTile;
   constexpr int kSel = FusedShape<D, R>::kSel;
-  constexpr int kPage = FusedShape<D, R>::kPage;
   constexpr int kSlice = FusedShape<D, R>::kSlice;
   constexpr int G8 = NT * 8;
   extern __shared__ uint8_t smem_raw[];
@@ -99,22 +199,41 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   uint64_t* bar_b = bar_a + 1;
   float* lz = reinterpret_cast<float*>(smem + lay.norms);
   float* lc = lz + kMaxGroup;
-  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 anchored
+  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 listed
   uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.sel_bits);  // [tcap]
   uint32_t* rep_bits = reinterpret_cast<uint32_t*>(smem + lay.rep_bits);  // [tcap]
   uint32_t* anc_bits = reinterpret_cast<uint32_t*>(smem + lay.anc_bits);  // [tcap]
   int* offsets = reinterpret_cast<int*>(smem + lay.offsets);             // [tcap + 1]
   int* rep_list = reinterpret_cast<int*>(smem + lay.rep_list);           // [tcap]
   int* anc_off = reinterpret_cast<int*>(smem + lay.anc_off);             // [tcap + 1]
-  int* anchored = reinterpret_cast<int*>(smem + lay.anchored);           // [tcap * 32]
+  int* blist = reinterpret_cast<int*>(smem + lay.anchored);              // [tcap * 32]
 
-  const int h = blockIdx.x, part = blockIdx.y;
-  const int t_lo = static_cast<int>(static_cast<long long>(p.tiles) * part / p.parts);
-  const int t_hi = static_cast<int>(static_cast<long long>(p.tiles) * (part + 1) / p.parts);
+  // This CTA's row and part.
+  const int c = blockIdx.x;
+  const int P = p.parts_base, X = p.parts_extra;
+  int h, part, parts_h;
+  if (c < X * (P + 1)) {
+    h = c / (P + 1);
+    part = c - h * (P + 1);
+    parts_h = P + 1;
+  } else {
+    const int c2 = c - X * (P + 1);
+    h = X + c2 / P;
+    part = c2 - (c2 / P) * P;
+    parts_h = P;
+  }
+  const int first_cta = c - part;
+  const int lse_parts = P + (X > 0 ? 1 : 0);
+  const int t_lo = static_cast<int>(static_cast<long long>(p.tiles) * part / parts_h);
+  const int t_hi = static_cast<int>(static_cast<long long>(p.tiles) * (part + 1) / parts_h);
   const int n_t = t_hi - t_lo;
   const int64_t* counts = p.counts + static_cast<size_t>(p.seq.sequence(h)) * p.blocks;
   const char* q = static_cast<const char*>(p.query) +
                   static_cast<size_t>(h) * p.group * p.dim * (p.query_f32 ? 4 : 2);
+  unsigned* arrive_a = p.bar_words + h;
+  unsigned* gen_a = arrive_a + p.bar_stride;
+  unsigned* arrive_b = gen_a + p.bar_stride;
+  unsigned* gen_b = arrive_b + p.bar_stride;
 
   if (lane == 0) {
     mbar_init(bar_a, 1);
@@ -133,6 +252,10 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     tma_prefetch_desc(&maps.value_mean);
     tma_prefetch_desc(&maps.key_pages);
     tma_prefetch_desc(&maps.value_pages);
+    if (p.has_suffix) {
+      tma_prefetch_desc(&maps.key_suffix);
+      tma_prefetch_desc(&maps.value_suffix);
+    }
     for (int i = 0; i < 8; ++i) flags[i] = 0;
   }
   for (int i = threadIdx.x; i * 128 < p.group * p.dim * (p.query_f32 ? 4 : 2); i += blockDim.x) {
@@ -140,15 +263,28 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
   pdl_wait();
-  // This row's barrier generation before our arrival (it can only move once
-  // every part, this one included, has arrived).
-  unsigned seen_gen = 0;
+  // Every CTA of this grid has started once all have passed here, so a grid
+  // launched early behind this one can never hold an SM one of ours needs.
+  pdl_launch_dependents();
+  // The row's barrier generations before this part's arrivals (they move only
+  // once every part, this one included, has arrived).
+  unsigned seen_a = 0, seen_b = 0;
   if (threadIdx.x == 0) {
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(seen_gen) : "l"(p.row_gen + h)
-                 : "memory");
+    seen_a = read_generation(gen_a);
+    seen_b = read_generation(gen_b);
+  }
+  int suffix_len = 0;
+  if (p.has_suffix) {
+    suffix_len = p.suffix_len_ptr != nullptr ? *p.suffix_len_ptr : p.suffix_len_host;
+    if (suffix_len < 0 || suffix_len > p.suffix_capacity) {
+      if (threadIdx.x == 0) atomicOr(p.status, kStatusBadInput);
+      suffix_len = suffix_len < 0 ? 0 : p.suffix_capacity;
+    }
   }
   const int blocks_h = p.seq.blocks(h, p.blocks);
+  const int prompt_h = p.seq.prompt(h, p.prompt_length);
   const int n_stat = max(0, min(t_hi, (blocks_h + T - 1) / T) - t_lo);  // tiles with real blocks
+  const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
   const uint64_t policy = l2_evict_first_policy();
   uint32_t uses_a = 0, uses_b = 0;  // completed waits per barrier (parity = uses & 1)
   bool aborted = false;
@@ -158,10 +294,10 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   };
 
   // Anchored blocks of the range, one bit per block (known before any statistics).
-  const bool stream = p.stream_anchors != 0 && p.anchor != nullptr;
   for (int k = warp; k < n_t; k += W) {
     const int b = (t_lo + k) * T + lane;
-    const bool a = stream && b < blocks_h && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+    const bool a = p.anchor != nullptr && b < blocks_h &&
+                   p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, a);
     if (lane == 0) anc_bits[k] = bits;
   }
@@ -331,38 +467,89 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
         const bool writer = PACK4 ? lane < 2 : lane < 4;
         const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
         if (writer && g < p.group) {
-          float* out = p.lse + ((static_cast<size_t>(h) * p.group + g) * p.parts * W +
+          float* out = p.lse + ((static_cast<size_t>(h) * p.group + g) * lse_parts * W +
                                 static_cast<size_t>(part) * W + warp) * 4;
           *reinterpret_cast<float4*>(out) = make_float4(mz, sz, mc, sc);
         }
       }
   }
   __syncthreads();
+  if (threadIdx.x == 0) arrive(arrive_a, gen_a, parts_h);
 
-  // ---------------- per-row barrier ----------------------------------------
-  if (threadIdx.x == 0) {
-    __threadfence();  // this CTA's z, delta and partials before the arrival
-    const unsigned before = atomicAdd(p.row_arrive + h, 1u);
-    if (before == static_cast<unsigned>(p.parts) - 1u) {
-      atomicExch(p.row_arrive + h, 0u);
-      __threadfence();
-      atomicAdd(p.row_gen + h, 1u);
+  // The anchored list (block order) while the other parts finish phase A.
+  if (warp == (W > 1 ? 1 : 0)) {
+    int acc = 0;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int cnt = k < n_t ? __popc(anc_bits[k]) : 0;
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) anc_off[k] = acc + incl - cnt;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (!wait_generation(p.row_gen + h, seen_gen)) {
-      atomicOr(p.status, kStatusTimeout);
-      flags[3] = 1;
-    }
+    if (lane == 0) flags[2] = acc;
   }
   __syncthreads();
-  // Every CTA that gets here was resident; the attention grid may launch once
-  // all have (it then waits for this grid's completion before reading).
-  pdl_launch_dependents();
+  for (int k = warp; k < n_t; k += W) {
+    const uint32_t ab = anc_bits[k];
+    if ((ab >> lane) & 1u) blist[anc_off[k] + __popc(ab & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
+  }
+  __syncthreads();
+
+  // ---------------- attention known before the decisions -------------------
+  float m[NT][2], l[NT][2], o[D / 16][NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m[nt][0] = m[nt][1] = -INFINITY;
+    l[nt][0] = l[nt][1] = 0.f;
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
+  }
+  const bool split = p.split_probs != 0;
+  uint32_t qb[D / 16][NT][2];
+  load_query_frags<D, NT>(qb, q, p.query_f32, p.group, p.dim, lane, false);
+  // A page of block `block`: physical page (page table), valid rows.
+  auto page_item = [&](int block) {
+    int page = block;
+    if (p.page_table != nullptr) {
+      page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride +
+                   block);
+      if (page < 0 || page >= p.pool_pages) {  // flag the call; read page 0 instead
+        if (lane == 0) atomicOr(p.status, kStatusBadInput);
+        page = 0;
+      }
+    }
+    return make_int4(0, page, min(R, prompt_h - block * R), pool_head);
+  };
+  const int n_anc = flags[2];
+  const int n_suffix = (suffix_len + R - 1) / R;                          // chunks of the row
+  const int my_suffix = n_suffix > part ? (n_suffix - part + parts_h - 1) / parts_h : 0;
+  {
+    const int n1 = n_anc + my_suffix;
+    const int mine = n1 > warp ? (n1 - warp + W - 1) / W : 0;
+    auto item = [&](int j) {
+      const int i = warp + j * W;
+      if (i < n_anc) return page_item(blist[i]);
+      const int chunk = part + (i - n_anc) * parts_h;
+      return make_int4(1, chunk * R, min(R, suffix_len - chunk * R), h);
+    };
+    if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
+                                            qb, p.scale, split, m, l, o, policy, lane)) {
+      timeout();
+    }
+  }
 
   // ---------------- phase B: row normalisers, decisions ---------------------
+  if (threadIdx.x == 0 && !wait_generation(gen_a, seen_a)) atomicOr(p.status, kStatusTimeout);
+  __syncthreads();
   for (int g = warp; g < p.group; g += W) {
-    const float* in = p.lse + (static_cast<size_t>(h) * p.group + g) * p.parts * W * 4;
+    const float* in = p.lse + (static_cast<size_t>(h) * p.group + g) * lse_parts * W * 4;
     float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    const int n_part = p.parts * W;
+    const int n_part = parts_h * W;
     for (int k0 = lane; k0 < n_part; k0 += 32 * 8) {
       float4 v[8];
 #pragma unroll
@@ -437,7 +624,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       sel = dec || bad || bad_global || anc;
     }
     if (b < p.blocks) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
-    const uint32_t listed = __ballot_sync(0xffffffffu, sel && !(stream && anc));
+    const uint32_t listed = __ballot_sync(0xffffffffu, sel && !anc);
     const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
     if (lane == 0) {
       sel_bits[k] = listed;
@@ -446,21 +633,21 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
 
-  // Compaction: warp 0 the attention list and the tiles with representatives,
-  // warp 1 (or 0) the anchored list; deterministic (block order).
+  // Compaction (block order): the selected blocks that are not anchored, and
+  // the tiles holding representatives.
   if (warp == 0) {
     int acc = 0, nreps = 0;
     for (int k0 = 0; k0 < n_t; k0 += 32) {
       const int k = k0 + lane;
-      const int c = k < n_t ? __popc(sel_bits[k]) : 0;
+      const int cnt = k < n_t ? __popc(sel_bits[k]) : 0;
       const bool has_rep = k < n_t && rep_bits[k] != 0u;
-      int incl = c;
+      int incl = cnt;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, incl, off);
         if (lane >= off) incl += y;
       }
-      if (k < n_t) offsets[k] = acc + incl - c;
+      if (k < n_t) offsets[k] = acc + incl - cnt;
       acc += __shfl_sync(0xffffffffu, incl, 31);
       const uint32_t rb = __ballot_sync(0xffffffffu, has_rep);
       if (has_rep) rep_list[nreps + __popc(rb & ((1u << lane) - 1u))] = k;
@@ -468,136 +655,28 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     }
     if (lane == 0) {
       flags[1] = nreps;
-      p.seg_count[h * p.parts + part] = acc;
+      flags[2] = acc;
     }
-  }
-  if (warp == (W > 1 ? 1 : 0)) {
-    int acc = 0;
-    for (int k0 = 0; k0 < n_t; k0 += 32) {
-      const int k = k0 + lane;
-      const int c = k < n_t ? __popc(anc_bits[k]) : 0;
-      int incl = c;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-      }
-      if (k < n_t) anc_off[k] = acc + incl - c;
-      acc += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) flags[2] = acc;
   }
   __syncthreads();
-  {
-    int* ids = p.sel_ids + (static_cast<size_t>(h) * p.parts + part) * p.seg_cap;
-    for (int k = warp; k < n_t; k += W) {
-      const uint32_t below = (1u << lane) - 1u;
-      const uint32_t sb = sel_bits[k], ab = anc_bits[k];
-      const int b = (t_lo + k) * T + lane;
-      if ((sb >> lane) & 1u) ids[offsets[k] + __popc(sb & below)] = b;
-      if ((ab >> lane) & 1u) anchored[anc_off[k] + __popc(ab & below)] = b;
-    }
+  for (int k = warp; k < n_t; k += W) {
+    const uint32_t sb = sel_bits[k];
+    if ((sb >> lane) & 1u) blist[offsets[k] + __popc(sb & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
   }
   __syncthreads();
 
-  // ---------------- anchored pages, then representatives --------------------
-  const int n_anc = flags[2], n_reps = flags[1];
-  float m[NT][2], l[NT][2], o[D / 16][NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    m[nt][0] = m[nt][1] = -INFINITY;
-    l[nt][0] = l[nt][1] = 0.f;
-#pragma unroll
-    for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
-  }
-  const bool split = p.split_probs != 0;
-  const int my_anc = n_anc > warp ? (n_anc - warp + W - 1) / W : 0;
-  if (my_anc > 0) {
-    uint32_t qb[D / 16][NT][2];
-    load_query_frags<D, NT>(qb, q, p.query_f32, p.group, p.dim, lane, false);
-    const int prompt_h = p.seq.prompt(h, p.prompt_length);
-    const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
-    // item j of this warp: block, physical page, valid rows
-    auto item = [&](int j, int& page, int& valid) {
-      const int block = anchored[warp + j * W];
-      page = block;
-      if (p.page_table != nullptr) {
-        page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride +
-                     block);
-        if (page < 0 || page >= p.pool_pages) {
-          if (lane == 0) atomicOr(p.status, kStatusBadInput);
-          page = 0;
-        }
-      }
-      valid = min(R, prompt_h - block * R);
-    };
-    auto issue_k = [&](int page) {
-      if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar_a, kPage);
-        tma_page_hint<D>(slice, &maps.key_pages, bar_a, pool_head, page, R, policy);
-      }
-    };
-    auto issue_v = [&](int page) {
-      if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar_b, kPage);
-        tma_page_hint<D>(slice + kPage, &maps.value_pages, bar_b, pool_head, page, R, policy);
-      }
-    };
-    int page, valid;
-    item(0, page, valid);
-    issue_k(page);
-    issue_v(page);
-    int issued_a = 1, issued_b = 1;
-    for (int j = 0; j < my_anc && !aborted; ++j) {
-      if (!warp_wait(bar_a, uses_a & 1)) {
-        timeout();
-        break;
-      }
-      ++uses_a;
-      float logit[R / 16][NT][4];
-      score_tile<R, D, NT>(smem_addr(slice), qb, logit, lane);
-#pragma unroll
-      for (int mt = 0; mt < R / 16; ++mt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            logit[mt][nt][c] = r < valid ? logit[mt][nt][c] * p.scale : -INFINITY;
-        }
-      __syncwarp();
-      int next_page = 0, next_valid = 0;
-      const bool more = j + 1 < my_anc;
-      if (more) {
-        item(j + 1, next_page, next_valid);
-        issue_k(next_page);
-        ++issued_a;
-      }
-      softmax_update<R, D, NT>(logit, m, l, o);
-      uint32_t hi[R / 16][NT][2], lo[R / 16][NT][2];
-      prob_frags<R, NT>(logit, hi, lo, split);
-      if (!warp_wait(bar_b, uses_b & 1)) {
-        timeout();
-        break;
-      }
-      ++uses_b;
-      accumulate_values<R, D, NT>(smem_addr(slice + kPage), hi, o, lane);
-      if (split) accumulate_values<R, D, NT>(smem_addr(slice + kPage), lo, o, lane);
-      __syncwarp();
-      if (more) {
-        issue_v(next_page);
-        ++issued_b;
-      }
-      valid = next_valid;
+  // ---------------- selected pages, then representatives --------------------
+  const int n_sel = flags[2], n_reps = flags[1];
+  {
+    const int mine = n_sel > warp ? (n_sel - warp + W - 1) / W : 0;
+    auto item = [&](int j) { return page_item(blist[warp + j * W]); };
+    if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
+                                            qb, p.scale, split, m, l, o, policy, lane)) {
+      timeout();
     }
-    // Copies still in flight after a timeout must land before the slice is reused.
-    for (; uses_a < static_cast<uint32_t>(issued_a); ++uses_a) mbar_wait(bar_a, uses_a & 1);
-    for (; uses_b < static_cast<uint32_t>(issued_b); ++uses_b) mbar_wait(bar_b, uses_b & 1);
   }
-  // Representatives of this warp's tiles (value-mean tiles double-buffered
-  // on the two barriers); logit z, value the block's value mean.
+  // Value-mean tiles double-buffered on the two barriers; logit z, value the
+  // block's value mean.
   const int my_reps = n_reps > warp ? (n_reps - warp + W - 1) / W : 0;
   if (my_reps > 0 && !aborted) {
     auto issue_rep = [&](int j) {
@@ -617,20 +696,20 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
 #pragma unroll
       for (int mt = 0; mt < T / 16; ++mt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int r = mt * 16 + (lane >> 2) + (c >> 1) * 8;
+        for (int cc = 0; cc < 4; ++cc) {
+          const int r = mt * 16 + (lane >> 2) + (cc >> 1) * 8;
           const bool rep = (reps >> r) & 1u;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const int g = nt * 8 + 2 * (lane & 3) + (c & 1);
-            lg[mt][nt][c] =
+            const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
+            lg[mt][nt][cc] =
                 (rep && g < p.group)
                     ? __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r)
                     : -INFINITY;
           }
         }
     };
-    int issued_a = uses_a, issued_b = uses_b;
+    uint32_t issued_a = uses_a, issued_b = uses_b;
     issue_rep(0);
     ++issued_a;
     if (my_reps > 1) {
@@ -652,9 +731,9 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
 #pragma unroll
       for (int mt = 0; mt < T / 16; ++mt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) logit[mt][nt][c] = next_logit[mt][nt][c];
+          for (int nt = 0; nt < NT; ++nt) logit[mt][nt][cc] = next_logit[mt][nt][cc];
       load_logits(j + 1, next_logit);
       attend_tile<T, D, NT>(logit, smem_addr(slice + (odd ? kSel : 0)), m, l, o, split, lane);
       __syncwarp();
@@ -663,9 +742,11 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
         if (odd) ++issued_b; else ++issued_a;
       }
     }
-    for (; uses_a < static_cast<uint32_t>(issued_a); ++uses_a) mbar_wait(bar_a, uses_a & 1);
-    for (; uses_b < static_cast<uint32_t>(issued_b); ++uses_b) mbar_wait(bar_b, uses_b & 1);
+    for (; uses_a < issued_a; ++uses_a) mbar_wait(bar_a, uses_a & 1);
+    for (; uses_b < issued_b; ++uses_b) mbar_wait(bar_b, uses_b & 1);
   }
+
+  // ---------------- this part's partial, then the row's output ---------------
   reduce_l<NT>(l);
   __syncthreads();  // every slice is idle: park the warps' partials there
   float* st_m = reinterpret_cast<float*>(smem);
@@ -673,9 +754,57 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   float* st_o = st_l + W * G8;
   stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
   __syncthreads();
-  const size_t slot = static_cast<size_t>(h) * p.parts + part;
-  merge_stashed<D>(st_m, st_l, st_o, W, G8, p.rep_m + slot * G8, p.rep_l + slot * G8,
-                   p.rep_o + slot * G8 * D, threadIdx.x, blockDim.x);
+  merge_stashed<D>(st_m, st_l, st_o, W, G8, p.part_m + static_cast<size_t>(c) * G8,
+                   p.part_l + static_cast<size_t>(c) * G8,
+                   p.part_o + static_cast<size_t>(c) * G8 * D, threadIdx.x, blockDim.x);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    arrive(arrive_b, gen_b, parts_h);
+    if (!wait_generation(gen_b, seen_b)) atomicOr(p.status, kStatusTimeout);
+  }
+  __syncthreads();
+  // Weights of the row's parts per group row: w = exp(m - max m), then this
+  // part's output channels [d0, d1).
+  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] weights
+  float* top = wgt + parts_h * G8;              // [G8] maxima, then [G8] denominators
+  float* den = top + G8;
+  for (int g = threadIdx.x; g < G8; g += blockDim.x) {
+    float mx = -INFINITY;
+    for (int k = 0; k < parts_h; ++k) mx = fmaxf(mx, __ldcg(p.part_m + (first_cta + k) * G8 + g));
+    top[g] = mx == -INFINITY ? 0.f : mx;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < parts_h * G8; i += blockDim.x) {
+    const int k = i / G8, g = i - k * G8;
+    const float mk = __ldcg(p.part_m + (first_cta + k) * G8 + g);
+    wgt[i] = mk == -INFINITY ? 0.f : fexp(mk - top[g]);
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < G8; g += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < parts_h; ++k) {
+      const float w = wgt[k * G8 + g];
+      if (w != 0.f) s += w * __ldcg(p.part_l + (first_cta + k) * G8 + g);
+    }
+    den[g] = s;
+  }
+  __syncthreads();
+  const int d0 = p.dim * part / parts_h, d1 = p.dim * (part + 1) / parts_h;
+  for (int i = threadIdx.x; i < (d1 - d0) * p.group; i += blockDim.x) {
+    const int g = i / (d1 - d0), d = d0 + (i - g * (d1 - d0));
+    float acc = 0.f;
+    for (int k = 0; k < parts_h; ++k) {
+      const float w = wgt[k * G8 + g];
+      if (w != 0.f) acc += w * __ldcg(p.part_o + (static_cast<size_t>(first_cta + k) * D + d) * G8 + g);
+    }
+    const float out = acc / fmaxf(den[g], 1e-30f);
+    const size_t at_ = (static_cast<size_t>(h) * p.group + g) * p.dim + d;
+    if (p.query_f32) {
+      static_cast<float*>(p.out)[at_] = out;
+    } else {
+      static_cast<__nv_bfloat16*>(p.out)[at_] = __float2bfloat16_rn(out);
+    }
+  }
 }
 
 template <int D, int R, int NT, bool PACK4, int GM>
@@ -685,7 +814,7 @@ cudaError_t launch_t(const FusedMaps& maps, const FusedParams& p, int warps, siz
   cudaError_t err = ensure_smem_limit(reinterpret_cast<const void*>(kernel), smem);
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.heads, p.parts);
+  cfg.gridDim = dim3(fused_grid(p.heads, p.parts_base, p.parts_extra));
   cfg.blockDim = dim3(warps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -717,6 +846,10 @@ cudaError_t launch_r(const FusedMaps& maps, const FusedParams& p, int warps, siz
 }
 
 }  // namespace
+
+int fused_grid(int heads, int parts_base, int parts_extra) {
+  return heads * parts_base + parts_extra;
+}
 
 size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap) {
   (void)group;

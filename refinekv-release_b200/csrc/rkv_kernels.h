@@ -115,50 +115,55 @@ struct FinalParams {
   int* status;
 };
 
-// Fused selector (rkv_fused.cu): phases A and B of one (row, part) tile
-// range in one CTA with a per-row barrier between them, plus the exact
-// attention of the range's anchored pages, folded into the CTA's
-// representative partial.
+// One-kernel decode (rkv_fused.cu): for a (KV-head row, part) tile range, in
+// one CTA, the selector's two phases (a per-row barrier between them), the
+// attention of every page the range needs (anchored, selected, the part's
+// share of the suffix) and its representatives, and -- after a second
+// per-row barrier -- the row's output channels of this part merged from all
+// parts' partials.  Row h has parts_base + 1 parts if h < parts_extra, else
+// parts_base; CTA c is part c - first(h) of its row.
 struct FusedMaps {
   CUtensorMap key_mean;     // [32 x 64] bf16 boxes, like StatsMaps / FinalMaps
   CUtensorMap ellipsoid;
   CUtensorMap value_mean;
   CUtensorMap key_pages;    // 4-D page maps, like AttendMaps
   CUtensorMap value_pages;
+  CUtensorMap key_suffix;   // 3-D row maps, like AttendMaps
+  CUtensorMap value_suffix;
 };
 
 struct FusedParams {
   const void* query;  // (heads, group, dim)
   int query_f32;
   int dim;            // real head dim
+  void* out;          // (heads, group, dim) in the query dtype
   const int64_t* counts;
   int heads, group, blocks, tiles;
-  int parts;          // CTAs per row; part k owns tiles [tiles*k/parts, tiles*(k+1)/parts)
+  int parts_base, parts_extra;  // parts per row (see above)
   int tcap;           // the largest tile count of a part (shared-memory tables)
   float scale, eps;
   int reduction;
   float* z;           // (heads*group, blocks)
   float* delta;
-  float* lse;         // (heads*group, parts * warps, 4)
+  float* lse;         // (heads*group, (parts_base + 1) * warps, 4)
   const float* value_norm;
   const float* max_value_norm;
   const uint8_t* anchor;  // (heads, blocks) or null
   uint8_t* mask;
   int split_probs;
-  int stream_anchors;     // anchored pages attended here; the attention list omits them
-  int* seg_count;         // (heads, parts): blocks of the attention list per part
-  int* sel_ids;           // (heads, parts, seg_cap)
-  int seg_cap;
-  float* rep_m;           // (heads, parts, G8): representatives and anchored pages
-  float* rep_l;
-  float* rep_o;           // (heads, parts, dim, G8)
-  unsigned* row_arrive;   // (heads,) per-row barrier: arrivals of this call
-  unsigned* row_gen;      // (heads,) per-row barrier: completed generations
+  float* part_m;          // (grid, G8): one softmax partial per CTA
+  float* part_l;
+  float* part_o;          // (grid, dim, G8)
+  unsigned* bar_words;    // per row: arrivals A, generations A, arrivals B, generations B
+  int bar_stride;         // words between those four arrays
   SeqLayout seq;
   int page, prompt_length;
   const int32_t* page_table;
   int page_table_stride;
   int pool_pages;
+  int has_suffix, suffix_capacity;
+  const int* suffix_len_ptr;
+  int suffix_len_host;
   int* status;
 };
 
@@ -271,5 +276,6 @@ size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, in
                          int parts_b);
 size_t combine_smem_bytes(int heads, int parts_b, int group, int max_sources);
 size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap);
+int fused_grid(int heads, int parts_base, int parts_extra);
 
 }  // namespace rkv

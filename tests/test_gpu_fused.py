@@ -1,13 +1,12 @@
-"""The fused selector against the two-kernel selector and the oracle (needs a B200).
+"""The one-kernel decode against the four-kernel decode and the oracle (needs a B200).
 
-rkv_decode runs, by default, one kernel for the selector's two phases (a
-per-row barrier between them) that also attends the anchored pages; the
-attention kernel then streams only the other selected pages and the suffix.
-rkv_set_fused_selector(0) switches back to the stats and final kernels with
-every selected page in the attention kernel.  Both paths must give the same
-masks outside the eps margin and outputs within the parity tolerance (bf16:
-atol 4e-3 + rtol 2e-2, max-abs 2e-2; fp32 queries: 1e-4), and each must
-match the oracle.
+rkv_decode runs, by default, one kernel per layer and step: the selector's
+two phases (a per-row barrier between them), every page the step needs, the
+representatives and the combine (a second per-row barrier).
+rkv_set_fused_selector(0) switches back to the stats, final, attention and
+combine kernels.  Both paths must give the same masks outside the eps margin
+and outputs within the parity tolerance (bf16: atol 4e-3 + rtol 2e-2, max-abs
+2e-2; fp32 queries: 1e-4), and each must match the oracle.
 """
 
 import contextlib
@@ -56,7 +55,7 @@ def test_fused_and_two_kernel_selectors_agree_and_match_the_oracle(
     cfg = RefineKVConfig(block_size=block, eps=0.01, anchor_tokens=anchors)
     summary = build_summary(data.keys, data.values, cfg)
     lib = _native.load()
-    assert lib.rkv_decode_kernel_count(heads, group, summary.num_blocks, dim, block) == 3
+    assert lib.rkv_decode_kernel_count(heads, group, summary.num_blocks, dim, block) == 1
     anchor = None
     if anchors:
         aq = synthetic.make_queries(11, 0, -1, data.planted_mean, group, anchors)
