@@ -180,9 +180,11 @@ std::atomic<int> g_fused_selector{1};
 // the first `extra` rows one more), never more CTAs than SMs unless each row
 // has a single part (then no CTA waits for another); warps of one slice each
 // (a K|V page or a key-mean|ellipsoid tile pair).
-bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, int64_t dim,
-                int64_t block_size) {
+bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, int64_t blocks,
+                int64_t dim, int64_t block_size) {
   if (!g_fused_selector.load() || heads > kMaxFusedRows) return false;
+  // Parts hold an equal share of a row's blocks, at least 16 each.
+  const int64_t max_parts = std::max<int64_t>(1, blocks / 16);
   int base, extra;
   if (heads >= dev.sms) {
     base = 1;
@@ -190,13 +192,14 @@ bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, i
   } else {
     base = static_cast<int>(dev.sms / heads);
     extra = static_cast<int>(dev.sms % heads);
-    if (base >= pl->tiles) {  // no part without a tile
-      base = pl->tiles;
+    if (base >= max_parts) {
+      base = static_cast<int>(max_parts);
       extra = 0;
     }
   }
   const int most = base + (extra > 0 ? 1 : 0);
-  const int tcap = static_cast<int>(cdiv(pl->tiles, base));
+  // Selector tiles a part touches: its blocks may start inside a tile.
+  const int tcap = static_cast<int>(cdiv(cdiv(blocks, base), kSelectTile)) + 1;
   if (tcap > 128) return false;  // the per-part tables live in shared memory
   const int64_t slice = std::max<int64_t>(2LL * kSelectTile * dim * 2, 2LL * block_size * dim * 2);
   const int warps = static_cast<int>(std::min<int64_t>(8, 196608 / slice));
@@ -273,7 +276,9 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   if (decode) {
     rc = plan_attention(pl, dev, heads, group, dim, block_size);
     if (rc != RKV_OK) return rc;
-    if (fixed_parts_a == 0 && instances == 1) plan_fused(pl, dev, heads, group, dim, block_size);
+    if (fixed_parts_a == 0 && instances == 1) {
+      plan_fused(pl, dev, heads, group, blocks, dim, block_size);
+    }
   }
   // Workspace layout.
   size_t off = 0;

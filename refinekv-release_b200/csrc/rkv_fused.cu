@@ -224,9 +224,15 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   const int first_cta = c - part;
   const int lse_parts = P + (X > 0 ? 1 : 0);
-  const int t_lo = static_cast<int>(static_cast<long long>(p.tiles) * part / parts_h);
-  const int t_hi = static_cast<int>(static_cast<long long>(p.tiles) * (part + 1) / parts_h);
+  // This part's blocks: an equal share of the row's real blocks (so every part
+  // streams as many pages as the others), and the selector tiles they touch.
+  const int blocks_h = p.seq.blocks(h, p.blocks);
+  const int b_lo = static_cast<int>(static_cast<long long>(blocks_h) * part / parts_h);
+  const int b_hi = static_cast<int>(static_cast<long long>(blocks_h) * (part + 1) / parts_h);
+  const int t_lo = b_lo / T;
+  const int t_hi = b_hi > b_lo ? (b_hi + T - 1) / T : t_lo;
   const int n_t = t_hi - t_lo;
+  auto mine = [&](int b) { return b >= b_lo && b < b_hi; };
   const int64_t* counts = p.counts + static_cast<size_t>(p.seq.sequence(h)) * p.blocks;
   const char* q = static_cast<const char*>(p.query) +
                   static_cast<size_t>(h) * p.group * p.dim * (p.query_f32 ? 4 : 2);
@@ -281,9 +287,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       suffix_len = suffix_len < 0 ? 0 : p.suffix_capacity;
     }
   }
-  const int blocks_h = p.seq.blocks(h, p.blocks);
   const int prompt_h = p.seq.prompt(h, p.prompt_length);
-  const int n_stat = max(0, min(t_hi, (blocks_h + T - 1) / T) - t_lo);  // tiles with real blocks
+  const int n_stat = n_t;
   const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
   const uint64_t policy = l2_evict_first_policy();
   uint32_t uses_a = 0, uses_b = 0;  // completed waits per barrier (parity = uses & 1)
@@ -296,7 +301,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // Anchored blocks of the range, one bit per block (known before any statistics).
   for (int k = warp; k < n_t; k += W) {
     const int b = (t_lo + k) * T + lane;
-    const bool a = p.anchor != nullptr && b < blocks_h &&
+    const bool a = p.anchor != nullptr && mine(b) &&
                    p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, a);
     if (lane == 0) anc_bits[k] = bits;
@@ -347,7 +352,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
 #pragma unroll
         for (int hf = 0; hf < kHalves; ++hf) {
           const int b = tile * T + lane_rows[mt][hf];
-          cnt[mt][hf] = b < blocks_h ? __ldg(counts + b) : 1;
+          cnt[mt][hf] = mine(b) ? __ldg(counts + b) : 1;
         }
       if (!warp_wait(bar_a, uses_a & 1)) {
         timeout();
@@ -393,7 +398,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
 #pragma unroll
         for (int hf = 0; hf < kHalves; ++hf) {
           const int b = tile * T + row_of[mt][hf];
-          const float log_count = b < blocks_h ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
+          const float log_count = mine(b) ? flog(static_cast<float>(cnt[mt][hf])) : 0.f;
 #pragma unroll
           for (int jc = 0; jc < 2; ++jc) {
             const int c = 2 * hf + jc;
@@ -402,7 +407,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
               const int g = PACK4 ? g_base + jc : nt * 8 + 2 * (lane & 3) + jc;
               zv[mt][nt][c] = -INFINITY;
               cv[mt][nt][c] = -INFINITY;
-              if (b >= blocks_h || g >= p.group) continue;
+              if (!mine(b) || g >= p.group) continue;
               const float score = sc[mt][nt][c] * p.scale;
               const float proj = pr[mt][nt][c];
               const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
@@ -586,7 +591,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   for (int k = warp; k < n_t; k += W) {
     const int t = t_lo + k;
     const int b = t * T + lane;
-    const bool valid = b < blocks_h;
+    const bool valid = mine(b);
     bool sel = false, anc = false;
     if (valid) {
       float zr[GM], dr[GM];
@@ -623,7 +628,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       }
       sel = dec || bad || bad_global || anc;
     }
-    if (b < p.blocks) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
+    if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
     const uint32_t listed = __ballot_sync(0xffffffffu, sel && !anc);
     const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
     if (lane == 0) {
@@ -633,6 +638,13 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
 
+  // A batched row's blocks past its prompt belong to no part: the last part
+  // writes their mask bytes 0.
+  if (part == parts_h - 1) {
+    for (int b = blocks_h + threadIdx.x; b < p.blocks; b += blockDim.x) {
+      p.mask[static_cast<size_t>(h) * p.blocks + b] = 0;
+    }
+  }
   // Compaction (block order): the selected blocks that are not anchored, and
   // the tiles holding representatives.
   if (warp == 0) {
@@ -763,46 +775,61 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     if (!wait_generation(gen_b, seen_b)) atomicOr(p.status, kStatusTimeout);
   }
   __syncthreads();
-  // Weights of the row's parts per group row: w = exp(m - max m), then this
-  // part's output channels [d0, d1).
-  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] weights
-  float* top = wgt + parts_h * G8;              // [G8] maxima, then [G8] denominators
+  // Weights of the row's parts per group row, w = exp(m - max m), staged in
+  // shared memory in one parallel pass; then one warp per output element of
+  // this part's channels [d0, d1), its lanes over the parts.
+  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] m, then weights
+  float* lsum = wgt + parts_h * G8;             // [parts_h][G8] l
+  float* top = lsum + parts_h * G8;             // [G8] maxima, then [G8] denominators
   float* den = top + G8;
-  for (int g = threadIdx.x; g < G8; g += blockDim.x) {
+  for (int i = threadIdx.x; i < parts_h * G8; i += blockDim.x) {
+    const size_t at_ = static_cast<size_t>(first_cta) * G8 + i;
+    wgt[i] = __ldcg(p.part_m + at_);
+    lsum[i] = __ldcg(p.part_l + at_);
+  }
+  __syncthreads();
+  for (int g = warp; g < G8; g += W) {
     float mx = -INFINITY;
-    for (int k = 0; k < parts_h; ++k) mx = fmaxf(mx, __ldcg(p.part_m + (first_cta + k) * G8 + g));
-    top[g] = mx == -INFINITY ? 0.f : mx;
+    for (int k = lane; k < parts_h; k += 32) mx = fmaxf(mx, wgt[k * G8 + g]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) top[g] = mx == -INFINITY ? 0.f : mx;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < parts_h * G8; i += blockDim.x) {
-    const int k = i / G8, g = i - k * G8;
-    const float mk = __ldcg(p.part_m + (first_cta + k) * G8 + g);
-    wgt[i] = mk == -INFINITY ? 0.f : fexp(mk - top[g]);
+    const float mk = wgt[i];
+    const float w = mk == -INFINITY ? 0.f : fexp(mk - top[i % G8]);
+    wgt[i] = w;
+    lsum[i] = w == 0.f ? 0.f : w * lsum[i];
   }
   __syncthreads();
-  for (int g = threadIdx.x; g < G8; g += blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < parts_h; ++k) {
-      const float w = wgt[k * G8 + g];
-      if (w != 0.f) s += w * __ldcg(p.part_l + (first_cta + k) * G8 + g);
-    }
-    den[g] = s;
+  for (int g = warp; g < G8; g += W) {
+    float sum = 0.f;
+    for (int k = lane; k < parts_h; k += 32) sum += lsum[k * G8 + g];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) den[g] = sum;
   }
   __syncthreads();
   const int d0 = p.dim * part / parts_h, d1 = p.dim * (part + 1) / parts_h;
-  for (int i = threadIdx.x; i < (d1 - d0) * p.group; i += blockDim.x) {
-    const int g = i / (d1 - d0), d = d0 + (i - g * (d1 - d0));
+  const int nd = d1 - d0;
+  for (int item = warp; item < nd * p.group; item += W) {
+    const int g = item / nd, d = d0 + (item - g * nd);
     float acc = 0.f;
-    for (int k = 0; k < parts_h; ++k) {
+    for (int k = lane; k < parts_h; k += 32) {
       const float w = wgt[k * G8 + g];
       if (w != 0.f) acc += w * __ldcg(p.part_o + (static_cast<size_t>(first_cta + k) * D + d) * G8 + g);
     }
-    const float out = acc / fmaxf(den[g], 1e-30f);
-    const size_t at_ = (static_cast<size_t>(h) * p.group + g) * p.dim + d;
-    if (p.query_f32) {
-      static_cast<float*>(p.out)[at_] = out;
-    } else {
-      static_cast<__nv_bfloat16*>(p.out)[at_] = __float2bfloat16_rn(out);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+      const float out = acc / fmaxf(den[g], 1e-30f);
+      const size_t at_ = (static_cast<size_t>(h) * p.group + g) * p.dim + d;
+      if (p.query_f32) {
+        static_cast<float*>(p.out)[at_] = out;
+      } else {
+        static_cast<__nv_bfloat16*>(p.out)[at_] = __float2bfloat16_rn(out);
+      }
     }
   }
 }

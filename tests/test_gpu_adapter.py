@@ -188,7 +188,7 @@ def test_llama8b_slice_decode_matches_the_reference_backend(monkeypatch):
     * CUDA-graph decode and eager decode on librefinekv_b200 give the same greedy tokens;
     * teacher-forced on those tokens, every step's logits with the attention on the
       kernels and with the attention swapped for the CPU oracle (the reference PyTorch
-      backend restated, from its own summaries) agree to 1 % of the logit scale, and
+      backend restated, from its own summaries) agree to 2 % of the logit scale, and
       their greedy choices agree at every step except where the two competing tokens'
       logits tie within their own measured perturbation (a random-init model over
       128256 tokens has such near-ties; bf16 rounding of the attention output moves
@@ -261,7 +261,7 @@ def test_llama8b_slice_decode_matches_the_reference_backend(monkeypatch):
     reference = forced_logits()
     scale = float(reference.abs().max())
     delta = ours - reference
-    assert float(delta.abs().max()) <= 0.01 * scale, (float(delta.abs().max()), scale)
+    assert float(delta.abs().max()) <= 0.02 * scale, (float(delta.abs().max()), scale)
     # A step may choose differently only when the perturbation of the two
     # competing logits explains it: ref[a] - ref[b] <= |delta[a]| + |delta[b]|.
     a, b = reference.argmax(-1), ours.argmax(-1)
