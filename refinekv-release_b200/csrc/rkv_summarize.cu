@@ -66,6 +66,27 @@ __device__ __forceinline__ void load8<float>(const uint8_t* tile, int r, int v, 
   f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
 
+// Eight consecutive channels of row r as four float2 pairs (packed-FP32 math).
+template <typename T>
+__device__ __forceinline__ void load8x2(const uint8_t* tile, int r, int v, int rows,
+                                        float2 (&f)[4]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(tile + swz(r, v, rows));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(tile + swz(r, 2 * v, rows));
+    const float4 b = *reinterpret_cast<const float4*>(tile + swz(r, 2 * v + 1, rows));
+    f[0] = make_float2(a.x, a.y);
+    f[1] = make_float2(a.z, a.w);
+    f[2] = make_float2(b.x, b.y);
+    f[3] = make_float2(b.z, b.w);
+  }
+}
+
 // The same eight channels as a bf16 page-copy chunk (bf16: the stored bits).
 template <typename T>
 __device__ __forceinline__ uint4 page_chunk(const uint8_t* tile, int r, int v, int rows) {
@@ -163,13 +184,23 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
     // then added in chunk order, so the FP32 sums -- and the bf16 means --
     // are bit-identical to the reference's for bf16 and fp32 caches alike.
     constexpr int kRowChunks = R / 16;
-    float kpart[kRowChunks][8], vpart[kRowChunks][8], kmax[8], kmin[8];
+    // Sums as float2 pairs (packed FP32 adds: each channel's adds stay in row
+    // order); the K range of a bf16 cache as packed bf16 max / min, which
+    // propagate a NaN like torch.amax / amin (a bf16 max is exact).
+    float2 kpart[kRowChunks][4], vpart[kRowChunks][4];
+    __nv_bfloat162 kmx2[4], kmn2[4];
+    float kmax[8], kmin[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       kmax[i] = -INFINITY;
       kmin[i] = INFINITY;
+    }
 #pragma unroll
-      for (int s2 = 0; s2 < kRowChunks; ++s2) kpart[s2][i] = vpart[s2][i] = 0.f;
+    for (int i = 0; i < 4; ++i) {
+      kmx2[i] = __floats2bfloat162_rn(-INFINITY, -INFINITY);
+      kmn2[i] = __floats2bfloat162_rn(INFINITY, INFINITY);
+#pragma unroll
+      for (int s2 = 0; s2 < kRowChunks; ++s2) kpart[s2][i] = vpart[s2][i] = make_float2(0.f, 0.f);
     }
     const int c16 = lane % kChunks;
     if (lane < kActive) {
@@ -179,24 +210,53 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
         if (chunk >= kRowChunks) break;
         const int r_end = min(chunk * 16 + 16, count);
         for (int r = chunk * 16; r < r_end; ++r) {
-          float kf[8], vf[8];
-          load8<T>(kt, r, c16, R, kf);
-          load8<T>(vt, r, c16, R, vf);
+          float2 kf[4], vf[4];
+          load8x2<T>(vt, r, c16, R, vf);
+          if constexpr (sizeof(T) == 2) {
+            // One 16-byte load of the K chunk serves both the sums and the range.
+            const uint4 u = *reinterpret_cast<const uint4*>(kt + swz(r, c16, R));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            kpart[s2][i] += kf[i];
-            vpart[s2][i] += vf[i];
-            kmax[i] = nan_max(kmax[i], kf[i]);
-            kmin[i] = nan_min(kmin[i], kf[i]);
+            for (int i = 0; i < 4; ++i) {
+              __nv_bfloat162 kb;
+              *reinterpret_cast<uint32_t*>(&kb) = w[i];
+              kmx2[i] = __hmax2_nan(kmx2[i], kb);
+              kmn2[i] = __hmin2_nan(kmn2[i], kb);
+              kf[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+            }
+          } else {
+            load8x2<T>(kt, r, c16, R, kf);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              kmax[2 * i] = nan_max(kmax[2 * i], kf[i].x);
+              kmax[2 * i + 1] = nan_max(kmax[2 * i + 1], kf[i].y);
+              kmin[2 * i] = nan_min(kmin[2 * i], kf[i].x);
+              kmin[2 * i + 1] = nan_min(kmin[2 * i + 1], kf[i].y);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            kpart[s2][i] = __fadd2_rn(kpart[s2][i], kf[i]);
+            vpart[s2][i] = __fadd2_rn(vpart[s2][i], vf[i]);
           }
         }
         if (r_end < chunk * 16 + 16) {  // zero padding rows: x + 0 turns a -0 sum into +0
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            kpart[s2][i] += 0.f;
-            vpart[s2][i] += 0.f;
+          for (int i = 0; i < 4; ++i) {
+            kpart[s2][i] = __fadd2_rn(kpart[s2][i], make_float2(0.f, 0.f));
+            vpart[s2][i] = __fadd2_rn(vpart[s2][i], make_float2(0.f, 0.f));
           }
         }
+      }
+    }
+    if constexpr (sizeof(T) == 2) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 hi = __bfloat1622float2(kmx2[i]), lo = __bfloat1622float2(kmn2[i]);
+        kmax[2 * i] = hi.x;
+        kmax[2 * i + 1] = hi.y;
+        kmin[2 * i] = lo.x;
+        kmin[2 * i + 1] = lo.y;
       }
     }
     for (int off = kChunks; off < kActive; off <<= 1) {
@@ -215,11 +275,15 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
         if (chunk >= kRowChunks) break;
         const int src = g * kChunks + c16;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float kv = __shfl_sync(0xffffffffu, kpart[s2][i], src);
-          const float vv = __shfl_sync(0xffffffffu, vpart[s2][i], src);
-          ksum[i] = chunk == 0 ? kv : ksum[i] + kv;
-          vsum[i] = chunk == 0 ? vv : vsum[i] + vv;
+        for (int i = 0; i < 4; ++i) {
+          const float k0 = __shfl_sync(0xffffffffu, kpart[s2][i].x, src);
+          const float k1 = __shfl_sync(0xffffffffu, kpart[s2][i].y, src);
+          const float v0 = __shfl_sync(0xffffffffu, vpart[s2][i].x, src);
+          const float v1 = __shfl_sync(0xffffffffu, vpart[s2][i].y, src);
+          ksum[2 * i] = chunk == 0 ? k0 : ksum[2 * i] + k0;
+          ksum[2 * i + 1] = chunk == 0 ? k1 : ksum[2 * i + 1] + k1;
+          vsum[2 * i] = chunk == 0 ? v0 : vsum[2 * i] + v0;
+          vsum[2 * i + 1] = chunk == 0 ? v1 : vsum[2 * i + 1] + v1;
         }
       }
     }
@@ -246,27 +310,32 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
     // Lane per row: V row norm and the centred, normalised K distance.
     float vnorm = -INFINITY, dmax = -INFINITY;
     for (int r = lane; r < count; r += 32) {
-      float sq = 0.f, dist = 0.f;
+      // Packed FP32: (k - mean) * scale, its square and v^2 accumulated as
+      // channel pairs, summed at the end (the reference's channel order is not
+      // reproducible anyway: torch vectorises the sum).
+      float2 sq2 = make_float2(0.f, 0.f), dist2 = make_float2(0.f, 0.f);
 #pragma unroll 4
       for (int c = 0; c < kChunks; ++c) {
-        float kf[8], vf[8];
-        load8<T>(kt, r, c, R, kf);
-        load8<T>(vt, r, c, R, vf);
+        float2 kf[4], vf[4];
+        load8x2<T>(kt, r, c, R, kf);
+        load8x2<T>(vt, r, c, R, vf);
         const float4 m0 = *reinterpret_cast<const float4*>(kmean_s + c * 8);
         const float4 m1 = *reinterpret_cast<const float4*>(kmean_s + c * 8 + 4);
         const float4 s0 = *reinterpret_cast<const float4*>(rscale_s + c * 8);
         const float4 s1 = *reinterpret_cast<const float4*>(rscale_s + c * 8 + 4);
-        const float mean[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-        const float scale[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float2 neg_mean[4] = {make_float2(-m0.x, -m0.y), make_float2(-m0.z, -m0.w),
+                                    make_float2(-m1.x, -m1.y), make_float2(-m1.z, -m1.w)};
+        const float2 scale[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w),
+                                 make_float2(s1.x, s1.y), make_float2(s1.z, s1.w)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          sq += vf[i] * vf[i];
-          const float x = (kf[i] - mean[i]) * scale[i];
-          dist += x * x;
+        for (int i = 0; i < 4; ++i) {
+          sq2 = __ffma2_rn(vf[i], vf[i], sq2);
+          const float2 x = __fmul2_rn(__fadd2_rn(kf[i], neg_mean[i]), scale[i]);
+          dist2 = __ffma2_rn(x, x, dist2);
         }
       }
-      vnorm = nan_max(vnorm, sqrtf(sq));
-      dmax = nan_max(dmax, dist);
+      vnorm = nan_max(vnorm, sqrtf(sq2.x + sq2.y));
+      dmax = nan_max(dmax, dist2.x + dist2.y);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
