@@ -32,11 +32,12 @@ namespace rkv {
 namespace {
 
 // Shared-memory layout (also sized by the host): a TMA slice per warp, two
-// mbarriers per warp, row normalisers, per-tile bit masks and lists, and the
-// list of the part's selected blocks.  The warps' final partials, then the
-// parts' weights, are parked in the slices.
+// mbarriers per warp, row normalisers, per-tile bit masks and lists, and one
+// block list (anchored blocks, then the selected non-anchored ones).  The
+// warps' final partials, then the parts' (max, sum), are parked in the slices.
 struct FusedLayout {
-  size_t bars, norms, flags, sel_bits, rep_bits, anc_bits, offsets, rep_list, blocks, bytes;
+  size_t bars, norms, flags, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off, anchored,
+      bytes;
   __host__ __device__ FusedLayout(int warps, int slice, int tcap) {
     const size_t t = static_cast<size_t>(tcap);
     size_t off = static_cast<size_t>(warps) * slice;
@@ -53,7 +54,8 @@ struct FusedLayout {
     anc_bits = take(t * 4);        // [tcap] uint32
     offsets = take((t + 1) * 4);   // [tcap + 1] int
     rep_list = take(t * 4);        // [tcap] int
-    blocks = take(t * kSelectTile * 4);  // [tcap * 32] int: the selected blocks
+    anc_off = take((t + 1) * 4);   // [tcap + 1] int
+    anchored = take(t * kSelectTile * 4);  // [tcap * 32] int
     bytes = off + kSmemSlack;
   }
 };
@@ -203,7 +205,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   uint32_t* anc_bits = reinterpret_cast<uint32_t*>(smem + lay.anc_bits);  // [tcap]
   int* offsets = reinterpret_cast<int*>(smem + lay.offsets);             // [tcap + 1]
   int* rep_list = reinterpret_cast<int*>(smem + lay.rep_list);           // [tcap]
-  int* blist = reinterpret_cast<int*>(smem + lay.blocks);                // [tcap * 32]
+  int* anc_off = reinterpret_cast<int*>(smem + lay.anc_off);             // [tcap + 1]
+  int* blist = reinterpret_cast<int*>(smem + lay.anchored);              // [tcap * 32]
 
   // This CTA's row and part.
   const int c = blockIdx.x;
@@ -302,26 +305,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                    p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, a);
     if (lane == 0) anc_bits[k] = bits;
-  }
-
-  __syncthreads();
-  // The first pages this warp will stream (blocks b_lo + warp and
-  // b_lo + warp + W when they are anchored, hence selected whatever the
-  // decisions) go to L2 now: DRAM would otherwise idle through the
-  // statistics and the decisions.
-  if (lane == 0) {
-    for (int j = 0; j < 2; ++j) {
-      const int b = b_lo + warp + j * W;
-      if (b < b_hi && ((anc_bits[(b / T) - t_lo] >> (b % T)) & 1u)) {
-        int page = b;
-        if (p.page_table != nullptr) {
-          page = __ldg(p.page_table + static_cast<size_t>(p.seq.sequence(h)) * p.page_table_stride + b);
-          page = (page < 0 || page >= p.pool_pages) ? 0 : page;
-        }
-        tma_prefetch_page<D>(&maps.key_pages, pool_head, page);
-        tma_prefetch_page<D>(&maps.value_pages, pool_head, page);
-      }
-    }
   }
 
   // ---------------- phase A: statistics of this warp's tiles ----------------
@@ -497,6 +480,32 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
   if (threadIdx.x == 0) arrive(arrive_a, gen_a, parts_h);
+
+  // The anchored list (block order) while the other parts finish phase A.
+  if (warp == (W > 1 ? 1 : 0)) {
+    int acc = 0;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int cnt = k < n_t ? __popc(anc_bits[k]) : 0;
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) anc_off[k] = acc + incl - cnt;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) flags[2] = acc;
+  }
+  __syncthreads();
+  for (int k = warp; k < n_t; k += W) {
+    const uint32_t ab = anc_bits[k];
+    if ((ab >> lane) & 1u) blist[anc_off[k] + __popc(ab & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
+  }
+  __syncthreads();
+
+  // ---------------- attention known before the decisions -------------------
   float m[NT][2], l[NT][2], o[D / 16][NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -506,6 +515,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     for (int dt = 0; dt < D / 16; ++dt) o[dt][nt][0] = o[dt][nt][1] = o[dt][nt][2] = o[dt][nt][3] = 0.f;
   }
   const bool split = p.split_probs != 0;
+  uint32_t qb[D / 16][NT][2];
+  load_query_frags<D, NT>(qb, q, p.query_f32, p.group, p.dim, lane, false);
   // A page of block `block`: physical page (page table), valid rows.
   auto page_item = [&](int block) {
     int page = block;
@@ -519,8 +530,23 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     }
     return make_int4(0, page, min(R, prompt_h - block * R), pool_head);
   };
+  const int n_anc = flags[2];
   const int n_suffix = (suffix_len + R - 1) / R;                          // chunks of the row
   const int my_suffix = n_suffix > part ? (n_suffix - part + parts_h - 1) / parts_h : 0;
+  {
+    const int n1 = n_anc + my_suffix;
+    const int mine = n1 > warp ? (n1 - warp + W - 1) / W : 0;
+    auto item = [&](int j) {
+      const int i = warp + j * W;
+      if (i < n_anc) return page_item(blist[i]);
+      const int chunk = part + (i - n_anc) * parts_h;
+      return make_int4(1, chunk * R, min(R, suffix_len - chunk * R), h);
+    };
+    if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
+                                            qb, p.scale, split, m, l, o, policy, lane)) {
+      timeout();
+    }
+  }
 
   // ---------------- phase B: row normalisers, decisions ---------------------
   if (threadIdx.x == 0 && !wait_generation(gen_a, seen_a)) atomicOr(p.status, kStatusTimeout);
@@ -603,7 +629,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       sel = dec || bad || bad_global || anc;
     }
     if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
-    const uint32_t listed = __ballot_sync(0xffffffffu, sel);
+    const uint32_t listed = __ballot_sync(0xffffffffu, sel && !anc);
     const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
     if (lane == 0) {
       sel_bits[k] = listed;
@@ -619,8 +645,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       p.mask[static_cast<size_t>(h) * p.blocks + b] = 0;
     }
   }
-  // Compaction (block order): the selected blocks (anchored ones included),
-  // and the tiles holding representatives.
+  // Compaction (block order): the selected blocks that are not anchored, and
+  // the tiles holding representatives.
   if (warp == 0) {
     int acc = 0, nreps = 0;
     for (int k0 = 0; k0 < n_t; k0 += 32) {
@@ -651,19 +677,11 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
 
-  // ---------------- selected pages, this part's suffix, representatives ----
+  // ---------------- selected pages, then representatives --------------------
   const int n_sel = flags[2], n_reps = flags[1];
   {
-    uint32_t qb[D / 16][NT][2];
-    load_query_frags<D, NT>(qb, q, p.query_f32, p.group, p.dim, lane, false);
-    const int n1 = n_sel + my_suffix;
-    const int mine = n1 > warp ? (n1 - warp + W - 1) / W : 0;
-    auto item = [&](int j) {
-      const int i = warp + j * W;
-      if (i < n_sel) return page_item(blist[i]);
-      const int chunk = part + (i - n_sel) * parts_h;
-      return make_int4(1, chunk * R, min(R, suffix_len - chunk * R), h);
-    };
+    const int mine = n_sel > warp ? (n_sel - warp + W - 1) / W : 0;
+    auto item = [&](int j) { return page_item(blist[warp + j * W]); };
     if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
                                             qb, p.scale, split, m, l, o, policy, lane)) {
       timeout();
