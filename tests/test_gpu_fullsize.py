@@ -9,9 +9,9 @@ CUDA path; at steps 0, 1, 63 and 127 of every layer the step is judged
 against the CPU oracle (a restatement of the reference PyTorch backend
 pinned to the reference's own outputs):
 
-* summaries: counts exact, bf16 means / ellipsoid within 2 bf16 ulp on under
-  2 % of elements, norms within 2e-6 relative, against the oracle's own
-  summary of the same K/V;
+* summaries: counts and bf16 means bit-exact, the ellipsoid within 2 bf16 ulp
+  on under 2 % of elements, norms within 2e-6 relative, against the oracle's
+  own summary of the same K/V;
 * masks: equal to the oracle's outside the eps margin (blocks whose decisive
   risk lies within 1e-3 relative of eps), with the oracle deciding from the
   GPU's summary; margin blocks are counted and reported;
@@ -75,7 +75,10 @@ def _summary_ulps(gpu, want):
     for name in ("key_mean", "value_mean", "ellipsoid"):
         ulp = bf16_ulp_diff(getattr(gpu, name).cpu(), getattr(want, name))
         worst[name] = (int(ulp.max()), float((ulp > 0).float().mean()))
-        assert worst[name][0] <= 2 and worst[name][1] < 0.02, (name, worst[name])
+        # The means are sums in the reference's own FP32 order: bit-exact.  The
+        # ellipsoid's centred radius sums channels in another order (<= 2 ulp).
+        limit = 0 if name != "ellipsoid" else 2
+        assert worst[name][0] <= limit and worst[name][1] < 0.02, (name, worst[name])
     torch.testing.assert_close(gpu.value_norm.cpu(), want.value_norm, rtol=2e-6, atol=1e-6)
     torch.testing.assert_close(gpu.max_value_norm.cpu(), want.max_value_norm, rtol=2e-6,
                                atol=1e-6)

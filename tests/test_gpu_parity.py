@@ -1,8 +1,9 @@
 """CUDA path vs. the CPU oracle and the reference's golden outputs (needs a B200).
 
 Tolerances (stated by the north star and the reference tests):
-* summaries: counts and page copies exact; bf16 means/ellipsoid within 1-2
-  bf16 ulp (FP32 summation order differs from torch's CPU kernels);
+* summaries: counts, page copies and bf16 means exact (the K/V sums follow
+  the reference's FP32 order); the ellipsoid within 1-2 bf16 ulp (its
+  channel sum is vectorised in another order by torch's CPU kernels);
 * masks: identical except blocks whose decisive risk lies within 1e-3
   (relative) of eps, which are counted and reported separately;
 * outputs: atol 4e-3 + rtol 2e-2 (reference test_attention.py:183) and a
@@ -28,12 +29,15 @@ def _gpu(t):
 
 
 def assert_summary_close(gpu, want, *, max_ulp=2):
+    """Means bit-exact (the summarizer adds in the reference's FP32 order); the
+    ellipsoid within `max_ulp` bf16 ulp on under 2 % of elements."""
     assert torch.equal(gpu.counts.cpu(), want["counts"] if isinstance(want, dict) else want.counts)
     get = (lambda n: want[n]) if isinstance(want, dict) else (lambda n: getattr(want, n))
-    for name in ("key_mean", "value_mean", "ellipsoid"):
-        ulp = bf16_ulp_diff(getattr(gpu, name).cpu(), get(name))
-        assert int(ulp.max()) <= max_ulp, (name, int(ulp.max()))
-        assert float((ulp > 0).float().mean()) < 0.02, name
+    for name in ("key_mean", "value_mean"):
+        assert torch.equal(getattr(gpu, name).cpu(), get(name)), name
+    ulp = bf16_ulp_diff(gpu.ellipsoid.cpu(), get("ellipsoid"))
+    assert int(ulp.max()) <= max_ulp, ("ellipsoid", int(ulp.max()))
+    assert float((ulp > 0).float().mean()) < 0.02, "ellipsoid"
     torch.testing.assert_close(gpu.value_norm.cpu(), get("value_norm"), rtol=2e-6, atol=1e-6)
     torch.testing.assert_close(gpu.max_value_norm.cpu(), get("max_value_norm"), rtol=2e-6,
                                atol=1e-6)
