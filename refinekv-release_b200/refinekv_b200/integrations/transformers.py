@@ -408,7 +408,9 @@ class RefineKV:
     }
 
     def _graph_arguments(self, args, kwargs):
-        """Validation of ``transformers.py:304-382``; returns (input_ids, max_new_tokens, penalty, mask)."""
+        """Restates the reference's graph-generation contract (``transformers.py:304-382``):
+        the same whitelist, checks and messages, so callers see the same errors.
+        Returns (input_ids, max_new_tokens, penalty, mask)."""
         unsupported = set(kwargs) - self._GRAPH_KWARGS
         if unsupported:
             raise ValueError(f"CUDA Graph generation does not support {sorted(unsupported)}")
@@ -463,7 +465,8 @@ class RefineKV:
         return input_ids, max_new_tokens, penalty, mask
 
     def _generate_cuda_graph(self, *args, **kwargs):
-        """Prefill eagerly, capture one greedy decode step, replay it (``transformers.py:302-440``)."""
+        """Prefill eagerly, capture one greedy decode step, replay it: restates the
+        reference's warm-up, capture and replay protocol (``transformers.py:302-440``)."""
         input_ids, max_new_tokens, penalty, mask = self._graph_arguments(args, kwargs)
         device = input_ids.device
         rows, prompt_length = input_ids.shape
