@@ -288,13 +288,30 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
       }
     }
     const float cnt = static_cast<float>(count);
+    // A full page holds a power-of-two count: x * 2^-k is the correctly
+    // rounded x / 2^k (both round the same real number), so the means take a
+    // multiply there and the IEEE division only on a partial last page.
+    if ((count & (count - 1)) == 0) {
+      const float inv = __frcp_rn(cnt);  // exact: cnt is a power of two
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ksum[i] *= inv;
+        vsum[i] *= inv;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ksum[i] /= cnt;
+        vsum[i] /= cnt;
+      }
+    }
     float width2[8];
     if (lane < kChunks) {
       float kmean[8], vmean[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        kmean[i] = bf16_round(ksum[i] / cnt);
-        vmean[i] = bf16_round(vsum[i] / cnt);
+        kmean[i] = bf16_round(ksum[i]);
+        vmean[i] = bf16_round(vsum[i]);
         float w = nan_max(kmax[i] - kmean[i], kmean[i] - kmin[i]);
         w = w < 1e-6f ? 1e-6f : w;
         width2[i] = bf16_round(w * w);
