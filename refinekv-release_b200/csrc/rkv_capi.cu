@@ -314,7 +314,7 @@ int make_plan(Plan* pl, int64_t heads, int64_t group, int64_t blocks, int64_t di
   if (pl->fused) {  // the one-kernel decode's regions, after the same header
     off = kHeaderBytes;
     const int most = pl->parts_base + (pl->parts_extra > 0 ? 1 : 0);
-    pl->f_lse = take(rowsg * most * pl->warps_f * 4 * 4);
+    pl->f_lse = take(rowsg * most * 4 * 4);  // one (max, sum) pair of z and of c per part
     pl->f_z = take(rowsg * blocks * 4);
     pl->f_delta = take(rowsg * blocks * 4);
     pl->f_part_m = take(static_cast<size_t>(pl->grid_f) * pl->g8 * 4);

@@ -8,18 +8,20 @@
 // (the host sizes it; one CTA per SM by shared memory).  A CTA:
 //   1. phase A: z and delta of every (group row, block) of its tiles from the
 //      key-mean and ellipsoid tiles (TMA, mma.sync), stored for phase B, and
-//      one log-sum-exp partial per warp; arrives at the row's barrier A;
+//      one log-sum-exp partial per part; arrives at the row's barrier A;
 //   2. streams, without waiting, the pages whose attention is known before
 //      any decision: its anchored blocks (selected whatever the risk,
 //      reference.py:54-55) and its share of the generated suffix;
-//   3. waits at barrier A (by then normally passed), merges the row's
-//      partials into log Z / log C, decides every block of its tiles (risk,
-//      GQA reduction, non-finite override, anchors), writes the mask, and
-//      streams its selected non-anchored pages and the representatives of
-//      its unselected blocks (value means, logit z);
-//   4. merges its warps into one softmax partial, arrives at barrier B, and
-//      once every part of the row is there writes its slice of the row's
-//      output channels from all parts' partials.
+//   3. unless every block of its range is anchored: waits at barrier A (by
+//      then normally passed), merges the row's partials into log Z / log C,
+//      decides every block of its tiles (risk, GQA reduction, non-finite
+//      override), writes the mask, and streams its selected non-anchored
+//      pages and the representatives of its unselected blocks (value means,
+//      logit z);
+//   4. merges its warps into one softmax partial; in a row of at most
+//      kLastParts parts the part that arrives last writes the row's output
+//      from all parts' partials, in a longer row the parts meet at barrier B
+//      and each writes its slice of the output channels.
 // Every wait is bounded (status bit on timeout).  The order of the work is
 // static (block order, warps round-robin), so results are deterministic.
 // The page arithmetic is the attention kernel's (rkv_attend.cu): the same
@@ -36,8 +38,8 @@ namespace {
 // block list (anchored blocks, then the selected non-anchored ones).  The
 // warps' final partials, then the parts' (max, sum), are parked in the slices.
 struct FusedLayout {
-  size_t bars, norms, flags, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off, anchored,
-      bytes;
+  size_t bars, norms, flags, lse, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off,
+      anchored, bytes;
   __host__ __device__ FusedLayout(int warps, int slice, int tcap) {
     const size_t t = static_cast<size_t>(tcap);
     size_t off = static_cast<size_t>(warps) * slice;
@@ -49,6 +51,7 @@ struct FusedLayout {
     bars = take(static_cast<size_t>(warps) * 2 * 8);
     norms = take(2 * kMaxGroup * 4);
     flags = take(8 * 4);
+    lse = take(static_cast<size_t>(warps) * kMaxGroup * 16);  // [warps][16] float4
     sel_bits = take(t * 4);        // [tcap] uint32
     rep_bits = take(t * 4);        // [tcap] uint32
     anc_bits = take(t * 4);        // [tcap] uint32
@@ -79,17 +82,35 @@ __device__ __forceinline__ bool wait_generation(const unsigned* word, unsigned s
   }
 }
 
-// Arrival of one part at a row barrier (thread 0, after the CTA's writes and a
-// CTA barrier): the last of `parts` arrivals resets the count and moves the
-// generation on, so the words are clean for the next call.
-__device__ __forceinline__ void arrive(unsigned* count, unsigned* gen, int parts) {
-  __threadfence();
-  const unsigned before = atomicAdd(count, 1u);
-  if (before == static_cast<unsigned>(parts) - 1u) {
-    atomicExch(count, 0u);
-    __threadfence();
-    atomicAdd(gen, 1u);
-  }
+// Release/acquire at GPU scope: an arrival publishes the writes that precede
+// it (its own and, through a CTA or warp barrier, its CTA's), and the last
+// arrival acquires everyone's before it moves the generation on.
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* word, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+               : "=r"(old) : "l"(word), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void red_add_release(unsigned* word, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(word), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void store_relaxed(unsigned* word, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(word), "r"(v) : "memory");
+}
+
+// Arrival of one part at a row barrier (one thread, after a CTA or warp
+// barrier that follows the writes it publishes): the last of `parts`
+// arrivals resets the count and moves the generation on, so the words are
+// clean for the next call (which starts after this grid has completed).
+// Returns whether this was the last arrival.
+__device__ __forceinline__ bool arrive(unsigned* count, unsigned* gen, int parts) {
+  const unsigned before = atom_add_acq_rel(count, 1u);
+  if (before != static_cast<unsigned>(parts) - 1u) return false;
+  store_relaxed(count, 0u);
+  if (gen != nullptr) red_add_release(gen, 1u);
+  return true;
 }
 
 __device__ __forceinline__ unsigned read_generation(const unsigned* word) {
@@ -101,17 +122,22 @@ __device__ __forceinline__ unsigned read_generation(const unsigned* word) {
 // Streams `count` items of one warp -- K|V pages or suffix chunks of R rows --
 // through the warp's slice with separate K and V barriers (K refilled as soon
 // as the scores are done), into the running softmax (m, l, o).  item(j)
-// returns {suffix?, page or first suffix row, valid rows, head coordinate}.
+// returns {suffix?, page or first suffix row, valid rows, head coordinate};
+// pre() runs once, after the first page's copies are issued (or at once when
+// there is nothing to stream).
 // False on a timeout, after the copies in flight have landed.
-template <int R, int D, int NT, typename ItemFn>
-__device__ __forceinline__ bool stream_items(int count, ItemFn item, const FusedMaps& maps,
+template <int R, int D, int NT, typename ItemFn, typename PreFn>
+__device__ __forceinline__ bool stream_items(int count, ItemFn item, PreFn pre, const FusedMaps& maps,
                                              uint8_t* slice, uint64_t* bar_a, uint64_t* bar_b,
                                              uint32_t& uses_a, uint32_t& uses_b,
                                              const uint32_t (&qb)[D / 16][NT][2], float scale,
                                              bool split, float (&m)[NT][2], float (&l)[NT][2],
                                              float (&o)[D / 16][NT][4], uint64_t policy,
                                              int lane) {
-  if (count <= 0) return true;
+  if (count <= 0) {
+    pre();
+    return true;
+  }
   constexpr int kPage = R * D * 2;
   auto issue = [&](const int4& it, bool value) {
     if (lane == 0) {
@@ -131,6 +157,7 @@ __device__ __forceinline__ bool stream_items(int count, ItemFn item, const Fused
   int4 cur = item(0);
   issue(cur, false);
   issue(cur, true);
+  pre();  // runs while the first page lands
   uint32_t issued_a = uses_a + 1, issued_b = uses_b + 1;
   bool ok = true;
   for (int j = 0; j < count; ++j) {
@@ -180,6 +207,43 @@ __device__ __forceinline__ bool stream_items(int count, ItemFn item, const Fused
   return ok;
 }
 
+// Rows of at most this many parts are merged by the part that arrives last.
+constexpr int kLastParts = 32;
+
+// Row stride of a stashed warp partial: 4 floats of padding keep the stash's
+// stores (lanes 2 group rows apart) and the merge's loads (lanes one group row
+// apart) on distinct banks.
+template <int D>
+constexpr int kStashStride = D + 4;
+
+// A warp's final (m, l, o^T) into shared memory: m[W][G8], l[W][G8] and
+// o[W][G8][kStashStride].
+template <int D, int NT>
+__device__ __forceinline__ void stash_padded(float* sm_m, float* sm_l, float* sm_o, int warp,
+                                             int lane, const float (&m)[NT][2],
+                                             const float (&l)[NT][2],
+                                             const float (&o)[D / 16][NT][4]) {
+  constexpr int G8 = NT * 8;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int g = nt * 8 + 2 * (lane & 3) + j;
+      if (lane < 4) {
+        sm_m[warp * G8 + g] = m[nt][j];
+        sm_l[warp * G8 + g] = l[nt][j];
+      }
+      float* row = sm_o + (warp * G8 + g) * kStashStride<D>;
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        const int d0 = dt * 16 + (lane >> 2);
+        row[d0] = o[dt][nt][j];
+        row[d0 + 8] = o[dt][nt][2 + j];
+      }
+    }
+  }
+}
+
 // PACK4: group of at most 4 rows (q and q^2 share one n8 tile); GM: group
 // rows evaluated per block in phase B (padded to 4, 8 or 16).
 template <int D, int R, int NT, bool PACK4, int GM>
@@ -199,7 +263,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   uint64_t* bar_b = bar_a + 1;
   float* lz = reinterpret_cast<float*>(smem + lay.norms);
   float* lc = lz + kMaxGroup;
-  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 listed
+  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 listed, 3 last
+  float4* lse_s = reinterpret_cast<float4*>(smem + lay.lse);              // [W][kMaxGroup]
   uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.sel_bits);  // [tcap]
   uint32_t* rep_bits = reinterpret_cast<uint32_t*>(smem + lay.rep_bits);  // [tcap]
   uint32_t* anc_bits = reinterpret_cast<uint32_t*>(smem + lay.anc_bits);  // [tcap]
@@ -272,6 +337,14 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // Every CTA of this grid has started once all have passed here, so a grid
   // launched early behind this one can never hold an SM one of ours needs.
   pdl_launch_dependents();
+  const uint64_t policy = l2_evict_first_policy();
+  // This warp's first phase-A tile is in flight while the anchor bits, the
+  // query and the counts load.
+  if (lane == 0 && warp < n_t) {
+    mbar_expect_tx(bar_a, 2 * kSel);
+    tma_tile_hint<D>(slice, &maps.key_mean, bar_a, (t_lo + warp) * T, h, T, policy);
+    tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, (t_lo + warp) * T, h, T, policy);
+  }
   // The row's barrier generations before this part's arrivals (they move only
   // once every part, this one included, has arrived).
   unsigned seen_a = 0, seen_b = 0;
@@ -290,7 +363,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   const int prompt_h = p.seq.prompt(h, p.prompt_length);
   const int n_stat = n_t;
   const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
-  const uint64_t policy = l2_evict_first_policy();
   uint32_t uses_a = 0, uses_b = 0;  // completed waits per barrier (parity = uses & 1)
   bool aborted = false;
   auto timeout = [&]() {
@@ -305,6 +377,29 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                    p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, a);
     if (lane == 0) anc_bits[k] = bits;
+  }
+  __syncthreads();
+  // The anchored list (block order) while the first phase-A tiles land.
+  if (warp == (W > 1 ? 1 : 0)) {
+    int acc = 0;
+    for (int k0 = 0; k0 < n_t; k0 += 32) {
+      const int k = k0 + lane;
+      const int cnt = k < n_t ? __popc(anc_bits[k]) : 0;
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      if (k < n_t) anc_off[k] = acc + incl - cnt;
+      acc += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) flags[2] = acc;
+  }
+  __syncthreads();
+  for (int k = warp; k < n_t; k += W) {
+    const uint32_t ab = anc_bits[k];
+    if ((ab >> lane) & 1u) blist[anc_off[k] + __popc(ab & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
   }
 
   // ---------------- phase A: statistics of this warp's tiles ----------------
@@ -337,10 +432,12 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     for (int k = warp; k < n_stat && !aborted; k += W) {
       const int tile = t_lo + k;
       if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar_a, 2 * kSel);
-        tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
-        tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
+        if (k != warp) {  // the first tile was issued after the dependency wait
+          fence_proxy_async();
+          mbar_expect_tx(bar_a, 2 * kSel);
+          tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
+          tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
+        }
         if (k + W < n_stat) {  // one stage per warp: warm L2 with the next tile meanwhile
           tma_prefetch_tile<D>(&maps.key_mean, (tile + W) * T, h);
           tma_prefetch_tile<D>(&maps.ellipsoid, (tile + W) * T, h);
@@ -471,39 +568,28 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
         }
         const bool writer = PACK4 ? lane < 2 : lane < 4;
         const int g = PACK4 ? 2 * lane + j : nt * 8 + 2 * lane + j;
-        if (writer && g < p.group) {
-          float* out = p.lse + ((static_cast<size_t>(h) * p.group + g) * lse_parts * W +
-                                static_cast<size_t>(part) * W + warp) * 4;
-          *reinterpret_cast<float4*>(out) = make_float4(mz, sz, mc, sc);
-        }
+        if (writer && g < p.group) lse_s[warp * kMaxGroup + g] = make_float4(mz, sz, mc, sc);
       }
   }
   __syncthreads();
-  if (threadIdx.x == 0) arrive(arrive_a, gen_a, parts_h);
-
-  // The anchored list (block order) while the other parts finish phase A.
-  if (warp == (W > 1 ? 1 : 0)) {
-    int acc = 0;
-    for (int k0 = 0; k0 < n_t; k0 += 32) {
-      const int k = k0 + lane;
-      const int cnt = k < n_t ? __popc(anc_bits[k]) : 0;
-      int incl = cnt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
+  // One partial per part and group row, the warps' pairs merged in warp order
+  // (warps without tiles hold empty pairs), by the last warp, which then
+  // arrives at barrier A -- while its first page lands.
+  auto publish_stats = [&]() {
+    if (warp != W - 1) return;
+    if (lane < p.group) {
+      float4 acc = lse_s[lane];
+      for (int w = 1; w < W; ++w) {
+        const float4 v = lse_s[w * kMaxGroup + lane];
+        lse_merge(acc.x, acc.y, v.x, v.y);
+        lse_merge(acc.z, acc.w, v.z, v.w);
       }
-      if (k < n_t) anc_off[k] = acc + incl - cnt;
-      acc += __shfl_sync(0xffffffffu, incl, 31);
+      *reinterpret_cast<float4*>(
+          p.lse + ((static_cast<size_t>(h) * p.group + lane) * lse_parts + part) * 4) = acc;
     }
-    if (lane == 0) flags[2] = acc;
-  }
-  __syncthreads();
-  for (int k = warp; k < n_t; k += W) {
-    const uint32_t ab = anc_bits[k];
-    if ((ab >> lane) & 1u) blist[anc_off[k] + __popc(ab & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
-  }
-  __syncthreads();
+    __syncwarp();
+    if (lane == 0) arrive(arrive_a, gen_a, parts_h);
+  };
 
   // ---------------- attention known before the decisions -------------------
   float m[NT][2], l[NT][2], o[D / 16][NT][4];
@@ -542,67 +628,92 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       const int chunk = part + (i - n_anc) * parts_h;
       return make_int4(1, chunk * R, min(R, suffix_len - chunk * R), h);
     };
-    if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
-                                            qb, p.scale, split, m, l, o, policy, lane)) {
+    if (aborted) {
+      publish_stats();
+    } else if (!stream_items<R, D, NT>(mine, item, publish_stats, maps, slice, bar_a, bar_b,
+                                       uses_a, uses_b, qb, p.scale, split, m, l, o, policy,
+                                       lane)) {
       timeout();
     }
   }
 
   // ---------------- phase B: row normalisers, decisions ---------------------
-  if (threadIdx.x == 0 && !wait_generation(gen_a, seen_a)) atomicOr(p.status, kStatusTimeout);
-  __syncthreads();
-  for (int g = warp; g < p.group; g += W) {
-    const float* in = p.lse + (static_cast<size_t>(h) * p.group + g) * lse_parts * W * 4;
-    float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
-    const int n_part = parts_h * W;
-    for (int k0 = lane; k0 < n_part; k0 += 32 * 8) {
-      float4 v[8];
+  // A part whose every block is anchored decides nothing: its blocks are
+  // selected whatever the risk (reference.py:54-55) and it holds no
+  // representatives, so it neither waits for the row's normalisers nor reads
+  // its statistics back.
+  const bool all_anchored = n_anc == b_hi - b_lo;
+  if (!all_anchored) {
+    if (threadIdx.x == 0 && !wait_generation(gen_a, seen_a)) atomicOr(p.status, kStatusTimeout);
+    __syncthreads();
+    for (int g = warp; g < p.group; g += W) {
+      const float* in = p.lse + (static_cast<size_t>(h) * p.group + g) * lse_parts * 4;
+      float m0 = -INFINITY, s0 = 0.f, m1 = -INFINITY, s1 = 0.f;
+      for (int k0 = lane; k0 < parts_h; k0 += 32 * 8) {
+        float4 v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int k = k0 + 32 * u;
-        v[u] = k < n_part ? __ldcg(reinterpret_cast<const float4*>(in + 4 * k))
-                          : make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
+        for (int u = 0; u < 8; ++u) {
+          const int k = k0 + 32 * u;
+          v[u] = k < parts_h ? __ldcg(reinterpret_cast<const float4*>(in + 4 * k))
+                             : make_float4(-INFINITY, 0.f, -INFINITY, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          lse_merge(m0, s0, v[u].x, v[u].y);
+          lse_merge(m1, s1, v[u].z, v[u].w);
+        }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        lse_merge(m0, s0, v[u].x, v[u].y);
-        lse_merge(m1, s1, v[u].z, v[u].w);
+      for (int off = 16; off > 0; off >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m0, off);
+        const float os = __shfl_xor_sync(0xffffffffu, s0, off);
+        const float pm = __shfl_xor_sync(0xffffffffu, m1, off);
+        const float ps = __shfl_xor_sync(0xffffffffu, s1, off);
+        lse_merge(m0, s0, om, os);
+        lse_merge(m1, s1, pm, ps);
       }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, m0, off);
-      const float os = __shfl_xor_sync(0xffffffffu, s0, off);
-      const float pm = __shfl_xor_sync(0xffffffffu, m1, off);
-      const float ps = __shfl_xor_sync(0xffffffffu, s1, off);
-      lse_merge(m0, s0, om, os);
-      lse_merge(m1, s1, pm, ps);
-    }
-    if (lane == 0) {
-      const float zl = m0 + flog(s0), cl = m1 + flog(s1);
-      lz[g] = zl;
-      lc[g] = cl;
-      if (!finite(zl) || !finite(cl)) atomicOr(&flags[0], 1);
+      if (lane == 0) {
+        const float zl = m0 + flog(s0), cl = m1 + flog(s1);
+        lz[g] = zl;
+        lc[g] = cl;
+        if (!finite(zl) || !finite(cl)) atomicOr(&flags[0], 1);
+      }
     }
   }
   __syncthreads();
   const bool bad_global = flags[0] != 0;
-  const float vmax = __ldg(p.max_value_norm + h);
-  for (int k = warp; k < n_t; k += W) {
-    const int t = t_lo + k;
-    const int b = t * T + lane;
-    const bool valid = mine(b);
-    bool sel = false, anc = false;
-    if (valid) {
-      float zr[GM], dr[GM];
+  const float vmax = all_anchored ? 0.f : __ldg(p.max_value_norm + h);
+  // A lane's block of tile k needs a decision when it is this part's and not
+  // anchored; the statistics of the warp's next tile load while this tile's
+  // risks are evaluated.
+  float zr[GM], dr[GM], vn = 0.f;
+  auto load_stats = [&](int k, float (&zs)[GM], float (&ds)[GM], float& v) {
+    const int b = (t_lo + k) * T + lane;
+    const bool need = k < n_t && mine(b) && !((anc_bits[k] >> lane) & 1u);
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        const size_t row = static_cast<size_t>(h) * p.group + (g < p.group ? g : 0);
-        zr[g] = __ldcg(p.z + row * p.blocks + b);
-        dr[g] = __ldcg(p.delta + row * p.blocks + b);
-      }
-      const float vn = __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
-      anc = p.anchor != nullptr && p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
+    for (int g = 0; g < GM; ++g) {
+      const size_t row = static_cast<size_t>(h) * p.group + g;
+      const bool live = need && g < p.group;
+      zs[g] = live ? __ldcg(p.z + row * p.blocks + b) : 0.f;
+      ds[g] = live ? __ldcg(p.delta + row * p.blocks + b) : 0.f;
+    }
+    v = need ? __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b) : 0.f;
+  };
+  // (Sixteen group rows keep one tile's statistics live at a time: registers.)
+  constexpr bool kAhead = GM <= 8;
+  if (kAhead && warp < n_t) load_stats(warp, zr, dr, vn);
+  for (int k = warp; k < n_t; k += W) {
+    float zn[GM] = {}, dn[GM] = {}, vnn = 0.f;
+    if constexpr (kAhead) {
+      if (k + W < n_t) load_stats(k + W, zn, dn, vnn);
+    } else {
+      load_stats(k, zr, dr, vn);
+    }
+    const int b = (t_lo + k) * T + lane;
+    const bool valid = mine(b);
+    const bool anc = (anc_bits[k] >> lane) & 1u;
+    bool sel = anc;
+    if (valid && !anc) {
       float agg = p.reduction == kMax ? -INFINITY : 0.f;
       bool any = false, bad = false;
 #pragma unroll
@@ -626,15 +737,21 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       } else {
         dec = any;
       }
-      sel = dec || bad || bad_global || anc;
+      sel = dec || bad || bad_global;
     }
     if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
-    const uint32_t listed = __ballot_sync(0xffffffffu, sel && !anc);
+    const uint32_t listed = __ballot_sync(0xffffffffu, valid && sel && !anc);
     const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
     if (lane == 0) {
       sel_bits[k] = listed;
       rep_bits[k] = reps;
     }
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      zr[g] = zn[g];
+      dr[g] = dn[g];
+    }
+    vn = vnn;
   }
   __syncthreads();
 
@@ -682,8 +799,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   {
     const int mine = n_sel > warp ? (n_sel - warp + W - 1) / W : 0;
     auto item = [&](int j) { return page_item(blist[warp + j * W]); };
-    if (!aborted && !stream_items<R, D, NT>(mine, item, maps, slice, bar_a, bar_b, uses_a, uses_b,
-                                            qb, p.scale, split, m, l, o, policy, lane)) {
+    if (!aborted && !stream_items<R, D, NT>(mine, item, [] {}, maps, slice, bar_a, bar_b, uses_a,
+                                            uses_b, qb, p.scale, split, m, l, o, policy, lane)) {
       timeout();
     }
   }
@@ -761,31 +878,100 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // ---------------- this part's partial, then the row's output ---------------
   reduce_l<NT>(l);
   __syncthreads();  // every slice is idle: park the warps' partials there
-  float* st_m = reinterpret_cast<float*>(smem);
-  float* st_l = st_m + W * G8;
-  float* st_o = st_l + W * G8;
-  stash_warp_partial<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
-  __syncthreads();
-  merge_stashed<D>(st_m, st_l, st_o, W, G8, p.part_m + static_cast<size_t>(c) * G8,
-                   p.part_l + static_cast<size_t>(c) * G8,
-                   p.part_o + static_cast<size_t>(c) * G8 * D, threadIdx.x, blockDim.x);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    arrive(arrive_b, gen_b, parts_h);
-    if (!wait_generation(gen_b, seen_b)) atomicOr(p.status, kStatusTimeout);
+  {
+    float* st_m = reinterpret_cast<float*>(smem);      // [W][G8]
+    float* st_l = st_m + W * G8;                       // [W][G8]
+    float* st_w = st_l + W * G8;                       // [W][G8] merge weights
+    float* st_o = st_w + W * G8;                       // [W][G8][kStashStride]
+    stash_padded<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
+    __syncthreads();
+    if (threadIdx.x < G8) {  // per group row: the part's max, weights, sum
+      const int g = threadIdx.x;
+      float top = -INFINITY;
+      for (int w = 0; w < W; ++w) top = fmaxf(top, st_m[w * G8 + g]);
+      const float ref = top == -INFINITY ? 0.f : top;
+      float den = 0.f;
+      for (int w = 0; w < W; ++w) {
+        const float mw = st_m[w * G8 + g];
+        const float sw = mw == -INFINITY ? 0.f : __expf(mw - ref);
+        st_w[w * G8 + g] = sw;
+        den += sw * st_l[w * G8 + g];
+      }
+      p.part_m[static_cast<size_t>(c) * G8 + g] = top;
+      p.part_l[static_cast<size_t>(c) * G8 + g] = den;
+    }
+    __syncthreads();
+    float* out_o = p.part_o + static_cast<size_t>(c) * G8 * D;
+    for (int idx = threadIdx.x; idx < G8 * D; idx += blockDim.x) {
+      const int d = idx / G8, g = idx - d * G8;
+      float acc = 0.f;
+      for (int w = 0; w < W; ++w) acc += st_w[w * G8 + g] * st_o[(w * G8 + g) * kStashStride<D> + d];
+      out_o[idx] = acc;  // o^T: [d][g]
+    }
   }
   __syncthreads();
-  // Weights of the row's parts per group row, w = exp(m - max m), staged in
-  // shared memory in one parallel pass; then one warp per output element of
-  // this part's channels [d0, d1), its lanes over the parts.
+  // Rows of at most kLastParts parts: the part that arrives last merges the
+  // whole row (no part waits for another).  Longer rows meet at barrier B and
+  // every part writes its slice of the channels.
+  int c0 = 0, c1 = p.dim;
+  if (parts_h <= kLastParts) {
+    if (threadIdx.x == 0) flags[3] = arrive(arrive_b, nullptr, parts_h) ? 1 : 0;
+    __syncthreads();
+    if (flags[3] == 0) return;
+  } else {
+    if (threadIdx.x == 0) {
+      arrive(arrive_b, gen_b, parts_h);
+      if (!wait_generation(gen_b, seen_b)) atomicOr(p.status, kStatusTimeout);
+    }
+    __syncthreads();
+    c0 = p.dim * part / parts_h;
+    c1 = p.dim * (part + 1) / parts_h;
+  }
+  // The row's output from its parts' partials: teams of tp threads per
+  // (channel, 4 group rows), each thread over every tp-th part.  The first
+  // pass's partial rows load first, then the parts' (max, sum) pairs are
+  // staged in shared memory as weights w = exp(m - max m) and sums w * l.
+  const int g4s = (p.group + 3) >> 2;
+  const int items = (c1 - c0) * g4s;
+  int tp = 32;
+  while (tp > 1 && tp * items > static_cast<int>(blockDim.x)) tp >>= 1;
+  const int teams = blockDim.x / tp, t_in = threadIdx.x % tp;
+  constexpr int kAheadParts = 16;  // partial rows a thread holds while the weights are staged
+  float4 ahead[kAheadParts];
+  {
+    const int item = threadIdx.x / tp;
+    const bool ok = item < items;
+    const int d = c0 + (ok ? item / g4s : 0), g0 = ok ? 4 * (item % g4s) : 0;
+#pragma unroll
+    for (int u = 0; u < kAheadParts; ++u) {
+      const int k = u * tp + t_in;
+      ahead[u] = ok && k < parts_h
+                     ? __ldcg(reinterpret_cast<const float4*>(
+                           p.part_o + (static_cast<size_t>(first_cta + k) * D + d) * G8 + g0))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] m, then weights
-  float* lsum = wgt + parts_h * G8;             // [parts_h][G8] l
-  float* top = lsum + parts_h * G8;             // [G8] maxima, then [G8] denominators
-  float* den = top + G8;
-  for (int i = threadIdx.x; i < parts_h * G8; i += blockDim.x) {
-    const size_t at_ = static_cast<size_t>(first_cta) * G8 + i;
-    wgt[i] = __ldcg(p.part_m + at_);
-    lsum[i] = __ldcg(p.part_l + at_);
+  float* lsum = wgt + parts_h * G8;             // [parts_h][G8] l, then w * l
+  float* top = lsum + parts_h * G8;             // [G8] maxima
+  float* den = top + G8;                        // [G8] denominators
+  for (int i0 = 0; i0 < parts_h * G8; i0 += 4 * blockDim.x) {
+    float mv[4], lv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * blockDim.x + threadIdx.x;
+      const size_t at_ = static_cast<size_t>(first_cta) * G8 + i;
+      mv[u] = i < parts_h * G8 ? __ldcg(p.part_m + at_) : 0.f;
+      lv[u] = i < parts_h * G8 ? __ldcg(p.part_l + at_) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * blockDim.x + threadIdx.x;
+      if (i < parts_h * G8) {
+        wgt[i] = mv[u];
+        lsum[i] = lv[u];
+      }
+    }
   }
   __syncthreads();
   for (int g = warp; g < G8; g += W) {
@@ -811,24 +997,62 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     if (lane == 0) den[g] = sum;
   }
   __syncthreads();
-  const int d0 = p.dim * part / parts_h, d1 = p.dim * (part + 1) / parts_h;
-  const int nd = d1 - d0;
-  for (int item = warp; item < nd * p.group; item += W) {
-    const int g = item / nd, d = d0 + (item - g * nd);
-    float acc = 0.f;
-    for (int k = lane; k < parts_h; k += 32) {
-      const float w = wgt[k * G8 + g];
-      if (w != 0.f) acc += w * __ldcg(p.part_o + (static_cast<size_t>(first_cta + k) * D + d) * G8 + g);
-    }
+  auto add_part = [&](float4& acc, int k, int g0, const float4& v) {
+    const float4 w = *reinterpret_cast<const float4*>(wgt + k * G8 + g0);
+    acc.x += w.x != 0.f ? w.x * v.x : 0.f;
+    acc.y += w.y != 0.f ? w.y * v.y : 0.f;
+    acc.z += w.z != 0.f ? w.z * v.z : 0.f;
+    acc.w += w.w != 0.f ? w.w * v.w : 0.f;
+  };
+  for (int base = 0; base < items; base += teams) {  // uniform trip count: shuffles below
+    const int item = base + threadIdx.x / tp;
+    const bool ok = item < items;
+    const int d = c0 + (ok ? item / g4s : 0), g0 = ok ? 4 * (item % g4s) : 0;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int k_from = 0;
+    if (base == 0) {  // the rows loaded ahead
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) {
-      const float out = acc / fmaxf(den[g], 1e-30f);
-      const size_t at_ = (static_cast<size_t>(h) * p.group + g) * p.dim + d;
-      if (p.query_f32) {
-        static_cast<float*>(p.out)[at_] = out;
-      } else {
-        static_cast<__nv_bfloat16*>(p.out)[at_] = __float2bfloat16_rn(out);
+      for (int u = 0; u < kAheadParts; ++u) {
+        const int k = u * tp + t_in;
+        if (ok && k < parts_h) add_part(acc, k, g0, ahead[u]);
+      }
+      k_from = kAheadParts * tp;
+    }
+    for (int k0 = k_from; k0 < parts_h; k0 += 8 * tp) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int k = k0 + u * tp + t_in;
+        v[u] = ok && k < parts_h
+                   ? __ldcg(reinterpret_cast<const float4*>(
+                         p.part_o + (static_cast<size_t>(first_cta + k) * D + d) * G8 + g0))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int k = k0 + u * tp + t_in;
+        if (ok && k < parts_h) add_part(acc, k, g0, v[u]);
+      }
+    }
+    for (int off = tp >> 1; off > 0; off >>= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+      acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+      acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+    }
+    if (ok && t_in == 0) {
+      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int g = g0 + j;
+        if (g >= p.group) break;
+        const float out = a4[j] / fmaxf(den[g], 1e-30f);
+        const size_t at_ = (static_cast<size_t>(h) * p.group + g) * p.dim + d;
+        if (p.query_f32) {
+          static_cast<float*>(p.out)[at_] = out;
+        } else {
+          static_cast<__nv_bfloat16*>(p.out)[at_] = __float2bfloat16_rn(out);
+        }
       }
     }
   }

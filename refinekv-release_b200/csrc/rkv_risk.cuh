@@ -27,7 +27,10 @@ __device__ __forceinline__ float log_cosh(float delta) {
 }
 
 // Risk of one (row, block): distortion ("mass") + importance ("value") terms,
-// evaluated in the same operation order as reference.py:25-34.
+// evaluated in the same operation order as reference.py:25-34.  1/t is the
+// correctly rounded reciprocal (the value of the reference's t.reciprocal());
+// the tanh quotients take the fast division (within 2 ulp), like the
+// exponentials far inside the eps margin.
 // Only the branch the reference selects is evaluated (delta <= 10, else the
 // large-delta forms; a NaN takes the latter, as torch.where does).
 __device__ __forceinline__ float block_risk(float z, float delta, float log_z, float log_c,
@@ -36,15 +39,15 @@ __device__ __forceinline__ float block_risk(float z, float delta, float log_z, f
   float mass, tanh_half;
   if (delta <= kDeltaSplit) {
     const float t = fexp(delta);
-    mass = (two_vmax * fexp(z - log_c)) * (0.5f * (t + 1.f / t) - 1.f);
-    tanh_half = (t - 1.f) / (t + 1.f);
+    mass = (two_vmax * fexp(z - log_c)) * (0.5f * (t + __frcp_rn(t)) - 1.f);
+    tanh_half = __fdividef(t - 1.f, t + 1.f);
   } else {
     const float e_neg = fexp(-delta);
     float one_minus = 1.f - e_neg;
     one_minus = one_minus < 1e-30f ? 1e-30f : one_minus;
     const float lcm1 = (delta + 2.f * flog(one_minus)) - 0.693147182464599609375f;
     mass = two_vmax * fexp((z - log_c) + lcm1);
-    tanh_half = (1.f - e_neg) / (1.f + e_neg);
+    tanh_half = __fdividef(1.f - e_neg, 1.f + e_neg);
   }
   const float importance = ((2.f * vnorm) * fexp(z - log_z)) * tanh_half;
   return mass + importance;
