@@ -713,7 +713,23 @@ def run_b200(args):
     unselected = launches * heads_local * nb - pages
     summary_bytes = (heads_local * nb * D * 2 * 2 + nb * 8 + heads_local * nb * 4 + heads_local * 4
                      + heads_local * nb * (2 if args.anchors else 1))
-    step_bytes = args.layers * (summary_bytes + qo_bytes) + (
+
+    def statistics_rows(L, counts):
+        # The one-kernel decode reads no statistics (key means, ellipsoids,
+        # norms, counts) for a row whose every real block is anchored: none of
+        # its blocks is decided or represented.
+        if not fused or L.anchor is None:
+            return heads_local
+        real = (counts if counts.ndim == 2 else counts.expand(heads_local, -1)) > 0
+        return heads_local - int((L.anchor | ~real).all(dim=1).sum())
+
+    stat_rows_layers = [statistics_rows(L, c) for L, c in zip(layers, counts_all)]
+    mask_bytes = heads_local * nb * (2 if args.anchors else 1)
+    stat_bytes_layers = [
+        summary_bytes if r == heads_local else
+        r * nb * (D * 2 * 2 + 4) + (nb * 8 + heads_local * 4 if r else 0) + mask_bytes
+        for r in stat_rows_layers]
+    step_bytes = sum(stat_bytes_layers) + args.layers * qo_bytes + (
         tokens_refined * D * 4 + unselected * D * 2 + suffix_total * D * 4) / args.steps
     # Per launch.  One-kernel decode: the whole layer-step (summaries, value
     # means of the unselected blocks, every selected page, the suffix, q and
@@ -960,6 +976,9 @@ def run_b200(args):
                  "attend_achieved_gbs": round(attend_gbs, 1)}),
             "one_kernel_decode": fused,
             "anchored_fraction": round(anchored_pages / (args.layers * heads_local * nb), 5),
+            # layer-rows decoded without statistics (every block anchored)
+            "rows_without_statistics": round(
+                1.0 - sum(stat_rows_layers) / (args.layers * heads_local), 4),
             "selected_fraction": round(pages / (launches * heads_local * nb), 5),
             # median over layers (layer 0 carries one-time module loading)
             "summarize_us_per_layer": round(statistics.median(summarize_ms) * 1e3, 1),

@@ -90,7 +90,7 @@ struct Plan {
   // parts_extra parts per row, tcap_f the largest tile range of a part; its
   // own workspace regions (the same allocation, another layout).
   bool fused = false;
-  int warps_f = 8, parts_base = 1, parts_extra = 0, tcap_f = 1, grid_f = 0;
+  int warps_f = 8, parts_base = 1, parts_extra = 0, tcap_f = 1, grid_f = 0, zd_f = 0;
   size_t smem_f = 0;
   size_t f_lse = 0, f_z = 0, f_delta = 0, f_part_m = 0, f_part_l = 0, f_part_o = 0;
   // workspace offsets (bytes)
@@ -198,14 +198,21 @@ bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, i
     }
   }
   const int most = base + (extra > 0 ? 1 : 0);
+  if (most > 320) return false;  // the combine's lanes hold up to 10 parts each
   // Selector tiles a part touches: its blocks may start inside a tile.
   const int tcap = static_cast<int>(cdiv(cdiv(blocks, base), kSelectTile)) + 1;
   if (tcap > 128) return false;  // the per-part tables live in shared memory
   const int64_t slice = std::max<int64_t>(2LL * kSelectTile * dim * 2, 2LL * block_size * dim * 2);
   const int warps = static_cast<int>(std::min<int64_t>(8, 196608 / slice));
   if (warps < 2) return false;
-  const size_t smem = fused_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), warps,
-                                       static_cast<int>(group), tcap);
+  // z and delta of the part's tiles stay in shared memory when they fit.
+  int zd = static_cast<int>(group);
+  size_t smem = fused_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), warps, tcap,
+                                 zd);
+  if (smem > static_cast<size_t>(dev.smem_optin)) {
+    zd = 0;
+    smem = fused_smem_bytes(static_cast<int>(dim), static_cast<int>(block_size), warps, tcap, 0);
+  }
   if (smem > static_cast<size_t>(dev.smem_optin)) return false;
   pl->fused = true;
   pl->warps_f = warps;
@@ -213,8 +220,8 @@ bool plan_fused(Plan* pl, const DeviceInfo& dev, int64_t heads, int64_t group, i
   pl->parts_base = base;
   pl->parts_extra = extra;
   pl->tcap_f = tcap;
+  pl->zd_f = zd;
   pl->grid_f = fused_grid(static_cast<int>(heads), base, extra);
-  (void)most;
   return true;
 }
 
@@ -616,6 +623,7 @@ int run_fused_decode(const Plan& pl, const rkv_summary* s, const void* q, int qd
   p.parts_base = pl.parts_base;
   p.parts_extra = pl.parts_extra;
   p.tcap = pl.tcap_f;
+  p.zd_group = pl.zd_f;
   p.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
   p.eps = eps;
   p.reduction = reduction;

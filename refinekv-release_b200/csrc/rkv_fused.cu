@@ -2,10 +2,10 @@
 // the reference's GPU form is six Triton kernels, kernels/selection.py:47-223
 // and kernels/attention.py:13-329).
 //
-// One CTA per (KV-head row, part); a row's parts split its selector tiles
-// into contiguous ranges, and the grid never has more CTAs than SMs (unless
-// every row has a single part), so all parts of a row are resident together
-// (the host sizes it; one CTA per SM by shared memory).  A CTA:
+// One CTA per (KV-head row, part); a row's parts split its blocks into equal
+// contiguous ranges, and the grid never has more CTAs than SMs (unless every
+// row has a single part), so all parts of a row are resident together (the
+// host sizes it; one CTA per SM by shared memory).  A CTA:
 //   1. phase A: z and delta of every (group row, block) of its tiles from the
 //      key-mean and ellipsoid tiles (TMA, mma.sync), stored for phase B, and
 //      one log-sum-exp partial per part; arrives at the row's barrier A;
@@ -39,8 +39,11 @@ namespace {
 // warps' final partials, then the parts' (max, sum), are parked in the slices.
 struct FusedLayout {
   size_t bars, norms, flags, lse, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off,
-      anchored, bytes;
-  __host__ __device__ FusedLayout(int warps, int slice, int tcap) {
+      anchored, zs, ds, vs, bytes;
+  // zd_group > 0: z and delta of the part's tiles stay in shared memory,
+  // [tcap][zd_group][32] each, instead of the workspace, with the blocks'
+  // value norms [tcap][32].
+  __host__ __device__ FusedLayout(int warps, int slice, int tcap, int zd_group) {
     const size_t t = static_cast<size_t>(tcap);
     size_t off = static_cast<size_t>(warps) * slice;
     auto take = [&](size_t bytes_) {
@@ -59,6 +62,10 @@ struct FusedLayout {
     rep_list = take(t * 4);        // [tcap] int
     anc_off = take((t + 1) * 4);   // [tcap + 1] int
     anchored = take(t * kSelectTile * 4);  // [tcap * 32] int
+    const size_t zd = t * static_cast<size_t>(zd_group) * kSelectTile * 4;
+    zs = take(zd);
+    ds = take(zd);
+    vs = take(zd_group > 0 ? t * kSelectTile * 4 : 0);
     bytes = off + kSmemSlack;
   }
 };
@@ -257,7 +264,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   uint8_t* smem = align_smem(smem_raw);
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const FusedLayout lay(W, kSlice, p.tcap);
+  const FusedLayout lay(W, kSlice, p.tcap, p.zd_group);
   uint8_t* slice = smem + static_cast<size_t>(warp) * kSlice;
   uint64_t* bar_a = reinterpret_cast<uint64_t*>(smem + lay.bars) + warp * 2;
   uint64_t* bar_b = bar_a + 1;
@@ -272,6 +279,10 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   int* rep_list = reinterpret_cast<int*>(smem + lay.rep_list);           // [tcap]
   int* anc_off = reinterpret_cast<int*>(smem + lay.anc_off);             // [tcap + 1]
   int* blist = reinterpret_cast<int*>(smem + lay.anchored);              // [tcap * 32]
+  float* zsm = reinterpret_cast<float*>(smem + lay.zs);  // [tcap][group][32] when p.zd_group
+  float* dsm = reinterpret_cast<float*>(smem + lay.ds);
+  float* vsm = reinterpret_cast<float*>(smem + lay.vs);  // [tcap][32] when p.zd_group
+  const bool zd_local = p.zd_group != 0;
 
   // This CTA's row and part.
   const int c = blockIdx.x;
@@ -332,6 +343,27 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   for (int i = threadIdx.x; i * 128 < p.group * p.dim * (p.query_f32 ? 4 : 2); i += blockDim.x) {
     prefetch_l2(q + i * 128);
   }
+  // The part's value norms, counts and anchor bytes, read one tile at a time
+  // by the decisions and phase A, go to L2 now (prefetches only).
+  if (b_hi > b_lo) {
+    const int nvn = (b_hi - b_lo) * 4, ncn = (b_hi - b_lo) * 8, nan_ = b_hi - b_lo;
+    const char* vn = reinterpret_cast<const char*>(p.value_norm + static_cast<size_t>(h) * p.blocks + b_lo);
+    const char* cn = reinterpret_cast<const char*>(counts + b_lo);
+    const char* an = p.anchor != nullptr
+                         ? reinterpret_cast<const char*>(p.anchor + static_cast<size_t>(h) * p.blocks + b_lo)
+                         : nullptr;
+    const int lines_vn = (nvn + 127) / 128, lines_cn = (ncn + 127) / 128;
+    const int lines_an = an != nullptr ? (nan_ + 127) / 128 : 0;
+    for (int i = threadIdx.x; i < lines_vn + lines_cn + lines_an; i += blockDim.x) {
+      if (i < lines_vn) {
+        prefetch_l2(vn + i * 128);
+      } else if (i < lines_vn + lines_cn) {
+        prefetch_l2(cn + (i - lines_vn) * 128);
+      } else {
+        prefetch_l2(an + (i - lines_vn - lines_cn) * 128);
+      }
+    }
+  }
   __syncthreads();
   pdl_wait();
   // Every CTA of this grid has started once all have passed here, so a grid
@@ -371,14 +403,47 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   };
 
   // Anchored blocks of the range, one bit per block (known before any statistics).
+  int range_anchored = 1;
   for (int k = warp; k < n_t; k += W) {
     const int b = (t_lo + k) * T + lane;
     const bool a = p.anchor != nullptr && mine(b) &&
                    p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
     const uint32_t bits = __ballot_sync(0xffffffffu, a);
     if (lane == 0) anc_bits[k] = bits;
+    range_anchored &= bits == __ballot_sync(0xffffffffu, mine(b));
   }
-  __syncthreads();
+  // A row whose every block is anchored needs no statistics at all: all its
+  // blocks are selected whatever the risk (reference.py:54-55) and none is
+  // represented, so every part of it skips phase A and barrier A (they all
+  // find the same, from the same mask).  Checked beyond this part's range
+  // only when the range itself is anchored throughout.
+  bool row_anchored = false;
+  if (__syncthreads_and(range_anchored) && p.anchor != nullptr && blocks_h > 0) {
+    const uint8_t* row = p.anchor + static_cast<size_t>(h) * p.blocks;
+    int ok = 1;
+    if ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+      const int n16 = blocks_h >> 4;
+      for (int i0 = 0; i0 < n16; i0 += 8 * blockDim.x) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = i0 + u * blockDim.x + threadIdx.x;
+          v[u] = i < n16 ? __ldg(reinterpret_cast<const uint4*>(row) + i)
+                         : make_uint4(~0u, ~0u, ~0u, ~0u);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t w4[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ok &= ((w4[e] - 0x01010101u) & ~w4[e] & 0x80808080u) == 0u;
+        }
+      }
+      for (int b = (n16 << 4) + threadIdx.x; b < blocks_h; b += blockDim.x) ok &= row[b] != 0;
+    } else {
+      for (int b = threadIdx.x; b < blocks_h; b += blockDim.x) ok &= row[b] != 0;
+    }
+    row_anchored = __syncthreads_and(ok) != 0;
+  }
   // The anchored list (block order) while the first phase-A tiles land.
   if (warp == (W > 1 ? 1 : 0)) {
     int acc = 0;
@@ -403,7 +468,17 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
 
   // ---------------- phase A: statistics of this warp's tiles ----------------
-  {
+  if (row_anchored) {
+    // The first tile issued after the dependency wait lands before its slice
+    // takes pages.
+    if (warp < n_t) {
+      if (!warp_wait(bar_a, uses_a & 1)) {
+        timeout();
+        mbar_wait(bar_a, uses_a & 1);  // bounded: the copy must land before the CTA exits
+      }
+      ++uses_a;
+    }
+  } else {
     int lane_rows[T / 16][2];
     constexpr int kHalves = PACK4 ? 1 : 2;
 #pragma unroll
@@ -451,6 +526,11 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
           const int b = tile * T + lane_rows[mt][hf];
           cnt[mt][hf] = mine(b) ? __ldg(counts + b) : 1;
         }
+      if (zd_local) {  // the decisions' value norms, while the tile lands
+        const int b = tile * T + lane;
+        vsm[k * T + lane] =
+            mine(b) ? __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b) : 0.f;
+      }
       if (!warp_wait(bar_a, uses_a & 1)) {
         timeout();
         mbar_wait(bar_a, uses_a & 1);  // bounded: the copy must land before the CTA exits
@@ -509,9 +589,15 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
               const float proj = pr[mt][nt][c];
               const float delta = (sqrtf(proj < 0.f ? 0.f : proj) * p.scale) * kInflate;
               const float z = score + log_count;
-              const size_t rowg = static_cast<size_t>(h) * p.group + g;
-              p.z[rowg * p.blocks + b] = z;
-              p.delta[rowg * p.blocks + b] = delta;
+              if (zd_local) {
+                const int at_ = ((tile - t_lo) * p.group + g) * T + row_of[mt][hf];
+                zsm[at_] = z;
+                dsm[at_] = delta;
+              } else {
+                const size_t rowg = static_cast<size_t>(h) * p.group + g;
+                p.z[rowg * p.blocks + b] = z;
+                p.delta[rowg * p.blocks + b] = delta;
+              }
               zv[mt][nt][c] = z;
               cv[mt][nt][c] = z + log_cosh(delta);
             }
@@ -576,7 +662,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // (warps without tiles hold empty pairs), by the last warp, which then
   // arrives at barrier A -- while its first page lands.
   auto publish_stats = [&]() {
-    if (warp != W - 1) return;
+    if (warp != W - 1 || row_anchored) return;
     if (lane < p.group) {
       float4 acc = lse_s[lane];
       for (int w = 1; w < W; ++w) {
@@ -684,8 +770,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   const bool bad_global = flags[0] != 0;
   const float vmax = all_anchored ? 0.f : __ldg(p.max_value_norm + h);
   // A lane's block of tile k needs a decision when it is this part's and not
-  // anchored; the statistics of the warp's next tile load while this tile's
-  // risks are evaluated.
+  // anchored; its statistics come from shared memory (or the workspace when
+  // they did not fit there).
   float zr[GM], dr[GM], vn = 0.f;
   auto load_stats = [&](int k, float (&zs)[GM], float (&ds)[GM], float& v) {
     const int b = (t_lo + k) * T + lane;
@@ -694,21 +780,20 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     for (int g = 0; g < GM; ++g) {
       const size_t row = static_cast<size_t>(h) * p.group + g;
       const bool live = need && g < p.group;
-      zs[g] = live ? __ldcg(p.z + row * p.blocks + b) : 0.f;
-      ds[g] = live ? __ldcg(p.delta + row * p.blocks + b) : 0.f;
+      if (zd_local) {
+        zs[g] = live ? zsm[(k * p.group + g) * T + lane] : 0.f;
+        ds[g] = live ? dsm[(k * p.group + g) * T + lane] : 0.f;
+      } else {
+        zs[g] = live ? __ldcg(p.z + row * p.blocks + b) : 0.f;
+        ds[g] = live ? __ldcg(p.delta + row * p.blocks + b) : 0.f;
+      }
     }
-    v = need ? __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b) : 0.f;
+    v = !need ? 0.f
+              : zd_local ? vsm[k * T + lane]
+                         : __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
   };
-  // (Sixteen group rows keep one tile's statistics live at a time: registers.)
-  constexpr bool kAhead = GM <= 8;
-  if (kAhead && warp < n_t) load_stats(warp, zr, dr, vn);
   for (int k = warp; k < n_t; k += W) {
-    float zn[GM] = {}, dn[GM] = {}, vnn = 0.f;
-    if constexpr (kAhead) {
-      if (k + W < n_t) load_stats(k + W, zn, dn, vnn);
-    } else {
-      load_stats(k, zr, dr, vn);
-    }
+    load_stats(k, zr, dr, vn);
     const int b = (t_lo + k) * T + lane;
     const bool valid = mine(b);
     const bool anc = (anc_bits[k] >> lane) & 1u;
@@ -746,12 +831,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       sel_bits[k] = listed;
       rep_bits[k] = reps;
     }
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      zr[g] = zn[g];
-      dr[g] = dn[g];
-    }
-    vn = vnn;
   }
   __syncthreads();
 
@@ -831,10 +910,14 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
-            lg[mt][nt][cc] =
-                (rep && g < p.group)
-                    ? __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r)
-                    : -INFINITY;
+            if (!(rep && g < p.group)) {
+              lg[mt][nt][cc] = -INFINITY;
+            } else if (zd_local) {
+              lg[mt][nt][cc] = zsm[(k * p.group + g) * T + r];
+            } else {
+              lg[mt][nt][cc] =
+                  __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r);
+            }
           }
         }
     };
@@ -951,50 +1034,43 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] m, then weights
-  float* lsum = wgt + parts_h * G8;             // [parts_h][G8] l, then w * l
-  float* top = lsum + parts_h * G8;             // [G8] maxima
-  float* den = top + G8;                        // [G8] denominators
-  for (int i0 = 0; i0 < parts_h * G8; i0 += 4 * blockDim.x) {
-    float mv[4], lv[4];
+  // One warp per group row: the parts' maxima and sums straight from the
+  // partials (lanes over parts), weights w = exp(m - max m) into shared memory,
+  // denominator sum(w * l).
+  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] weights
+  float* den = wgt + parts_h * G8;              // [G8] denominators
+  constexpr int kLaneParts = 10;                // parts per lane: rows of up to 320 parts
+  for (int g = warp; g < p.group; g += W) {
+    float mv[kLaneParts], lv[kLaneParts];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * blockDim.x + threadIdx.x;
-      const size_t at_ = static_cast<size_t>(first_cta) * G8 + i;
-      mv[u] = i < parts_h * G8 ? __ldcg(p.part_m + at_) : 0.f;
-      lv[u] = i < parts_h * G8 ? __ldcg(p.part_l + at_) : 0.f;
+    for (int u = 0; u < kLaneParts; ++u) {
+      const int k = lane + 32 * u;
+      const size_t at_ = static_cast<size_t>(first_cta + k) * G8 + g;
+      mv[u] = k < parts_h ? __ldcg(p.part_m + at_) : -INFINITY;
+      lv[u] = k < parts_h ? __ldcg(p.part_l + at_) : 0.f;
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = i0 + u * blockDim.x + threadIdx.x;
-      if (i < parts_h * G8) {
-        wgt[i] = mv[u];
-        lsum[i] = lv[u];
-      }
-    }
-  }
-  __syncthreads();
-  for (int g = warp; g < G8; g += W) {
     float mx = -INFINITY;
-    for (int k = lane; k < parts_h; k += 32) mx = fmaxf(mx, wgt[k * G8 + g]);
+#pragma unroll
+    for (int u = 0; u < kLaneParts; ++u) mx = fmaxf(mx, mv[u]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if (lane == 0) top[g] = mx == -INFINITY ? 0.f : mx;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < parts_h * G8; i += blockDim.x) {
-    const float mk = wgt[i];
-    const float w = mk == -INFINITY ? 0.f : fexp(mk - top[i % G8]);
-    wgt[i] = w;
-    lsum[i] = w == 0.f ? 0.f : w * lsum[i];
-  }
-  __syncthreads();
-  for (int g = warp; g < G8; g += W) {
+    const float ref = mx == -INFINITY ? 0.f : mx;
     float sum = 0.f;
-    for (int k = lane; k < parts_h; k += 32) sum += lsum[k * G8 + g];
+#pragma unroll
+    for (int u = 0; u < kLaneParts; ++u) {
+      const int k = lane + 32 * u;
+      const float w = mv[u] == -INFINITY ? 0.f : fexp(mv[u] - ref);
+      if (k < parts_h) wgt[k * G8 + g] = w;
+      sum += w == 0.f ? 0.f : w * lv[u];
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     if (lane == 0) den[g] = sum;
+  }
+  // Weights of the padding group rows (read by the float4 loads below, unused).
+  for (int i = threadIdx.x; i < parts_h * (G8 - p.group); i += blockDim.x) {
+    const int k = i / (G8 - p.group), g = p.group + (i - k * (G8 - p.group));
+    wgt[k * G8 + g] = 0.f;
   }
   __syncthreads();
   auto add_part = [&](float4& acc, int k, int g0, const float4& v) {
@@ -1102,11 +1178,10 @@ int fused_grid(int heads, int parts_base, int parts_extra) {
   return heads * parts_base + parts_extra;
 }
 
-size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap) {
-  (void)group;
+size_t fused_smem_bytes(int dim, int page, int warps, int tcap, int zd_group) {
   const int sel = kSelectTile * dim * 2, pg = page * dim * 2;
   const int slice = 2 * sel > 2 * pg ? 2 * sel : 2 * pg;
-  return FusedLayout(warps, slice, tcap).bytes;
+  return FusedLayout(warps, slice, tcap, zd_group).bytes;
 }
 
 cudaError_t launch_fused(const FusedMaps& maps, const FusedParams& p, int dim, int warps,

@@ -141,6 +141,7 @@ struct FusedParams {
   int heads, group, blocks, tiles;
   int parts_base, parts_extra;  // parts per row (see above)
   int tcap;           // the largest tile count of a part (shared-memory tables)
+  int zd_group;       // > 0: z and delta stay in shared memory (else the workspace's z, delta)
   float scale, eps;
   int reduction;
   float* z;           // (heads*group, blocks)
@@ -275,7 +276,8 @@ size_t final_smem_bytes(int dim, int warps, int stages, int group, int tiles_per
 size_t attend_smem_bytes(int dim, int page, int warps, int stages, int group, int heads,
                          int parts_b);
 size_t combine_smem_bytes(int heads, int parts_b, int group, int max_sources);
-size_t fused_smem_bytes(int dim, int page, int warps, int group, int tcap);
+// zd_group > 0: the part's z and delta kept in shared memory for that many group rows.
+size_t fused_smem_bytes(int dim, int page, int warps, int tcap, int zd_group);
 int fused_grid(int heads, int parts_base, int parts_extra);
 
 }  // namespace rkv

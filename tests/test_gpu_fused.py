@@ -152,3 +152,42 @@ def test_one_workspace_across_geometries():
         fresh = sparse_attention(q, summary, empty, empty, return_selected=True)
         assert torch.equal(res.selected, fresh.selected)
         assert torch.equal(res.output, fresh.output)
+
+
+def test_rows_anchored_throughout_skip_the_statistics():
+    """A row whose every block is anchored skips the selector statistics in every
+    part; next to it, rows with one block or every third block left to decide
+    and a row without anchors.  Masks and outputs against the oracle and the
+    four-kernel decode."""
+    heads, group, dim, block, tokens = 4, 4, 128, 32, 40000
+    data = synthetic.make_layer(41, 0, heads, tokens, dim, block, device=DEV)
+    cfg = RefineKVConfig(block_size=block, eps=0.01)
+    summary = build_summary(data.keys, data.values, cfg)
+    nb = summary.num_blocks
+    anchor = torch.zeros(heads, nb, dtype=torch.bool, device=DEV)
+    anchor[0] = True                  # every block: no statistics for this row
+    anchor[1] = True
+    anchor[1, nb // 2] = False        # one block to decide
+    anchor[2, ::3] = True             # every third block
+    q = (synthetic.make_queries(41, 0, 0, data.planted_mean, group)[0].float() * 8.0).to(
+        torch.bfloat16)
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    ks = torch.randn(heads, 5, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    vs = torch.randn(heads, 5, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    ws = {}
+    res = sparse_attention(q, summary, ks, vs, cfg, anchor_mask=anchor, workspace=ws,
+                           return_selected=True)
+    out, sel = res.output.clone(), res.selected.clone()
+    assert device_status(ws) == 0
+    assert bool(sel[0].all()) and bool(sel[1].sum() >= nb - 1)
+    with unfused():
+        plain = sparse_attention(q, summary, ks, vs, cfg, anchor_mask=anchor, return_selected=True)
+    s_cpu = ora.as_cpu_summary(summary)
+    margin = ora.margin_blocks(q.cpu(), s_cpu, cfg.eps, cfg.gqa_reduction) & ~anchor.cpu()
+    want, z = ora.select_blocks(q.cpu(), s_cpu, cfg.eps, cfg.gqa_reduction)
+    want |= anchor.cpu()
+    assert not ((sel.cpu() != want) & ~margin).any()
+    assert not ((sel.cpu() != plain.selected.cpu()) & ~margin).any()
+    _close(out, plain.output, False)
+    ref = ora.mixed_attention(q.cpu(), s_cpu, ks.cpu(), vs.cpu(), sel.cpu(), z)
+    _close(out.cpu(), ref.to(torch.bfloat16), False)
