@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(warps) * S * kStage);
   float* scratch = reinterpret_cast<float*>(smem + static_cast<size_t>(warps) * S * kStage +
                                             round16(static_cast<size_t>(warps) * S * 8));
-  float* kmean_s = scratch + warp * 2 * D;  // this warp's [D] bf16-rounded K means
+  float* kmean_s = scratch + warp * 2 * D;  // this warp's [D] negated bf16-rounded K means
   float* rscale_s = kmean_s + D;            // and [D] reciprocal half widths
 
   const long long pages = static_cast<long long>(p.heads) * p.blocks;
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
         const int chunk = lane / kChunks + s2 * kLpc;
         if (chunk >= kRowChunks) break;
         const int r_end = min(chunk * 16 + 16, count);
-        for (int r = chunk * 16; r < r_end; ++r) {
+        auto add_row = [&](int r) {
           float2 kf[4], vf[4];
           load8x2<T>(vt, r, c16, R, vf);
           if constexpr (sizeof(T) == 2) {
@@ -239,6 +239,12 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
             kpart[s2][i] = __fadd2_rn(kpart[s2][i], kf[i]);
             vpart[s2][i] = __fadd2_rn(vpart[s2][i], vf[i]);
           }
+        };
+        if (r_end == chunk * 16 + 16) {  // a full chunk: row offsets known at compile time
+#pragma unroll
+          for (int i = 0; i < 16; ++i) add_row(chunk * 16 + i);
+        } else {
+          for (int r = chunk * 16; r < r_end; ++r) add_row(r);
         }
         if (r_end < chunk * 16 + 16) {  // zero padding rows: x + 0 turns a -0 sum into +0
 #pragma unroll
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
         float w = nan_max(kmax[i] - kmean[i], kmean[i] - kmin[i]);
         w = w < 1e-6f ? 1e-6f : w;
         width2[i] = bf16_round(w * w);
-        kmean_s[c16 * 8 + i] = kmean[i];
+        kmean_s[c16 * 8 + i] = -kmean[i];
         rscale_s[c16 * 8 + i] = __frsqrt_rn(width2[i]);
       }
       const size_t off = static_cast<size_t>(pg) * p.dim + c16 * 8;
@@ -331,8 +337,7 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
       // channel pairs, summed at the end (the reference's channel order is not
       // reproducible anyway: torch vectorises the sum).
       float2 sq2 = make_float2(0.f, 0.f), dist2 = make_float2(0.f, 0.f);
-#pragma unroll 4
-      for (int c = 0; c < kChunks; ++c) {
+      auto add_chunk = [&](int c) {
         float2 kf[4], vf[4];
         load8x2<T>(kt, r, c, R, kf);
         load8x2<T>(vt, r, c, R, vf);
@@ -340,8 +345,8 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
         const float4 m1 = *reinterpret_cast<const float4*>(kmean_s + c * 8 + 4);
         const float4 s0 = *reinterpret_cast<const float4*>(rscale_s + c * 8);
         const float4 s1 = *reinterpret_cast<const float4*>(rscale_s + c * 8 + 4);
-        const float2 neg_mean[4] = {make_float2(-m0.x, -m0.y), make_float2(-m0.z, -m0.w),
-                                    make_float2(-m1.x, -m1.y), make_float2(-m1.z, -m1.w)};
+        const float2 neg_mean[4] = {make_float2(m0.x, m0.y), make_float2(m0.z, m0.w),
+                                    make_float2(m1.x, m1.y), make_float2(m1.z, m1.w)};
         const float2 scale[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w),
                                  make_float2(s1.x, s1.y), make_float2(s1.z, s1.w)};
 #pragma unroll
@@ -350,6 +355,13 @@ __global__ void __launch_bounds__(384, 1) summarize_kernel(const __grid_constant
           const float2 x = __fmul2_rn(__fadd2_rn(kf[i], neg_mean[i]), scale[i]);
           dist2 = __ffma2_rn(x, x, dist2);
         }
+      };
+      if (kChunks == D / 8) {  // the full tile width: chunk offsets known at compile time
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) add_chunk(c);
+      } else {
+#pragma unroll 4
+        for (int c = 0; c < kChunks; ++c) add_chunk(c);
       }
       vnorm = nan_max(vnorm, sqrtf(sq2.x + sq2.y));
       dmax = nan_max(dmax, dist2.x + dist2.y);
