@@ -15,9 +15,9 @@
 //   3. unless every block of its range is anchored: waits at barrier A (by
 //      then normally passed), merges the row's partials into log Z / log C,
 //      decides every block of its tiles (risk, GQA reduction, non-finite
-//      override), writes the mask, and streams its selected non-anchored
-//      pages and the representatives of its unselected blocks (value means,
-//      logit z);
+//      override) and writes the mask, each tile's representatives (value
+//      means, logit z) joining the softmax while the next tile is decided,
+//      then streams its selected non-anchored pages;
 //   4. merges its warps into one softmax partial; in a row of at most
 //      kLastParts parts the part that arrives last writes the row's output
 //      from all parts' partials, in a longer row the parts meet at barrier B
@@ -38,7 +38,7 @@ namespace {
 // block list (anchored blocks, then the selected non-anchored ones).  The
 // warps' final partials, then the parts' (max, sum), are parked in the slices.
 struct FusedLayout {
-  size_t bars, norms, flags, lse, sel_bits, rep_bits, anc_bits, offsets, rep_list, anc_off,
+  size_t bars, norms, flags, lse, sel_bits, anc_bits, offsets, anc_off,
       anchored, zs, ds, vs, bytes;
   // zd_group > 0: z and delta of the part's tiles stay in shared memory,
   // [tcap][zd_group][32] each, instead of the workspace, with the blocks'
@@ -56,10 +56,8 @@ struct FusedLayout {
     flags = take(8 * 4);
     lse = take(static_cast<size_t>(warps) * kMaxGroup * 16);  // [warps][16] float4
     sel_bits = take(t * 4);        // [tcap] uint32
-    rep_bits = take(t * 4);        // [tcap] uint32
     anc_bits = take(t * 4);        // [tcap] uint32
     offsets = take((t + 1) * 4);   // [tcap + 1] int
-    rep_list = take(t * 4);        // [tcap] int
     anc_off = take((t + 1) * 4);   // [tcap + 1] int
     anchored = take(t * kSelectTile * 4);  // [tcap * 32] int
     const size_t zd = t * static_cast<size_t>(zd_group) * kSelectTile * 4;
@@ -270,13 +268,11 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   uint64_t* bar_b = bar_a + 1;
   float* lz = reinterpret_cast<float*>(smem + lay.norms);
   float* lc = lz + kMaxGroup;
-  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 1 reps, 2 listed, 3 last
+  int* flags = reinterpret_cast<int*>(smem + lay.flags);  // 0 bad row stat, 2 listed, 3 last
   float4* lse_s = reinterpret_cast<float4*>(smem + lay.lse);              // [W][kMaxGroup]
   uint32_t* sel_bits = reinterpret_cast<uint32_t*>(smem + lay.sel_bits);  // [tcap]
-  uint32_t* rep_bits = reinterpret_cast<uint32_t*>(smem + lay.rep_bits);  // [tcap]
   uint32_t* anc_bits = reinterpret_cast<uint32_t*>(smem + lay.anc_bits);  // [tcap]
   int* offsets = reinterpret_cast<int*>(smem + lay.offsets);             // [tcap + 1]
-  int* rep_list = reinterpret_cast<int*>(smem + lay.rep_list);           // [tcap]
   int* anc_off = reinterpret_cast<int*>(smem + lay.anc_off);             // [tcap + 1]
   int* blist = reinterpret_cast<int*>(smem + lay.anchored);              // [tcap * 32]
   float* zsm = reinterpret_cast<float*>(smem + lay.zs);  // [tcap][group][32] when p.zd_group
@@ -792,6 +788,51 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
               : zd_local ? vsm[k * T + lane]
                          : __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
   };
+  // The representatives of a decided tile join the running softmax while the
+  // warp decides its next one: its value-mean tile loads on one barrier (two
+  // tiles in flight at most, one per barrier); logit z, value the block's
+  // value mean.
+  auto rep_logits = [&](int k, uint32_t reps, float (&lg)[T / 16][NT][4]) {
+    const int tile = t_lo + k;
+#pragma unroll
+    for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int r = mt * 16 + (lane >> 2) + (cc >> 1) * 8;
+        const bool rep = (reps >> r) & 1u;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
+          if (!(rep && g < p.group)) {
+            lg[mt][nt][cc] = -INFINITY;
+          } else if (zd_local) {
+            lg[mt][nt][cc] = zsm[(k * p.group + g) * T + r];
+          } else {
+            lg[mt][nt][cc] =
+                __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r);
+          }
+        }
+      }
+  };
+  int pend_k = -1, pend_half = 0;
+  uint32_t pend_reps = 0u;
+  auto finish_pending = [&]() {
+    if (pend_k < 0) return;
+    uint64_t* bar = pend_half ? bar_b : bar_a;
+    uint32_t& uses = pend_half ? uses_b : uses_a;
+    if (!warp_wait(bar, uses & 1)) {
+      timeout();
+      mbar_wait(bar, uses & 1);  // bounded: the copy must land before the slice is reused
+    }
+    ++uses;
+    if (!aborted) {
+      float lg[T / 16][NT][4];
+      rep_logits(pend_k, pend_reps, lg);
+      attend_tile<T, D, NT>(lg, smem_addr(slice + pend_half * kSel), m, l, o, split, lane);
+    }
+    __syncwarp();
+    pend_k = -1;
+  };
   for (int k = warp; k < n_t; k += W) {
     load_stats(k, zr, dr, vn);
     const int b = (t_lo + k) * T + lane;
@@ -827,11 +868,22 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
     const uint32_t listed = __ballot_sync(0xffffffffu, valid && sel && !anc);
     const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
-    if (lane == 0) {
-      sel_bits[k] = listed;
-      rep_bits[k] = reps;
+    if (lane == 0) sel_bits[k] = listed;
+    if (reps != 0u && !aborted) {
+      const int half = pend_k >= 0 ? pend_half ^ 1 : 0;
+      if (lane == 0) {
+        uint64_t* bar = half ? bar_b : bar_a;
+        fence_proxy_async();
+        mbar_expect_tx(bar, kSel);
+        tma_tile_hint<D>(slice + half * kSel, &maps.value_mean, bar, (t_lo + k) * T, h, T, policy);
+      }
+      finish_pending();  // the previous tile's representatives while this one lands
+      pend_k = k;
+      pend_reps = reps;
+      pend_half = half;
     }
   }
+  finish_pending();
   __syncthreads();
 
   // A batched row's blocks past its prompt belong to no part: the last part
@@ -841,14 +893,12 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       p.mask[static_cast<size_t>(h) * p.blocks + b] = 0;
     }
   }
-  // Compaction (block order): the selected blocks that are not anchored, and
-  // the tiles holding representatives.
+  // Compaction (block order): the selected blocks that are not anchored.
   if (warp == 0) {
-    int acc = 0, nreps = 0;
+    int acc = 0;
     for (int k0 = 0; k0 < n_t; k0 += 32) {
       const int k = k0 + lane;
       const int cnt = k < n_t ? __popc(sel_bits[k]) : 0;
-      const bool has_rep = k < n_t && rep_bits[k] != 0u;
       int incl = cnt;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -857,14 +907,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       }
       if (k < n_t) offsets[k] = acc + incl - cnt;
       acc += __shfl_sync(0xffffffffu, incl, 31);
-      const uint32_t rb = __ballot_sync(0xffffffffu, has_rep);
-      if (has_rep) rep_list[nreps + __popc(rb & ((1u << lane) - 1u))] = k;
-      nreps += __popc(rb);
     }
-    if (lane == 0) {
-      flags[1] = nreps;
-      flags[2] = acc;
-    }
+    if (lane == 0) flags[2] = acc;
   }
   __syncthreads();
   for (int k = warp; k < n_t; k += W) {
@@ -873,8 +917,8 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
   __syncthreads();
 
-  // ---------------- selected pages, then representatives --------------------
-  const int n_sel = flags[2], n_reps = flags[1];
+  // ---------------- selected non-anchored pages ------------------------------
+  const int n_sel = flags[2];
   {
     const int mine = n_sel > warp ? (n_sel - warp + W - 1) / W : 0;
     auto item = [&](int j) { return page_item(blist[warp + j * W]); };
@@ -882,80 +926,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                                             uses_b, qb, p.scale, split, m, l, o, policy, lane)) {
       timeout();
     }
-  }
-  // Value-mean tiles double-buffered on the two barriers; logit z, value the
-  // block's value mean.
-  const int my_reps = n_reps > warp ? (n_reps - warp + W - 1) / W : 0;
-  if (my_reps > 0 && !aborted) {
-    auto issue_rep = [&](int j) {
-      if (lane == 0) {
-        uint64_t* bar = (j & 1) ? bar_b : bar_a;
-        fence_proxy_async();
-        mbar_expect_tx(bar, kSel);
-        tma_tile_hint<D>(slice + (j & 1) * kSel, &maps.value_mean, bar,
-                         (t_lo + rep_list[warp + j * W]) * T, h, T, policy);
-      }
-    };
-    auto load_logits = [&](int j, float (&lg)[T / 16][NT][4]) {
-      const bool have = j < my_reps;
-      const int k = have ? rep_list[warp + j * W] : 0;
-      const uint32_t reps = have ? rep_bits[k] : 0u;
-      const int tile = t_lo + k;
-#pragma unroll
-      for (int mt = 0; mt < T / 16; ++mt)
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int r = mt * 16 + (lane >> 2) + (cc >> 1) * 8;
-          const bool rep = (reps >> r) & 1u;
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
-            if (!(rep && g < p.group)) {
-              lg[mt][nt][cc] = -INFINITY;
-            } else if (zd_local) {
-              lg[mt][nt][cc] = zsm[(k * p.group + g) * T + r];
-            } else {
-              lg[mt][nt][cc] =
-                  __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r);
-            }
-          }
-        }
-    };
-    uint32_t issued_a = uses_a, issued_b = uses_b;
-    issue_rep(0);
-    ++issued_a;
-    if (my_reps > 1) {
-      issue_rep(1);
-      ++issued_b;
-    }
-    float next_logit[T / 16][NT][4];
-    load_logits(0, next_logit);
-    for (int j = 0; j < my_reps; ++j) {
-      const bool odd = j & 1;
-      uint64_t* bar = odd ? bar_b : bar_a;
-      uint32_t& uses = odd ? uses_b : uses_a;
-      if (!warp_wait(bar, uses & 1)) {
-        timeout();
-        break;
-      }
-      ++uses;
-      float logit[T / 16][NT][4];
-#pragma unroll
-      for (int mt = 0; mt < T / 16; ++mt)
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) logit[mt][nt][cc] = next_logit[mt][nt][cc];
-      load_logits(j + 1, next_logit);
-      attend_tile<T, D, NT>(logit, smem_addr(slice + (odd ? kSel : 0)), m, l, o, split, lane);
-      __syncwarp();
-      if (j + 2 < my_reps) {
-        issue_rep(j + 2);
-        if (odd) ++issued_b; else ++issued_a;
-      }
-    }
-    for (; uses_a < issued_a; ++uses_a) mbar_wait(bar_a, uses_a & 1);
-    for (; uses_b < issued_b; ++uses_b) mbar_wait(bar_b, uses_b & 1);
   }
 
   // ---------------- this part's partial, then the row's output ---------------
