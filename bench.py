@@ -748,9 +748,11 @@ def run_b200(args):
     traffic = profiled_traffic("decode_llama8b_128k.json" if fused
                                else "attend_llama8b_128k.json")
     traffic_per_launch = None
-    # A committed capture is of 32-token pages of 128 channels; its DRAM
-    # bytes scale with the pages a launch reads only for that page shape.
-    if traffic is not None and not split and (args.block_size, args.head_dim) == (32, 128):
+    # A committed capture is of one 128K layer of 8 KV heads in 32-token pages
+    # of 128 channels; its DRAM bytes scale with the pages a launch reads only
+    # for that workload.
+    if (traffic is not None and not split and (args.block_size, args.head_dim) == (32, 128)
+            and args.tokens == 131072 and heads_local == 8 and args.batch == 1):
         dram_bytes, pages_profiled = traffic
         traffic_per_launch = dram_bytes * (pages / launches) / pages_profiled
     step_bytes_all = sum_over_ranks(step_bytes, world)  # every rank joins the collective
