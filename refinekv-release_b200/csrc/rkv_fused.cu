@@ -336,6 +336,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     }
     for (int i = 0; i < 8; ++i) flags[i] = 0;
   }
+  for (int k = threadIdx.x; k < n_t; k += blockDim.x) anc_bits[k] = 0u;
   for (int i = threadIdx.x; i * 128 < p.group * p.dim * (p.query_f32 ? 4 : 2); i += blockDim.x) {
     prefetch_l2(q + i * 128);
   }
@@ -366,13 +367,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // launched early behind this one can never hold an SM one of ours needs.
   pdl_launch_dependents();
   const uint64_t policy = l2_evict_first_policy();
-  // This warp's first phase-A tile is in flight while the anchor bits, the
-  // query and the counts load.
-  if (lane == 0 && warp < n_t) {
-    mbar_expect_tx(bar_a, 2 * kSel);
-    tma_tile_hint<D>(slice, &maps.key_mean, bar_a, (t_lo + warp) * T, h, T, policy);
-    tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, (t_lo + warp) * T, h, T, policy);
-  }
   // The row's barrier generations before this part's arrivals (they move only
   // once every part, this one included, has arrived).
   unsigned seen_a = 0, seen_b = 0;
@@ -398,49 +392,64 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     aborted = true;
   };
 
-  // Anchored blocks of the range, one bit per block (known before any statistics).
-  int range_anchored = 1;
-  for (int k = warp; k < n_t; k += W) {
-    const int b = (t_lo + k) * T + lane;
-    const bool a = p.anchor != nullptr && mine(b) &&
-                   p.anchor[static_cast<size_t>(h) * p.blocks + b] != 0;
-    const uint32_t bits = __ballot_sync(0xffffffffu, a);
-    if (lane == 0) anc_bits[k] = bits;
-    range_anchored &= bits == __ballot_sync(0xffffffffu, mine(b));
-  }
-  // A row whose every block is anchored needs no statistics at all: all its
-  // blocks are selected whatever the risk (reference.py:54-55) and none is
-  // represented, so every part of it skips phase A and barrier A (they all
-  // find the same, from the same mask).  Checked beyond this part's range
-  // only when the range itself is anchored throughout.
-  bool row_anchored = false;
-  if (__syncthreads_and(range_anchored) && p.anchor != nullptr && blocks_h > 0) {
-    const uint8_t* row = p.anchor + static_cast<size_t>(h) * p.blocks;
-    int ok = 1;
-    if ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
-      const int n16 = blocks_h >> 4;
-      for (int i0 = 0; i0 < n16; i0 += 8 * blockDim.x) {
-        uint4 v[8];
+  // Anchored blocks of the range, one bit per block (known before any
+  // statistics), and whether every block of the row is anchored: a row whose
+  // every block is anchored needs no statistics at all -- all its blocks are
+  // selected whatever the risk (reference.py:54-55) and none is represented
+  // -- so every part of it skips phase A and barrier A (they all find the
+  // same, from the same mask).  One pass over the row's anchor bytes, 16 per
+  // thread (one round trip; from L2 after the first part's).
+  int row_ok = p.anchor != nullptr && blocks_h > 0;
+  const uint8_t* arow = p.anchor != nullptr ? p.anchor + static_cast<size_t>(h) * p.blocks : nullptr;
+  // A 16-block group's anchored bits into this part's tile words.
+  auto own_bits = [&](int b0, uint32_t bits16) {
+    const int lo = max(b0, b_lo), hi = min(b0 + 16, b_hi);
+    if (lo >= hi) return;
+    const uint32_t span = ((hi - lo) == 32 ? ~0u : ((1u << (hi - lo)) - 1u)) << (lo - b0);
+    const uint32_t mine16 = bits16 & span;
+    if (mine16 != 0u) atomicOr(&anc_bits[b0 / T - t_lo], mine16 << (b0 % T));
+  };
+  if (arow != nullptr && (reinterpret_cast<uintptr_t>(arow) & 15u) == 0) {
+    const int n16 = blocks_h >> 4;
+    for (int i0 = 0; i0 < n16; i0 += 8 * blockDim.x) {
+      uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = i0 + u * blockDim.x + threadIdx.x;
-          v[u] = i < n16 ? __ldg(reinterpret_cast<const uint4*>(row) + i)
-                         : make_uint4(~0u, ~0u, ~0u, ~0u);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t w4[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ok &= ((w4[e] - 0x01010101u) & ~w4[e] & 0x80808080u) == 0u;
-        }
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x + threadIdx.x;
+        v[u] = i < n16 ? __ldg(reinterpret_cast<const uint4*>(arow) + i) : make_uint4(0u, 0u, 0u, 0u);
       }
-      for (int b = (n16 << 4) + threadIdx.x; b < blocks_h; b += blockDim.x) ok &= row[b] != 0;
-    } else {
-      for (int b = threadIdx.x; b < blocks_h; b += blockDim.x) ok &= row[b] != 0;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * blockDim.x + threadIdx.x;
+        if (i >= n16) continue;
+        const uint32_t w4[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        uint32_t bits16 = 0u;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // one bit per nonzero byte
+          uint32_t t = w4[e] | (w4[e] >> 4);
+          t |= t >> 2;
+          t |= t >> 1;
+          t &= 0x01010101u;
+          bits16 |= ((t * 0x01020408u) >> 24) << (4 * e);
+        }
+        row_ok &= bits16 == 0xffffu;
+        own_bits(16 * i, bits16);
+      }
     }
-    row_anchored = __syncthreads_and(ok) != 0;
+    for (int b = (n16 << 4) + threadIdx.x; b < blocks_h; b += blockDim.x) {
+      const bool a = arow[b] != 0;
+      row_ok &= a;
+      if (a && b >= b_lo && b < b_hi) atomicOr(&anc_bits[b / T - t_lo], 1u << (b % T));
+    }
+  } else if (arow != nullptr) {
+    for (int b = threadIdx.x; b < blocks_h; b += blockDim.x) {
+      const bool a = arow[b] != 0;
+      row_ok &= a;
+      if (a && b >= b_lo && b < b_hi) atomicOr(&anc_bits[b / T - t_lo], 1u << (b % T));
+    }
   }
-  // The anchored list (block order) while the first phase-A tiles land.
+  const bool row_anchored = __syncthreads_and(row_ok) != 0;
+  // The anchored list (block order).
   if (warp == (W > 1 ? 1 : 0)) {
     int acc = 0;
     for (int k0 = 0; k0 < n_t; k0 += 32) {
@@ -464,17 +473,7 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   }
 
   // ---------------- phase A: statistics of this warp's tiles ----------------
-  if (row_anchored) {
-    // The first tile issued after the dependency wait lands before its slice
-    // takes pages.
-    if (warp < n_t) {
-      if (!warp_wait(bar_a, uses_a & 1)) {
-        timeout();
-        mbar_wait(bar_a, uses_a & 1);  // bounded: the copy must land before the CTA exits
-      }
-      ++uses_a;
-    }
-  } else {
+  if (!row_anchored) {
     int lane_rows[T / 16][2];
     constexpr int kHalves = PACK4 ? 1 : 2;
 #pragma unroll
@@ -503,12 +502,10 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     for (int k = warp; k < n_stat && !aborted; k += W) {
       const int tile = t_lo + k;
       if (lane == 0) {
-        if (k != warp) {  // the first tile was issued after the dependency wait
-          fence_proxy_async();
-          mbar_expect_tx(bar_a, 2 * kSel);
-          tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
-          tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
-        }
+        fence_proxy_async();
+        mbar_expect_tx(bar_a, 2 * kSel);
+        tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
+        tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
         if (k + W < n_stat) {  // one stage per warp: warm L2 with the next tile meanwhile
           tma_prefetch_tile<D>(&maps.key_mean, (tile + W) * T, h);
           tma_prefetch_tile<D>(&maps.ellipsoid, (tile + W) * T, h);
