@@ -722,7 +722,12 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   // representatives, so it neither waits for the row's normalisers nor reads
   // its statistics back.
   const bool all_anchored = n_anc == b_hi - b_lo;
-  if (!all_anchored) {
+  if (all_anchored) {
+    for (int k = warp; k < n_t; k += W) {
+      const int b = (t_lo + k) * T + lane;
+      if (mine(b)) p.mask[static_cast<size_t>(h) * p.blocks + b] = 1;
+    }
+  } else {
     if (threadIdx.x == 0 && !wait_generation(gen_a, seen_a)) atomicOr(p.status, kStatusTimeout);
     __syncthreads();
     for (int g = warp; g < p.group; g += W) {
@@ -758,131 +763,153 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
         if (!finite(zl) || !finite(cl)) atomicOr(&flags[0], 1);
       }
     }
-  }
-  __syncthreads();
-  const bool bad_global = flags[0] != 0;
-  const float vmax = all_anchored ? 0.f : __ldg(p.max_value_norm + h);
-  // A lane's block of tile k needs a decision when it is this part's and not
-  // anchored; its statistics come from shared memory (or the workspace when
-  // they did not fit there).
-  float zr[GM], dr[GM], vn = 0.f;
-  auto load_stats = [&](int k, float (&zs)[GM], float (&ds)[GM], float& v) {
-    const int b = (t_lo + k) * T + lane;
-    const bool need = k < n_t && mine(b) && !((anc_bits[k] >> lane) & 1u);
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      const size_t row = static_cast<size_t>(h) * p.group + g;
-      const bool live = need && g < p.group;
-      if (zd_local) {
-        zs[g] = live ? zsm[(k * p.group + g) * T + lane] : 0.f;
-        ds[g] = live ? dsm[(k * p.group + g) * T + lane] : 0.f;
-      } else {
-        zs[g] = live ? __ldcg(p.z + row * p.blocks + b) : 0.f;
-        ds[g] = live ? __ldcg(p.delta + row * p.blocks + b) : 0.f;
-      }
-    }
-    v = !need ? 0.f
-              : zd_local ? vsm[k * T + lane]
-                         : __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
-  };
-  // The representatives of a decided tile join the running softmax while the
-  // warp decides its next one: its value-mean tile loads on one barrier (two
-  // tiles in flight at most, one per barrier); logit z, value the block's
-  // value mean.
-  auto rep_logits = [&](int k, uint32_t reps, float (&lg)[T / 16][NT][4]) {
-    const int tile = t_lo + k;
-#pragma unroll
-    for (int mt = 0; mt < T / 16; ++mt)
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int r = mt * 16 + (lane >> 2) + (cc >> 1) * 8;
-        const bool rep = (reps >> r) & 1u;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
-          if (!(rep && g < p.group)) {
-            lg[mt][nt][cc] = -INFINITY;
-          } else if (zd_local) {
-            lg[mt][nt][cc] = zsm[(k * p.group + g) * T + r];
-          } else {
-            lg[mt][nt][cc] =
-                __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r);
-          }
-        }
-      }
-  };
-  int pend_k = -1, pend_half = 0;
-  uint32_t pend_reps = 0u;
-  auto finish_pending = [&]() {
-    if (pend_k < 0) return;
-    uint64_t* bar = pend_half ? bar_b : bar_a;
-    uint32_t& uses = pend_half ? uses_b : uses_a;
-    if (!warp_wait(bar, uses & 1)) {
-      timeout();
-      mbar_wait(bar, uses & 1);  // bounded: the copy must land before the slice is reused
-    }
-    ++uses;
-    if (!aborted) {
-      float lg[T / 16][NT][4];
-      rep_logits(pend_k, pend_reps, lg);
-      attend_tile<T, D, NT>(lg, smem_addr(slice + pend_half * kSel), m, l, o, split, lane);
-    }
-    __syncwarp();
-    pend_k = -1;
-  };
-  for (int k = warp; k < n_t; k += W) {
-    load_stats(k, zr, dr, vn);
-    const int b = (t_lo + k) * T + lane;
-    const bool valid = mine(b);
-    const bool anc = (anc_bits[k] >> lane) & 1u;
-    bool sel = anc;
-    if (valid && !anc) {
-      float agg = p.reduction == kMax ? -INFINITY : 0.f;
-      bool any = false, bad = false;
+    __syncthreads();
+    const bool bad_global = flags[0] != 0;
+    const float vmax = __ldg(p.max_value_norm + h);
+    // A lane's block of tile k needs a decision when it is this part's and not
+    // anchored; its statistics come from shared memory (or the workspace when
+    // they did not fit there).
+    float zr[GM], dr[GM], vn = 0.f;
+    auto load_stats = [&](int k, float (&zs)[GM], float (&ds)[GM], float& v) {
+      const int b = (t_lo + k) * T + lane;
+      const bool need = k < n_t && mine(b) && !((anc_bits[k] >> lane) & 1u);
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
-        if (g >= p.group) continue;
-        const float r = block_risk(zr[g], dr[g], lz[g], lc[g], vn, vmax);
-        bad |= !finite(r);
-        if (p.reduction == kMean) {
-          agg += r;
-        } else if (p.reduction == kMax) {
-          agg = (r > agg || r != r) ? r : agg;
+        const size_t row = static_cast<size_t>(h) * p.group + g;
+        const bool live = need && g < p.group;
+        if (zd_local) {
+          zs[g] = live ? zsm[(k * p.group + g) * T + lane] : 0.f;
+          ds[g] = live ? dsm[(k * p.group + g) * T + lane] : 0.f;
         } else {
-          any |= r > p.eps;
+          zs[g] = live ? __ldcg(p.z + row * p.blocks + b) : 0.f;
+          ds[g] = live ? __ldcg(p.delta + row * p.blocks + b) : 0.f;
         }
       }
-      bool dec;
-      if (p.reduction == kMean) {
-        dec = agg / static_cast<float>(p.group) > p.eps;
-      } else if (p.reduction == kMax) {
-        dec = agg > p.eps;
-      } else {
-        dec = any;
+      v = !need ? 0.f
+                : zd_local ? vsm[k * T + lane]
+                           : __ldg(p.value_norm + static_cast<size_t>(h) * p.blocks + b);
+    };
+    // The representatives of a decided tile join the running softmax while the
+    // warp decides its next one: its value-mean tile loads on one barrier (two
+    // tiles in flight at most, one per barrier); logit z, value the block's
+    // value mean.
+    auto rep_logits = [&](int k, uint32_t reps, float (&lg)[T / 16][NT][4]) {
+      const int tile = t_lo + k;
+#pragma unroll
+      for (int mt = 0; mt < T / 16; ++mt)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int r = mt * 16 + (lane >> 2) + (cc >> 1) * 8;
+          const bool rep = (reps >> r) & 1u;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int g = nt * 8 + 2 * (lane & 3) + (cc & 1);
+            if (!(rep && g < p.group)) {
+              lg[mt][nt][cc] = -INFINITY;
+            } else if (zd_local) {
+              lg[mt][nt][cc] = zsm[(k * p.group + g) * T + r];
+            } else {
+              lg[mt][nt][cc] =
+                  __ldcg(p.z + (static_cast<size_t>(h) * p.group + g) * p.blocks + tile * T + r);
+            }
+          }
+        }
+    };
+    int pend_k = -1, pend_half = 0;
+    uint32_t pend_reps = 0u;
+    auto finish_pending = [&]() {
+      if (pend_k < 0) return;
+      uint64_t* bar = pend_half ? bar_b : bar_a;
+      uint32_t& uses = pend_half ? uses_b : uses_a;
+      if (!warp_wait(bar, uses & 1)) {
+        timeout();
+        mbar_wait(bar, uses & 1);  // bounded: the copy must land before the slice is reused
       }
-      sel = dec || bad || bad_global;
-    }
-    if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
-    const uint32_t listed = __ballot_sync(0xffffffffu, valid && sel && !anc);
-    const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
-    if (lane == 0) sel_bits[k] = listed;
-    if (reps != 0u && !aborted) {
-      const int half = pend_k >= 0 ? pend_half ^ 1 : 0;
-      if (lane == 0) {
-        uint64_t* bar = half ? bar_b : bar_a;
-        fence_proxy_async();
-        mbar_expect_tx(bar, kSel);
-        tma_tile_hint<D>(slice + half * kSel, &maps.value_mean, bar, (t_lo + k) * T, h, T, policy);
+      ++uses;
+      if (!aborted) {
+        float lg[T / 16][NT][4];
+        rep_logits(pend_k, pend_reps, lg);
+        attend_tile<T, D, NT>(lg, smem_addr(slice + pend_half * kSel), m, l, o, split, lane);
       }
-      finish_pending();  // the previous tile's representatives while this one lands
-      pend_k = k;
-      pend_reps = reps;
-      pend_half = half;
+      __syncwarp();
+      pend_k = -1;
+    };
+    for (int k = warp; k < n_t; k += W) {
+      load_stats(k, zr, dr, vn);
+      const int b = (t_lo + k) * T + lane;
+      const bool valid = mine(b);
+      const bool anc = (anc_bits[k] >> lane) & 1u;
+      bool sel = anc;
+      if (valid && !anc) {
+        float agg = p.reduction == kMax ? -INFINITY : 0.f;
+        bool any = false, bad = false;
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          if (g >= p.group) continue;
+          const float r = block_risk(zr[g], dr[g], lz[g], lc[g], vn, vmax);
+          bad |= !finite(r);
+          if (p.reduction == kMean) {
+            agg += r;
+          } else if (p.reduction == kMax) {
+            agg = (r > agg || r != r) ? r : agg;
+          } else {
+            any |= r > p.eps;
+          }
+        }
+        bool dec;
+        if (p.reduction == kMean) {
+          dec = agg / static_cast<float>(p.group) > p.eps;
+        } else if (p.reduction == kMax) {
+          dec = agg > p.eps;
+        } else {
+          dec = any;
+        }
+        sel = dec || bad || bad_global;
+      }
+      if (valid) p.mask[static_cast<size_t>(h) * p.blocks + b] = sel ? 1 : 0;
+      const uint32_t listed = __ballot_sync(0xffffffffu, valid && sel && !anc);
+      const uint32_t reps = __ballot_sync(0xffffffffu, valid && !sel);
+      if (lane == 0) sel_bits[k] = listed;
+      if (reps != 0u && !aborted) {
+        const int half = pend_k >= 0 ? pend_half ^ 1 : 0;
+        if (lane == 0) {
+          uint64_t* bar = half ? bar_b : bar_a;
+          fence_proxy_async();
+          mbar_expect_tx(bar, kSel);
+          tma_tile_hint<D>(slice + half * kSel, &maps.value_mean, bar, (t_lo + k) * T, h, T, policy);
+        }
+        finish_pending();  // the previous tile's representatives while this one lands
+        pend_k = k;
+        pend_reps = reps;
+        pend_half = half;
+      }
     }
+    finish_pending();
+    __syncthreads();
+    // Compaction (block order): the selected blocks that are not anchored.
+    if (warp == 0) {
+      int acc = 0;
+      for (int k0 = 0; k0 < n_t; k0 += 32) {
+        const int k = k0 + lane;
+        const int cnt = k < n_t ? __popc(sel_bits[k]) : 0;
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += y;
+        }
+        if (k < n_t) offsets[k] = acc + incl - cnt;
+        acc += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) flags[2] = acc;
+    }
+    __syncthreads();
+    for (int k = warp; k < n_t; k += W) {
+      const uint32_t sb = sel_bits[k];
+      if ((sb >> lane) & 1u) blist[offsets[k] + __popc(sb & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
+    }
+    __syncthreads();
   }
-  finish_pending();
-  __syncthreads();
-
   // A batched row's blocks past its prompt belong to no part: the last part
   // writes their mask bytes 0.
   if (part == parts_h - 1) {
@@ -890,32 +917,9 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       p.mask[static_cast<size_t>(h) * p.blocks + b] = 0;
     }
   }
-  // Compaction (block order): the selected blocks that are not anchored.
-  if (warp == 0) {
-    int acc = 0;
-    for (int k0 = 0; k0 < n_t; k0 += 32) {
-      const int k = k0 + lane;
-      const int cnt = k < n_t ? __popc(sel_bits[k]) : 0;
-      int incl = cnt;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
-      }
-      if (k < n_t) offsets[k] = acc + incl - cnt;
-      acc += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) flags[2] = acc;
-  }
-  __syncthreads();
-  for (int k = warp; k < n_t; k += W) {
-    const uint32_t sb = sel_bits[k];
-    if ((sb >> lane) & 1u) blist[offsets[k] + __popc(sb & ((1u << lane) - 1u))] = (t_lo + k) * T + lane;
-  }
-  __syncthreads();
 
   // ---------------- selected non-anchored pages ------------------------------
-  const int n_sel = flags[2];
+  const int n_sel = all_anchored ? 0 : flags[2];
   {
     const int mine = n_sel > warp ? (n_sel - warp + W - 1) / W : 0;
     auto item = [&](int j) { return page_item(blist[warp + j * W]); };
