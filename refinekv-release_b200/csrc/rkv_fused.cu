@@ -1005,43 +1005,57 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  // One warp per group row: the parts' maxima and sums straight from the
-  // partials (lanes over parts), weights w = exp(m - max m) into shared memory,
-  // denominator sum(w * l).
-  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] weights
-  float* den = wgt + parts_h * G8;              // [G8] denominators
-  constexpr int kLaneParts = 10;                // parts per lane: rows of up to 320 parts
-  for (int g = warp; g < p.group; g += W) {
-    float mv[kLaneParts], lv[kLaneParts];
+  // The parts' (max, sum) pairs staged in shared memory with vector loads by
+  // all threads (in a long row every part reads them all: one request per 16
+  // bytes keeps those few L2 lines from becoming a hot spot), then one warp
+  // per group row: weights w = exp(m - max m) in place, denominator
+  // sum(w * l).
+  float* wgt = reinterpret_cast<float*>(smem);  // [parts_h][G8] m, then weights
+  float* lsum = wgt + parts_h * G8;             // [parts_h][G8] l
+  float* den = lsum + parts_h * G8;             // [G8] denominators
+  {
+    const int n4 = parts_h * G8 / 4;
+    const float4* m4 = reinterpret_cast<const float4*>(p.part_m + static_cast<size_t>(first_cta) * G8);
+    const float4* l4 = reinterpret_cast<const float4*>(p.part_l + static_cast<size_t>(first_cta) * G8);
+    for (int i0 = 0; i0 < n4; i0 += 4 * blockDim.x) {
+      float4 mv[4], lv[4];
 #pragma unroll
-    for (int u = 0; u < kLaneParts; ++u) {
-      const int k = lane + 32 * u;
-      const size_t at_ = static_cast<size_t>(first_cta + k) * G8 + g;
-      mv[u] = k < parts_h ? __ldcg(p.part_m + at_) : -INFINITY;
-      lv[u] = k < parts_h ? __ldcg(p.part_l + at_) : 0.f;
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * blockDim.x + threadIdx.x;
+        mv[u] = i < n4 ? __ldcg(m4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        lv[u] = i < n4 ? __ldcg(l4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * blockDim.x + threadIdx.x;
+        if (i < n4) {
+          reinterpret_cast<float4*>(wgt)[i] = mv[u];
+          reinterpret_cast<float4*>(lsum)[i] = lv[u];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G8; g += W) {
+    if (g >= p.group) {  // padding group rows: weight 0 (read by the float4 loads below)
+      for (int k = lane; k < parts_h; k += 32) wgt[k * G8 + g] = 0.f;
+      continue;
     }
     float mx = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < kLaneParts; ++u) mx = fmaxf(mx, mv[u]);
+    for (int k = lane; k < parts_h; k += 32) mx = fmaxf(mx, wgt[k * G8 + g]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     const float ref = mx == -INFINITY ? 0.f : mx;
     float sum = 0.f;
-#pragma unroll
-    for (int u = 0; u < kLaneParts; ++u) {
-      const int k = lane + 32 * u;
-      const float w = mv[u] == -INFINITY ? 0.f : fexp(mv[u] - ref);
-      if (k < parts_h) wgt[k * G8 + g] = w;
-      sum += w == 0.f ? 0.f : w * lv[u];
+    for (int k = lane; k < parts_h; k += 32) {
+      const float mk = wgt[k * G8 + g];
+      const float w = mk == -INFINITY ? 0.f : fexp(mk - ref);
+      wgt[k * G8 + g] = w;
+      sum += w == 0.f ? 0.f : w * lsum[k * G8 + g];
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     if (lane == 0) den[g] = sum;
-  }
-  // Weights of the padding group rows (read by the float4 loads below, unused).
-  for (int i = threadIdx.x; i < parts_h * (G8 - p.group); i += blockDim.x) {
-    const int k = i / (G8 - p.group), g = p.group + (i - k * (G8 - p.group));
-    wgt[k * G8 + g] = 0.f;
   }
   __syncthreads();
   auto add_part = [&](float4& acc, int k, int g0, const float4& v) {
