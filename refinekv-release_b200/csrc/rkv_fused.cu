@@ -935,31 +935,41 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
   {
     float* st_m = reinterpret_cast<float*>(smem);      // [W][G8]
     float* st_l = st_m + W * G8;                       // [W][G8]
-    float* st_w = st_l + W * G8;                       // [W][G8] merge weights
-    float* st_o = st_w + W * G8;                       // [W][G8][kStashStride]
+    float* st_o = st_l + W * G8;                       // [W][G8][kStashStride]
     stash_padded<D, NT>(st_m, st_l, st_o, warp, lane, m, l, o);
     __syncthreads();
-    if (threadIdx.x < G8) {  // per group row: the part's max, weights, sum
-      const int g = threadIdx.x;
-      float top = -INFINITY;
-      for (int w = 0; w < W; ++w) top = fmaxf(top, st_m[w * G8 + g]);
-      const float ref = top == -INFINITY ? 0.f : top;
+    // All of a thread's outputs share one group row (the block is a multiple
+    // of G8 threads): its warps' weights exp(m - max m), once.
+    const int g = threadIdx.x % G8;
+    float wts[8];
+    float top = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      if (w < W) top = fmaxf(top, st_m[w * G8 + g]);
+    }
+    const float ref = top == -INFINITY ? 0.f : top;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float mw = w < W ? st_m[w * G8 + g] : -INFINITY;
+      wts[w] = mw == -INFINITY ? 0.f : __expf(mw - ref);
+    }
+    if (threadIdx.x < G8) {  // the part's max and sum per group row
       float den = 0.f;
-      for (int w = 0; w < W; ++w) {
-        const float mw = st_m[w * G8 + g];
-        const float sw = mw == -INFINITY ? 0.f : __expf(mw - ref);
-        st_w[w * G8 + g] = sw;
-        den += sw * st_l[w * G8 + g];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        if (w < W) den += wts[w] * st_l[w * G8 + g];
       }
       p.part_m[static_cast<size_t>(c) * G8 + g] = top;
       p.part_l[static_cast<size_t>(c) * G8 + g] = den;
     }
-    __syncthreads();
     float* out_o = p.part_o + static_cast<size_t>(c) * G8 * D;
     for (int idx = threadIdx.x; idx < G8 * D; idx += blockDim.x) {
-      const int d = idx / G8, g = idx - d * G8;
+      const int d = idx / G8;
       float acc = 0.f;
-      for (int w = 0; w < W; ++w) acc += st_w[w * G8 + g] * st_o[(w * G8 + g) * kStashStride<D> + d];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        if (w < W) acc += wts[w] * st_o[(w * G8 + g) * kStashStride<D> + d];
+      }
       out_o[idx] = acc;  // o^T: [d][g]
     }
   }
