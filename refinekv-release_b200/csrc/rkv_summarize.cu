@@ -28,15 +28,6 @@
 namespace rkv {
 namespace {
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __low2float(p[i]);
-    f[2 * i + 1] = __high2float(p[i]);
-  }
-}
-
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   uint4 u;
   u.x = pack_bf16(f[0], f[1]);
@@ -46,16 +37,10 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
-// Eight consecutive channels (8 * v .. 8 * v + 7) of row r of a swizzled
-// tile: one 16-byte chunk of bf16, two of fp32.
+// Eight consecutive channels (8 * v .. 8 * v + 7) of row r of a swizzled fp32
+// tile (two 16-byte chunks).
 template <typename T>
 __device__ __forceinline__ void load8(const uint8_t* tile, int r, int v, int rows, float (&f)[8]);
-
-template <>
-__device__ __forceinline__ void load8<__nv_bfloat16>(const uint8_t* tile, int r, int v, int rows,
-                                                     float (&f)[8]) {
-  unpack8(*reinterpret_cast<const uint4*>(tile + swz(r, v, rows)), f);
-}
 
 template <>
 __device__ __forceinline__ void load8<float>(const uint8_t* tile, int r, int v, int rows,
