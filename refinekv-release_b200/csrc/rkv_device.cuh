@@ -158,6 +158,18 @@ __device__ __forceinline__ void tma_prefetch_tile(const CUtensorMap* map, int ro
   }
 }
 
+// The same for one page of a 4-D page map (all its rows).
+template <int D>
+__device__ __forceinline__ void tma_prefetch_page(const CUtensorMap* map, int head, int page) {
+#pragma unroll
+  for (int i = 0; i < D / 64; ++i) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(i * 64), "r"(0), "r"(head), "r"(page)
+                 : "memory");
+  }
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

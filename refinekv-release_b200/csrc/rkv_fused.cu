@@ -323,6 +323,14 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
       tma_prefetch_tile<D>(&maps.key_mean, (t_lo + warp) * T, h);
       tma_prefetch_tile<D>(&maps.ellipsoid, (t_lo + warp) * T, h);
     }
+    // So does the warp's first page when the anchor mask marks it -- a hint
+    // only: the mask is read again after the wait, and that read decides.
+    const int b_first = b_lo + warp;
+    if (p.anchor != nullptr && p.page_table == nullptr && b_first < b_hi &&
+        __ldcg(p.anchor + static_cast<size_t>(h) * p.blocks + b_first) != 0) {
+      tma_prefetch_page<D>(&maps.key_pages, h, b_first);
+      tma_prefetch_page<D>(&maps.value_pages, h, b_first);
+    }
   }
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&maps.key_mean);
