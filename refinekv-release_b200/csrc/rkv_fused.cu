@@ -6,8 +6,11 @@
 // contiguous ranges, and the grid never has more CTAs than SMs (unless every
 // row has a single part), so all parts of a row are resident together (the
 // host sizes it; one CTA per SM by shared memory).  A CTA:
+//   0. reads its row's anchor bytes once: its own blocks' anchor bits, and
+//      whether every block of the row is anchored (then no part of the row
+//      needs the selector statistics, and steps 1 and 3 are skipped);
 //   1. phase A: z and delta of every (group row, block) of its tiles from the
-//      key-mean and ellipsoid tiles (TMA, mma.sync), stored for phase B, and
+//      key-mean and ellipsoid tiles (TMA, mma.sync), kept for phase B, and
 //      one log-sum-exp partial per part; arrives at the row's barrier A;
 //   2. streams, without waiting, the pages whose attention is known before
 //      any decision: its anchored blocks (selected whatever the risk,
@@ -34,9 +37,11 @@ namespace rkv {
 namespace {
 
 // Shared-memory layout (also sized by the host): a TMA slice per warp, two
-// mbarriers per warp, row normalisers, per-tile bit masks and lists, and one
-// block list (anchored blocks, then the selected non-anchored ones).  The
-// warps' final partials, then the parts' (max, sum), are parked in the slices.
+// mbarriers per warp, row normalisers, flags, the warps' phase-A (max, sum)
+// pairs, per-tile bit masks and offsets, one block list (anchored blocks,
+// then the selected non-anchored ones) and, when they fit, the part's z,
+// delta and value norms.  The warps' final partials, then the row's parts'
+// weights, are parked in the slices.
 struct FusedLayout {
   size_t bars, norms, flags, lse, sel_bits, anc_bits, offsets, anc_off,
       anchored, zs, ds, vs, bytes;
@@ -391,7 +396,6 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
     }
   }
   const int prompt_h = p.seq.prompt(h, p.prompt_length);
-  const int n_stat = n_t;
   const int pool_head = p.page_table != nullptr ? h - p.seq.sequence(h) * p.seq.heads_per_seq : h;
   uint32_t uses_a = 0, uses_b = 0;  // completed waits per barrier (parity = uses & 1)
   bool aborted = false;
@@ -507,14 +511,14 @@ __global__ void __launch_bounds__(256, 1) fused_kernel(const __grid_constant__ F
         zm[nt][j] = cm[nt][j] = -INFINITY;
         zs[nt][j] = cs[nt][j] = 0.f;
       }
-    for (int k = warp; k < n_stat && !aborted; k += W) {
+    for (int k = warp; k < n_t && !aborted; k += W) {
       const int tile = t_lo + k;
       if (lane == 0) {
         fence_proxy_async();
         mbar_expect_tx(bar_a, 2 * kSel);
         tma_tile_hint<D>(slice, &maps.key_mean, bar_a, tile * T, h, T, policy);
         tma_tile_hint<D>(slice + kSel, &maps.ellipsoid, bar_a, tile * T, h, T, policy);
-        if (k + W < n_stat) {  // one stage per warp: warm L2 with the next tile meanwhile
+        if (k + W < n_t) {  // one stage per warp: warm L2 with the next tile meanwhile
           tma_prefetch_tile<D>(&maps.key_mean, (tile + W) * T, h);
           tma_prefetch_tile<D>(&maps.ellipsoid, (tile + W) * T, h);
         }
