@@ -191,3 +191,48 @@ def test_rows_anchored_throughout_skip_the_statistics():
     _close(out, plain.output, False)
     ref = ora.mixed_attention(q.cpu(), s_cpu, ks.cpu(), vs.cpu(), sel.cpu(), z)
     _close(out.cpu(), ref.to(torch.bfloat16), False)
+
+
+def test_ragged_batch_anchored_throughout():
+    """Rows of a ragged batch anchored on every real block skip the statistics;
+    their padding pages stay unselected (mask 0) and unread, and the result
+    matches the four-kernel decode and, per prompt, the oracle."""
+    from refinekv_b200 import build_summary_batch
+
+    heads, group, dim, block = 4, 4, 128, 32
+    lengths = [9000, 40000, 1234]
+    cfg = RefineKVConfig(eps=0.01)
+    layers = [synthetic.make_layer(50 + i, 0, heads, n, dim, block, device=DEV)
+              for i, n in enumerate(lengths)]
+    summary = build_summary_batch([d.keys for d in layers], [d.values for d in layers], cfg)
+    counts = summary.counts.repeat_interleave(heads, 0)
+    anchor = counts > 0                       # every real block of every row
+    anchor[heads + 1, 7] = False              # one row of the second prompt keeps a decision
+    q = torch.cat([synthetic.make_queries(50 + i, 0, 0, d.planted_mean, group)[0]
+                   for i, d in enumerate(layers)])
+    gen = torch.Generator(device=DEV).manual_seed(8)
+    ks = torch.randn(len(lengths) * heads, 3, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    vs = torch.randn(len(lengths) * heads, 3, dim, device=DEV, generator=gen).to(torch.bfloat16)
+    ws = {}
+    res = sparse_attention(q, summary, ks, vs, cfg, anchor_mask=anchor, workspace=ws,
+                           return_selected=True)
+    out, sel = res.output.clone(), res.selected.clone()
+    assert device_status(ws) == 0
+    assert not (sel & (counts == 0)).any()
+    assert bool((sel | (counts == 0)).sum(1)[[r for r in range(sel.shape[0]) if r != heads + 1]]
+                .eq(sel.shape[1]).all())
+    with unfused():
+        plain = sparse_attention(q, summary, ks, vs, cfg, anchor_mask=anchor, return_selected=True)
+    assert torch.equal(sel[:heads], plain.selected[:heads])
+    _close(out, plain.output, False)
+    for i, d in enumerate(layers):
+        rows = slice(i * heads, (i + 1) * heads)
+        nb = -(-lengths[i] // block)
+        s_cpu = ora.as_cpu_summary(build_summary(d.keys, d.values, cfg))
+        qi, ai = q[rows].cpu(), anchor[rows, :nb].cpu()
+        margin = ora.margin_blocks(qi, s_cpu, cfg.eps, cfg.gqa_reduction) & ~ai
+        want, z = ora.select_blocks(qi, s_cpu, cfg.eps, cfg.gqa_reduction)
+        want |= ai
+        assert not ((sel[rows, :nb].cpu() != want) & ~margin).any()
+        ref = ora.mixed_attention(qi, s_cpu, ks[rows].cpu(), vs[rows].cpu(), sel[rows, :nb].cpu(), z)
+        _close(out[rows].cpu(), ref.to(torch.bfloat16), False)
