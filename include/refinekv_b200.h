@@ -241,16 +241,17 @@ RKV_API size_t rkv_decode_workspace_size(int64_t heads, int64_t group, int64_t b
  *   output: (heads, group, head_dim) in query_dtype.
  *   selected: (heads, blocks) uint8 mask written by the call.
  *   phases: RKV_PHASE_ALL, or a subset for timing individual kernels (the
- *     phases must still run in order on the stream; with the fused selector
- *     STATS and FINAL go together, see rkv_decode_kernel_count).
- * The fused selector (the default for up to 480 KV-head rows) runs
- * heads x parts CTAs, at most one per SM, whose parts of a row wait for one
- * another at a bounded barrier.  Decode calls that run concurrently on
- * different streams of one GPU can keep each other's CTAs from becoming
- * resident; their barriers then give up after 1 s with RKV_DEVICE_TIMEOUT in
- * the status word.  Order such calls on one stream (one decode step of a
- * batch of sequences is one call: see the batched summary above), or switch
- * the fused selector off with rkv_set_fused_selector(0).
+ *     phases must still run in order on the stream); a subset always runs
+ *     the four-kernel form (stats, final, attention, combine).
+ * RKV_PHASE_ALL runs one kernel (the default for up to 480 KV-head rows,
+ * see rkv_decode_kernel_count): heads x parts CTAs, at most one per SM,
+ * whose parts of a row wait for one another at bounded barriers.  Decode
+ * calls that run concurrently on different streams of one GPU can keep each
+ * other's CTAs from becoming resident; their barriers then give up after 1 s
+ * with RKV_DEVICE_TIMEOUT in the status word.  Order such calls on one
+ * stream (one decode step of a batch of sequences is one call: see the
+ * batched summary above), or switch to the four-kernel form with
+ * rkv_set_fused_selector(0).
  */
 RKV_API int rkv_decode(const rkv_summary* summary, const void* query, int query_dtype, int64_t group,
                const void* key_suffix, const void* value_suffix, int64_t suffix_capacity,
@@ -330,23 +331,23 @@ RKV_API int rkv_decode_dense(const rkv_summary* pages, const void* query, int qu
                              int64_t suffix_length_host, void* output, void* workspace,
                              size_t workspace_size, void* stream);
 
-/* Kernel launches one rkv_decode call makes for the given phases on the
- * two-kernel selector path (4 for RKV_PHASE_ALL). */
+/* Kernel launches one rkv_decode call makes for the given phases in the
+ * four-kernel form (4 for RKV_PHASE_ALL). */
 RKV_API int rkv_decode_launch_count(unsigned phases);
 
 /*
  * Kernel launches of one rkv_decode call (RKV_PHASE_ALL) for this geometry on
- * the current device: 3 when the fused selector runs (one kernel for phases
- * STATS and FINAL that also attends the anchored pages; then attention and
- * combine), else 4; 0 for an unsupported geometry.  With the fused selector,
- * RKV_PHASE_STATS and RKV_PHASE_FINAL must be requested together.
+ * the current device: 1 when the one-kernel decode runs (selector, every
+ * page, the representatives and the combine in one launch), else 4 (stats,
+ * final, attention, combine); 0 for an unsupported geometry.
  */
 RKV_API int rkv_decode_kernel_count(int64_t heads, int64_t group, int64_t blocks,
                                     int64_t head_dim, int64_t block_size);
 
 /*
- * Process-wide switch of rkv_decode's fused selector (on by default).  With 0,
- * rkv_decode runs the two selector kernels (stats, final) and the attention
+ * Process-wide switch of rkv_decode's one-kernel form (on by default; the
+ * name is kept from when only the selector was fused).  With 0, rkv_decode
+ * runs four kernels (stats, final, attention, combine) and the attention
  * kernel streams every selected page, anchored or not -- for measurement and
  * cross-checks; the results agree within the summation-order tolerance.
  * Set it before planning a workspace: workspace sizes depend on it.  No
